@@ -1,0 +1,181 @@
+/*
+ * prana_cuda.h -- C ABI of the B200 (sm_100a) decode path for Prana.
+ *
+ * Plain pointers and sizes only.  Kernel-level entry points take DEVICE
+ * pointers and run on the context's stream; model-level entry points take HOST
+ * buffers for token ids and logits.  Every function returns 0 on success or a
+ * negative PRANA_E_* code; prana_last_error() gives a message for the calling
+ * thread (the null-on-failure / last-error convention of Prana's FFI layer,
+ * crates/prana-cactus/src/mock.rs:8-12).  No exception crosses the ABI.
+ *
+ * Each kernel entry point names the prana-kernels / prana-model function it
+ * replaces (file:line in the Prana workspace).  Calls on one context are not
+ * thread-safe; calls on different contexts are.
+ */
+#ifndef PRANA_CUDA_H
+#define PRANA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PRANA_OK 0
+#define PRANA_E_INVALID -1     /* bad argument, shape or layout (the reference asserts) */
+#define PRANA_E_CUDA -2        /* CUDA runtime / launch failure */
+#define PRANA_E_OOM -3         /* device or host allocation failed */
+#define PRANA_E_FORMAT -4      /* malformed GGUF (gguf.rs io::Error cases) */
+#define PRANA_E_UNSUPPORTED -5 /* valid input outside what this build implements */
+#define PRANA_E_TIMEOUT -6     /* a bounded device-side wait expired */
+#define PRANA_E_COMM -7        /* collective / peer setup failed */
+
+/* ggml tensor type ids (crates/prana-model/src/gguf.rs:33-38) */
+#define PRANA_TYPE_F32 0
+#define PRANA_TYPE_F16 1
+#define PRANA_TYPE_Q4_0 2
+#define PRANA_TYPE_Q8_0 8
+#define PRANA_TYPE_Q4_K 12
+#define PRANA_TYPE_Q6_K 14
+
+typedef struct prana_ctx prana_ctx;
+typedef struct prana_weight prana_weight;
+typedef struct prana_model prana_model;
+typedef struct prana_kv prana_kv;
+
+const char *prana_last_error(void);
+int prana_version(void);
+
+/* ---------------------------------------------------------------- context */
+int prana_ctx_create(int device, prana_ctx **out);
+int prana_ctx_destroy(prana_ctx *ctx); /* idempotent on NULL */
+/* run kernel-level calls on a caller-owned cudaStream_t (NULL = the context's own
+ * stream; pass cudaStreamLegacy, 0x1, for the legacy default stream) */
+int prana_ctx_set_stream(prana_ctx *ctx, void *cuda_stream);
+int prana_ctx_synchronize(prana_ctx *ctx);
+/* the context's own stream (model-level work always runs there), for event timing */
+int prana_ctx_stream(prana_ctx *ctx, void **cuda_stream);
+
+/* ---------------------------------------------------------------- weights
+ * Upload one [rows, cols] tensor given in its GGUF byte layout and repack it
+ * for 128-bit loads (replaces QuantMatrix::from_parts, matmul.rs:34-39, and
+ * KQuantMatrix::from_raw, kquant.rs:166-183).  F16 tensors are widened to F32
+ * (gguf.rs:208-267).  Q8_0/Q4_0 need cols % 32 == 0, Q4_K/Q6_K cols % 256 == 0. */
+int prana_weight_upload(prana_ctx *ctx, int ggml_type, size_t rows, size_t cols, const void *host_bytes,
+                        prana_weight **out);
+int prana_weight_free(prana_weight *w);
+/* device bytes the packed matrix occupies */
+int prana_weight_bytes(const prana_weight *w, size_t *bytes);
+
+/* ---------------------------------------------------------------- kernels (device pointers)
+ * quantize_acts (matmul.rs:105-127): per 32-group int8, f32 scale, i32 sum; rows of k values. */
+int prana_quantize_acts(prana_ctx *ctx, const float *x, size_t rows, size_t k, int8_t *q, float *scales,
+                        int32_t *sums);
+/* matmul_q8_f32 (matmul.rs:162-178) and matmul_kquant_f32 (kquant.rs:323-333):
+ * out[t, r] = row r of W . quantize_acts(a[t]); a is [n_tokens, cols]. */
+int prana_matmul_q8_f32(prana_ctx *ctx, const float *a, const prana_weight *w, size_t n_tokens, float *out);
+int prana_matmul_kquant_f32(prana_ctx *ctx, const float *a, const prana_weight *w, size_t n_tokens, float *out);
+/* matmul_q8_prefill (matmul.rs:185-187) / matmul_kquant_prefill (kquant.rs:368-370):
+ * already-quantized activation rows; out [n_tokens, rows]. */
+int prana_matmul_q8_prefill(prana_ctx *ctx, const int8_t *q, const float *scales, const int32_t *sums,
+                            size_t n_tokens, const prana_weight *w, float *out);
+int prana_matmul_kquant_prefill(prana_ctx *ctx, const int8_t *q, const float *scales, const int32_t *sums,
+                                size_t n_tokens, const prana_weight *w, float *out);
+/* matmul_f32 (matmul.rs:150-156) for F32 weights */
+int prana_matmul_f32(prana_ctx *ctx, const float *a, const prana_weight *w, size_t n_tokens, float *out);
+/* Per-block int32 dots of weight row `row` against one quantized activation row:
+ * the bit-exact quantities of dot_q8_q8_scalar (matmul.rs:395-406), dot_q40_q8_scalar
+ * (kquant.rs:240-252, value s - 8*sum), dot_q4k_q8_scalar (kquant.rs:257-282, s1/s2 per
+ * 32-group) and dot_q6k_q8_scalar (kquant.rs:287-318, one per 16-element sub-block). */
+int prana_block_dots(prana_ctx *ctx, const prana_weight *w, size_t row, const int8_t *q, const int32_t *sums,
+                     int32_t *out);
+
+/* rmsnorm (norms.rs:9-23) */
+int prana_rmsnorm(prana_ctx *ctx, const float *x, const float *weight, size_t rows, size_t dim, float eps,
+                  float *out);
+/* silu in place (norms.rs:27-31) and the SwiGLU gate product g = silu(g) * u (infer.rs:193-199) */
+int prana_silu(prana_ctx *ctx, float *x, size_t n);
+int prana_silu_mul(prana_ctx *ctx, float *gate, const float *up, size_t n);
+/* softmax over each of `rows` rows of n (norms.rs:44-56) */
+int prana_softmax(prana_ctx *ctx, const float *x, size_t rows, size_t n, float *out);
+/* rope_interleaved (attention.rs:90-101) / rope_neox (attention.rs:107-121) in place on
+ * `rows` rows of n values; row i is at position pos + i. */
+int prana_rope_interleaved(prana_ctx *ctx, float *x, size_t rows, size_t n, size_t pos, size_t head_dim,
+                           float theta);
+int prana_rope_neox(prana_ctx *ctx, float *x, size_t rows, size_t n, size_t pos, size_t head_dim, float theta);
+/* f16_kv_write (attention.rs:47-52): cache is f16 bits [capacity, kv_stride] */
+int prana_f16_kv_write(prana_ctx *ctx, uint16_t *cache, size_t first_row, size_t kv_stride, const float *src,
+                       size_t n);
+/* attention_decode (attention.rs:129-160) */
+int prana_attention_decode(prana_ctx *ctx, const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                           size_t pos, size_t n_heads, size_t n_kv_heads, size_t head_dim, float *out);
+/* attention_verify (attention.rs:296-333) */
+int prana_attention_verify(prana_ctx *ctx, const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                           size_t pos0, size_t seq, size_t n_heads, size_t n_kv_heads, size_t head_dim,
+                           float *out);
+/* attention (attention.rs:236-284): causal over f32 in-window K/V */
+int prana_attention(prana_ctx *ctx, const float *q, const float *k, const float *v, size_t seq, size_t n_heads,
+                    size_t n_kv_heads, size_t head_dim, float *out);
+/* first index of the row maximum (infer.rs:560-568, sampler.rs:40-48) */
+int prana_argmax(prana_ctx *ctx, const float *x, size_t rows, size_t n, uint32_t *out);
+
+/* ---------------------------------------------------------------- model (host buffers) */
+typedef struct prana_model_config {
+  int64_t dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len, head_dim;
+  float rope_theta, norm_eps;
+  int32_t rope_neox, has_bias, shared_classifier;
+  int64_t weight_bytes; /* device bytes of all packed projection/embedding weights */
+} prana_model_config;
+
+/* gguf::load (gguf.rs:338-460) for llama / qwen2 into the device arena */
+int prana_model_load_gguf(prana_ctx *ctx, const char *path, prana_model **out);
+int prana_model_free(prana_model *m); /* also frees the model's remaining KV caches */
+int prana_model_config_get(const prana_model *m, prana_model_config *out);
+/* KvCache::with_len (infer.rs:37-45): f16 K/V for `positions` rows per layer */
+int prana_kv_create(prana_model *m, size_t positions, prana_kv **out);
+int prana_kv_free(prana_kv *kv); /* only while its model is alive */
+/* copy one layer's K or V cache rows [0, rows) to host (f16 bits) */
+int prana_kv_read(prana_kv *kv, size_t layer, int is_v, size_t rows, uint16_t *host_out);
+
+/* overwrite one layer's K or V cache rows [0, rows) from host f16 bits */
+int prana_kv_write(prana_kv *kv, size_t layer, int is_v, size_t rows, const uint16_t *host_in);
+
+/* forward / forward_impl (infer.rs:134-211): one token at `pos`; writes the logits
+ * (host, may be NULL) and their argmax (may be NULL).  Runs as one CUDA graph whose
+ * only host traffic is the (token, pos) pair in and the sampled id out. */
+int prana_forward(prana_model *m, prana_kv *kv, uint32_t token, size_t pos, float *logits, uint32_t *next_token);
+/* Diagnostic form of prana_forward (the role PRANA_TIMING plays in infer.rs:83-130):
+ * one token, run eagerly, additionally returning every int8 activation row the pass
+ * quantized, in CPU-path order -- per layer the attention-norm input (dim), the
+ * attention output (n_heads*head_dim), the ffn-norm input (dim) and silu(gate)*up
+ * (hidden); then the final-norm input (dim) -- with their per-32 scales. */
+int prana_forward_trace(prana_model *m, prana_kv *kv, uint32_t token, size_t pos, float *logits, int8_t *q_out,
+                        float *scales_out, size_t capacity, size_t *n_out);
+/* prefill (infer.rs:220-286): tokens at positions 0..n, no logits */
+int prana_prefill(prana_model *m, prana_kv *kv, const uint32_t *tokens, size_t n);
+/* forward_batch (infer.rs:296-374): n tokens at pos0.., logits [n, vocab] (may be NULL)
+ * and per-row argmax (may be NULL) */
+int prana_forward_batch(prana_model *m, prana_kv *kv, const uint32_t *tokens, size_t n, size_t pos0,
+                        float *logits, uint32_t *argmax);
+/* generate (infer.rs:696-771), greedy, over token ids; stop_id < 0 disables stopping.
+ * out must hold `steps` ids; *n_out receives the count. */
+int prana_generate(prana_model *m, const uint32_t *prompt, size_t p, size_t steps, int64_t stop_id,
+                   uint32_t *out, size_t *n_out);
+/* generate_speculative (infer.rs:581-690), greedy; stats[0] = proposed, stats[1] = accepted */
+int prana_generate_speculative(prana_model *target, prana_model *draft, const uint32_t *prompt, size_t p,
+                               size_t steps, size_t k, int64_t stop_id, uint32_t *out, size_t *n_out,
+                               size_t *stats);
+
+/* Device-resident decode loop for throughput measurement: after
+ * prana_decode_begin(token, pos), each prana_decode_run(n) replays the per-token
+ * graph n times back to back (token fed back on device, no host round trip) and
+ * prana_decode_tokens copies the ids produced so far. */
+int prana_decode_begin(prana_model *m, prana_kv *kv, uint32_t token, size_t pos);
+int prana_decode_run(prana_model *m, prana_kv *kv, size_t n_steps);
+int prana_decode_tokens(prana_model *m, prana_kv *kv, uint32_t *out, size_t max, size_t *n_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

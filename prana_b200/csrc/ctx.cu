@@ -1,0 +1,553 @@
+// ctx.cu -- context, error reporting, weight upload/repack and the
+// kernel-level C-ABI entry points (the prana-kernels function surface).
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+
+#include "host.h"
+
+namespace prana {
+
+static thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int ctx_scratch(prana_ctx* ctx, size_t bytes, void** out) {
+  bytes = (bytes + 255) & ~(size_t)255;
+  if (ctx->scratch.bytes < bytes) {
+    if (ctx->scratch.base) {
+      PRANA_CK(cudaStreamSynchronize(ctx->stream));
+      cudaFree(ctx->scratch.base);
+      ctx->scratch.base = nullptr;
+      ctx->scratch.bytes = 0;
+    }
+    size_t want = bytes < ((size_t)16 << 20) ? ((size_t)16 << 20) : bytes;
+    if (cudaMalloc(&ctx->scratch.base, want) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(PRANA_E_OOM, "scratch allocation of %zu bytes failed", want);
+    }
+    ctx->scratch.bytes = want;
+  }
+  *out = ctx->scratch.base;
+  return PRANA_OK;
+}
+
+static uint32_t f32_bits(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+
+int ctx_rope(prana_ctx* ctx, int hd, float theta, int neox, int positions, const RopeTable** out) {
+  auto key = std::make_tuple(hd, f32_bits(theta), neox);
+  RopeTable& t = ctx->rope[key];
+  if (t.positions < positions) {
+    const int n = positions < 256 ? 256 : positions;
+    const int half = hd / 2;
+    std::vector<float> c((size_t)n * half), s((size_t)n * half);
+    for (int p = 0; p < n; p++)
+      for (int i = 0; i < half; i++) {
+        // interleaved: pair (2i, 2i+1), freq = theta^(-(2i)/hd)   (attention.rs:96)
+        // neox:        pair (i, i+hd/2), freq = theta^(-(2*i)/hd) (attention.rs:114)
+        const float freq = neox ? powf(theta, -(2.0f * (float)i) / (float)hd)
+                                : powf(theta, -((float)(2 * i)) / (float)hd);
+        const float ang = (float)p * freq;
+        c[(size_t)p * half + i] = cosf(ang);
+        s[(size_t)p * half + i] = sinf(ang);
+      }
+    if (t.cos) {
+      ctx->retired.push_back(t.cos);
+      ctx->retired.push_back(t.sin);
+      t.cos = t.sin = nullptr;
+      t.positions = 0;
+    }
+    PRANA_CK(cudaMalloc(&t.cos, c.size() * 4));
+    PRANA_CK(cudaMalloc(&t.sin, s.size() * 4));
+    PRANA_CK(cudaMemcpy(t.cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+    PRANA_CK(cudaMemcpy(t.sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+    t.positions = n;
+  }
+  *out = &t;
+  return PRANA_OK;
+}
+
+static float h2f_host(uint16_t h) {
+  const uint32_t sign = (h >> 15) & 1u, exp = (h >> 10) & 0x1fu, frac = h & 0x3ffu;
+  uint32_t bits;
+  if (exp == 0 && frac == 0) bits = sign << 31;
+  else if (exp == 0) {
+    const float v = (float)frac * 5.9604644775390625e-08f;
+    return sign ? -v : v;
+  } else if (exp == 0x1f) bits = (sign << 31) | 0x7f800000u | (frac << 13);
+  else bits = (sign << 31) | ((exp + 112u) << 23) | (frac << 13);
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+static size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Split GGUF blocks into the planes the GEMV streams (see common.cuh DevWeight).
+int upload_weight(prana_ctx* ctx, int type, size_t rows, size_t cols, const void* host, prana_weight* w) {
+  if (!rows || !cols) return fail(PRANA_E_INVALID, "empty weight [%zu, %zu]", rows, cols);
+  if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX) return fail(PRANA_E_INVALID, "weight too large");
+  const uint8_t* src = static_cast<const uint8_t*>(host);
+  const size_t n = rows * cols;
+  size_t off[4] = {0, 0, 0, 0}, total = 0;
+  std::vector<uint8_t> buf;
+  switch (type) {
+    case T_Q8_0: {
+      if (cols % 32) return fail(PRANA_E_INVALID, "Q8_0 needs cols %% 32 == 0 (cols=%zu)", cols);
+      off[1] = al256(n);
+      total = off[1] + al256(n / 32 * 2);
+      buf.resize(total);
+      int8_t* q = reinterpret_cast<int8_t*>(buf.data());
+      uint16_t* d = reinterpret_cast<uint16_t*>(buf.data() + off[1]);
+      for (size_t b = 0; b < n / 32; b++) {
+        memcpy(&d[b], src + b * 34, 2);
+        memcpy(q + b * 32, src + b * 34 + 2, 32);
+      }
+      break;
+    }
+    case T_Q4_0: {
+      if (cols % 32) return fail(PRANA_E_INVALID, "Q4_0 needs cols %% 32 == 0 (cols=%zu)", cols);
+      off[1] = al256(n / 2);
+      total = off[1] + al256(n / 32 * 2);
+      buf.resize(total);
+      uint16_t* d = reinterpret_cast<uint16_t*>(buf.data() + off[1]);
+      for (size_t b = 0; b < n / 32; b++) {
+        memcpy(&d[b], src + b * 18, 2);
+        memcpy(buf.data() + b * 16, src + b * 18 + 2, 16);
+      }
+      break;
+    }
+    case T_Q4_K: {
+      if (cols % 256) return fail(PRANA_E_INVALID, "Q4_K needs cols %% 256 == 0 (cols=%zu)", cols);
+      total = al256(n / 256 * 144);
+      buf.assign(src, src + n / 256 * 144);
+      buf.resize(total);
+      break;
+    }
+    case T_Q6_K: {
+      if (cols % 256) return fail(PRANA_E_INVALID, "Q6_K needs cols %% 256 == 0 (cols=%zu)", cols);
+      const size_t nb = n / 256;
+      off[1] = al256(n / 2);
+      off[2] = off[1] + al256(n / 4);
+      off[3] = off[2] + al256(n / 16);
+      total = off[3] + al256(nb * 2);
+      buf.resize(total);
+      for (size_t b = 0; b < nb; b++) {
+        const uint8_t* blk = src + b * 210;
+        memcpy(buf.data() + b * 128, blk, 128);
+        memcpy(buf.data() + off[1] + b * 64, blk + 128, 64);
+        memcpy(buf.data() + off[2] + b * 16, blk + 192, 16);
+        memcpy(buf.data() + off[3] + b * 2, blk + 208, 2);
+      }
+      break;
+    }
+    case T_F32:
+    case T_F16: {
+      total = al256(n * 4);
+      buf.resize(total);
+      float* f = reinterpret_cast<float*>(buf.data());
+      if (type == T_F32) memcpy(f, src, n * 4);
+      else
+        for (size_t i = 0; i < n; i++) {
+          uint16_t h;
+          memcpy(&h, src + 2 * i, 2);
+          f[i] = h2f_host(h);
+        }
+      type = T_F32;
+      break;
+    }
+    default:
+      return fail(PRANA_E_UNSUPPORTED, "ggml type %d is not supported", type);
+  }
+  void* mem = nullptr;
+  if (cudaMalloc(&mem, total) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(PRANA_E_OOM, "device allocation of %zu bytes failed", total);
+  }
+  if (cudaMemcpy(mem, buf.data(), total, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(mem);
+    return fail(PRANA_E_CUDA, "weight upload failed");
+  }
+  uint8_t* base = static_cast<uint8_t*>(mem);
+  DevWeight dw{};
+  dw.type = type;
+  dw.rows = (int)rows;
+  dw.cols = (int)cols;
+  switch (type) {
+    case T_Q8_0:
+    case T_Q4_0:
+      dw.qs = base;
+      dw.d = reinterpret_cast<const __half*>(base + off[1]);
+      break;
+    case T_Q4_K:
+      dw.qs = base;
+      break;
+    case T_Q6_K:
+      dw.qs = base;
+      dw.qh = base + off[1];
+      dw.sc = reinterpret_cast<const int8_t*>(base + off[2]);
+      dw.d = reinterpret_cast<const __half*>(base + off[3]);
+      break;
+    default:
+      dw.f32 = reinterpret_cast<const float*>(base);
+  }
+  w->ctx = ctx;
+  w->dw = dw;
+  w->mem = mem;
+  w->bytes = total;
+  return PRANA_OK;
+}
+
+void free_weight(prana_weight* w) {
+  if (w && w->mem) {
+    cudaFree(w->mem);
+    w->mem = nullptr;
+  }
+}
+
+}  // namespace prana
+
+using namespace prana;
+
+#define API_BEGIN try {
+#define API_END                                                    \
+  }                                                                \
+  catch (const std::bad_alloc&) {                                  \
+    return fail(PRANA_E_OOM, "host allocation failed");            \
+  }                                                                \
+  catch (...) {                                                    \
+    return fail(PRANA_E_INVALID, "unexpected host exception");     \
+  }
+
+#define NEED(cond, ...) \
+  if (!(cond)) return fail(PRANA_E_INVALID, __VA_ARGS__)
+
+extern "C" {
+
+const char* prana_last_error(void) { return g_last_error.c_str(); }
+int prana_version(void) { return 1; }
+
+int prana_ctx_create(int device, prana_ctx** out) {
+  API_BEGIN
+  NEED(out, "out is null");
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return fail(PRANA_E_CUDA, "no CUDA device available");
+  }
+  NEED(device >= 0 && device < n, "device %d out of range (%d devices)", device, n);
+  DevScope ds(device);
+  PRANA_CK(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  PRANA_CK(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) return fail(PRANA_E_UNSUPPORTED, "built for sm_100a; device is sm_%d%d", prop.major, prop.minor);
+  prana_ctx* c = new prana_ctx();
+  c->device = device;
+  c->sm_count = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&c->counters, 4096 * sizeof(unsigned)) != cudaSuccess ||
+      cudaMemset(c->counters, 0, 4096 * sizeof(unsigned)) != cudaSuccess) {
+    cudaGetLastError();
+    delete c;
+    return fail(PRANA_E_CUDA, "context setup failed");
+  }
+  c->stream = c->own;
+  *out = c;
+  return PRANA_OK;
+  API_END
+}
+
+int prana_ctx_destroy(prana_ctx* c) {
+  if (!c) return PRANA_OK;
+  DevScope ds(c->device);
+  cudaStreamSynchronize(c->stream);
+  for (auto& kv : c->rope) {
+    cudaFree(kv.second.cos);
+    cudaFree(kv.second.sin);
+  }
+  for (void* p : c->retired) cudaFree(p);
+  cudaFree(c->scratch.base);
+  cudaFree(c->counters);
+  cudaStreamDestroy(c->own);
+  delete c;
+  return PRANA_OK;
+}
+
+int prana_ctx_set_stream(prana_ctx* c, void* stream) {
+  NEED(c, "ctx is null");
+  c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own;
+  return PRANA_OK;
+}
+
+int prana_ctx_stream(prana_ctx* c, void** stream) {
+  NEED(c && stream, "null argument");
+  *stream = c->own;
+  return PRANA_OK;
+}
+
+int prana_ctx_synchronize(prana_ctx* c) {
+  NEED(c, "ctx is null");
+  DevScope ds(c->device);
+  PRANA_CK(cudaStreamSynchronize(c->stream));
+  return PRANA_OK;
+}
+
+int prana_weight_upload(prana_ctx* c, int type, size_t rows, size_t cols, const void* host, prana_weight** out) {
+  API_BEGIN
+  NEED(c && host && out, "null argument");
+  *out = nullptr;
+  DevScope ds(c->device);
+  prana_weight* w = new prana_weight();
+  int rc = upload_weight(c, type, rows, cols, host, w);
+  if (rc) {
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return PRANA_OK;
+  API_END
+}
+
+int prana_weight_free(prana_weight* w) {
+  if (!w) return PRANA_OK;
+  DevScope ds(w->ctx->device);
+  free_weight(w);
+  delete w;
+  return PRANA_OK;
+}
+
+int prana_weight_bytes(const prana_weight* w, size_t* bytes) {
+  NEED(w && bytes, "null argument");
+  *bytes = w->bytes;
+  return PRANA_OK;
+}
+
+int prana_quantize_acts(prana_ctx* c, const float* x, size_t rows, size_t k, int8_t* q, float* s, int32_t* sum) {
+  NEED(c && x && q && s && sum, "null argument");
+  NEED(k % 32 == 0, "k must be a multiple of 32 (k=%zu)", k);
+  if (!rows || !k) return PRANA_OK;
+  DevScope ds(c->device);
+  PRANA_CK(launch_quantize_acts(x, (int)rows, (int)k, q, s, sum, c->stream));
+  return PRANA_OK;
+}
+
+static int matmul_common(prana_ctx* c, const prana_weight* w, const float* a, const int8_t* q, const float* s,
+                         const int32_t* sum, size_t n_tokens, float* out) {
+  DevScope ds(c->device);
+  for (size_t t0 = 0; t0 < n_tokens; t0 += 8) {
+    const int m = (int)(n_tokens - t0 < 8 ? n_tokens - t0 : 8);
+    GemvArgs g{};
+    g.w = w->dw;
+    g.m = m;
+    const size_t K = (size_t)w->dw.cols, G = K / 32;
+    if (a) g.x = a + t0 * K;
+    if (q) {
+      g.aq = q + t0 * K;
+      g.as = s + t0 * G;
+      g.asum = sum + t0 * G;
+    }
+    g.out = out + t0 * w->dw.rows;
+    PRANA_CK(launch_gemv(g, a ? PRO_F32 : PRO_Q, EPI_STORE, c->stream, false));
+  }
+  return PRANA_OK;
+}
+
+int prana_matmul_q8_f32(prana_ctx* c, const float* a, const prana_weight* w, size_t n_tokens, float* out) {
+  NEED(c && a && w && out, "null argument");
+  NEED(w->dw.type == T_Q8_0, "matmul_q8_f32 needs a Q8_0 weight (type %d)", w->dw.type);
+  return matmul_common(c, w, a, nullptr, nullptr, nullptr, n_tokens, out);
+}
+
+int prana_matmul_kquant_f32(prana_ctx* c, const float* a, const prana_weight* w, size_t n_tokens, float* out) {
+  NEED(c && a && w && out, "null argument");
+  NEED(w->dw.type == T_Q4_0 || w->dw.type == T_Q4_K || w->dw.type == T_Q6_K,
+       "matmul_kquant_f32 needs a Q4_0/Q4_K/Q6_K weight (type %d)", w->dw.type);
+  return matmul_common(c, w, a, nullptr, nullptr, nullptr, n_tokens, out);
+}
+
+int prana_matmul_q8_prefill(prana_ctx* c, const int8_t* q, const float* s, const int32_t* sum, size_t n_tokens,
+                            const prana_weight* w, float* out) {
+  NEED(c && q && s && sum && w && out, "null argument");
+  NEED(w->dw.type == T_Q8_0, "matmul_q8_prefill needs a Q8_0 weight");
+  return matmul_common(c, w, nullptr, q, s, sum, n_tokens, out);
+}
+
+int prana_matmul_kquant_prefill(prana_ctx* c, const int8_t* q, const float* s, const int32_t* sum, size_t n_tokens,
+                                const prana_weight* w, float* out) {
+  NEED(c && q && s && sum && w && out, "null argument");
+  NEED(w->dw.type == T_Q4_0 || w->dw.type == T_Q4_K || w->dw.type == T_Q6_K,
+       "matmul_kquant_prefill needs a Q4_0/Q4_K/Q6_K weight");
+  return matmul_common(c, w, nullptr, q, s, sum, n_tokens, out);
+}
+
+int prana_matmul_f32(prana_ctx* c, const float* a, const prana_weight* w, size_t n_tokens, float* out) {
+  NEED(c && a && w && out, "null argument");
+  NEED(w->dw.type == T_F32, "matmul_f32 needs an F32 weight");
+  NEED((size_t)w->dw.cols * 8 * 4 <= 200 * 1024, "matmul_f32: cols too large for shared staging");
+  return matmul_common(c, w, a, nullptr, nullptr, nullptr, n_tokens, out);
+}
+
+int prana_block_dots(prana_ctx* c, const prana_weight* w, size_t row, const int8_t* q, const int32_t* sum,
+                     int32_t* out) {
+  NEED(c && w && q && sum && out, "null argument");
+  NEED(row < (size_t)w->dw.rows, "row %zu out of range", row);
+  NEED(w->dw.type != T_F32, "block dots need a quantized weight");
+  DevScope ds(c->device);
+  PRANA_CK(launch_block_dots(w->dw, (int)row, q, sum, out, c->stream));
+  return PRANA_OK;
+}
+
+int prana_rmsnorm(prana_ctx* c, const float* x, const float* w, size_t rows, size_t dim, float eps, float* out) {
+  NEED(c && x && w && out, "null argument");
+  if (!rows) return PRANA_OK;
+  DevScope ds(c->device);
+  PRANA_CK(launch_rmsnorm(x, w, (int)rows, (int)dim, eps, out, c->stream));
+  return PRANA_OK;
+}
+
+int prana_silu(prana_ctx* c, float* x, size_t n) {
+  NEED(c && x, "null argument");
+  if (!n) return PRANA_OK;
+  DevScope ds(c->device);
+  PRANA_CK(launch_silu(x, n, c->stream));
+  return PRANA_OK;
+}
+
+int prana_silu_mul(prana_ctx* c, float* g, const float* u, size_t n) {
+  NEED(c && g && u, "null argument");
+  if (!n) return PRANA_OK;
+  DevScope ds(c->device);
+  PRANA_CK(launch_silu_mul(g, u, n, c->stream));
+  return PRANA_OK;
+}
+
+int prana_softmax(prana_ctx* c, const float* x, size_t rows, size_t n, float* out) {
+  NEED(c && x && out, "null argument");
+  if (!rows || !n) return PRANA_OK;
+  DevScope ds(c->device);
+  PRANA_CK(launch_softmax(x, (int)rows, (int)n, out, c->stream));
+  return PRANA_OK;
+}
+
+static int rope_common(prana_ctx* c, float* x, size_t rows, size_t n, size_t pos, size_t hd, float theta, int neox) {
+  NEED(c && x, "null argument");
+  NEED(hd % 2 == 0, "head_dim must be even for RoPE");
+  NEED(hd && n % hd == 0, "row must be a whole number of heads");
+  if (!rows || !n) return PRANA_OK;
+  DevScope ds(c->device);
+  const RopeTable* t;
+  int rc = ctx_rope(c, (int)hd, theta, neox, (int)(pos + rows), &t);
+  if (rc) return rc;
+  PRANA_CK(launch_rope(x, (int)rows, (int)n, (int)pos, (int)hd, neox, t->cos, t->sin, c->stream));
+  return PRANA_OK;
+}
+
+int prana_rope_interleaved(prana_ctx* c, float* x, size_t rows, size_t n, size_t pos, size_t hd, float theta) {
+  return rope_common(c, x, rows, n, pos, hd, theta, 0);
+}
+int prana_rope_neox(prana_ctx* c, float* x, size_t rows, size_t n, size_t pos, size_t hd, float theta) {
+  return rope_common(c, x, rows, n, pos, hd, theta, 1);
+}
+
+int prana_f16_kv_write(prana_ctx* c, uint16_t* cache, size_t first_row, size_t kv_stride, const float* src, size_t n) {
+  NEED(c && cache && src, "null argument");
+  if (!n) return PRANA_OK;
+  DevScope ds(c->device);
+  PRANA_CK(launch_kv_write(reinterpret_cast<__half*>(cache), first_row * kv_stride, src, n, c->stream));
+  return PRANA_OK;
+}
+
+// Splits for one attention launch: enough CTAs to cover the SMs twice,
+// at least 32 positions each.
+static int pick_splits(prana_ctx* c, size_t positions, size_t n_kv) {
+  const int by_len = (int)((positions + 31) / 32);
+  const int by_sm = (int)((2 * c->sm_count + n_kv - 1) / n_kv);
+  int s = by_len < by_sm ? by_len : by_sm;
+  return s < 1 ? 1 : s;
+}
+
+static int attn_common(prana_ctx* c, const float* q, const uint16_t* kc, const uint16_t* vc, size_t pos0, size_t m,
+                       size_t nh, size_t nkv, size_t hd, float* out) {
+  NEED(c && q && kc && vc && out, "null argument");
+  NEED(nkv > 0 && nh % nkv == 0, "n_heads must be a multiple of n_kv_heads");
+  NEED(hd <= 256, "head_dim %zu exceeds 256", hd);
+  NEED(hd * (nh / nkv) <= 4096, "head_dim x group exceeds 4096");
+  if (!m) return PRANA_OK;
+  DevScope ds(c->device);
+  const int splits = pick_splits(c, pos0 + m, nkv);
+  const int group = (int)(nh / nkv);
+  const int rows_per_cta = 4096 / (int)(hd * group);
+  const size_t vh = (size_t)(rows_per_cta < (int)m ? rows_per_cta : (int)m) * group;
+  const size_t ml = nkv * splits * vh * 2, po = nkv * splits * vh * hd;
+  void* sp;
+  int rc = ctx_scratch(c, (ml + po) * 4, &sp);
+  if (rc) return rc;
+  NEED(nkv <= 4096, "too many kv heads");
+  AttnArgs a{};
+  a.q = q;
+  a.kc = reinterpret_cast<const __half*>(kc);
+  a.vc = reinterpret_cast<const __half*>(vc);
+  a.m = (int)m;
+  a.pos0 = (int)pos0;
+  a.n_heads = (int)nh;
+  a.n_kv = (int)nkv;
+  a.hd = (int)hd;
+  a.n_splits = splits;
+  a.part_ml = static_cast<float*>(sp);
+  a.part_o = static_cast<float*>(sp) + ml;
+  a.counters = c->counters;
+  a.out = out;
+  cudaError_t e = launch_attn_decode(a, c->stream, false);
+  if (e == cudaErrorInvalidValue) return fail(PRANA_E_UNSUPPORTED, "attention: head_dim %zu not built", hd);
+  PRANA_CK(e);
+  return PRANA_OK;
+}
+
+int prana_attention_decode(prana_ctx* c, const float* q, const uint16_t* kc, const uint16_t* vc, size_t pos,
+                           size_t nh, size_t nkv, size_t hd, float* out) {
+  return attn_common(c, q, kc, vc, pos, 1, nh, nkv, hd, out);
+}
+
+int prana_attention_verify(prana_ctx* c, const float* q, const uint16_t* kc, const uint16_t* vc, size_t pos0,
+                           size_t seq, size_t nh, size_t nkv, size_t hd, float* out) {
+  return attn_common(c, q, kc, vc, pos0, seq, nh, nkv, hd, out);
+}
+
+int prana_attention(prana_ctx* c, const float* q, const float* k, const float* v, size_t seq, size_t nh, size_t nkv,
+                    size_t hd, float* out) {
+  NEED(c && q && k && v && out, "null argument");
+  NEED(nkv > 0 && nh % nkv == 0, "n_heads must be a multiple of n_kv_heads");
+  NEED(hd * (nh / nkv) <= 4096, "head_dim x group exceeds 4096");
+  if (!seq) return PRANA_OK;
+  DevScope ds(c->device);
+  PrefillAttnArgs a{q, k, v, (int)seq, (int)nh, (int)nkv, (int)hd, out};
+  cudaError_t e = launch_attn_prefill(a, c->stream);
+  if (e == cudaErrorInvalidValue) return fail(PRANA_E_UNSUPPORTED, "attention: head_dim %zu not built", hd);
+  PRANA_CK(e);
+  return PRANA_OK;
+}
+
+int prana_argmax(prana_ctx* c, const float* x, size_t rows, size_t n, uint32_t* out) {
+  NEED(c && x && out, "null argument");
+  NEED(n > 0, "argmax of an empty row");
+  if (!rows) return PRANA_OK;
+  DevScope ds(c->device);
+  PRANA_CK(launch_argmax(x, (int)rows, (int)n, out, c->stream));
+  return PRANA_OK;
+}
+
+}  // extern "C"

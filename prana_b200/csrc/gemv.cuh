@@ -1,0 +1,273 @@
+// gemv.cuh -- the quantized GEMV core: one warp streams whole weight rows with
+// 128-bit loads, dequantizes in registers and accumulates int8 x int8 block
+// dots with dp4a against activations staged in shared memory.
+//
+// Work unit per lane (a "unit"):
+//   Q8_0: one 32-weight block (32 B int8 + f16 d)
+//   Q4_0: one 32-weight block (16 B nibbles + f16 d)
+//   Q4_K: one 64-weight pair of a super-block (32 B nibbles + the super-block's 16 B header)
+//   Q6_K: one 64-weight quarter of a super-block (16 B low nibbles x2 + 16 B high bits + scales)
+// Lanes take consecutive units, so a warp reads a contiguous stretch of the row.
+//
+// The per-block integer dots are exactly the reference's:
+//   Q8_0 Σ qa·qw (matmul.rs:395-406), Q4_0 Σ qa·q − 8·Σqa (kquant.rs:240-252),
+//   Q4_K Σ qa·nibble per 32-group (kquant.rs:257-282), Q6_K Σ qa·(q6−32) per
+//   16-element sub-block (kquant.rs:287-318); only the f32 sum order differs.
+#pragma once
+#include "common.cuh"
+
+namespace prana {
+
+// Activations of up to M rows staged in shared memory.
+struct Acts {
+  const int8_t* q;    // [M][K]
+  const float* s;     // [M][G]
+  const int32_t* sum; // [M][G]
+  int K, G;
+};
+
+__host__ __device__ inline int units_per_row(int type, int cols) {
+  return (type == T_Q4_K || type == T_Q6_K) ? cols / 64 : cols / 32;
+}
+
+template <int T> struct Unit;
+template <> struct Unit<T_Q8_0> { uint4 a, b; unsigned short d; };
+template <> struct Unit<T_Q4_0> { uint4 q; unsigned short d; };
+template <> struct Unit<T_Q4_K> { uint4 a, b, meta; };
+template <> struct Unit<T_Q6_K> { uint4 lo, hi, qh; uint2 sc; unsigned short d; };
+
+template <int T> __device__ __forceinline__ Unit<T> load_unit(const DevWeight& w, int row, int u);
+
+template <> __device__ __forceinline__ Unit<T_Q8_0> load_unit<T_Q8_0>(const DevWeight& w, int row, int u) {
+  Unit<T_Q8_0> x;
+  const uint8_t* p = w.qs + (size_t)row * w.cols + (size_t)u * 32;
+  x.a = ld_stream16(p);
+  x.b = ld_stream16(p + 16);
+  x.d = ld_stream_u16(w.d + (size_t)row * (w.cols / 32) + u);
+  return x;
+}
+template <> __device__ __forceinline__ Unit<T_Q4_0> load_unit<T_Q4_0>(const DevWeight& w, int row, int u) {
+  Unit<T_Q4_0> x;
+  x.q = ld_stream16(w.qs + (size_t)row * (w.cols / 2) + (size_t)u * 16);
+  x.d = ld_stream_u16(w.d + (size_t)row * (w.cols / 32) + u);
+  return x;
+}
+template <> __device__ __forceinline__ Unit<T_Q4_K> load_unit<T_Q4_K>(const DevWeight& w, int row, int u) {
+  Unit<T_Q4_K> x;
+  const uint8_t* sb = w.qs + (size_t)row * (w.cols / 256) * 144 + (size_t)(u >> 2) * 144;
+  x.a = ld_stream16(sb + 16 + (u & 3) * 32);
+  x.b = ld_stream16(sb + 32 + (u & 3) * 32);
+  x.meta = ld_stream16(sb);
+  return x;
+}
+template <> __device__ __forceinline__ Unit<T_Q6_K> load_unit<T_Q6_K>(const DevWeight& w, int row, int u) {
+  Unit<T_Q6_K> x;
+  const int b = u >> 2, h = (u >> 1) & 1, l0 = (u & 1) * 16;
+  const uint8_t* ql = w.qs + (size_t)row * (w.cols / 2) + (size_t)b * 128 + h * 64 + l0;
+  x.lo = ld_stream16(ql);
+  x.hi = ld_stream16(ql + 32);
+  x.qh = ld_stream16(w.qh + (size_t)row * (w.cols / 4) + (size_t)b * 64 + h * 32 + l0);
+  x.sc = ld_stream8(w.sc + (size_t)row * (w.cols / 16) + (size_t)b * 16 + h * 8);
+  x.d = ld_stream_u16(w.d + (size_t)row * (w.cols / 256) + b);
+  return x;
+}
+
+__device__ __forceinline__ int dp4(unsigned a, int b, int c) { return __dp4a((int)a, b, c); }
+
+// ---- per-unit integer dots (exact) ----
+__device__ __forceinline__ int idot_q8(const Unit<T_Q8_0>& x, const int8_t* a) {
+  const int4 a0 = *reinterpret_cast<const int4*>(a), a1 = *reinterpret_cast<const int4*>(a + 16);
+  int s = dp4(x.a.x, a0.x, 0);
+  s = dp4(x.a.y, a0.y, s); s = dp4(x.a.z, a0.z, s); s = dp4(x.a.w, a0.w, s);
+  s = dp4(x.b.x, a1.x, s); s = dp4(x.b.y, a1.y, s); s = dp4(x.b.z, a1.z, s); s = dp4(x.b.w, a1.w, s);
+  return s;
+}
+// Σ qa·q with raw nibbles (0..15); caller subtracts 8·Σqa.
+__device__ __forceinline__ int idot_q4_0(const Unit<T_Q4_0>& x, const int8_t* a) {
+  const int4 a0 = *reinterpret_cast<const int4*>(a), a1 = *reinterpret_cast<const int4*>(a + 16);
+  const unsigned m = 0x0F0F0F0Fu;
+  int s = dp4(x.q.x & m, a0.x, 0);
+  s = dp4(x.q.y & m, a0.y, s); s = dp4(x.q.z & m, a0.z, s); s = dp4(x.q.w & m, a0.w, s);
+  s = dp4((x.q.x >> 4) & m, a1.x, s); s = dp4((x.q.y >> 4) & m, a1.y, s);
+  s = dp4((x.q.z >> 4) & m, a1.z, s); s = dp4((x.q.w >> 4) & m, a1.w, s);
+  return s;
+}
+// Q4_K pair: s1 = Σ a_lo·(q & 0xF), s2 = Σ a_hi·(q >> 4) over the pair's 32 bytes.
+__device__ __forceinline__ void idot_q4_k(const Unit<T_Q4_K>& x, const int8_t* a, int& s1, int& s2) {
+  const unsigned m = 0x0F0F0F0Fu;
+  const int4 l0 = *reinterpret_cast<const int4*>(a), l1 = *reinterpret_cast<const int4*>(a + 16);
+  const int4 h0 = *reinterpret_cast<const int4*>(a + 32), h1 = *reinterpret_cast<const int4*>(a + 48);
+  int s = dp4(x.a.x & m, l0.x, 0);
+  s = dp4(x.a.y & m, l0.y, s); s = dp4(x.a.z & m, l0.z, s); s = dp4(x.a.w & m, l0.w, s);
+  s = dp4(x.b.x & m, l1.x, s); s = dp4(x.b.y & m, l1.y, s); s = dp4(x.b.z & m, l1.z, s); s = dp4(x.b.w & m, l1.w, s);
+  int t = dp4((x.a.x >> 4) & m, h0.x, 0);
+  t = dp4((x.a.y >> 4) & m, h0.y, t); t = dp4((x.a.z >> 4) & m, h0.z, t); t = dp4((x.a.w >> 4) & m, h0.w, t);
+  t = dp4((x.b.x >> 4) & m, h1.x, t); t = dp4((x.b.y >> 4) & m, h1.y, t);
+  t = dp4((x.b.z >> 4) & m, h1.z, t); t = dp4((x.b.w >> 4) & m, h1.w, t);
+  s1 = s;
+  s2 = t;
+}
+// Q4_K (scale, min) pair j from the 12 packed bytes (kquant.rs:52-61).
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t* s, int& sc, int& mn) {
+  if (j < 4) {
+    sc = s[j] & 63;
+    mn = s[j + 4] & 63;
+  } else {
+    sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+    mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+  }
+}
+// Q6_K quarter: per-group (g = 0..3) sums over 16 elements of (q6 − 32)·qa.
+__device__ __forceinline__ void q6_words(unsigned lo, unsigned hi, unsigned qh, unsigned q[4]) {
+  const unsigned m4 = 0x0F0F0F0Fu, m2 = 0x03030303u;
+  q[0] = __vsub4((lo & m4) | ((qh & m2) << 4), 0x20202020u);
+  q[1] = __vsub4((hi & m4) | (((qh >> 2) & m2) << 4), 0x20202020u);
+  q[2] = __vsub4(((lo >> 4) & m4) | (((qh >> 4) & m2) << 4), 0x20202020u);
+  q[3] = __vsub4(((hi >> 4) & m4) | (((qh >> 6) & m2) << 4), 0x20202020u);
+}
+__device__ __forceinline__ void idot_q6_k(const Unit<T_Q6_K>& x, const int8_t* a /* block base + h*128 + l0 */,
+                                          int s[4]) {
+  const unsigned lo[4] = {x.lo.x, x.lo.y, x.lo.z, x.lo.w}, hi[4] = {x.hi.x, x.hi.y, x.hi.z, x.hi.w},
+                 qh[4] = {x.qh.x, x.qh.y, x.qh.z, x.qh.w};
+  int4 av[4];
+#pragma unroll
+  for (int g = 0; g < 4; g++) av[g] = *reinterpret_cast<const int4*>(a + g * 32);
+  s[0] = s[1] = s[2] = s[3] = 0;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    unsigned q[4];
+    q6_words(lo[k], hi[k], qh[k], q);
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+      const int aw = k == 0 ? av[g].x : (k == 1 ? av[g].y : (k == 2 ? av[g].z : av[g].w));
+      s[g] = dp4(q[g], aw, s[g]);
+    }
+  }
+}
+
+// ---- per-unit float accumulation for M activation rows ----
+template <int T, int M>
+__device__ __forceinline__ void accum_unit(const Unit<T>& x, int u, const Acts& a, int m_rt, float (&acc)[M]);
+
+template <int M>
+__device__ __forceinline__ void accum_unit(const Unit<T_Q8_0>& x, int u, const Acts& a, int m_rt, float (&acc)[M]) {
+  const float d = h2f(x.d);
+#pragma unroll
+  for (int m = 0; m < M; m++)
+    if (m < m_rt) {
+      const int s = idot_q8(x, a.q + m * a.K + u * 32);
+      acc[m] = fmaf(__fmul_rn(d, a.s[m * a.G + u]), (float)s, acc[m]);
+    }
+}
+template <int M>
+__device__ __forceinline__ void accum_unit(const Unit<T_Q4_0>& x, int u, const Acts& a, int m_rt, float (&acc)[M]) {
+  const float d = h2f(x.d);
+#pragma unroll
+  for (int m = 0; m < M; m++)
+    if (m < m_rt) {
+      const int s = idot_q4_0(x, a.q + m * a.K + u * 32) - 8 * a.sum[m * a.G + u];
+      acc[m] = fmaf(__fmul_rn(d, a.s[m * a.G + u]), (float)s, acc[m]);
+    }
+}
+template <int M>
+__device__ __forceinline__ void accum_unit(const Unit<T_Q4_K>& x, int u, const Acts& a, int m_rt, float (&acc)[M]) {
+  const float d = h2f((unsigned short)(x.meta.x & 0xffffu)), dmin = h2f((unsigned short)(x.meta.x >> 16));
+  uint8_t sb[12];
+  *reinterpret_cast<unsigned*>(sb) = x.meta.y;
+  *reinterpret_cast<unsigned*>(sb + 4) = x.meta.z;
+  *reinterpret_cast<unsigned*>(sb + 8) = x.meta.w;
+  const int p = u & 3;
+  int sc1, m1, sc2, m2;
+  q4k_scale_min(2 * p, sb, sc1, m1);
+  q4k_scale_min(2 * p + 1, sb, sc2, m2);
+  const float dsc1 = __fmul_rn(d, (float)sc1), dm1 = __fmul_rn(dmin, (float)m1);
+  const float dsc2 = __fmul_rn(d, (float)sc2), dm2 = __fmul_rn(dmin, (float)m2);
+  const int g_lo = (u >> 2) * 8 + 2 * p;
+#pragma unroll
+  for (int m = 0; m < M; m++)
+    if (m < m_rt) {
+      int s1, s2;
+      idot_q4_k(x, a.q + m * a.K + g_lo * 32, s1, s2);
+      const float t1 = __fsub_rn(__fmul_rn(dsc1, (float)s1), __fmul_rn(dm1, (float)a.sum[m * a.G + g_lo]));
+      const float t2 = __fsub_rn(__fmul_rn(dsc2, (float)s2), __fmul_rn(dm2, (float)a.sum[m * a.G + g_lo + 1]));
+      acc[m] = fmaf(a.s[m * a.G + g_lo], t1, acc[m]);
+      acc[m] = fmaf(a.s[m * a.G + g_lo + 1], t2, acc[m]);
+    }
+}
+template <int M>
+__device__ __forceinline__ void accum_unit(const Unit<T_Q6_K>& x, int u, const Acts& a, int m_rt, float (&acc)[M]) {
+  const float d = h2f(x.d);
+  const int b = u >> 2, h = (u >> 1) & 1, half16 = u & 1;
+  const int8_t* scb = reinterpret_cast<const int8_t*>(&x.sc);
+#pragma unroll
+  for (int m = 0; m < M; m++)
+    if (m < m_rt) {
+      int s[4];
+      idot_q6_k(x, a.q + m * a.K + b * 256 + h * 128 + half16 * 16, s);
+#pragma unroll
+      for (int g = 0; g < 4; g++) {
+        const float sa = a.s[m * a.G + b * 8 + h * 4 + g];
+        acc[m] = fmaf(__fmul_rn(__fmul_rn(d, sa), (float)scb[g * 2 + half16]), (float)s[g], acc[m]);
+      }
+    }
+}
+
+// Warp computes NR rows (rows[r] < 0 = idle) x up to M activation rows.
+// UNR units per lane are loaded before any is consumed, so NR*UNR 128-bit
+// loads per lane are in flight.
+template <int T, int NR, int M, int UNR>
+__device__ __forceinline__ void warp_dot(const DevWeight& w, const int (&rows)[NR], const Acts& a, int m_rt,
+                                         float (&acc)[NR][M]) {
+  const int lane = threadIdx.x & 31;
+  const int nu = units_per_row(T, w.cols);
+#pragma unroll
+  for (int r = 0; r < NR; r++)
+#pragma unroll
+    for (int m = 0; m < M; m++) acc[r][m] = 0.0f;
+  for (int u0 = 0; u0 < nu; u0 += 32 * UNR) {
+    Unit<T> buf[NR][UNR];
+#pragma unroll
+    for (int r = 0; r < NR; r++)
+#pragma unroll
+      for (int j = 0; j < UNR; j++) {
+        const int u = u0 + j * 32 + lane;
+        if (u < nu && rows[r] >= 0) buf[r][j] = load_unit<T>(w, rows[r], u);
+      }
+#pragma unroll
+    for (int r = 0; r < NR; r++)
+#pragma unroll
+      for (int j = 0; j < UNR; j++) {
+        const int u = u0 + j * 32 + lane;
+        if (u < nu && rows[r] >= 0) accum_unit<M>(buf[r][j], u, a, m_rt, acc[r]);
+      }
+  }
+#pragma unroll
+  for (int r = 0; r < NR; r++)
+#pragma unroll
+    for (int m = 0; m < M; m++) acc[r][m] = warp_sum(acc[r][m]);
+}
+
+// Per-block integer dots of one row (debug/parity entry): one value per
+// 32-group (Q8_0, Q4_0, Q4_K) or per 16-element sub-block (Q6_K).
+template <int T>
+__device__ __forceinline__ void unit_block_dots(const DevWeight& w, int row, int u, const Acts& a, int32_t* out) {
+  Unit<T> x = load_unit<T>(w, row, u);
+  if constexpr (T == T_Q8_0) {
+    out[u] = idot_q8(x, a.q + u * 32);
+  } else if constexpr (T == T_Q4_0) {
+    out[u] = idot_q4_0(x, a.q + u * 32) - 8 * a.sum[u];
+  } else if constexpr (T == T_Q4_K) {
+    int s1, s2;
+    const int g_lo = (u >> 2) * 8 + 2 * (u & 3);
+    idot_q4_k(x, a.q + g_lo * 32, s1, s2);
+    out[g_lo] = s1;
+    out[g_lo + 1] = s2;
+  } else {
+    const int b = u >> 2, h = (u >> 1) & 1, half16 = u & 1;
+    int s[4];
+    idot_q6_k(x, a.q + b * 256 + h * 128 + half16 * 16, s);
+    for (int g = 0; g < 4; g++) out[b * 16 + h * 8 + g * 2 + half16] = s[g];
+  }
+}
+
+}  // namespace prana

@@ -1,0 +1,79 @@
+// host.h -- host-side objects behind the opaque C-ABI handles.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/prana_cuda.h"
+#include "internal.h"
+
+namespace prana {
+
+int fail(int code, const char* fmt, ...);
+#define PRANA_CK(expr)                                                                                \
+  do {                                                                                                \
+    cudaError_t e_ = (expr);                                                                          \
+    if (e_ != cudaSuccess) return ::prana::fail(PRANA_E_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+// (cos, sin) tables of the two RoPE forms, computed on the host with libm
+// exactly as the CPU loops compute them (attention.rs:96-99, 114-117).
+struct RopeTable {
+  float* cos = nullptr;
+  float* sin = nullptr;
+  int positions = 0;
+};
+
+// Device scratch that grows on demand; `counters` are zero between launches
+// (every kernel that takes a ticket resets its counter).
+struct Scratch {
+  void* base = nullptr;
+  size_t bytes = 0;
+};
+
+}  // namespace prana
+
+struct prana_ctx {
+  int device = 0;
+  int sm_count = 148;
+  cudaStream_t own = nullptr;
+  cudaStream_t stream = nullptr;
+  prana::Scratch scratch;
+  unsigned* counters = nullptr;  // 4096 zeroed ticket counters
+  std::map<std::tuple<int, uint32_t, int>, prana::RopeTable> rope;
+  std::vector<void*> retired;  // outgrown RoPE tables: captured graphs may still point at them
+};
+
+struct prana_weight {
+  prana_ctx* ctx = nullptr;
+  prana::DevWeight dw{};
+  void* mem = nullptr;
+  size_t bytes = 0;
+};
+
+namespace prana {
+// Grow the context scratch to at least `bytes` (synchronizes when it grows).
+int ctx_scratch(prana_ctx* ctx, size_t bytes, void** out);
+// Table for (head_dim, theta, neox) covering at least `positions` rows.
+int ctx_rope(prana_ctx* ctx, int head_dim, float theta, int neox, int positions, const RopeTable** out);
+// Repack GGUF bytes of a [rows, cols] tensor into device layout.
+int upload_weight(prana_ctx* ctx, int type, size_t rows, size_t cols, const void* host, prana_weight* w);
+void free_weight(prana_weight* w);
+struct DevScope {
+  int prev = -1;
+  explicit DevScope(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DevScope() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+}  // namespace prana

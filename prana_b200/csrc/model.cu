@@ -1,0 +1,1068 @@
+// model.cu -- the device-resident model: GGUF load into HBM
+// (crates/prana-model/src/gguf.rs:157-460), the KV cache (infer.rs:25-45) and
+// the forward paths (infer.rs:142-374) as one stream of fused kernels per
+// token, captured once into a CUDA graph whose only host traffic is the token
+// id in and the sampled id out.  generate / generate_speculative
+// (infer.rs:581-771) run on top.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <new>
+
+#include "host.h"
+
+namespace prana {
+
+// ------------------------------------------------------------------ GGUF (subset)
+
+struct GgufTensor {
+  std::string name;
+  std::vector<uint64_t> dims;  // dims[0] is the contiguous (column) dimension
+  uint32_t type = 0;
+  uint64_t offset = 0;
+};
+
+struct Gguf {
+  const uint8_t* data = nullptr;
+  size_t len = 0;
+  size_t off = 0;
+  size_t data_start = 0;
+  std::map<std::string, int64_t> ints;
+  std::map<std::string, double> floats;
+  std::map<std::string, std::string> strs;
+  std::map<std::string, uint64_t> arr_len;
+  std::map<std::string, GgufTensor> tensors;
+
+  bool rd(void* dst, size_t n) {
+    if (off + n > len) return false;
+    memcpy(dst, data + off, n);
+    off += n;
+    return true;
+  }
+  template <typename T>
+  bool get(T& v) {
+    return rd(&v, sizeof(T));
+  }
+  bool str(std::string* out) {
+    uint64_t n;
+    if (!get(n) || off + n > len) return false;
+    if (out) out->assign(reinterpret_cast<const char*>(data + off), n);
+    off += n;
+    return true;
+  }
+  // gguf.rs:110-134 value types 0..12
+  bool value(uint32_t ty, const std::string* key) {
+    switch (ty) {
+      case 0: case 1: case 7: { uint8_t v; if (!get(v)) return false; if (key) ints[*key] = ty == 1 ? (int8_t)v : v; return true; }
+      case 2: case 3: { uint16_t v; if (!get(v)) return false; if (key) ints[*key] = ty == 3 ? (int16_t)v : v; return true; }
+      case 4: case 5: { uint32_t v; if (!get(v)) return false; if (key) ints[*key] = ty == 5 ? (int64_t)(int32_t)v : v; return true; }
+      case 6: { float v; if (!get(v)) return false; if (key) floats[*key] = v; return true; }
+      case 8: { std::string s; if (!str(key ? &s : nullptr)) return false; if (key) strs[*key] = s; return true; }
+      case 9: {
+        uint32_t et;
+        uint64_t n;
+        if (!get(et) || !get(n)) return false;
+        if (key) arr_len[*key] = n;
+        for (uint64_t i = 0; i < n; i++)
+          if (!value(et, nullptr)) return false;
+        return true;
+      }
+      case 10: case 11: { uint64_t v; if (!get(v)) return false; if (key) ints[*key] = (int64_t)v; return true; }
+      case 12: { double v; if (!get(v)) return false; if (key) floats[*key] = v; return true; }
+    }
+    return false;
+  }
+};
+
+static size_t type_size(uint32_t t, uint64_t n) {
+  switch (t) {
+    case T_F32: return n * 4;
+    case T_F16: return n * 2;
+    case T_Q4_0: return n / 32 * 18;
+    case T_Q8_0: return n / 32 * 34;
+    case T_Q4_K: return n / 256 * 144;
+    case T_Q6_K: return n / 256 * 210;
+  }
+  return 0;
+}
+
+// gguf.rs:157-196 Gguf::from_bytes
+static int gguf_parse(Gguf& g) {
+  uint32_t magic, ver;
+  uint64_t nt, nkv;
+  if (!g.get(magic) || magic != 0x46554747u) return fail(PRANA_E_FORMAT, "not a GGUF file (bad magic)");
+  if (!g.get(ver) || ver < 2 || ver > 3) return fail(PRANA_E_FORMAT, "unsupported GGUF version %u", ver);
+  if (!g.get(nt) || !g.get(nkv)) return fail(PRANA_E_FORMAT, "gguf truncated");
+  for (uint64_t i = 0; i < nkv; i++) {
+    std::string key;
+    uint32_t ty;
+    if (!g.str(&key) || !g.get(ty) || !g.value(ty, &key)) return fail(PRANA_E_FORMAT, "gguf truncated");
+  }
+  for (uint64_t i = 0; i < nt; i++) {
+    GgufTensor t;
+    uint32_t nd;
+    if (!g.str(&t.name) || !g.get(nd) || nd > 4) return fail(PRANA_E_FORMAT, "gguf truncated");
+    t.dims.resize(nd);
+    for (uint32_t d = 0; d < nd; d++)
+      if (!g.get(t.dims[d])) return fail(PRANA_E_FORMAT, "gguf truncated");
+    if (!g.get(t.type) || !g.get(t.offset)) return fail(PRANA_E_FORMAT, "gguf truncated");
+    g.tensors[t.name] = t;
+  }
+  int64_t al = 32;
+  auto it = g.ints.find("general.alignment");
+  if (it != g.ints.end() && it->second > 0 && (it->second & (it->second - 1)) == 0) al = it->second;
+  g.data_start = (g.off + al - 1) / al * al;
+  return PRANA_OK;
+}
+
+static int tensor_raw(const Gguf& g, const std::string& name, const GgufTensor** t, const uint8_t** raw) {
+  auto it = g.tensors.find(name);
+  if (it == g.tensors.end()) return fail(PRANA_E_FORMAT, "missing tensor '%s'", name.c_str());
+  uint64_t n = 1;
+  for (auto d : it->second.dims) n *= d;
+  const size_t bytes = type_size(it->second.type, n);
+  if (!bytes) return fail(PRANA_E_UNSUPPORTED, "tensor '%s': unsupported ggml type %u", name.c_str(), it->second.type);
+  if (g.data_start + it->second.offset + bytes > g.len)
+    return fail(PRANA_E_FORMAT, "tensor '%s' data out of range", name.c_str());
+  *t = &it->second;
+  *raw = g.data + g.data_start + it->second.offset;
+  return PRANA_OK;
+}
+
+static float f16_host(uint16_t h) {
+  const uint32_t sign = (h >> 15) & 1u, exp = (h >> 10) & 0x1fu, frac = h & 0x3ffu;
+  uint32_t bits;
+  if (exp == 0 && frac == 0) bits = sign << 31;
+  else if (exp == 0) {
+    const float v = (float)frac * 5.9604644775390625e-08f;
+    return sign ? -v : v;
+  } else if (exp == 0x1f) bits = (sign << 31) | 0x7f800000u | (frac << 13);
+  else bits = (sign << 31) | ((exp + 112u) << 23) | (frac << 13);
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+// tensor_f32 for the 1-D tensors the model reads (norms, biases)
+static int vec_f32(const Gguf& g, const std::string& name, size_t n, std::vector<float>& out) {
+  const GgufTensor* t;
+  const uint8_t* raw;
+  int rc = tensor_raw(g, name, &t, &raw);
+  if (rc) return rc;
+  uint64_t cnt = 1;
+  for (auto d : t->dims) cnt *= d;
+  if (cnt != n) return fail(PRANA_E_FORMAT, "tensor '%s' has %llu values, expected %zu", name.c_str(), (unsigned long long)cnt, n);
+  out.resize(n);
+  if (t->type == T_F32) memcpy(out.data(), raw, n * 4);
+  else if (t->type == T_F16)
+    for (size_t i = 0; i < n; i++) {
+      uint16_t h;
+      memcpy(&h, raw + 2 * i, 2);
+      out[i] = f16_host(h);
+    }
+  else return fail(PRANA_E_UNSUPPORTED, "tensor '%s': only F32/F16 vectors supported", name.c_str());
+  return PRANA_OK;
+}
+
+}  // namespace prana
+
+using namespace prana;
+
+// ------------------------------------------------------------------ model objects
+
+namespace {
+
+struct LayerW {
+  prana_weight wq, wk, wv, wo, w1, w2, w3;
+  float *rms_att = nullptr, *rms_ffn = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
+};
+
+// Activation buffers for `rows` rows (decode: 8; prefill: the prompt length).
+struct Bufs {
+  size_t rows = 0;
+  float *x = nullptr, *q = nullptr, *att = nullptr, *kf = nullptr, *vf = nullptr, *g = nullptr, *u = nullptr;
+  int8_t* hq = nullptr;
+  float* hs = nullptr;
+  int32_t* hsum = nullptr;
+  float* logits = nullptr;
+  uint32_t* toks = nullptr;     // input ids [rows]
+  uint32_t* tok_out = nullptr;  // argmax per row [rows]
+  std::vector<void*> owned;
+  ~Bufs() {
+    for (void* p : owned) cudaFree(p);
+  }
+  template <typename T>
+  int alloc(T*& p, size_t n) {
+    void* v = nullptr;
+    if (cudaMalloc(&v, std::max<size_t>(n, 1) * sizeof(T)) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(PRANA_E_OOM, "activation buffer allocation failed");
+    }
+    owned.push_back(v);
+    p = static_cast<T*>(v);
+    return PRANA_OK;
+  }
+};
+
+}  // namespace
+
+struct prana_model {
+  prana_ctx* ctx = nullptr;
+  prana_model_config cfg{};
+  prana_weight emb;
+  std::vector<LayerW> layers;
+  float* rms_final = nullptr;
+  prana_weight head;
+  bool head_is_emb = false;
+  const RopeTable* rope = nullptr;
+  std::vector<void*> owned;  // norms / biases
+  std::unique_ptr<Bufs> dec;
+  // head argmax scratch
+  float* part_val = nullptr;
+  int* part_idx = nullptr;
+  int n_parts = 0;
+  unsigned* head_ctr = nullptr;
+  int* d_tokpos = nullptr;  // [token, pos] for the graph-driven step
+  int* h_io = nullptr;      // pinned mirror
+  uint32_t* h_tok = nullptr;
+  bool pdl = true;
+  std::vector<prana_kv*> caches;  // live KV caches (freed with the model)
+};
+
+struct prana_kv {
+  prana_model* m = nullptr;
+  size_t positions = 0;
+  __half* k = nullptr;
+  __half* v = nullptr;
+  int n_splits = 1;
+  float* part_ml = nullptr;
+  float* part_o = nullptr;
+  unsigned* counters = nullptr;
+  uint32_t* ring = nullptr;
+  int* ring_n = nullptr;
+  cudaGraphExec_t g_step = nullptr;
+  cudaGraphExec_t g_loop = nullptr;
+  size_t loop_pos = 0;  // host mirror of the device-loop position
+  bool loop_active = false;
+};
+
+namespace {
+
+int dev_vec(prana_model* m, const std::vector<float>& h, float** out) {
+  void* p = nullptr;
+  if (cudaMalloc(&p, h.size() * 4) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(PRANA_E_OOM, "allocation failed");
+  }
+  m->owned.push_back(p);
+  if (cudaMemcpy(p, h.data(), h.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    return fail(PRANA_E_CUDA, "upload failed");
+  *out = static_cast<float*>(p);
+  return PRANA_OK;
+}
+
+// Linear loading rule of gguf.rs:271-305: Q8_0 (cols%32), Q4_0 (cols%32),
+// Q4_K/Q6_K (cols%256) stay quantized.  Dense projections are not built.
+int load_linear(prana_model* m, const Gguf& g, const std::string& name, size_t rows, size_t cols, prana_weight* w) {
+  const GgufTensor* t;
+  const uint8_t* raw;
+  int rc = tensor_raw(g, name, &t, &raw);
+  if (rc) return rc;
+  if (t->dims.size() != 2) return fail(PRANA_E_FORMAT, "tensor '%s' is not 2-D", name.c_str());
+  if (t->dims[0] != cols || t->dims[1] != rows)
+    return fail(PRANA_E_FORMAT, "tensor '%s' is [%llu, %llu], expected [%zu, %zu]", name.c_str(),
+                (unsigned long long)t->dims[1], (unsigned long long)t->dims[0], rows, cols);
+  const uint32_t ty = t->type;
+  const bool ok = (ty == T_Q8_0 && cols % 32 == 0) || (ty == T_Q4_0 && cols % 32 == 0) ||
+                  ((ty == T_Q4_K || ty == T_Q6_K) && cols % 256 == 0);
+  if (!ok)
+    return fail(PRANA_E_UNSUPPORTED, "tensor '%s': type %u with %zu cols would run the dense f32 matmul, not built",
+                name.c_str(), ty, cols);
+  return upload_weight(m->ctx, (int)ty, rows, cols, raw, w);
+}
+
+void destroy_kv(prana_kv* kv);
+
+void free_model(prana_model* m) {
+  if (!m) return;
+  DevScope ds(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->own);
+  while (!m->caches.empty()) destroy_kv(m->caches.back());
+  free_weight(&m->emb);
+  if (!m->head_is_emb) free_weight(&m->head);
+  for (auto& L : m->layers) {
+    free_weight(&L.wq); free_weight(&L.wk); free_weight(&L.wv); free_weight(&L.wo);
+    free_weight(&L.w1); free_weight(&L.w2); free_weight(&L.w3);
+  }
+  for (void* p : m->owned) cudaFree(p);
+  m->dec.reset();
+  if (m->h_io) cudaFreeHost(m->h_io);
+  delete m;
+}
+
+int make_bufs(prana_model* m, size_t rows, bool window, Bufs& b) {
+  const auto& c = m->cfg;
+  const size_t q_dim = c.n_heads * c.head_dim, kv_dim = c.n_kv_heads * c.head_dim;
+  b.rows = rows;
+  int rc = 0;
+  rc |= b.alloc(b.x, rows * c.dim);
+  rc |= b.alloc(b.q, rows * q_dim);
+  rc |= b.alloc(b.att, rows * q_dim);
+  rc |= b.alloc(b.hq, rows * c.hidden_dim);
+  rc |= b.alloc(b.hs, rows * c.hidden_dim / 32);
+  rc |= b.alloc(b.hsum, rows * c.hidden_dim / 32);
+  rc |= b.alloc(b.g, rows * c.hidden_dim);
+  rc |= b.alloc(b.u, rows * c.hidden_dim);
+  rc |= b.alloc(b.toks, rows);
+  rc |= b.alloc(b.tok_out, rows);
+  if (window) {
+    rc |= b.alloc(b.kf, rows * kv_dim);
+    rc |= b.alloc(b.vf, rows * kv_dim);
+  } else {
+    rc |= b.alloc(b.logits, rows * c.vocab_size);
+  }
+  return rc ? PRANA_E_OOM : PRANA_OK;
+}
+
+enum { MODE_CACHE = 0, MODE_WINDOW = 1 };
+
+// Diagnostic trace of every quantized activation row of a one-token pass, in
+// the order the CPU path quantizes them: per layer the attention-norm input,
+// the attention output, the ffn-norm input and silu(g)*u; then the final norm.
+struct Trace {
+  int8_t* q = nullptr;
+  float* s = nullptr;
+  size_t nq = 0, ns = 0;
+  void site(GemvArgs& g, int k) {
+    g.trace_q = q + nq;
+    g.trace_s = s + ns;
+    nq += (size_t)k;
+    ns += (size_t)k / 32;
+  }
+};
+
+// One pass of n rows through the model (infer.rs:142-211 for n = 1 and
+// :296-374 / :220-286 for the batched forms).  Rows are positions pos0.. (or
+// *pos_dev.. when pos_dev is set, n == 1).  MODE_WINDOW attends over the f32
+// in-window K/V (prefill); MODE_CACHE over the f16 cache (decode, verify).
+int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* toks_dev, const int* tok_dev,
+                 int pos0, const int* pos_dev, int mode, bool head, bool pdl, Trace* tr = nullptr) {
+  const auto& c = m->cfg;
+  cudaStream_t st = m->ctx->own;
+  const int dim = (int)c.dim, hd = (int)c.head_dim, hid = (int)c.hidden_dim;
+  const int q_dim = (int)(c.n_heads * c.head_dim), kv_dim = (int)(c.n_kv_heads * c.head_dim);
+  const size_t lstride = kv->positions * (size_t)kv_dim;
+  PRANA_CK(launch_embed(m->emb.dw, toks_dev, tok_dev, n, b.x, st, false));
+  for (size_t l = 0; l < m->layers.size(); l++) {
+    LayerW& L = m->layers[l];
+    __half* kc = kv->k + l * lstride;
+    __half* vc = kv->v + l * lstride;
+    // --- rmsnorm + Q|K|V + bias + RoPE + KV write, grouped by weight type
+    const prana_weight* segs[3] = {&L.wq, &L.wk, &L.wv};
+    const float* biases[3] = {L.bq, L.bk, L.bv};
+    const int pairs[3] = {q_dim / 2, kv_dim / 2, kv_dim / 2};
+    for (int s0 = 0; s0 < 3;) {
+      int s1 = s0 + 1;
+      while (s1 < 3 && segs[s1]->dw.type == segs[s0]->dw.type) s1++;
+      for (int c0 = 0; c0 < n; c0 += 8) {
+        const int mc = std::min(8, n - c0);
+        QkvArgs a{};
+        a.a.m = mc;
+        a.a.x = b.x + (size_t)c0 * dim;
+        a.a.norm_w = L.rms_att;
+        a.a.eps = c.norm_eps;
+        a.nseg = s1 - s0;
+        a.pair_start[0] = 0;
+        for (int s = s0; s < s1; s++) {
+          a.w[s - s0] = segs[s]->dw;
+          a.kind[s - s0] = s;
+          a.bias[s - s0] = biases[s];
+          a.pair_start[s - s0 + 1] = a.pair_start[s - s0] + pairs[s];
+        }
+        a.hd = hd;
+        a.neox = c.rope_neox;
+        a.q_dim = q_dim;
+        a.kv_dim = kv_dim;
+        a.cos_t = m->rope->cos;
+        a.sin_t = m->rope->sin;
+        a.pos0 = pos0 + c0;
+        a.pos_dev = pos_dev;
+        a.cap = (int)kv->positions;
+        a.q_out = b.q + (size_t)c0 * q_dim;
+        a.kc = kc;
+        a.vc = vc;
+        if (mode == MODE_WINDOW) {
+          a.k_f32 = b.kf + (size_t)c0 * kv_dim;
+          a.v_f32 = b.vf + (size_t)c0 * kv_dim;
+        }
+        if (tr && s0 == 0) tr->site(a.a, dim);
+        PRANA_CK(launch_qkv(a, PRO_NORM, st, pdl));
+      }
+      s0 = s1;
+    }
+    // --- attention
+    if (mode == MODE_WINDOW) {
+      PrefillAttnArgs a{b.q, b.kf, b.vf, n, (int)c.n_heads, (int)c.n_kv_heads, hd, b.att};
+      PRANA_CK(launch_attn_prefill(a, st));
+    } else {
+      AttnArgs a{};
+      a.q = b.q;
+      a.kc = kc;
+      a.vc = vc;
+      a.m = n;
+      a.pos0 = pos0;
+      a.pos_dev = pos_dev;
+      a.n_heads = (int)c.n_heads;
+      a.n_kv = (int)c.n_kv_heads;
+      a.hd = hd;
+      a.n_splits = kv->n_splits;
+      a.part_ml = kv->part_ml;
+      a.part_o = kv->part_o;
+      a.counters = kv->counters;
+      a.out = b.att;
+      PRANA_CK(launch_attn_decode(a, st, pdl));
+    }
+    // --- wo + residual (activations quantized in the GEMV prologue)
+    for (int c0 = 0; c0 < n; c0 += 8) {
+      GemvArgs g{};
+      g.w = L.wo.dw;
+      g.m = std::min(8, n - c0);
+      g.x = b.att + (size_t)c0 * q_dim;
+      g.out = b.x + (size_t)c0 * dim;
+      if (tr) tr->site(g, q_dim);
+      PRANA_CK(launch_gemv(g, PRO_F32, EPI_RESID, st, pdl));
+    }
+    // --- rmsnorm + gate|up + silu*up + quantize
+    const bool fused = L.w1.dw.type == L.w3.dw.type && hid % 32 == 0;
+    for (int c0 = 0; c0 < n; c0 += 8) {
+      const int mc = std::min(8, n - c0);
+      if (fused) {
+        SwigluArgs a{};
+        a.a.m = mc;
+        a.a.x = b.x + (size_t)c0 * dim;
+        a.a.norm_w = L.rms_ffn;
+        a.a.eps = c.norm_eps;
+        a.w1 = L.w1.dw;
+        a.w3 = L.w3.dw;
+        a.hq = b.hq + (size_t)c0 * hid;
+        a.hs = b.hs + (size_t)c0 * (hid / 32);
+        a.hsum = b.hsum + (size_t)c0 * (hid / 32);
+        if (tr) tr->site(a.a, dim);
+        PRANA_CK(launch_swiglu(a, PRO_NORM, st, pdl));
+      } else {
+        GemvArgs g{};
+        g.m = mc;
+        g.x = b.x + (size_t)c0 * dim;
+        g.norm_w = L.rms_ffn;
+        g.eps = c.norm_eps;
+        g.w = L.w1.dw;
+        g.out = b.g + (size_t)c0 * hid;
+        if (tr) tr->site(g, dim);
+        PRANA_CK(launch_gemv(g, PRO_NORM, EPI_STORE, st, pdl));
+        g.trace_q = nullptr;
+        g.trace_s = nullptr;
+        g.w = L.w3.dw;
+        g.out = b.u + (size_t)c0 * hid;
+        PRANA_CK(launch_gemv(g, PRO_NORM, EPI_STORE, st, pdl));
+        PRANA_CK(launch_silu_mul(b.g + (size_t)c0 * hid, b.u + (size_t)c0 * hid, (size_t)mc * hid, st));
+        PRANA_CK(launch_quantize_acts(b.g + (size_t)c0 * hid, mc, hid, b.hq + (size_t)c0 * hid,
+                                      b.hs + (size_t)c0 * (hid / 32), b.hsum + (size_t)c0 * (hid / 32), st));
+      }
+    }
+    if (tr) {
+      PRANA_CK(cudaMemcpyAsync(tr->q + tr->nq, b.hq, (size_t)hid, cudaMemcpyDeviceToDevice, st));
+      PRANA_CK(cudaMemcpyAsync(tr->s + tr->ns, b.hs, (size_t)hid / 32 * 4, cudaMemcpyDeviceToDevice, st));
+      tr->nq += (size_t)hid;
+      tr->ns += (size_t)hid / 32;
+    }
+    // --- w2 + residual
+    for (int c0 = 0; c0 < n; c0 += 8) {
+      GemvArgs g{};
+      g.w = L.w2.dw;
+      g.m = std::min(8, n - c0);
+      g.aq = b.hq + (size_t)c0 * hid;
+      g.as = b.hs + (size_t)c0 * (hid / 32);
+      g.asum = b.hsum + (size_t)c0 * (hid / 32);
+      g.out = b.x + (size_t)c0 * dim;
+      PRANA_CK(launch_gemv(g, PRO_Q, EPI_RESID, st, pdl));
+    }
+  }
+  if (!head) return PRANA_OK;
+  // --- final rmsnorm + LM head + argmax (Model::logits, checkpoint.rs:239-248)
+  for (int c0 = 0; c0 < n; c0 += 8) {
+    GemvArgs g{};
+    g.w = m->head.dw;
+    g.m = std::min(8, n - c0);
+    g.x = b.x + (size_t)c0 * dim;
+    g.norm_w = m->rms_final;
+    g.eps = c.norm_eps;
+    g.out = b.logits + (size_t)c0 * c.vocab_size;
+    g.part_val = m->part_val;
+    g.part_idx = m->part_idx;
+    g.counter = m->head_ctr;
+    g.n_parts = m->n_parts;
+    g.token_out = b.tok_out + c0;
+    g.token_next = (n == 1 && tok_dev) ? const_cast<int*>(tok_dev) : nullptr;
+    if (tr) tr->site(g, dim);
+    PRANA_CK(launch_gemv(g, PRO_NORM, EPI_ARGMAX, st, pdl));
+  }
+  return PRANA_OK;
+}
+
+int capture(prana_model* m, prana_kv* kv, bool loop, cudaGraphExec_t* out) {
+  cudaStream_t st = m->ctx->own;
+  for (int attempt = 0; attempt < 2; attempt++) {
+    const bool pdl = m->pdl && attempt == 0;
+    cudaGraph_t graph = nullptr;
+    PRANA_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
+    int rc = enqueue_rows(m, kv, *m->dec, 1, nullptr, m->d_tokpos, 0, m->d_tokpos + 1, MODE_CACHE, true, pdl);
+    if (!rc && loop) {
+      cudaError_t e = launch_advance(m->d_tokpos, m->d_tokpos + 1, kv->ring, (int)kv->positions, kv->ring_n, st, pdl);
+      if (e != cudaSuccess) rc = fail(PRANA_E_CUDA, "advance launch: %s", cudaGetErrorString(e));
+    }
+    cudaError_t ec = cudaStreamEndCapture(st, &graph);
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      cudaGetLastError();
+      return rc;
+    }
+    if (ec == cudaSuccess) {
+      cudaError_t ei = cudaGraphInstantiate(out, graph, 0);
+      cudaGraphDestroy(graph);
+      if (ei == cudaSuccess) return PRANA_OK;
+    } else if (graph) {
+      cudaGraphDestroy(graph);
+    }
+    cudaGetLastError();
+    m->pdl = false;  // retry once without programmatic dependent launches
+  }
+  return fail(PRANA_E_CUDA, "decode graph capture failed");
+}
+
+int ensure_graphs(prana_model* m, prana_kv* kv, bool loop) {
+  if (!kv->g_step) {
+    int rc = capture(m, kv, false, &kv->g_step);
+    if (rc) return rc;
+  }
+  if (loop && !kv->g_loop) {
+    int rc = capture(m, kv, true, &kv->g_loop);
+    if (rc) return rc;
+  }
+  return PRANA_OK;
+}
+
+void destroy_kv(prana_kv* kv) {
+  if (!kv) return;
+  DevScope ds(kv->m->ctx->device);
+  cudaStreamSynchronize(kv->m->ctx->own);
+  auto& cs = kv->m->caches;
+  cs.erase(std::remove(cs.begin(), cs.end(), kv), cs.end());
+  if (kv->g_step) cudaGraphExecDestroy(kv->g_step);
+  if (kv->g_loop) cudaGraphExecDestroy(kv->g_loop);
+  cudaFree(kv->k);
+  cudaFree(kv->v);
+  cudaFree(kv->part_ml);
+  cudaFree(kv->counters);
+  cudaFree(kv->ring);
+  delete kv;
+}
+
+}  // namespace
+
+#define API_BEGIN try {
+#define API_END                                                    \
+  }                                                                \
+  catch (const std::bad_alloc&) {                                  \
+    return fail(PRANA_E_OOM, "host allocation failed");            \
+  }                                                                \
+  catch (...) {                                                    \
+    return fail(PRANA_E_INVALID, "unexpected host exception");     \
+  }
+#define NEED(cond, ...) \
+  if (!(cond)) return fail(PRANA_E_INVALID, __VA_ARGS__)
+
+extern "C" {
+
+int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
+  API_BEGIN
+  NEED(ctx && path && out, "null argument");
+  *out = nullptr;
+  DevScope ds(ctx->device);
+  const int fd = open(path, O_RDONLY);
+  if (fd < 0) return fail(PRANA_E_INVALID, "cannot open %s", path);
+  struct stat sb;
+  if (fstat(fd, &sb) != 0 || sb.st_size <= 0) {
+    close(fd);
+    return fail(PRANA_E_FORMAT, "cannot stat %s", path);
+  }
+  void* map = mmap(nullptr, (size_t)sb.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (map == MAP_FAILED) return fail(PRANA_E_FORMAT, "cannot map %s", path);
+  struct Unmap {
+    void* p;
+    size_t n;
+    ~Unmap() { munmap(p, n); }
+  } unmap{map, (size_t)sb.st_size};
+  Gguf g;
+  g.data = static_cast<const uint8_t*>(map);
+  g.len = (size_t)sb.st_size;
+  int rc = gguf_parse(g);
+  if (rc) return rc;
+
+  auto arch_it = g.strs.find("general.architecture");
+  if (arch_it == g.strs.end()) return fail(PRANA_E_FORMAT, "missing general.architecture");
+  const std::string arch = arch_it->second;
+  if (arch != "llama" && arch != "qwen2")
+    return fail(PRANA_E_UNSUPPORTED, "unsupported architecture '%s' (llama, qwen2)", arch.c_str());
+  auto meta_int = [&](const std::string& k, int64_t* v) -> bool {
+    auto it = g.ints.find(arch + "." + k);
+    if (it == g.ints.end() || it->second < 0) return false;
+    *v = it->second;
+    return true;
+  };
+  auto meta_f = [&](const std::string& k, float dflt) -> float {
+    auto it = g.floats.find(arch + "." + k);
+    return it == g.floats.end() ? dflt : (float)it->second;
+  };
+  std::unique_ptr<prana_model, void (*)(prana_model*)> m(new prana_model(), free_model);
+  m->ctx = ctx;
+  auto& c = m->cfg;
+  if (!meta_int("embedding_length", &c.dim)) return fail(PRANA_E_FORMAT, "missing metadata '%s.embedding_length'", arch.c_str());
+  if (!meta_int("block_count", &c.n_layers)) return fail(PRANA_E_FORMAT, "missing metadata '%s.block_count'", arch.c_str());
+  if (!meta_int("attention.head_count", &c.n_heads)) return fail(PRANA_E_FORMAT, "missing metadata '%s.attention.head_count'", arch.c_str());
+  if (!meta_int("attention.head_count_kv", &c.n_kv_heads)) c.n_kv_heads = c.n_heads;
+  if (!meta_int("feed_forward_length", &c.hidden_dim)) return fail(PRANA_E_FORMAT, "missing metadata '%s.feed_forward_length'", arch.c_str());
+  if (!meta_int("context_length", &c.seq_len)) return fail(PRANA_E_FORMAT, "missing metadata '%s.context_length'", arch.c_str());
+  c.rope_theta = meta_f("rope.freq_base", 10000.0f);
+  if (!meta_int("attention.key_length", &c.head_dim)) c.head_dim = c.n_heads ? c.dim / c.n_heads : 0;
+  c.norm_eps = meta_f("attention.layer_norm_rms_epsilon", 1e-5f);
+  c.rope_neox = arch != "llama";
+  auto vt = g.arr_len.find("tokenizer.ggml.tokens");
+  if (vt == g.arr_len.end()) return fail(PRANA_E_FORMAT, "missing tokenizer.ggml.tokens");
+  c.vocab_size = (int64_t)vt->second;
+  NEED(c.dim > 0 && c.n_layers > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.n_heads % c.n_kv_heads == 0,
+       "inconsistent model metadata");
+  NEED(c.head_dim > 0 && c.head_dim % 2 == 0 && c.head_dim <= 256, "head_dim %lld not supported", (long long)c.head_dim);
+  NEED(c.dim % 32 == 0 && c.hidden_dim % 32 == 0, "dim and hidden must be multiples of 32");
+  const size_t dim = (size_t)c.dim, hid = (size_t)c.hidden_dim, q_dim = (size_t)(c.n_heads * c.head_dim),
+               kv_dim = (size_t)(c.n_kv_heads * c.head_dim);
+  NEED(q_dim % 32 == 0, "q_dim must be a multiple of 32");
+
+  // token embedding (gguf.rs:309-326)
+  {
+    const GgufTensor* t;
+    const uint8_t* raw;
+    rc = tensor_raw(g, "token_embd.weight", &t, &raw);
+    if (rc) return rc;
+    uint64_t nv = 1;
+    for (auto d : t->dims) nv *= d;
+    if (nv != (uint64_t)c.vocab_size * dim) return fail(PRANA_E_FORMAT, "token_embd.weight size mismatch with vocab");
+    rc = upload_weight(ctx, (int)t->type, (size_t)c.vocab_size, dim, raw, &m->emb);
+    if (rc) return rc;
+  }
+  m->layers.resize((size_t)c.n_layers);
+  for (size_t i = 0; i < m->layers.size(); i++) {
+    LayerW& L = m->layers[i];
+    const std::string p = "blk." + std::to_string(i) + ".";
+    std::vector<float> v;
+    if ((rc = vec_f32(g, p + "attn_norm.weight", dim, v)) || (rc = dev_vec(m.get(), v, &L.rms_att))) return rc;
+    if ((rc = vec_f32(g, p + "ffn_norm.weight", dim, v)) || (rc = dev_vec(m.get(), v, &L.rms_ffn))) return rc;
+    if ((rc = load_linear(m.get(), g, p + "attn_q.weight", q_dim, dim, &L.wq))) return rc;
+    if ((rc = load_linear(m.get(), g, p + "attn_k.weight", kv_dim, dim, &L.wk))) return rc;
+    if ((rc = load_linear(m.get(), g, p + "attn_v.weight", kv_dim, dim, &L.wv))) return rc;
+    if ((rc = load_linear(m.get(), g, p + "attn_output.weight", dim, q_dim, &L.wo))) return rc;
+    if ((rc = load_linear(m.get(), g, p + "ffn_gate.weight", hid, dim, &L.w1))) return rc;
+    if ((rc = load_linear(m.get(), g, p + "ffn_down.weight", dim, hid, &L.w2))) return rc;
+    if ((rc = load_linear(m.get(), g, p + "ffn_up.weight", hid, dim, &L.w3))) return rc;
+    // gguf.rs:388-394: each bias optional
+    const char* bn[3] = {"attn_q.bias", "attn_k.bias", "attn_v.bias"};
+    float** bd[3] = {&L.bq, &L.bk, &L.bv};
+    const size_t bl[3] = {q_dim, kv_dim, kv_dim};
+    for (int j = 0; j < 3; j++)
+      if (g.tensors.count(p + bn[j])) {
+        if ((rc = vec_f32(g, p + bn[j], bl[j], v)) || (rc = dev_vec(m.get(), v, bd[j]))) return rc;
+        c.has_bias = 1;
+      }
+  }
+  {
+    std::vector<float> v;
+    if ((rc = vec_f32(g, "output_norm.weight", dim, v)) || (rc = dev_vec(m.get(), v, &m->rms_final))) return rc;
+  }
+  if (g.tensors.count("output.weight")) {
+    if ((rc = load_linear(m.get(), g, "output.weight", (size_t)c.vocab_size, dim, &m->head))) return rc;
+  } else {
+    // tied classifier over a packed table runs the quantized kernel (checkpoint.rs:246)
+    c.shared_classifier = 1;
+    const int et = m->emb.dw.type;
+    if (et != T_Q4_0 && et != T_Q4_K && et != T_Q6_K)
+      return fail(PRANA_E_UNSUPPORTED, "tied classifier over a dense table is not built");
+    m->head = m->emb;
+    m->head_is_emb = true;
+  }
+  // weight bytes
+  size_t wb = m->emb.bytes + (m->head_is_emb ? 0 : m->head.bytes);
+  for (auto& L : m->layers) wb += L.wq.bytes + L.wk.bytes + L.wv.bytes + L.wo.bytes + L.w1.bytes + L.w2.bytes + L.w3.bytes;
+  c.weight_bytes = (int64_t)wb;
+  // RoPE table over the whole context (never regrown: graphs hold its address)
+  rc = ctx_rope(ctx, (int)c.head_dim, c.rope_theta, c.rope_neox, (int)c.seq_len + 8, &m->rope);
+  if (rc) return rc;
+  // decode buffers and head argmax scratch
+  m->dec.reset(new Bufs());
+  if ((rc = make_bufs(m.get(), 8, false, *m->dec))) return rc;
+  m->n_parts = (int)((c.vocab_size + 7) / 8);
+  void* p = nullptr;
+  PRANA_CK(cudaMalloc(&p, (size_t)8 * m->n_parts * 8 + 256));
+  m->owned.push_back(p);
+  m->part_val = static_cast<float*>(p);
+  m->part_idx = reinterpret_cast<int*>(static_cast<float*>(p) + (size_t)8 * m->n_parts);
+  PRANA_CK(cudaMalloc(&p, 256));
+  m->owned.push_back(p);
+  PRANA_CK(cudaMemset(p, 0, 256));
+  m->head_ctr = static_cast<unsigned*>(p);
+  m->d_tokpos = reinterpret_cast<int*>(static_cast<uint8_t*>(p) + 64);
+  PRANA_CK(cudaHostAlloc((void**)&m->h_io, 64, cudaHostAllocDefault));
+  m->h_tok = reinterpret_cast<uint32_t*>(m->h_io + 4);
+  const char* e = getenv("PRANA_PDL");
+  m->pdl = !(e && e[0] == '0');
+  *out = m.release();
+  return PRANA_OK;
+  API_END
+}
+
+int prana_model_free(prana_model* m) {
+  free_model(m);
+  return PRANA_OK;
+}
+
+int prana_model_config_get(const prana_model* m, prana_model_config* out) {
+  NEED(m && out, "null argument");
+  *out = m->cfg;
+  return PRANA_OK;
+}
+
+int prana_kv_create(prana_model* m, size_t positions, prana_kv** out) {
+  API_BEGIN
+  NEED(m && out, "null argument");
+  *out = nullptr;
+  DevScope ds(m->ctx->device);
+  const auto& c = m->cfg;
+  if (positions > (size_t)c.seq_len) positions = (size_t)c.seq_len;
+  NEED(positions > 0, "kv cache needs at least one position");
+  std::unique_ptr<prana_kv, void (*)(prana_kv*)> kv(new prana_kv(), destroy_kv);
+  kv->m = m;
+  kv->positions = positions;
+  const size_t kv_dim = (size_t)(c.n_kv_heads * c.head_dim);
+  const size_t per = (size_t)c.n_layers * positions * kv_dim;
+  if (cudaMalloc(&kv->k, per * 2) != cudaSuccess || cudaMalloc(&kv->v, per * 2) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(PRANA_E_OOM, "kv cache allocation (%zu bytes) failed", per * 4);
+  }
+  PRANA_CK(cudaMemset(kv->k, 0, per * 2));
+  PRANA_CK(cudaMemset(kv->v, 0, per * 2));
+  // attention splits for this capacity: >= 2 CTAs per SM at full length
+  const int by_len = (int)((positions + 31) / 32);
+  const int by_sm = (int)((2 * m->ctx->sm_count + c.n_kv_heads - 1) / c.n_kv_heads);
+  kv->n_splits = std::max(1, std::min(by_len, by_sm));
+  const int group = (int)(c.n_heads / c.n_kv_heads);
+  const int rows_cta = std::max(1, 4096 / (int)(c.head_dim * group));
+  const size_t vh = (size_t)rows_cta * group;  // largest row chunk one attention CTA takes
+  const size_t ml = (size_t)c.n_kv_heads * kv->n_splits * vh * 2;
+  const size_t po = (size_t)c.n_kv_heads * kv->n_splits * vh * c.head_dim;
+  PRANA_CK(cudaMalloc(&kv->part_ml, (ml + po) * 4));
+  kv->part_o = kv->part_ml + ml;
+  PRANA_CK(cudaMalloc(&kv->counters, 1024 * sizeof(unsigned)));
+  PRANA_CK(cudaMemset(kv->counters, 0, 1024 * sizeof(unsigned)));
+  PRANA_CK(cudaMalloc(&kv->ring, (positions + 64) * sizeof(uint32_t)));
+  kv->ring_n = reinterpret_cast<int*>(kv->ring + positions + 32);
+  m->caches.push_back(kv.get());
+  *out = kv.release();
+  return PRANA_OK;
+  API_END
+}
+
+int prana_kv_free(prana_kv* kv) {
+  destroy_kv(kv);
+  return PRANA_OK;
+}
+
+int prana_kv_read(prana_kv* kv, size_t layer, int is_v, size_t rows, uint16_t* host) {
+  NEED(kv && host, "null argument");
+  const auto& c = kv->m->cfg;
+  NEED(layer < (size_t)c.n_layers && rows <= kv->positions, "layer/rows out of range");
+  DevScope ds(kv->m->ctx->device);
+  const size_t kv_dim = (size_t)(c.n_kv_heads * c.head_dim);
+  const __half* base = (is_v ? kv->v : kv->k) + layer * kv->positions * kv_dim;
+  PRANA_CK(cudaStreamSynchronize(kv->m->ctx->own));
+  PRANA_CK(cudaMemcpy(host, base, rows * kv_dim * 2, cudaMemcpyDeviceToHost));
+  return PRANA_OK;
+}
+
+int prana_forward(prana_model* m, prana_kv* kv, uint32_t token, size_t pos, float* logits, uint32_t* next) {
+  API_BEGIN
+  NEED(m && kv && kv->m == m, "null or mismatched argument");
+  NEED(pos < kv->positions, "position %zu beyond kv capacity %zu", pos, kv->positions);
+  NEED(token < (uint64_t)m->cfg.vocab_size, "token %u out of vocabulary", token);
+  DevScope ds(m->ctx->device);
+  int rc = ensure_graphs(m, kv, false);
+  if (rc) return rc;
+  cudaStream_t st = m->ctx->own;
+  m->h_io[0] = (int)token;
+  m->h_io[1] = (int)pos;
+  PRANA_CK(cudaMemcpyAsync(m->d_tokpos, m->h_io, 8, cudaMemcpyHostToDevice, st));
+  PRANA_CK(cudaGraphLaunch(kv->g_step, st));
+  PRANA_CK(cudaMemcpyAsync(m->h_tok, m->dec->tok_out, 4, cudaMemcpyDeviceToHost, st));
+  if (logits) PRANA_CK(cudaMemcpyAsync(logits, m->dec->logits, (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, st));
+  PRANA_CK(cudaStreamSynchronize(st));
+  if (next) *next = m->h_tok[0];
+  kv->loop_active = false;
+  return PRANA_OK;
+  API_END
+}
+
+int prana_forward_trace(prana_model* m, prana_kv* kv, uint32_t token, size_t pos, float* logits, int8_t* q_host,
+                        float* s_host, size_t cap, size_t* n_out) {
+  API_BEGIN
+  NEED(m && kv && kv->m == m && q_host && s_host && n_out, "null or mismatched argument");
+  NEED(pos < kv->positions, "position %zu beyond kv capacity %zu", pos, kv->positions);
+  NEED(token < (uint64_t)m->cfg.vocab_size, "token %u out of vocabulary", token);
+  const auto& c = m->cfg;
+  const size_t need = (size_t)c.n_layers * (2 * c.dim + c.n_heads * c.head_dim + c.hidden_dim) + c.dim;
+  NEED(cap >= need, "trace buffer holds %zu values, %zu needed", cap, need);
+  DevScope ds(m->ctx->device);
+  cudaStream_t st = m->ctx->own;
+  Trace tr;
+  PRANA_CK(cudaMalloc(&tr.q, need));
+  PRANA_CK(cudaMalloc(&tr.s, need / 32 * 4 + 4));
+  struct Free {
+    Trace& t;
+    ~Free() {
+      cudaFree(t.q);
+      cudaFree(t.s);
+    }
+  } fr{tr};
+  uint32_t* tok_d = m->dec->toks;
+  PRANA_CK(cudaMemcpyAsync(tok_d, &token, 4, cudaMemcpyHostToDevice, st));
+  int rc = enqueue_rows(m, kv, *m->dec, 1, tok_d, nullptr, (int)pos, nullptr, MODE_CACHE, true, false, &tr);
+  if (rc) return rc;
+  PRANA_CK(cudaMemcpyAsync(q_host, tr.q, tr.nq, cudaMemcpyDeviceToHost, st));
+  PRANA_CK(cudaMemcpyAsync(s_host, tr.s, tr.ns * 4, cudaMemcpyDeviceToHost, st));
+  if (logits) PRANA_CK(cudaMemcpyAsync(logits, m->dec->logits, (size_t)c.vocab_size * 4, cudaMemcpyDeviceToHost, st));
+  PRANA_CK(cudaStreamSynchronize(st));
+  *n_out = tr.nq;
+  kv->loop_active = false;
+  return PRANA_OK;
+  API_END
+}
+
+int prana_kv_write(prana_kv* kv, size_t layer, int is_v, size_t rows, const uint16_t* host) {
+  NEED(kv && host, "null argument");
+  const auto& c = kv->m->cfg;
+  NEED(layer < (size_t)c.n_layers && rows <= kv->positions, "layer/rows out of range");
+  DevScope ds(kv->m->ctx->device);
+  const size_t kv_dim = (size_t)(c.n_kv_heads * c.head_dim);
+  __half* base = (is_v ? kv->v : kv->k) + layer * kv->positions * kv_dim;
+  PRANA_CK(cudaStreamSynchronize(kv->m->ctx->own));
+  PRANA_CK(cudaMemcpy(base, host, rows * kv_dim * 2, cudaMemcpyHostToDevice));
+  return PRANA_OK;
+}
+
+int prana_prefill(prana_model* m, prana_kv* kv, const uint32_t* tokens, size_t n) {
+  API_BEGIN
+  NEED(m && kv && kv->m == m && tokens, "null or mismatched argument");
+  if (!n) return PRANA_OK;
+  NEED(n <= kv->positions, "prefill of %zu tokens beyond kv capacity %zu", n, kv->positions);
+  for (size_t i = 0; i < n; i++) NEED(tokens[i] < (uint64_t)m->cfg.vocab_size, "token out of vocabulary");
+  DevScope ds(m->ctx->device);
+  Bufs b;
+  int rc = make_bufs(m, n, true, b);
+  if (rc) return rc;
+  cudaStream_t st = m->ctx->own;
+  PRANA_CK(cudaMemcpyAsync(b.toks, tokens, n * 4, cudaMemcpyHostToDevice, st));
+  rc = enqueue_rows(m, kv, b, (int)n, b.toks, nullptr, 0, nullptr, MODE_WINDOW, false, false);
+  if (rc) return rc;
+  PRANA_CK(cudaStreamSynchronize(st));
+  kv->loop_active = false;
+  return PRANA_OK;
+  API_END
+}
+
+int prana_forward_batch(prana_model* m, prana_kv* kv, const uint32_t* tokens, size_t n, size_t pos0, float* logits,
+                        uint32_t* argmax) {
+  API_BEGIN
+  NEED(m && kv && kv->m == m && tokens, "null or mismatched argument");
+  if (!n) return PRANA_OK;
+  NEED(pos0 + n <= kv->positions, "rows %zu..%zu beyond kv capacity %zu", pos0, pos0 + n, kv->positions);
+  for (size_t i = 0; i < n; i++) NEED(tokens[i] < (uint64_t)m->cfg.vocab_size, "token out of vocabulary");
+  DevScope ds(m->ctx->device);
+  cudaStream_t st = m->ctx->own;
+  std::unique_ptr<Bufs> tmp;
+  Bufs* b = m->dec.get();
+  if (n > b->rows) {
+    tmp.reset(new Bufs());
+    int rc = make_bufs(m, n, false, *tmp);
+    if (rc) return rc;
+    b = tmp.get();
+  }
+  PRANA_CK(cudaMemcpyAsync(b->toks, tokens, n * 4, cudaMemcpyHostToDevice, st));
+  int rc = enqueue_rows(m, kv, *b, (int)n, b->toks, nullptr, (int)pos0, nullptr, MODE_CACHE, true, false);
+  if (rc) return rc;
+  if (logits) PRANA_CK(cudaMemcpyAsync(logits, b->logits, n * (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, st));
+  if (argmax) PRANA_CK(cudaMemcpyAsync(argmax, b->tok_out, n * 4, cudaMemcpyDeviceToHost, st));
+  PRANA_CK(cudaStreamSynchronize(st));
+  kv->loop_active = false;
+  return PRANA_OK;
+  API_END
+}
+
+int prana_decode_begin(prana_model* m, prana_kv* kv, uint32_t token, size_t pos) {
+  API_BEGIN
+  NEED(m && kv && kv->m == m, "null or mismatched argument");
+  NEED(pos < kv->positions, "position beyond kv capacity");
+  NEED(token < (uint64_t)m->cfg.vocab_size, "token out of vocabulary");
+  DevScope ds(m->ctx->device);
+  int rc = ensure_graphs(m, kv, true);
+  if (rc) return rc;
+  cudaStream_t st = m->ctx->own;
+  m->h_io[0] = (int)token;
+  m->h_io[1] = (int)pos;
+  PRANA_CK(cudaMemcpyAsync(m->d_tokpos, m->h_io, 8, cudaMemcpyHostToDevice, st));
+  PRANA_CK(cudaMemsetAsync(kv->ring_n, 0, sizeof(int), st));
+  PRANA_CK(cudaStreamSynchronize(st));
+  kv->loop_pos = pos;
+  kv->loop_active = true;
+  return PRANA_OK;
+  API_END
+}
+
+int prana_decode_run(prana_model* m, prana_kv* kv, size_t n_steps) {
+  NEED(m && kv && kv->m == m && kv->loop_active, "decode loop not started");
+  NEED(kv->loop_pos + n_steps <= kv->positions, "decode loop would pass kv capacity %zu", kv->positions);
+  DevScope ds(m->ctx->device);
+  for (size_t i = 0; i < n_steps; i++) PRANA_CK(cudaGraphLaunch(kv->g_loop, m->ctx->own));
+  kv->loop_pos += n_steps;
+  return PRANA_OK;
+}
+
+int prana_decode_tokens(prana_model* m, prana_kv* kv, uint32_t* out, size_t max, size_t* n_out) {
+  NEED(m && kv && kv->m == m && n_out, "null argument");
+  DevScope ds(m->ctx->device);
+  int n = 0;
+  PRANA_CK(cudaStreamSynchronize(m->ctx->own));
+  PRANA_CK(cudaMemcpy(&n, kv->ring_n, sizeof(int), cudaMemcpyDeviceToHost));
+  size_t cnt = std::min((size_t)n, std::min(max, kv->positions));
+  if (cnt && out) PRANA_CK(cudaMemcpy(out, kv->ring, cnt * 4, cudaMemcpyDeviceToHost));
+  *n_out = cnt;
+  return PRANA_OK;
+}
+
+int prana_generate(prana_model* m, const uint32_t* prompt, size_t p, size_t steps, int64_t stop_id, uint32_t* out,
+                   size_t* n_out) {
+  API_BEGIN
+  NEED(m && prompt && n_out && (out || !steps), "null argument");
+  NEED(p > 0, "prompt encoded to zero tokens");
+  *n_out = 0;
+  const size_t max_pos = std::min((size_t)m->cfg.seq_len, p + steps);
+  prana_kv* kv = nullptr;
+  int rc = prana_kv_create(m, max_pos, &kv);
+  if (rc) return rc;
+  std::unique_ptr<prana_kv, void (*)(prana_kv*)> guard(kv, destroy_kv);
+  size_t start = 0;
+  uint32_t token = prompt[0];
+  if (p > 1 && p <= max_pos) {
+    if ((rc = prana_prefill(m, kv, prompt, p - 1))) return rc;
+    start = p - 1;
+    token = prompt[p - 1];
+  }
+  size_t produced = 0;
+  // teacher-forced positions (only when the prompt overflows the context)
+  size_t pos = start;
+  for (; pos + 1 < p && pos < max_pos; pos++) {
+    if ((rc = prana_forward(m, kv, token, pos, nullptr, nullptr))) return rc;
+    token = prompt[pos + 1];
+  }
+  if (pos + 1 < max_pos) {
+    // every remaining position samples: run them on the device back to back
+    const size_t n = max_pos - 1 - pos;
+    if ((rc = prana_decode_begin(m, kv, token, pos))) return rc;
+    if ((rc = prana_decode_run(m, kv, n))) return rc;
+    std::vector<uint32_t> ids(n);
+    size_t got = 0;
+    if ((rc = prana_decode_tokens(m, kv, ids.data(), n, &got))) return rc;
+    for (size_t i = 0; i < got && produced < steps; i++) {
+      if (stop_id >= 0 && ids[i] == (uint64_t)stop_id) break;
+      out[produced++] = ids[i];
+    }
+  }
+  *n_out = produced;
+  return PRANA_OK;
+  API_END
+}
+
+int prana_generate_speculative(prana_model* target, prana_model* draft, const uint32_t* prompt, size_t p,
+                               size_t steps, size_t k, int64_t stop_id, uint32_t* out, size_t* n_out,
+                               size_t* stats) {
+  API_BEGIN
+  NEED(target && draft && prompt && n_out && (out || !steps), "null argument");
+  NEED(k >= 1, "draft length must be >= 1");
+  NEED(p > 0, "prompt encoded to zero tokens");
+  NEED(target->cfg.vocab_size == draft->cfg.vocab_size, "draft and target must share a vocabulary");
+  *n_out = 0;
+  const size_t max_pos = std::min((size_t)target->cfg.seq_len, p + steps);
+  prana_kv *tkv = nullptr, *dkv = nullptr;
+  int rc = prana_kv_create(target, max_pos, &tkv);
+  if (rc) return rc;
+  std::unique_ptr<prana_kv, void (*)(prana_kv*)> g1(tkv, destroy_kv);
+  if ((rc = prana_kv_create(draft, max_pos, &dkv))) return rc;
+  std::unique_ptr<prana_kv, void (*)(prana_kv*)> g2(dkv, destroy_kv);
+  NEED(dkv->positions >= max_pos, "draft context shorter than target's");
+  if (p > 1) {
+    if ((rc = prana_prefill(target, tkv, prompt, p - 1)) || (rc = prana_prefill(draft, dkv, prompt, p - 1))) return rc;
+  }
+  size_t pos = p - 1, generated = 0, proposed = 0, accepted = 0;
+  uint32_t last = prompt[p - 1];
+  std::vector<uint32_t> drafts(k), inputs(k + 1), tnext(k + 1);
+  bool stop = false;
+  while (!stop && pos + 1 < max_pos) {
+    const size_t budget = std::min(max_pos - 1 - pos, k);
+    uint32_t d = last;
+    for (size_t j = 0; j < budget; j++) {
+      if ((rc = prana_forward(draft, dkv, d, pos + j, nullptr, &d))) return rc;
+      drafts[j] = d;
+    }
+    proposed += budget;
+    inputs[0] = last;
+    for (size_t j = 0; j < budget; j++) inputs[j + 1] = drafts[j];
+    if ((rc = prana_forward_batch(target, tkv, inputs.data(), budget + 1, pos, nullptr, tnext.data()))) return rc;
+    for (size_t i = 0; i <= budget; i++) {
+      const uint32_t tn = tnext[i];
+      if (i < budget && tn == drafts[i]) accepted++;
+      if (stop_id >= 0 && tn == (uint64_t)stop_id) {
+        stop = true;
+        break;
+      }
+      out[generated++] = tn;
+      pos++;
+      last = tn;
+      if (generated >= steps || pos + 1 >= max_pos) {
+        stop = true;
+        break;
+      }
+      if (i == budget || tn != drafts[i]) break;
+    }
+  }
+  if (stats) {
+    stats[0] = proposed;
+    stats[1] = accepted;
+  }
+  *n_out = generated;
+  return PRANA_OK;
+  API_END
+}
+
+}  // extern "C"

@@ -1,0 +1,207 @@
+"""The `prana-model` decode API (crates/prana-model/src/lib.rs:17-23) on B200.
+
+`Model.load` reads a GGUF file into HBM (gguf.rs:338-460); `KvCache`, `forward`,
+`prefill`, `forward_batch`, `generate` and `generate_speculative` keep the
+reference's names and semantics over token ids (the tokenizer is not on the
+decode path).  Host buffers cross the ABI; only token ids and, on request,
+logits leave the device.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import weakref
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _ffi
+from ._ffi import ModelConfig, call
+from .kernels import context
+
+
+def _u32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.uint32).reshape(-1))
+
+
+@dataclass
+class Config:
+    """checkpoint.rs:32-65 Config (the fields the decode path reads)."""
+
+    dim: int
+    hidden_dim: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    vocab_size: int
+    seq_len: int
+    head_dim: int
+    rope_theta: float
+    norm_eps: float
+    rope_neox: bool
+    has_bias: bool
+    shared_classifier: bool
+    weight_bytes: int
+
+    def kv_dim(self) -> int:
+        return self.n_kv_heads * self.head_dim
+
+    def q_dim(self) -> int:
+        return self.n_heads * self.head_dim
+
+
+class Model:
+    def __init__(self, handle: C.c_void_p, device: int):
+        self._h = handle
+        self.device = device
+        self._caches: "weakref.WeakSet[KvCache]" = weakref.WeakSet()
+        c = ModelConfig()
+        call("prana_model_config_get", handle, C.byref(c))
+        self.config = Config(c.dim, c.hidden_dim, c.n_layers, c.n_heads, c.n_kv_heads, c.vocab_size, c.seq_len,
+                             c.head_dim, c.rope_theta, c.norm_eps, bool(c.rope_neox), bool(c.has_bias),
+                             bool(c.shared_classifier), c.weight_bytes)
+
+    @classmethod
+    def load(cls, path: str, device: int = 0) -> "Model":
+        h = C.c_void_p()
+        call("prana_model_load_gguf", context(device), str(path).encode(), C.byref(h))
+        return cls(h, device)
+
+    @property
+    def handle(self) -> C.c_void_p:
+        return self._h
+
+    def stream(self) -> int:
+        """cudaStream_t (as int) all model-level work runs on."""
+        s = C.c_void_p()
+        call("prana_ctx_stream", context(self.device), C.byref(s))
+        return s.value or 0
+
+    def close(self):
+        """Free the model and every KV cache still attached to it."""
+        for cache in list(getattr(self, "_caches", ())):
+            cache.close()
+        if getattr(self, "_h", None) is not None and self._h.value:
+            _ffi.lib().prana_model_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class KvCache:
+    """KvCache::with_len (infer.rs:37-45): f16 K/V rows in HBM."""
+
+    def __init__(self, model: Model, positions: int | None = None):
+        self.model = model
+        self.positions = min(positions or model.config.seq_len, model.config.seq_len)
+        self._h = C.c_void_p()
+        call("prana_kv_create", model.handle, self.positions, C.byref(self._h))
+        model._caches.add(self)
+
+    @property
+    def handle(self) -> C.c_void_p:
+        return self._h
+
+    def read(self, layer: int, is_v: bool, rows: int) -> np.ndarray:
+        out = np.empty((rows, self.model.config.kv_dim()), dtype=np.uint16)
+        call("prana_kv_read", self._h, layer, int(is_v), rows, out.ctypes.data_as(C.c_void_p))
+        return out
+
+    def write(self, layer: int, is_v: bool, rows: np.ndarray) -> None:
+        rows = np.ascontiguousarray(rows, dtype=np.uint16)
+        call("prana_kv_write", self._h, layer, int(is_v), rows.shape[0], rows.ctypes.data_as(C.c_void_p))
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            _ffi.lib().prana_kv_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def forward(model: Model, cache: KvCache, token: int, pos: int, want_logits: bool = True):
+    """forward (infer.rs:134-136): returns (logits or None, argmax token)."""
+    logits = np.empty(model.config.vocab_size, dtype=np.float32) if want_logits else None
+    nxt = C.c_uint32()
+    call("prana_forward", model.handle, cache.handle, token, pos,
+         logits.ctypes.data_as(C.c_void_p) if logits is not None else None, C.byref(nxt))
+    return logits, nxt.value
+
+
+def forward_trace(model: Model, cache: KvCache, token: int, pos: int):
+    """Diagnostic forward: (logits, int8 activation rows, their scales) in CPU-path order."""
+    c = model.config
+    n = c.n_layers * (2 * c.dim + c.q_dim() + c.hidden_dim) + c.dim
+    q = np.empty(n, np.int8)
+    s = np.empty(n // 32, np.float32)
+    logits = np.empty(c.vocab_size, np.float32)
+    got = C.c_size_t()
+    call("prana_forward_trace", model.handle, cache.handle, token, pos, logits.ctypes.data_as(C.c_void_p),
+         q.ctypes.data_as(C.c_void_p), s.ctypes.data_as(C.c_void_p), n, C.byref(got))
+    assert got.value == n
+    return logits, q, s
+
+
+def prefill(model: Model, cache: KvCache, tokens) -> None:
+    """prefill (infer.rs:220-286)."""
+    t = _u32(tokens)
+    call("prana_prefill", model.handle, cache.handle, t.ctypes.data_as(C.c_void_p), t.size)
+
+
+def forward_batch(model: Model, cache: KvCache, tokens, pos0: int, want_logits: bool = True):
+    """forward_batch (infer.rs:296-374): returns (logits [n, vocab] or None, argmax per row)."""
+    t = _u32(tokens)
+    n = t.size
+    logits = np.empty((n, model.config.vocab_size), dtype=np.float32) if want_logits else None
+    am = np.empty(n, dtype=np.uint32)
+    call("prana_forward_batch", model.handle, cache.handle, t.ctypes.data_as(C.c_void_p), n, pos0,
+         logits.ctypes.data_as(C.c_void_p) if logits is not None else None, am.ctypes.data_as(C.c_void_p))
+    return logits, am
+
+
+def generate(model: Model, prompt, steps: int, stop_id: int = -1) -> np.ndarray:
+    """generate (infer.rs:696-771), greedy, over token ids."""
+    p = _u32(prompt)
+    out = np.empty(max(steps, 1), dtype=np.uint32)
+    n = C.c_size_t()
+    call("prana_generate", model.handle, p.ctypes.data_as(C.c_void_p), p.size, steps, stop_id,
+         out.ctypes.data_as(C.c_void_p), C.byref(n))
+    return out[: n.value].copy()
+
+
+def generate_speculative(target: Model, draft: Model, prompt, steps: int, k: int, stop_id: int = -1):
+    """generate_speculative (infer.rs:581-690): returns (ids, (proposed, accepted))."""
+    p = _u32(prompt)
+    out = np.empty(max(steps, 1), dtype=np.uint32)
+    n = C.c_size_t()
+    stats = (C.c_size_t * 2)()
+    call("prana_generate_speculative", target.handle, draft.handle, p.ctypes.data_as(C.c_void_p), p.size, steps, k,
+         stop_id, out.ctypes.data_as(C.c_void_p), C.byref(n), stats)
+    return out[: n.value].copy(), (stats[0], stats[1])
+
+
+class DecodeLoop:
+    """Device-resident greedy decode: the per-token graph replays back to back
+    with the sampled id fed back on the device."""
+
+    def __init__(self, model: Model, cache: KvCache):
+        self.model, self.cache = model, cache
+
+    def begin(self, token: int, pos: int) -> None:
+        call("prana_decode_begin", self.model.handle, self.cache.handle, token, pos)
+
+    def run(self, n_steps: int) -> None:
+        call("prana_decode_run", self.model.handle, self.cache.handle, n_steps)
+
+    def tokens(self, max_n: int) -> np.ndarray:
+        out = np.empty(max(max_n, 1), dtype=np.uint32)
+        n = C.c_size_t()
+        call("prana_decode_tokens", self.model.handle, self.cache.handle, out.ctypes.data_as(C.c_void_p), max_n, C.byref(n))
+        return out[: n.value].copy()
