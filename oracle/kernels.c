@@ -10,24 +10,8 @@
 
 #include "prana_oracle.h"
 
-/* crates/prana-kernels/src/lib.rs:57-73 */
-float or_f16_to_f32(uint16_t h) {
-  uint32_t sign = (h >> 15) & 1u, exp = (h >> 10) & 0x1fu, frac = h & 0x3ffu, bits;
-  if (exp == 0 && frac == 0) {
-    bits = sign << 31;
-  } else if (exp == 0) {
-    /* subnormal: frac * 2^-24, exact in f32 */
-    float v = (float)frac * 5.9604644775390625e-08f;
-    return sign ? -v : v;
-  } else if (exp == 0x1f) {
-    bits = (sign << 31) | 0x7f800000u | (frac << 13);
-  } else {
-    bits = (sign << 31) | ((exp + 127 - 15) << 23) | (frac << 13);
-  }
-  float f;
-  memcpy(&f, &bits, 4);
-  return f;
-}
+/* crates/prana-kernels/src/lib.rs:57-73 (inline body in prana_oracle.h) */
+float or_f16_to_f32(uint16_t h) { return or_f16_to_f32_inline(h); }
 
 /* crates/prana-kernels/src/lib.rs:78-113 (round-to-nearest-even) */
 uint16_t or_f32_to_f16(float x) {
@@ -427,7 +411,7 @@ static void decode_one_head(const float *q, const uint16_t *kc, const uint16_t *
   const float *qv = q + h * hd;
   for (size_t t = 0; t <= pos; t++) {
     const uint16_t *kr = kc + t * kv_stride + kv_h * hd;
-    for (size_t d = 0; d < hd; d++) tmp[d] = or_f16_to_f32(kr[d]);
+    for (size_t d = 0; d < hd; d++) tmp[d] = or_f16_to_f32_inline(kr[d]);
     float dot = 0.0f;
     for (size_t d = 0; d < hd; d++) dot += qv[d] * tmp[d];
     scores[t] = dot * scale;
@@ -437,7 +421,7 @@ static void decode_one_head(const float *q, const uint16_t *kc, const uint16_t *
   for (size_t t = 0; t <= pos; t++) {
     const uint16_t *vr = vc + t * kv_stride + kv_h * hd;
     float p = probs[t];
-    for (size_t d = 0; d < hd; d++) dst[d] += p * or_f16_to_f32(vr[d]);
+    for (size_t d = 0; d < hd; d++) dst[d] += p * or_f16_to_f32_inline(vr[d]);
   }
 }
 

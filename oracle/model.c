@@ -523,13 +523,14 @@ static void logits(const or_model *m, const float *x, float *out) {
 /* Diagnostic trace of the quantized activation rows a forward pass feeds its
  * integer dots (the same quantize_acts the matmuls run internally). */
 static __thread int8_t *tr_q;
-static __thread float *tr_s;
+static __thread float *tr_s, *tr_v;
 static __thread size_t tr_nq, tr_cap;
 
 static void trace_site(const float *x, size_t n) {
   if (!tr_q || tr_nq + n > tr_cap) return;
   int32_t *sums = malloc(sizeof(int32_t) * (n / 32));
   or_quantize_acts(x, n, tr_q + tr_nq, tr_s + tr_nq / 32, sums);
+  if (tr_v) memcpy(tr_v + tr_nq, x, n * sizeof(float));
   free(sums);
   tr_nq += n;
 }
@@ -583,9 +584,10 @@ void or_forward(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float 
 }
 
 size_t or_forward_trace(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float *logits, int8_t *q,
-                        float *s, size_t cap) {
+                        float *s, float *vals, size_t cap) {
   tr_q = q;
   tr_s = s;
+  tr_v = vals;
   tr_nq = 0;
   tr_cap = cap;
   or_forward(m, kv, token, pos, logits);

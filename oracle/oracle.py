@@ -91,7 +91,7 @@ def lib() -> C.CDLL:
             "or_kv_free": ([P], None),
             "or_kv_layer": ([P, C.c_int, C.c_int], P),
             "or_forward": ([P, P, C.c_uint32, SZ, P], None),
-            "or_forward_trace": ([P, P, C.c_uint32, SZ, P, P, P, SZ], SZ),
+            "or_forward_trace": ([P, P, C.c_uint32, SZ, P, P, P, P, SZ], SZ),
             "or_prefill": ([P, P, P, SZ], None),
             "or_forward_batch": ([P, P, P, SZ, SZ, P], None),
             "or_generate": ([P, P, SZ, SZ, C.c_int64, P], SZ),
@@ -197,14 +197,17 @@ class OModel:
         c = self.c
         return c.n_layers * (2 * c.dim + c.n_heads * c.head_dim + c.hidden_dim) + c.dim
 
-    def forward_trace(self, kv: "OKv", token: int, pos: int):
+    def forward_trace(self, kv: "OKv", token: int, pos: int, with_values: bool = False):
+        """(logits, int8 activation rows, scales[, the f32 values quantized]) in forward order."""
         n = self.trace_len()
         q = np.empty(n, np.int8)
         s = np.empty(n // 32, np.float32)
+        v = np.empty(n, np.float32) if with_values else None
         lg = np.empty(self.c.vocab_size, np.float32)
-        got = lib().or_forward_trace(self.h, kv.h, token, pos, ptr(lg), ptr(q), ptr(s), n)
+        got = lib().or_forward_trace(self.h, kv.h, token, pos, ptr(lg), ptr(q), ptr(s),
+                                     ptr(v) if v is not None else None, n)
         assert got == n
-        return lg, q, s
+        return (lg, q, s, v) if with_values else (lg, q, s)
 
     def prefill(self, kv: "OKv", tokens):
         t = np.ascontiguousarray(tokens, np.uint32)

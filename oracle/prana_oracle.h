@@ -44,6 +44,22 @@ enum { OR_TIER_AUTO = 0, OR_TIER_SCALAR = 1, OR_TIER_AVX2 = 2, OR_TIER_VNNI = 3 
 
 /* ---- f16 (lib.rs:57-113) ---- */
 float or_f16_to_f32(uint16_t h);
+/* inline form used by the attention loops (the Rust version inlines too) */
+static inline float or_f16_to_f32_inline(uint16_t h) {
+  uint32_t sign = (h >> 15) & 1u, exp = (h >> 10) & 0x1fu, frac = h & 0x3ffu, bits;
+  if (exp == 0 && frac == 0) {
+    bits = sign << 31;
+  } else if (exp == 0) {
+    float v = (float)frac * 5.9604644775390625e-08f; /* frac * 2^-24, exact */
+    return sign ? -v : v;
+  } else if (exp == 0x1f) {
+    bits = (sign << 31) | 0x7f800000u | (frac << 13);
+  } else {
+    bits = (sign << 31) | ((exp + 127 - 15) << 23) | (frac << 13);
+  }
+  union { uint32_t u; float f; } cv = {bits};
+  return cv.f;
+}
 uint16_t or_f32_to_f16(float x);
 
 /* ---- activation / weight quantization (matmul.rs:61-127) ---- */
@@ -146,7 +162,7 @@ void or_forward(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float 
 /* or_forward that also records every quantized activation row (per layer: attn-norm
  * input, attention output, ffn-norm input, silu(g)*u; then the final-norm input) */
 size_t or_forward_trace(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float *logits, int8_t *q,
-                        float *s, size_t cap);
+                        float *s, float *vals /* f32 values quantized, may be NULL */, size_t cap);
 /* batched prompt, no logits (infer.rs:220-286) */
 void or_prefill(const or_model *m, or_kv *kv, const uint32_t *tokens, size_t n);
 /* verify pass: logits [n][vocab] (infer.rs:296-374) */

@@ -16,14 +16,22 @@ float or_dot_q40_q8_scalar(const int8_t *aq, const float *as, const int32_t *asu
 float or_dot_q4k_q8_scalar(const int8_t *aq, const float *as, const int32_t *asum, size_t k,
                            const uint8_t *row, const float *ds);
 
-/* simd_x86.rs:18-29 */
+/* simd_x86.rs:18-29: detected once (the reference caches in a OnceLock) */
+static int simd_cached = -1, vnni_cached = -1;
+
 int or_simd_available(void) {
-  __builtin_cpu_init();
-  return __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma");
+  if (simd_cached < 0) {
+    __builtin_cpu_init();
+    simd_cached = __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma");
+  }
+  return simd_cached;
 }
 int or_vnni_available(void) {
-  __builtin_cpu_init();
-  return or_simd_available() && __builtin_cpu_supports("avxvnni");
+  if (vnni_cached < 0) {
+    __builtin_cpu_init();
+    vnni_cached = or_simd_available() && __builtin_cpu_supports("avxvnni");
+  }
+  return vnni_cached;
 }
 int or_default_tier(void) {
   if (or_vnni_available()) return OR_TIER_VNNI;

@@ -19,8 +19,8 @@ CSRC = PKG / "csrc"
 LIB = PKG / "_lib"
 ROOT = PKG.parent
 
-CUDA_SOURCES = ["kernels.cu", "attention.cu", "ctx.cu", "model.cu"]
-CUDA_HEADERS = ["common.cuh", "gemv.cuh", "internal.h", "host.h"]
+CUDA_SOURCES = ["kernels.cu", "attention.cu", "decode.cu", "ctx.cu", "model.cu"]
+CUDA_HEADERS = ["common.cuh", "gemv.cuh", "tma.cuh", "finish.cuh", "internal.h", "host.h"]
 NVCC_FLAGS = [
     "-O3",
     "-std=c++17",

@@ -13,6 +13,7 @@
 // one CTA per (query-row chunk, kv head), no split.
 #include <climits>
 
+#include "finish.cuh"
 #include "internal.h"
 
 namespace prana {
@@ -187,6 +188,11 @@ __device__ void attn_body(const float* __restrict__ q, int q_stride, const void*
 }
 
 template <int HD>
+__device__ void attn_merge_splits(const AttnArgs& a, int kvh, int split, int row0, int VH, int group, int q_stride,
+                                  float (&acc)[(AT_MAX_VHD / 2 + AT_THREADS - 1) / AT_THREADS][2], const float* m_row,
+                                  const float* l_row, unsigned* ticket);
+
+template <int HD>
 __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs a, int row0, int n_rows) {
   extern __shared__ __align__(16) float sm[];
   constexpr int NP = (AT_MAX_VHD / 2 + AT_THREADS - 1) / AT_THREADS;
@@ -205,6 +211,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
   pdl_trigger();
   const int tid = threadIdx.x;
   const int q_stride = a.n_heads * HD;
+  __shared__ unsigned ticket;
   if (a.n_splits == 1) {
 #pragma unroll
     for (int i = 0; i < NP; i++) {
@@ -217,9 +224,36 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
       o[0] = acc[i][0] * inv;
       o[1] = acc[i][1] * inv;
     }
-    return;
+  } else {
+    attn_merge_splits<HD>(a, kvh, split, row0, VH, group, q_stride, acc, m_row, l_row, &ticket);
+    if (ticket != (unsigned)a.n_splits - 1) return;
   }
-  // publish this split's partials
+  // every kv head of these rows finished: quantize the rows for the wo projection
+  if (a.out_q) {
+    __shared__ float red[8 * (AT_THREADS / 32)];
+    __shared__ float inv_s[8];
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) ticket = atomicAdd(a.counters + a.n_kv, 1u);
+    __syncthreads();
+    if (ticket != (unsigned)a.n_kv - 1) return;
+    __threadfence();
+    block_quantize_rows(a.out + (size_t)row0 * q_stride, nullptr, 0.0f, n_rows, q_stride,
+                        a.out_q + (size_t)row0 * q_stride, a.out_s + (size_t)row0 * (q_stride / 32),
+                        a.out_sum + (size_t)row0 * (q_stride / 32), red, inv_s, AT_THREADS, 1);
+    if (tid == 0) a.counters[a.n_kv] = 0u;
+  }
+}
+
+// Publish this split's (max, sum, o) and, in the last split CTA of the kv head
+// to finish, merge all splits into the output.  `ticket` tells the caller
+// whether this CTA merged (== n_splits - 1).
+template <int HD>
+__device__ void attn_merge_splits(const AttnArgs& a, int kvh, int split, int row0, int VH, int group, int q_stride,
+                                  float (&acc)[(AT_MAX_VHD / 2 + AT_THREADS - 1) / AT_THREADS][2], const float* m_row,
+                                  const float* l_row, unsigned* ticket) {
+  constexpr int NP = (AT_MAX_VHD / 2 + AT_THREADS - 1) / AT_THREADS;
+  const int tid = threadIdx.x;
   const size_t base = ((size_t)kvh * a.n_splits + split) * VH;
   for (int vh = tid; vh < VH; vh += AT_THREADS) {
     a.part_ml[(base + vh) * 2] = m_row[vh];
@@ -234,10 +268,9 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
   }
   __threadfence();
   __syncthreads();
-  __shared__ unsigned ticket;
-  if (tid == 0) ticket = atomicAdd(a.counters + kvh, 1u);
+  if (tid == 0) *ticket = atomicAdd(a.counters + kvh, 1u);
   __syncthreads();
-  if (ticket != (unsigned)a.n_splits - 1) return;
+  if (*ticket != (unsigned)a.n_splits - 1) return;
   __threadfence();
   // last CTA of this kv head: merge all splits
 #pragma unroll

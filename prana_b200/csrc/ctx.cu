@@ -266,6 +266,7 @@ int prana_ctx_create(int device, prana_ctx** out) {
     return fail(PRANA_E_CUDA, "context setup failed");
   }
   c->stream = c->own;
+  c->err = c->counters + 4095;
   *out = c;
   return PRANA_OK;
   API_END
@@ -345,23 +346,51 @@ int prana_quantize_acts(prana_ctx* c, const float* x, size_t rows, size_t k, int
   return PRANA_OK;
 }
 
+// out[t] = W . quantize_acts(a[t]) (or the given quantized rows), 8 rows per
+// launch of the streaming GEMV (decode.cu); dense F32 weights use the f32 GEMV.
 static int matmul_common(prana_ctx* c, const prana_weight* w, const float* a, const int8_t* q, const float* s,
                          const int32_t* sum, size_t n_tokens, float* out) {
   DevScope ds(c->device);
+  const size_t K = (size_t)w->dw.cols, G = K / 32;
+  if (w->dw.type == T_F32) {
+    for (size_t t0 = 0; t0 < n_tokens; t0 += 8) {
+      GemvArgs g{};
+      g.w = w->dw;
+      g.m = (int)(n_tokens - t0 < 8 ? n_tokens - t0 : 8);
+      g.x = a + t0 * K;
+      g.out = out + t0 * w->dw.rows;
+      PRANA_CK(launch_gemv(g, PRO_F32, EPI_STORE, c->stream, false));
+    }
+    return PRANA_OK;
+  }
+  if (a) {  // quantize_acts into scratch first (matmul.rs:169, kquant.rs:329)
+    void* sp;
+    const size_t qb = (n_tokens * K + 255) & ~(size_t)255;
+    int rc = ctx_scratch(c, qb + n_tokens * G * 8 + 256, &sp);
+    if (rc) return rc;
+    int8_t* qq = static_cast<int8_t*>(sp);
+    float* ss = reinterpret_cast<float*>(qq + qb);
+    int32_t* mm = reinterpret_cast<int32_t*>(ss + n_tokens * G);
+    PRANA_CK(launch_quantize_acts(a, (int)n_tokens, (int)K, qq, ss, mm, c->stream));
+    q = qq;
+    s = ss;
+    sum = mm;
+  }
   for (size_t t0 = 0; t0 < n_tokens; t0 += 8) {
     const int m = (int)(n_tokens - t0 < 8 ? n_tokens - t0 : 8);
-    GemvArgs g{};
-    g.w = w->dw;
-    g.m = m;
-    const size_t K = (size_t)w->dw.cols, G = K / 32;
-    if (a) g.x = a + t0 * K;
-    if (q) {
-      g.aq = q + t0 * K;
-      g.as = s + t0 * G;
-      g.asum = sum + t0 * G;
-    }
-    g.out = out + t0 * w->dw.rows;
-    PRANA_CK(launch_gemv(g, a ? PRO_F32 : PRO_Q, EPI_STORE, c->stream, false));
+    StreamArgs sa{};
+    sa.K = (int)K;
+    sa.N = w->dw.rows;
+    sa.m = m;
+    sa.aq = q + t0 * K;
+    sa.as = s + t0 * G;
+    sa.asum = sum + t0 * G;
+    sa.out = out + t0 * w->dw.rows;
+    sa.err = c->err;
+    const int mt = m <= 1 ? 1 : (m <= 2 ? 2 : (m <= 4 ? 4 : 8));
+    if (!plan_tiles(w->dw, mt, STREAM_SMEM_BUDGET, 1, sa.plan))
+      return fail(PRANA_E_UNSUPPORTED, "no tile plan for a [%d x %d] weight", w->dw.rows, w->dw.cols);
+    PRANA_CK(launch_stream(sa, w->dw.type, EPI_STORE, PRO_Q, c->stream, false));
   }
   return PRANA_OK;
 }

@@ -30,6 +30,39 @@ __host__ __device__ inline int units_per_row(int type, int cols) {
   return (type == T_Q4_K || type == T_Q6_K) ? cols / 64 : cols / 32;
 }
 
+// Bulk-prefetch the bytes of rows [r0, r0 + R) of every plane toward L2.
+// Ranges are widened to 16-byte boundaries; planes are 256-byte padded, so the
+// widened range stays inside the allocation.
+__device__ __forceinline__ void prefetch_span(const void* base, size_t off, size_t bytes) {
+  const uintptr_t a = (reinterpret_cast<uintptr_t>(base) + off) & ~(uintptr_t)15;
+  const uintptr_t e = (reinterpret_cast<uintptr_t>(base) + off + bytes + 15) & ~(uintptr_t)15;
+  if (e > a) prefetch_l2_bulk(reinterpret_cast<const void*>(a), (uint32_t)(e - a));
+}
+__device__ __forceinline__ void prefetch_rows(const DevWeight& w, int r0, int R) {
+  if (r0 >= w.rows) return;
+  if (r0 + R > w.rows) R = w.rows - r0;
+  const size_t K = (size_t)w.cols;
+  switch (w.type) {
+    case T_Q8_0:
+      prefetch_span(w.qs, r0 * K, R * K);
+      prefetch_span(w.d, r0 * K / 16, R * K / 16);
+      break;
+    case T_Q4_0:
+      prefetch_span(w.qs, r0 * K / 2, R * K / 2);
+      prefetch_span(w.d, r0 * K / 16, R * K / 16);
+      break;
+    case T_Q4_K:
+      prefetch_span(w.qs, r0 * (K / 256) * 144, R * (K / 256) * 144);
+      break;
+    case T_Q6_K:
+      prefetch_span(w.qs, r0 * K / 2, R * K / 2);
+      prefetch_span(w.qh, r0 * K / 4, R * K / 4);
+      prefetch_span(w.sc, r0 * K / 16, R * K / 16);
+      prefetch_span(w.d, r0 * K / 128, R * K / 128);
+      break;
+  }
+}
+
 template <int T> struct Unit;
 template <> struct Unit<T_Q8_0> { uint4 a, b; unsigned short d; };
 template <> struct Unit<T_Q4_0> { uint4 q; unsigned short d; };
@@ -245,6 +278,47 @@ __device__ __forceinline__ void warp_dot(const DevWeight& w, const int (&rows)[N
   for (int r = 0; r < NR; r++)
 #pragma unroll
     for (int m = 0; m < M; m++) acc[r][m] = warp_sum(acc[r][m]);
+}
+
+// Element i of token row `tok` of an embedding table, dequantized exactly like
+// the CPU tables (checkpoint.rs:169-174; kquant.rs:39-112 for packed formats;
+// Q8_0 tables are f32 `q * d` in gguf.rs:238-247).
+__device__ __forceinline__ float embed_value(const DevWeight& w, uint32_t tok, int i) {
+  const int dim = w.cols;
+  const size_t r = tok;
+  switch (w.type) {
+    case T_Q8_0:
+      return __fmul_rn((float)(int8_t)w.qs[r * dim + i], h2f(__half_as_ushort(w.d[r * (dim / 32) + i / 32])));
+    case T_Q4_0: {
+      const int b = i / 32, e = i % 32;
+      const uint8_t byte = w.qs[r * (dim / 2) + b * 16 + (e & 15)];
+      const int q = e < 16 ? (byte & 0xF) : (byte >> 4);
+      return __fmul_rn(h2f(__half_as_ushort(w.d[r * (dim / 32) + b])), __fsub_rn((float)q, 8.0f));
+    }
+    case T_Q4_K: {
+      const uint8_t* sb = w.qs + r * (dim / 256) * 144 + (size_t)(i / 256) * 144;
+      const int e = i % 256, pair = e / 64, hi = (e % 64) / 32, l = e % 32;
+      int sc, mn;
+      q4k_scale_min(pair * 2 + hi, sb + 4, sc, mn);
+      const float d = h2f((unsigned short)(sb[0] | (sb[1] << 8))), dmin = h2f((unsigned short)(sb[2] | (sb[3] << 8)));
+      const uint8_t byte = sb[16 + pair * 32 + l];
+      const int q = hi ? (byte >> 4) : (byte & 0xF);
+      return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)mn));
+    }
+    case T_Q6_K: {
+      const int b = i / 256, e = i % 256, h = e / 128, g = (e % 128) / 32, l = e % 32;
+      const uint8_t* ql = w.qs + r * (dim / 2) + (size_t)b * 128 + h * 64;
+      const uint8_t* qh = w.qh + r * (dim / 4) + (size_t)b * 64 + h * 32;
+      const int8_t* sc = w.sc + r * (dim / 16) + (size_t)b * 16;
+      const int lo = (g & 1) ? ql[l + 32] : ql[l];
+      const int nib = (g >> 1) ? (lo >> 4) : (lo & 0xF);
+      const int q = (int)(int8_t)(nib | (((qh[l] >> (2 * g)) & 3) << 4)) - 32;
+      const float d = h2f(__half_as_ushort(w.d[r * (dim / 256) + b]));
+      return __fmul_rn(__fmul_rn(d, (float)sc[h * 8 + l / 16 + 2 * g]), (float)q);
+    }
+    default:
+      return w.f32[r * dim + i];
+  }
 }
 
 // Per-block integer dots of one row (debug/parity entry): one value per

@@ -45,6 +45,7 @@ struct prana_ctx {
   cudaStream_t stream = nullptr;
   prana::Scratch scratch;
   unsigned* counters = nullptr;  // 4096 zeroed ticket counters
+  unsigned* err = nullptr;       // device error flag of kernel-level calls (counters + 4095)
   std::map<std::tuple<int, uint32_t, int>, prana::RopeTable> rope;
   std::vector<void*> retired;  // outgrown RoPE tables: captured graphs may still point at them
 };

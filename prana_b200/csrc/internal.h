@@ -41,35 +41,6 @@ struct GemvArgs {
   float* trace_s;   // [m][K/32]
 };
 
-struct QkvArgs {
-  GemvArgs a;          // prologue inputs (m, x, norm_w, eps or aq/as/asum)
-  DevWeight w[3];
-  int kind[3];         // 0 = q, 1 = k, 2 = v
-  const float* bias[3];
-  int nseg;
-  int pair_start[4];   // prefix sums of row-pairs per segment
-  int hd, neox, q_dim, kv_dim;
-  const float* cos_t;  // [positions][hd/2]
-  const float* sin_t;
-  int pos0;            // first position (used when pos_dev is null)
-  const int* pos_dev;
-  int cap;             // cache rows; positions >= cap are not written
-  float* q_out;        // [m][q_dim]
-  __half* kc;          // layer K cache [positions][kv_dim]
-  __half* vc;
-  float* k_f32;        // optional in-window f32 copies [m][kv_dim] (prefill attention)
-  float* v_f32;
-};
-
-struct SwigluArgs {
-  GemvArgs a;
-  DevWeight w1, w3;  // gate, up: [hidden][dim]
-  int8_t* hq;        // quantized silu(gate)*up [m][hidden]
-  float* hs;         // [m][hidden/32]
-  int32_t* hsum;
-  float* h_f32;      // optional f32 copy [m][hidden]
-};
-
 struct AttnArgs {
   const float* q;        // [m][n_heads*hd]
   const __half* kc;      // [positions][n_kv*hd]
@@ -81,8 +52,12 @@ struct AttnArgs {
   int n_splits;
   float* part_ml;        // [n_kv][n_splits][m*group][2]
   float* part_o;         // [n_kv][n_splits][m*group][hd]
-  unsigned* counters;    // [n_kv], zero between launches
+  unsigned* counters;    // [n_kv + 1], zero between launches
   float* out;            // [m][n_heads*hd]
+  // optional finisher: quantize the whole output rows for the next projection
+  int8_t* out_q;
+  float* out_s;
+  int32_t* out_sum;
 };
 
 struct PrefillAttnArgs {
@@ -93,9 +68,85 @@ struct PrefillAttnArgs {
   float* out;
 };
 
+// ---------------------------------------------------------------- streaming GEMV (decode.cu)
+enum : int { EPI_QKV = 3, EPI_SWIGLU = 4 };
+
+// How a weight streams through shared memory: R rows per tile (a tile is
+// R contiguous rows of every plane), wpr warps per row (K split when R < 8),
+// `stages` tiles in flight.
+struct TilePlan {
+  int R, wpr, stages, stage_bytes, nplanes;
+  const uint8_t* plane[4];
+  int row_bytes[4];
+  int smem_off[4];
+};
+
+// Q|K|V epilogue: the stored matrix concatenates projections of one weight
+// type; RoPE partners are adjacent stored rows (NeoX rows permuted at upload).
+struct QkvMap {
+  int nseg;
+  int seg_start[4];  // stored-row offsets of each projection (+ end)
+  int kind[3];       // 0 = q, 1 = k, 2 = v
+  const float* bias[3];
+  int hd, neox, q_dim, kv_dim;
+  const float* cos_t;
+  const float* sin_t;
+  int pos0;
+  const int* pos_dev;
+  int cap;
+  float* q_out;
+  __half* kc;
+  __half* vc;
+  float* k_f32;
+  float* v_f32;
+};
+
+struct StreamArgs {
+  int K, N, m;
+  TilePlan plan;
+  const int8_t* aq;  // PRO_Q: quantized activation rows [m][K] (+ scales, sums [m][K/32])
+  const float* as;
+  const int32_t* asum;
+  const float* x;       // PRO_F32 / PRO_NORM: f32 rows [m][K]
+  const float* norm_w;  // PRO_NORM: rmsnorm weight [K]
+  float eps;
+  int8_t* trace_q;      // diagnostic: CTA 0 copies the staged rows here
+  float* trace_s;
+  float* out;          // STORE / RESID / ARGMAX logits [m][N]; SWIGLU h [m][N/2]
+  const float* bias;   // STORE
+  unsigned* err;       // device error flag
+  // ARGMAX
+  float* part_val;
+  int* part_idx;
+  int n_parts;
+  uint32_t* token_out;
+  int* token_next;
+  // last-CTA completion: argmax merge and/or finisher; counter is zero between launches
+  unsigned* counter;
+  const float* fin_x;     // rows [m][fin_n] to (normalize and) quantize
+  const float* fin_norm;  // rmsnorm weight, or null for plain quantization
+  float fin_eps;
+  int fin_n;
+  int8_t* fin_q;
+  float* fin_s;
+  int32_t* fin_sum;
+  QkvMap qkv;
+};
+
+// Shared-memory budget of one streaming-GEMV CTA: small enough that the next
+// kernel's CTA fits on the same SM, so under programmatic dependent launch its
+// producer starts streaming weights while this kernel drains.
+constexpr int STREAM_SMEM_BUDGET = 112 * 1024;
+
+bool plan_tiles(const DevWeight& w, int M, int budget, int min_rows_multiple, TilePlan& tp);
+int row_plane_bytes(int type, int K, int* rb);
+cudaError_t launch_stream(const StreamArgs& g, int type, int epi, int pro, cudaStream_t st, bool pdl);
+// embedding rows -> x, then rmsnorm + quantize into (q, s, sum) for the first projection
+cudaError_t launch_embed_norm(const DevWeight& emb, const uint32_t* toks, const int* tok_single, int m, float* x,
+                              const float* norm_w, float eps, int8_t* q, float* s, int32_t* sum, cudaStream_t st,
+                              bool pdl);
+
 cudaError_t launch_gemv(const GemvArgs& g, int pro, int epi, cudaStream_t st, bool pdl);
-cudaError_t launch_qkv(const QkvArgs& g, int pro, cudaStream_t st, bool pdl);
-cudaError_t launch_swiglu(const SwigluArgs& g, int pro, cudaStream_t st, bool pdl);
 cudaError_t launch_quantize_acts(const float* x, int rows, int k, int8_t* q, float* s, int32_t* sum, cudaStream_t st);
 cudaError_t launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps, float* out, cudaStream_t st);
 cudaError_t launch_rope(float* x, int rows, int n, int pos0, int hd, int neox, const float* c, const float* s,

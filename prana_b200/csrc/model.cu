@@ -178,18 +178,42 @@ using namespace prana;
 
 namespace {
 
+// A weight that streams through stream_gemv, with a tile plan per activation-row bucket.
+struct StreamW {
+  prana_weight w;
+  bool owns = true;
+  TilePlan plan[4];  // M buckets 1, 2, 4, 8
+  bool planned[4] = {false, false, false, false};
+  int pair_rows = 1;  // tiles must hold whole (q/k rope, gate/up) pairs
+  int bucket(int m) const { return m <= 1 ? 0 : (m <= 2 ? 1 : (m <= 4 ? 2 : 3)); }
+  const TilePlan* plan_for(int m) {
+    const int b = bucket(m);
+    if (!planned[b]) {
+      if (!plan_tiles(w.dw, 1 << b, STREAM_SMEM_BUDGET, pair_rows, plan[b])) return nullptr;
+      planned[b] = true;
+    }
+    return &plan[b];
+  }
+};
+
+struct QkvPart {
+  StreamW sw;
+  int nseg = 0;
+  int seg_start[4] = {0, 0, 0, 0};
+  int kind[3] = {0, 0, 0};
+};
+
 struct LayerW {
-  prana_weight wq, wk, wv, wo, w1, w2, w3;
+  std::vector<QkvPart> qkv;
+  StreamW wo, gu, w1, w3, w2;  // gu: gate/up rows interleaved; w1/w3 when their types differ
+  bool fused_gu = false;
   float *rms_att = nullptr, *rms_ffn = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
 };
 
 // Activation buffers for `rows` rows (decode: 8; prefill: the prompt length).
 struct Bufs {
   size_t rows = 0;
-  float *x = nullptr, *q = nullptr, *att = nullptr, *kf = nullptr, *vf = nullptr, *g = nullptr, *u = nullptr;
-  int8_t* hq = nullptr;
-  float* hs = nullptr;
-  int32_t* hsum = nullptr;
+  float *x = nullptr, *q = nullptr, *att = nullptr, *kf = nullptr, *vf = nullptr, *h = nullptr, *u = nullptr;
   float* logits = nullptr;
   uint32_t* toks = nullptr;     // input ids [rows]
   uint32_t* tok_out = nullptr;  // argmax per row [rows]
@@ -218,18 +242,17 @@ struct prana_model {
   prana_weight emb;
   std::vector<LayerW> layers;
   float* rms_final = nullptr;
-  prana_weight head;
-  bool head_is_emb = false;
+  StreamW head;
   const RopeTable* rope = nullptr;
-  std::vector<void*> owned;  // norms / biases
+  std::vector<void*> owned;  // norms / biases / scratch
   std::unique_ptr<Bufs> dec;
-  // head argmax scratch
-  float* part_val = nullptr;
+  float* part_val = nullptr;  // LM-head argmax partials [8][n_parts]
   int* part_idx = nullptr;
   int n_parts = 0;
-  unsigned* head_ctr = nullptr;
-  int* d_tokpos = nullptr;  // [token, pos] for the graph-driven step
-  int* h_io = nullptr;      // pinned mirror
+  unsigned* ctr = nullptr;    // ticket counter of the streaming kernels
+  unsigned* err = nullptr;    // device error flag
+  int* d_tokpos = nullptr;    // [token, pos] of the graph-driven step
+  int* h_io = nullptr;        // pinned mirror
   uint32_t* h_tok = nullptr;
   bool pdl = true;
   std::vector<prana_kv*> caches;  // live KV caches (freed with the model)
@@ -267,12 +290,11 @@ int dev_vec(prana_model* m, const std::vector<float>& h, float** out) {
   return PRANA_OK;
 }
 
-// Linear loading rule of gguf.rs:271-305: Q8_0 (cols%32), Q4_0 (cols%32),
+// The linear loading rule of gguf.rs:271-305: Q8_0 (cols%32), Q4_0 (cols%32),
 // Q4_K/Q6_K (cols%256) stay quantized.  Dense projections are not built.
-int load_linear(prana_model* m, const Gguf& g, const std::string& name, size_t rows, size_t cols, prana_weight* w) {
+int linear_raw(const Gguf& g, const std::string& name, size_t rows, size_t cols, uint32_t* type, const uint8_t** raw) {
   const GgufTensor* t;
-  const uint8_t* raw;
-  int rc = tensor_raw(g, name, &t, &raw);
+  int rc = tensor_raw(g, name, &t, raw);
   if (rc) return rc;
   if (t->dims.size() != 2) return fail(PRANA_E_FORMAT, "tensor '%s' is not 2-D", name.c_str());
   if (t->dims[0] != cols || t->dims[1] != rows)
@@ -284,7 +306,20 @@ int load_linear(prana_model* m, const Gguf& g, const std::string& name, size_t r
   if (!ok)
     return fail(PRANA_E_UNSUPPORTED, "tensor '%s': type %u with %zu cols would run the dense f32 matmul, not built",
                 name.c_str(), ty, cols);
-  return upload_weight(m->ctx, (int)ty, rows, cols, raw, w);
+  *type = ty;
+  return PRANA_OK;
+}
+
+size_t gguf_row_bytes(uint32_t type, size_t cols) { return type_size(type, cols); }
+
+int upload_stream(prana_model* m, uint32_t type, size_t rows, size_t cols, const uint8_t* bytes, int pair_rows,
+                  StreamW* sw) {
+  sw->pair_rows = pair_rows;
+  return upload_weight(m->ctx, (int)type, rows, cols, bytes, &sw->w);
+}
+
+void free_stream(StreamW& s) {
+  if (s.owns) free_weight(&s.w);
 }
 
 void destroy_kv(prana_kv* kv);
@@ -295,10 +330,14 @@ void free_model(prana_model* m) {
   cudaStreamSynchronize(m->ctx->own);
   while (!m->caches.empty()) destroy_kv(m->caches.back());
   free_weight(&m->emb);
-  if (!m->head_is_emb) free_weight(&m->head);
+  free_stream(m->head);
   for (auto& L : m->layers) {
-    free_weight(&L.wq); free_weight(&L.wk); free_weight(&L.wv); free_weight(&L.wo);
-    free_weight(&L.w1); free_weight(&L.w2); free_weight(&L.w3);
+    for (auto& p : L.qkv) free_stream(p.sw);
+    free_stream(L.wo);
+    free_stream(L.gu);
+    free_stream(L.w1);
+    free_stream(L.w3);
+    free_stream(L.w2);
   }
   for (void* p : m->owned) cudaFree(p);
   m->dec.reset();
@@ -308,17 +347,14 @@ void free_model(prana_model* m) {
 
 int make_bufs(prana_model* m, size_t rows, bool window, Bufs& b) {
   const auto& c = m->cfg;
-  const size_t q_dim = c.n_heads * c.head_dim, kv_dim = c.n_kv_heads * c.head_dim;
+  const size_t q_dim = c.n_heads * c.head_dim, kv_dim = c.n_kv_heads * c.head_dim, dim = c.dim, hid = c.hidden_dim;
   b.rows = rows;
   int rc = 0;
-  rc |= b.alloc(b.x, rows * c.dim);
+  rc |= b.alloc(b.x, rows * dim);
   rc |= b.alloc(b.q, rows * q_dim);
   rc |= b.alloc(b.att, rows * q_dim);
-  rc |= b.alloc(b.hq, rows * c.hidden_dim);
-  rc |= b.alloc(b.hs, rows * c.hidden_dim / 32);
-  rc |= b.alloc(b.hsum, rows * c.hidden_dim / 32);
-  rc |= b.alloc(b.g, rows * c.hidden_dim);
-  rc |= b.alloc(b.u, rows * c.hidden_dim);
+  rc |= b.alloc(b.h, rows * hid);
+  rc |= b.alloc(b.u, rows * hid);
   rc |= b.alloc(b.toks, rows);
   rc |= b.alloc(b.tok_out, rows);
   if (window) {
@@ -335,76 +371,93 @@ enum { MODE_CACHE = 0, MODE_WINDOW = 1 };
 // Diagnostic trace of every quantized activation row of a one-token pass, in
 // the order the CPU path quantizes them: per layer the attention-norm input,
 // the attention output, the ffn-norm input and silu(g)*u; then the final norm.
+// Each site is the int8 rows a streaming kernel staged (CTA 0 copies them out).
 struct Trace {
   int8_t* q = nullptr;
   float* s = nullptr;
   size_t nq = 0, ns = 0;
-  void site(GemvArgs& g, int k) {
-    g.trace_q = q + nq;
-    g.trace_s = s + ns;
+  void site(StreamArgs& a, int k) {
+    a.trace_q = q + nq;
+    a.trace_s = s + ns;
     nq += (size_t)k;
     ns += (size_t)k / 32;
   }
 };
 
+StreamArgs stream_args(prana_model* m, StreamW& w, int mrows, const float* x, const float* norm_w) {
+  StreamArgs a{};
+  a.K = w.w.dw.cols;
+  a.N = w.w.dw.rows;
+  a.m = mrows;
+  a.x = x;
+  a.norm_w = norm_w;
+  a.eps = m->cfg.norm_eps;
+  a.err = m->err;
+  return a;
+}
+
+int run_stream(prana_model* m, StreamW& w, StreamArgs& a, int epi, int pro, bool pdl) {
+  const TilePlan* tp = w.plan_for(a.m);
+  if (!tp) return fail(PRANA_E_UNSUPPORTED, "no tile plan for a [%d x %d] weight of type %d", w.w.dw.rows, w.w.dw.cols,
+                       w.w.dw.type);
+  a.plan = *tp;
+  PRANA_CK(launch_stream(a, w.w.dw.type, epi, pro, m->ctx->own, pdl));
+  return PRANA_OK;
+}
+
 // One pass of n rows through the model (infer.rs:142-211 for n = 1 and
-// :296-374 / :220-286 for the batched forms).  Rows are positions pos0.. (or
-// *pos_dev.. when pos_dev is set, n == 1).  MODE_WINDOW attends over the f32
-// in-window K/V (prefill); MODE_CACHE over the f16 cache (decode, verify).
-int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* toks_dev, const int* tok_dev,
-                 int pos0, const int* pos_dev, int mode, bool head, bool pdl, Trace* tr = nullptr) {
+// :296-374 / :220-286 for the batched forms).  Rows sit at positions pos0..
+// (or *pos_dev.. when pos_dev is set, n == 1).  MODE_WINDOW attends over the
+// f32 in-window K/V (prefill); MODE_CACHE over the f16 cache (decode, verify).
+// Every projection's kernel normalizes / quantizes its own input rows in its
+// prologue while its first weight tiles are already streaming in.
+int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* toks_dev, const int* tok_dev, int pos0,
+                 const int* pos_dev, int mode, bool head, bool pdl, Trace* tr = nullptr) {
   const auto& c = m->cfg;
   cudaStream_t st = m->ctx->own;
   const int dim = (int)c.dim, hd = (int)c.head_dim, hid = (int)c.hidden_dim;
   const int q_dim = (int)(c.n_heads * c.head_dim), kv_dim = (int)(c.n_kv_heads * c.head_dim);
   const size_t lstride = kv->positions * (size_t)kv_dim;
-  PRANA_CK(launch_embed(m->emb.dw, toks_dev, tok_dev, n, b.x, st, false));
+  int rc;
+  PRANA_CK(launch_embed(m->emb.dw, toks_dev, tok_dev, n, b.x, st, pdl));
   for (size_t l = 0; l < m->layers.size(); l++) {
     LayerW& L = m->layers[l];
     __half* kc = kv->k + l * lstride;
     __half* vc = kv->v + l * lstride;
-    // --- rmsnorm + Q|K|V + bias + RoPE + KV write, grouped by weight type
-    const prana_weight* segs[3] = {&L.wq, &L.wk, &L.wv};
-    const float* biases[3] = {L.bq, L.bk, L.bv};
-    const int pairs[3] = {q_dim / 2, kv_dim / 2, kv_dim / 2};
-    for (int s0 = 0; s0 < 3;) {
-      int s1 = s0 + 1;
-      while (s1 < 3 && segs[s1]->dw.type == segs[s0]->dw.type) s1++;
+    // --- rmsnorm -> Q|K|V -> bias -> RoPE -> KV-cache write
+    bool first_part = true;
+    for (auto& part : L.qkv) {
       for (int c0 = 0; c0 < n; c0 += 8) {
         const int mc = std::min(8, n - c0);
-        QkvArgs a{};
-        a.a.m = mc;
-        a.a.x = b.x + (size_t)c0 * dim;
-        a.a.norm_w = L.rms_att;
-        a.a.eps = c.norm_eps;
-        a.nseg = s1 - s0;
-        a.pair_start[0] = 0;
-        for (int s = s0; s < s1; s++) {
-          a.w[s - s0] = segs[s]->dw;
-          a.kind[s - s0] = s;
-          a.bias[s - s0] = biases[s];
-          a.pair_start[s - s0 + 1] = a.pair_start[s - s0] + pairs[s];
+        StreamArgs a = stream_args(m, part.sw, mc, b.x + (size_t)c0 * dim, L.rms_att);
+        if (tr && first_part) tr->site(a, dim);
+        QkvMap& q = a.qkv;
+        q.nseg = part.nseg;
+        for (int s = 0; s <= part.nseg; s++) q.seg_start[s] = part.seg_start[s];
+        const float* biases[3] = {L.bq, L.bk, L.bv};
+        for (int s = 0; s < part.nseg; s++) {
+          q.kind[s] = part.kind[s];
+          q.bias[s] = biases[part.kind[s]];
         }
-        a.hd = hd;
-        a.neox = c.rope_neox;
-        a.q_dim = q_dim;
-        a.kv_dim = kv_dim;
-        a.cos_t = m->rope->cos;
-        a.sin_t = m->rope->sin;
-        a.pos0 = pos0 + c0;
-        a.pos_dev = pos_dev;
-        a.cap = (int)kv->positions;
-        a.q_out = b.q + (size_t)c0 * q_dim;
-        a.kc = kc;
-        a.vc = vc;
+        q.hd = hd;
+        q.neox = c.rope_neox;
+        q.q_dim = q_dim;
+        q.kv_dim = kv_dim;
+        q.cos_t = m->rope->cos;
+        q.sin_t = m->rope->sin;
+        q.pos0 = pos0 + c0;
+        q.pos_dev = pos_dev;
+        q.cap = (int)kv->positions;
+        q.q_out = b.q + (size_t)c0 * q_dim;
+        q.kc = kc;
+        q.vc = vc;
         if (mode == MODE_WINDOW) {
-          a.k_f32 = b.kf + (size_t)c0 * kv_dim;
-          a.v_f32 = b.vf + (size_t)c0 * kv_dim;
+          q.k_f32 = b.kf + (size_t)c0 * kv_dim;
+          q.v_f32 = b.vf + (size_t)c0 * kv_dim;
         }
-        if (tr && s0 == 0) tr->site(a.a, dim);
-        PRANA_CK(launch_qkv(a, PRO_NORM, st, pdl));
+        if ((rc = run_stream(m, part.sw, a, EPI_QKV, PRO_NORM, pdl))) return rc;
       }
-      s0 = s1;
+      first_part = false;
     }
     // --- attention
     if (mode == MODE_WINDOW) {
@@ -428,89 +481,67 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       a.out = b.att;
       PRANA_CK(launch_attn_decode(a, st, pdl));
     }
-    // --- wo + residual (activations quantized in the GEMV prologue)
-    for (int c0 = 0; c0 < n; c0 += 8) {
-      GemvArgs g{};
-      g.w = L.wo.dw;
-      g.m = std::min(8, n - c0);
-      g.x = b.att + (size_t)c0 * q_dim;
-      g.out = b.x + (size_t)c0 * dim;
-      if (tr) tr->site(g, q_dim);
-      PRANA_CK(launch_gemv(g, PRO_F32, EPI_RESID, st, pdl));
-    }
-    // --- rmsnorm + gate|up + silu*up + quantize
-    const bool fused = L.w1.dw.type == L.w3.dw.type && hid % 32 == 0;
+    // --- quantize(attn) -> wo -> residual
     for (int c0 = 0; c0 < n; c0 += 8) {
       const int mc = std::min(8, n - c0);
-      if (fused) {
-        SwigluArgs a{};
-        a.a.m = mc;
-        a.a.x = b.x + (size_t)c0 * dim;
-        a.a.norm_w = L.rms_ffn;
-        a.a.eps = c.norm_eps;
-        a.w1 = L.w1.dw;
-        a.w3 = L.w3.dw;
-        a.hq = b.hq + (size_t)c0 * hid;
-        a.hs = b.hs + (size_t)c0 * (hid / 32);
-        a.hsum = b.hsum + (size_t)c0 * (hid / 32);
-        if (tr) tr->site(a.a, dim);
-        PRANA_CK(launch_swiglu(a, PRO_NORM, st, pdl));
+      StreamArgs a = stream_args(m, L.wo, mc, b.att + (size_t)c0 * q_dim, nullptr);
+      if (tr) tr->site(a, q_dim);
+      a.out = b.x + (size_t)c0 * dim;
+      if ((rc = run_stream(m, L.wo, a, EPI_RESID, PRO_F32, pdl))) return rc;
+    }
+    // --- rmsnorm -> gate|up -> silu(gate) * up
+    for (int c0 = 0; c0 < n; c0 += 8) {
+      const int mc = std::min(8, n - c0);
+      if (L.fused_gu) {
+        StreamArgs a = stream_args(m, L.gu, mc, b.x + (size_t)c0 * dim, L.rms_ffn);
+        if (tr) tr->site(a, dim);
+        a.out = b.h + (size_t)c0 * hid;
+        if ((rc = run_stream(m, L.gu, a, EPI_SWIGLU, PRO_NORM, pdl))) return rc;
       } else {
-        GemvArgs g{};
-        g.m = mc;
-        g.x = b.x + (size_t)c0 * dim;
-        g.norm_w = L.rms_ffn;
-        g.eps = c.norm_eps;
-        g.w = L.w1.dw;
-        g.out = b.g + (size_t)c0 * hid;
-        if (tr) tr->site(g, dim);
-        PRANA_CK(launch_gemv(g, PRO_NORM, EPI_STORE, st, pdl));
-        g.trace_q = nullptr;
-        g.trace_s = nullptr;
-        g.w = L.w3.dw;
-        g.out = b.u + (size_t)c0 * hid;
-        PRANA_CK(launch_gemv(g, PRO_NORM, EPI_STORE, st, pdl));
-        PRANA_CK(launch_silu_mul(b.g + (size_t)c0 * hid, b.u + (size_t)c0 * hid, (size_t)mc * hid, st));
-        PRANA_CK(launch_quantize_acts(b.g + (size_t)c0 * hid, mc, hid, b.hq + (size_t)c0 * hid,
-                                      b.hs + (size_t)c0 * (hid / 32), b.hsum + (size_t)c0 * (hid / 32), st));
+        StreamArgs a = stream_args(m, L.w1, mc, b.x + (size_t)c0 * dim, L.rms_ffn);
+        if (tr) tr->site(a, dim);
+        a.out = b.h + (size_t)c0 * hid;
+        if ((rc = run_stream(m, L.w1, a, EPI_STORE, PRO_NORM, pdl))) return rc;
+        StreamArgs u = stream_args(m, L.w3, mc, b.x + (size_t)c0 * dim, L.rms_ffn);
+        u.out = b.u + (size_t)c0 * hid;
+        if ((rc = run_stream(m, L.w3, u, EPI_STORE, PRO_NORM, pdl))) return rc;
+        PRANA_CK(launch_silu_mul(b.h + (size_t)c0 * hid, b.u + (size_t)c0 * hid, (size_t)mc * hid, st));
       }
     }
-    if (tr) {
-      PRANA_CK(cudaMemcpyAsync(tr->q + tr->nq, b.hq, (size_t)hid, cudaMemcpyDeviceToDevice, st));
-      PRANA_CK(cudaMemcpyAsync(tr->s + tr->ns, b.hs, (size_t)hid / 32 * 4, cudaMemcpyDeviceToDevice, st));
-      tr->nq += (size_t)hid;
-      tr->ns += (size_t)hid / 32;
-    }
-    // --- w2 + residual
+    // --- quantize(h) -> w2 -> residual
     for (int c0 = 0; c0 < n; c0 += 8) {
-      GemvArgs g{};
-      g.w = L.w2.dw;
-      g.m = std::min(8, n - c0);
-      g.aq = b.hq + (size_t)c0 * hid;
-      g.as = b.hs + (size_t)c0 * (hid / 32);
-      g.asum = b.hsum + (size_t)c0 * (hid / 32);
-      g.out = b.x + (size_t)c0 * dim;
-      PRANA_CK(launch_gemv(g, PRO_Q, EPI_RESID, st, pdl));
+      const int mc = std::min(8, n - c0);
+      StreamArgs a = stream_args(m, L.w2, mc, b.h + (size_t)c0 * hid, nullptr);
+      if (tr) tr->site(a, hid);
+      a.out = b.x + (size_t)c0 * dim;
+      if ((rc = run_stream(m, L.w2, a, EPI_RESID, PRO_F32, pdl))) return rc;
     }
   }
   if (!head) return PRANA_OK;
-  // --- final rmsnorm + LM head + argmax (Model::logits, checkpoint.rs:239-248)
+  // --- final rmsnorm -> LM head -> argmax (Model::logits, checkpoint.rs:239-248; infer.rs:560-568)
   for (int c0 = 0; c0 < n; c0 += 8) {
-    GemvArgs g{};
-    g.w = m->head.dw;
-    g.m = std::min(8, n - c0);
-    g.x = b.x + (size_t)c0 * dim;
-    g.norm_w = m->rms_final;
-    g.eps = c.norm_eps;
-    g.out = b.logits + (size_t)c0 * c.vocab_size;
-    g.part_val = m->part_val;
-    g.part_idx = m->part_idx;
-    g.counter = m->head_ctr;
-    g.n_parts = m->n_parts;
-    g.token_out = b.tok_out + c0;
-    g.token_next = (n == 1 && tok_dev) ? const_cast<int*>(tok_dev) : nullptr;
-    if (tr) tr->site(g, dim);
-    PRANA_CK(launch_gemv(g, PRO_NORM, EPI_ARGMAX, st, pdl));
+    const int mc = std::min(8, n - c0);
+    StreamArgs a = stream_args(m, m->head, mc, b.x + (size_t)c0 * dim, m->rms_final);
+    if (tr) tr->site(a, dim);
+    a.out = b.logits + (size_t)c0 * c.vocab_size;
+    a.part_val = m->part_val;
+    a.part_idx = m->part_idx;
+    a.n_parts = m->n_parts;
+    a.counter = m->ctr;
+    a.token_out = b.tok_out + c0;
+    a.token_next = (n == 1 && tok_dev) ? const_cast<int*>(tok_dev) : nullptr;
+    if ((rc = run_stream(m, m->head, a, EPI_ARGMAX, PRO_NORM, pdl))) return rc;
+  }
+  return PRANA_OK;
+}
+
+int check_err(prana_model* m) {
+  unsigned e = 0;
+  PRANA_CK(cudaMemcpyAsync(&e, m->err, 4, cudaMemcpyDeviceToHost, m->ctx->own));
+  PRANA_CK(cudaStreamSynchronize(m->ctx->own));
+  if (e) {
+    cudaMemsetAsync(m->err, 0, 4, m->ctx->own);
+    return fail(PRANA_E_TIMEOUT, "a bounded device-side wait expired (error %u)", e);
   }
   return PRANA_OK;
 }
@@ -572,6 +603,12 @@ void destroy_kv(prana_kv* kv) {
   cudaFree(kv->ring);
   delete kv;
 }
+
+// Rows of a GGUF tensor reordered / interleaved into one stored matrix.
+struct RowSrc {
+  const uint8_t* raw;
+  size_t row_bytes;
+};
 
 }  // namespace
 
@@ -667,19 +704,77 @@ int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
     if (rc) return rc;
   }
   m->layers.resize((size_t)c.n_layers);
+  const size_t half = (size_t)c.head_dim / 2;
   for (size_t i = 0; i < m->layers.size(); i++) {
     LayerW& L = m->layers[i];
     const std::string p = "blk." + std::to_string(i) + ".";
     std::vector<float> v;
     if ((rc = vec_f32(g, p + "attn_norm.weight", dim, v)) || (rc = dev_vec(m.get(), v, &L.rms_att))) return rc;
     if ((rc = vec_f32(g, p + "ffn_norm.weight", dim, v)) || (rc = dev_vec(m.get(), v, &L.rms_ffn))) return rc;
-    if ((rc = load_linear(m.get(), g, p + "attn_q.weight", q_dim, dim, &L.wq))) return rc;
-    if ((rc = load_linear(m.get(), g, p + "attn_k.weight", kv_dim, dim, &L.wk))) return rc;
-    if ((rc = load_linear(m.get(), g, p + "attn_v.weight", kv_dim, dim, &L.wv))) return rc;
-    if ((rc = load_linear(m.get(), g, p + "attn_output.weight", dim, q_dim, &L.wo))) return rc;
-    if ((rc = load_linear(m.get(), g, p + "ffn_gate.weight", hid, dim, &L.w1))) return rc;
-    if ((rc = load_linear(m.get(), g, p + "ffn_down.weight", dim, hid, &L.w2))) return rc;
-    if ((rc = load_linear(m.get(), g, p + "ffn_up.weight", hid, dim, &L.w3))) return rc;
+    // Q|K|V: concatenate runs of one weight type; RoPE partners become adjacent rows
+    const char* names[3] = {"attn_q.weight", "attn_k.weight", "attn_v.weight"};
+    const size_t seg_rows[3] = {q_dim, kv_dim, kv_dim};
+    uint32_t types[3];
+    const uint8_t* raws[3];
+    for (int s = 0; s < 3; s++)
+      if ((rc = linear_raw(g, p + names[s], seg_rows[s], dim, &types[s], &raws[s]))) return rc;
+    for (int s0 = 0; s0 < 3;) {
+      int s1 = s0 + 1;
+      while (s1 < 3 && types[s1] == types[s0]) s1++;
+      const size_t rb = gguf_row_bytes(types[s0], dim);
+      size_t total_rows = 0;
+      for (int s = s0; s < s1; s++) total_rows += seg_rows[s];
+      std::vector<uint8_t> buf(total_rows * rb);
+      QkvPart part;
+      part.nseg = s1 - s0;
+      size_t at = 0;
+      for (int s = s0; s < s1; s++) {
+        part.seg_start[s - s0] = (int)at;
+        part.kind[s - s0] = s;
+        for (size_t pp = 0; pp < seg_rows[s] / 2; pp++) {
+          size_t ra = 2 * pp, rbw = 2 * pp + 1;
+          if (s != 2 && c.rope_neox) {
+            ra = (pp / half) * (size_t)c.head_dim + pp % half;
+            rbw = ra + half;
+          }
+          memcpy(&buf[(at + 2 * pp) * rb], raws[s] + ra * rb, rb);
+          memcpy(&buf[(at + 2 * pp + 1) * rb], raws[s] + rbw * rb, rb);
+        }
+        at += seg_rows[s];
+      }
+      part.seg_start[part.nseg] = (int)at;
+      L.qkv.push_back(part);
+      if ((rc = upload_stream(m.get(), types[s0], total_rows, dim, buf.data(), 2, &L.qkv.back().sw))) return rc;
+      s0 = s1;
+    }
+    uint32_t ty;
+    const uint8_t* raw;
+    if ((rc = linear_raw(g, p + "attn_output.weight", dim, q_dim, &ty, &raw)) ||
+        (rc = upload_stream(m.get(), ty, dim, q_dim, raw, 1, &L.wo)))
+      return rc;
+    // gate|up: interleave rows (gate j, up j) when both have one type
+    uint32_t t1, t3;
+    const uint8_t *r1, *r3;
+    if ((rc = linear_raw(g, p + "ffn_gate.weight", hid, dim, &t1, &r1)) ||
+        (rc = linear_raw(g, p + "ffn_up.weight", hid, dim, &t3, &r3)))
+      return rc;
+    if (t1 == t3) {
+      const size_t rb = gguf_row_bytes(t1, dim);
+      std::vector<uint8_t> buf(2 * hid * rb);
+      for (size_t j = 0; j < hid; j++) {
+        memcpy(&buf[(2 * j) * rb], r1 + j * rb, rb);
+        memcpy(&buf[(2 * j + 1) * rb], r3 + j * rb, rb);
+      }
+      L.fused_gu = true;
+      if ((rc = upload_stream(m.get(), t1, 2 * hid, dim, buf.data(), 2, &L.gu))) return rc;
+    } else {
+      if ((rc = upload_stream(m.get(), t1, hid, dim, r1, 1, &L.w1)) ||
+          (rc = upload_stream(m.get(), t3, hid, dim, r3, 1, &L.w3)))
+        return rc;
+    }
+    if ((rc = linear_raw(g, p + "ffn_down.weight", dim, hid, &ty, &raw)) ||
+        (rc = upload_stream(m.get(), ty, dim, hid, raw, 1, &L.w2)))
+      return rc;
     // gguf.rs:388-394: each bias optional
     const char* bn[3] = {"attn_q.bias", "attn_k.bias", "attn_v.bias"};
     float** bd[3] = {&L.bq, &L.bk, &L.bv};
@@ -695,36 +790,44 @@ int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
     if ((rc = vec_f32(g, "output_norm.weight", dim, v)) || (rc = dev_vec(m.get(), v, &m->rms_final))) return rc;
   }
   if (g.tensors.count("output.weight")) {
-    if ((rc = load_linear(m.get(), g, "output.weight", (size_t)c.vocab_size, dim, &m->head))) return rc;
+    uint32_t ty;
+    const uint8_t* raw;
+    if ((rc = linear_raw(g, "output.weight", (size_t)c.vocab_size, dim, &ty, &raw)) ||
+        (rc = upload_stream(m.get(), ty, (size_t)c.vocab_size, dim, raw, 1, &m->head)))
+      return rc;
   } else {
     // tied classifier over a packed table runs the quantized kernel (checkpoint.rs:246)
     c.shared_classifier = 1;
     const int et = m->emb.dw.type;
     if (et != T_Q4_0 && et != T_Q4_K && et != T_Q6_K)
       return fail(PRANA_E_UNSUPPORTED, "tied classifier over a dense table is not built");
-    m->head = m->emb;
-    m->head_is_emb = true;
+    m->head.w = m->emb;
+    m->head.owns = false;
   }
-  // weight bytes
-  size_t wb = m->emb.bytes + (m->head_is_emb ? 0 : m->head.bytes);
-  for (auto& L : m->layers) wb += L.wq.bytes + L.wk.bytes + L.wv.bytes + L.wo.bytes + L.w1.bytes + L.w2.bytes + L.w3.bytes;
+  // weight bytes on the device
+  size_t wb = m->emb.bytes + (m->head.owns ? m->head.w.bytes : 0);
+  for (auto& L : m->layers) {
+    for (auto& q : L.qkv) wb += q.sw.w.bytes;
+    wb += L.wo.w.bytes + L.gu.w.bytes + L.w1.w.bytes + L.w3.w.bytes + L.w2.w.bytes;
+  }
   c.weight_bytes = (int64_t)wb;
   // RoPE table over the whole context (never regrown: graphs hold its address)
   rc = ctx_rope(ctx, (int)c.head_dim, c.rope_theta, c.rope_neox, (int)c.seq_len + 8, &m->rope);
   if (rc) return rc;
-  // decode buffers and head argmax scratch
+  // decode buffers, argmax partials, counters, error flag
   m->dec.reset(new Bufs());
   if ((rc = make_bufs(m.get(), 8, false, *m->dec))) return rc;
-  m->n_parts = (int)((c.vocab_size + 7) / 8);
+  m->n_parts = 1024;
   void* p = nullptr;
-  PRANA_CK(cudaMalloc(&p, (size_t)8 * m->n_parts * 8 + 256));
+  PRANA_CK(cudaMalloc(&p, (size_t)8 * m->n_parts * 8));
   m->owned.push_back(p);
   m->part_val = static_cast<float*>(p);
   m->part_idx = reinterpret_cast<int*>(static_cast<float*>(p) + (size_t)8 * m->n_parts);
   PRANA_CK(cudaMalloc(&p, 256));
   m->owned.push_back(p);
   PRANA_CK(cudaMemset(p, 0, 256));
-  m->head_ctr = static_cast<unsigned*>(p);
+  m->ctr = static_cast<unsigned*>(p);
+  m->err = m->ctr + 4;
   m->d_tokpos = reinterpret_cast<int*>(static_cast<uint8_t*>(p) + 64);
   PRANA_CK(cudaHostAlloc((void**)&m->h_io, 64, cudaHostAllocDefault));
   m->h_tok = reinterpret_cast<uint32_t*>(m->h_io + 4);
@@ -821,7 +924,7 @@ int prana_forward(prana_model* m, prana_kv* kv, uint32_t token, size_t pos, floa
   PRANA_CK(cudaStreamSynchronize(st));
   if (next) *next = m->h_tok[0];
   kv->loop_active = false;
-  return PRANA_OK;
+  return check_err(m);
   API_END
 }
 
@@ -856,7 +959,7 @@ int prana_forward_trace(prana_model* m, prana_kv* kv, uint32_t token, size_t pos
   PRANA_CK(cudaStreamSynchronize(st));
   *n_out = tr.nq;
   kv->loop_active = false;
-  return PRANA_OK;
+  return check_err(m);
   API_END
 }
 
@@ -888,7 +991,7 @@ int prana_prefill(prana_model* m, prana_kv* kv, const uint32_t* tokens, size_t n
   if (rc) return rc;
   PRANA_CK(cudaStreamSynchronize(st));
   kv->loop_active = false;
-  return PRANA_OK;
+  return check_err(m);
   API_END
 }
 
@@ -916,7 +1019,7 @@ int prana_forward_batch(prana_model* m, prana_kv* kv, const uint32_t* tokens, si
   if (argmax) PRANA_CK(cudaMemcpyAsync(argmax, b->tok_out, n * 4, cudaMemcpyDeviceToHost, st));
   PRANA_CK(cudaStreamSynchronize(st));
   kv->loop_active = false;
-  return PRANA_OK;
+  return check_err(m);
   API_END
 }
 
@@ -958,7 +1061,7 @@ int prana_decode_tokens(prana_model* m, prana_kv* kv, uint32_t* out, size_t max,
   size_t cnt = std::min((size_t)n, std::min(max, kv->positions));
   if (cnt && out) PRANA_CK(cudaMemcpy(out, kv->ring, cnt * 4, cudaMemcpyDeviceToHost));
   *n_out = cnt;
-  return PRANA_OK;
+  return check_err(m);
 }
 
 int prana_generate(prana_model* m, const uint32_t* prompt, size_t p, size_t steps, int64_t stop_id, uint32_t* out,

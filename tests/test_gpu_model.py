@@ -95,20 +95,26 @@ def test_forward_teacher_forced_flip_aware(models, name):
             for is_v in (False, True):
                 gkv.write(layer, is_v, okv.layer(layer, is_v)[:pos])
         tok = int(rng.integers(c.vocab_size))
-        lg_o, q_o, s_o = om.forward_trace(okv, tok, pos)
+        lg_o, q_o, s_o, v_o = om.forward_trace(okv, tok, pos, with_values=True)
         lg_g, q_g, s_g = pm.forward_trace(gm, gkv, tok, pos)
         first = None
         for off, n in sites:
+            if first is not None:
+                break  # downstream of a flip the inputs legitimately differ
             d = q_g[off:off + n].astype(np.int32) - q_o[off:off + n]
             so, sg = s_o[off // 32:(off + n) // 32], s_g[off // 32:(off + n) // 32]
-            # group scales follow the f32 values: a few ulps apart before any flip (the
-            # rmsnorm sum of squares is a tree sum here, sequential on the CPU)
+            # group scales follow the f32 values: a few ulps apart (the rmsnorm sum of
+            # squares is a tree sum here, sequential on the CPU)
             srel = float(np.max(np.abs(sg.astype(np.float64) - so) / np.abs(so)))
-            assert srel <= (1e-5 if first is None else 1e-2), f"{name} pos {pos}: scales differ by {srel:.1e}"
-            assert np.max(np.abs(d)) <= 1, f"{name} pos {pos}: int8 activations differ by >1 (a bug, not a flip)"
+            assert srel <= 1e-5, f"{name} pos {pos}: scales differ by {srel:.1e}"
             total += n
-            flips += int(np.count_nonzero(d))
-            if np.any(d) and first is None:
+            if np.any(d):
+                assert np.max(np.abs(d)) <= 1, f"{name} pos {pos}: int8 activations differ by >1 (a bug, not a flip)"
+                idx = np.nonzero(d)[0]
+                t = v_o[off + idx].astype(np.float64) / np.repeat(so, 32)[idx]
+                tie = np.abs(np.abs(t - np.trunc(t)) - 0.5)
+                assert np.all(tie < 1e-3), f"{name} pos {pos}: a flip away from a rounding tie ({tie.max():.2e})"
+                flips += int(idx.size)
                 first = off
         if first is None:
             assert rel(lg_g, lg_o) < LOGIT_TOL, f"{name} pos {pos}: no flip but logits differ"
@@ -117,8 +123,12 @@ def test_forward_teacher_forced_flip_aware(models, name):
         else:
             flip_steps += 1
             assert rel(lg_g, lg_o) < 5e-2
-    assert flip_steps <= steps // 2, f"{name}: {flip_steps}/{steps} steps had rounding flips"
-    assert flips <= max(16, total // 1000), f"{name}: {flips} flipped activations of {total}"
+    # Every flip was proven a rounding tie above, and flipped elements stay a small
+    # minority.  Steps with a flip can be common: Q4_0 embedding rows put whole
+    # groups on exact ties at the first layer's input, so only require that some
+    # steps went end-to-end flip-free and had their logits checked at LOGIT_TOL.
+    assert flip_steps < steps, f"{name}: every step had a rounding flip"
+    assert flips <= max(32, total // 200), f"{name}: {flips} flipped activations of {total}"
 
 
 @pytest.mark.parametrize("name", ["llama_q8", "qwen2_mix", "llama_kq"])
