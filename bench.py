@@ -30,6 +30,7 @@ import json
 import os
 import statistics
 import subprocess
+import threading
 import sys
 import time
 from pathlib import Path
@@ -46,7 +47,7 @@ UNIT = "tok/s"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=128)
+    p.add_argument("--steps", type=int, default=512)
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--impl", default="prana", choices=["prana", "reference"])
     p.add_argument("--workload", default="llama3_8b_q4_0")
@@ -93,7 +94,7 @@ def launches_per_step(spec) -> int:
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """nvidia-smi samples (every 100 ms) kept only when they fall inside the timed region."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -102,23 +103,42 @@ class Clocks:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
+        self.lines = []
+        self.reader = None
 
     def start(self):
+        """Start sampling; returns once the first sample is in, so the region that follows is covered."""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except FileNotFoundError:
             self.proc = None
+            return
 
-    def stop(self):
+        def read():
+            for line in self.proc.stdout:
+                self.lines.append((time.monotonic(), line))
+
+        self.reader = threading.Thread(target=read, daemon=True)
+        self.reader.start()
+        t_end = time.monotonic() + 10.0
+        while not self.lines and time.monotonic() < t_end and self.proc.poll() is None:
+            time.sleep(0.02)
+
+    def stop(self, t0, t1):
         if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
         self.proc.terminate()
-        out, _ = self.proc.communicate(timeout=10)
+        try:
+            self.proc.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.reader.join(timeout=5)
+        inside = [ln for ts, ln in self.lines if t0 <= ts <= t1]
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        for line in inside:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -263,12 +283,13 @@ def prana_arm(args):
     barrier()
     clocks = Clocks(local)
     clocks.start()
+    t_region = time.monotonic()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     loop.run(args.steps)
     e1.record(stream)
     barrier()
-    clk = clocks.stop()
+    clk = clocks.stop(t_region, time.monotonic())
     ms = e0.elapsed_time(e1) / args.steps
     toks = loop.tokens(args.warmup + args.steps)
     # ---- e2e: C-ABI call per token with host buffers

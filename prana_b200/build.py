@@ -20,7 +20,7 @@ LIB = PKG / "_lib"
 ROOT = PKG.parent
 
 CUDA_SOURCES = ["kernels.cu", "attention.cu", "decode.cu", "ctx.cu", "model.cu"]
-CUDA_HEADERS = ["common.cuh", "gemv.cuh", "tma.cuh", "finish.cuh", "internal.h", "host.h"]
+CUDA_HEADERS = ["common.cuh", "gemv.cuh", "finish.cuh", "mbar.cuh", "internal.h", "host.h"]
 NVCC_FLAGS = [
     "-O3",
     "-std=c++17",

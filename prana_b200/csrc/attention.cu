@@ -1,19 +1,19 @@
 // attention.cu -- grouped-query attention for the decode path.
 //
-// Decode / verify (attention.rs:129-195, 296-333): the f16 KV cache of one
-// layer is split along positions into n_splits ranges; CTA (split, kv_head)
-// streams its K/V tiles through shared memory with cp.async double buffering
-// and runs an online softmax for every query head that shares the kv head and
-// every query row (verify rows i see positions <= pos0 + i).  Partial
-// (max, sum, o) triples go to scratch; the last CTA of a kv head to finish
-// (ticket counter, no waiting) merges them and writes the output.
+// Decode / verify (attention.rs:129-195, 296-333): flash-decoding over the f16
+// KV cache of one layer.  The positions are split into n_splits ranges; CTA
+// (split, kv_head) runs an online softmax for every query head that shares the
+// kv head and every query row (verify rows i see positions <= pos0 + i).
+// Partial (max, sum, o) triples go to scratch; the last CTA of a kv head to
+// finish (ticket counter, no waiting) merges them and writes the output.
 //
-// Prefill (attention.rs:236-284): the same kernel body over the f32 in-window
-// K/V of the prompt (the CPU path attends over f32 there, not the f16 cache),
-// one CTA per (query-row chunk, kv head), no split.
+// Prefill (attention.rs:236-284): a tiled body over the f32 in-window K/V of
+// the prompt (the CPU path attends over f32 there, not the f16 cache), one CTA
+// per (query-row chunk, kv head), no split.
 #include <climits>
 
-#include "finish.cuh"
+#include <algorithm>
+
 #include "internal.h"
 
 namespace prana {
@@ -187,118 +187,332 @@ __device__ void attn_body(const float* __restrict__ q, int q_stride, const void*
   }
 }
 
-template <int HD>
-__device__ void attn_merge_splits(const AttnArgs& a, int kvh, int split, int row0, int VH, int group, int q_stride,
-                                  float (&acc)[(AT_MAX_VHD / 2 + AT_THREADS - 1) / AT_THREADS][2], const float* m_row,
-                                  const float* l_row, unsigned* ticket);
+// ---------------------------------------------------------------- decode / verify over the f16 cache
+//
+// Flash-decoding split: CTA (split, kv_head) owns a contiguous range of cache
+// positions and moves it through shared memory AD_C positions at a time, every
+// K and V row of a pass requested at once (cp.async, 16 bytes per request).
+// Rows written by earlier decode steps (positions < pos0) do not depend on the
+// Q|K|V kernel that precedes this one, so they are requested before the
+// programmatic-launch wait; q and this step's rows are read after it.
+//
+// Work layout (256 threads): scores take one position and half of the head
+// dims per thread for AD_VG query heads at once (8 independent FMA chains);
+// P.V takes one pair of dims and a slice of the positions per thread, again
+// for AD_VG heads, and the slices meet in shared memory.  The running output
+// lives in shared memory and is rescaled once per pass (online softmax).
+constexpr int AD_THREADS = 256;
+constexpr int AD_C = 128;  // positions per pass
+constexpr int AD_VG = 4;   // query heads per compute chunk
+
+// Splits for a cache of `positions` rows: one pass per CTA at full length,
+// at most ~4 CTAs per SM, and few enough that the (max, sum, weight) triples of
+// every split fit in the merging CTA's idle K/V buffers.
+int attn_splits(int positions, int n_kv, int hd, int sm_count) {
+  const int by_len = (positions + AD_C - 1) / AD_C;
+  const int by_sm = (4 * sm_count + n_kv - 1) / n_kv;
+  const int by_smem = AD_C * (hd + 8) * hd / (3 * AT_MAX_VHD);
+  return std::max(1, std::min(std::min(by_len, by_sm), by_smem));
+}
 
 template <int HD>
-__global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs a, int row0, int n_rows) {
-  extern __shared__ __align__(16) float sm[];
-  constexpr int NP = (AT_MAX_VHD / 2 + AT_THREADS - 1) / AT_THREADS;
-  const int kvh = blockIdx.y, split = blockIdx.x;
+struct AdSmem {
+  static constexpr int ROW = HD + 8;  // halves; 16 bytes of padding per row
+  static constexpr int RED = 2048;    // floats: (threads / (HD/2)) slices x AD_VG x HD
+  static size_t bytes(int vh) {
+    return 2 * sizeof(__half) * (size_t)AD_C * ROW  // K, V
+           + sizeof(float) * (size_t)vh * HD        // q
+           + sizeof(float) * (size_t)vh * HD        // running output
+           + sizeof(float) * (size_t)vh * AD_C      // scores / probabilities
+           + sizeof(float) * RED                    // P.V slices
+           + sizeof(float) * 3 * (size_t)vh;        // running max, sum, rescale
+  }
+};
+
+// Ticket of a cross-CTA completion count: the CTA's writes (ordered before
+// this by the caller's __syncthreads) are released at gpu scope, and the CTA
+// that draws the last ticket acquires every other CTA's writes.
+__device__ __forceinline__ unsigned ticket_acq_rel(unsigned* counter) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+  return old;
+}
+
+// End of a decode CTA: (m_run, l_run, o_s) hold this CTA's softmax state for
+// its VH virtual heads (o_s unnormalized).  With one split the rows are final;
+// otherwise they are published as a partial and the last CTA of the kv head
+// to finish merges every split.  `smem_raw` is shared memory the caller no
+// longer needs (>= 3 x VH x n_splits floats), `red` >= 4 KB.
+template <int HD>
+__device__ __forceinline__ void attn_finish(const AttnArgs& a, int kvh, int split, int row0, int VH, int group,
+                                            const float* o_s, const float* m_run, float* l_run, uint8_t* smem_raw,
+                                            float* red) {
+  const int tid = threadIdx.x, lane = tid & 31, wi = tid >> 5;
+  const int q_stride = a.n_heads * HD;
+  if (a.n_splits == 1) {
+    for (int e = tid; e < VH * HD; e += AD_THREADS) {
+      const int vh = e / HD, d = e - vh * HD;
+      const int row = vh / group, head = kvh * group + vh % group;
+      a.out[(size_t)(row0 + row) * q_stride + head * HD + d] = o_s[e] / l_run[vh];
+    }
+    return;
+  }
+  // ---- publish this split's (max, sum, o); the last split CTA of the kv head merges
+  const size_t base = ((size_t)kvh * a.n_splits + split) * VH;
+  for (int vh = tid; vh < VH; vh += AD_THREADS)
+    reinterpret_cast<float2*>(a.part_ml)[base + vh] = make_float2(m_run[vh], l_run[vh]);
+  for (int e = tid; e < VH * HD / 4; e += AD_THREADS)
+    reinterpret_cast<float4*>(a.part_o + base * HD)[e] = reinterpret_cast<const float4*>(o_s)[e];
+  __shared__ unsigned ticket;
+  __syncthreads();
+  if (tid == 0) ticket = ticket_acq_rel(a.counters + kvh);
+  __syncthreads();
+  if (ticket != (unsigned)a.n_splits - 1) return;
+  // (max, sum) of every split in one round trip, then the split weights
+  // exp(m_s - max) (attn_splits keeps 3 x VH x NS floats in range)
+  const int NS = a.n_splits;
+  float2* ml_s = reinterpret_cast<float2*>(smem_raw);  // [VH][NS]
+  const size_t hb = (size_t)kvh * NS * VH;  // this kv head's first partial
+  for (int i = tid; i < VH * NS; i += AD_THREADS) {
+    const int vh = i / NS, s = i - vh * NS;
+    ml_s[i] = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + hb + (size_t)s * VH + vh);
+  }
+  __syncthreads();
+  float* w_s = reinterpret_cast<float*>(ml_s + VH * NS);  // [VH][NS]
+  for (int vh = wi; vh < VH; vh += AD_THREADS / 32) {
+    float mx = -INFINITY;
+    for (int s = lane; s < NS; s += 32) mx = fmaxf(mx, ml_s[vh * NS + s].x);
+    mx = warp_max(mx);
+    float lsum = 0.0f;
+    for (int s = lane; s < NS; s += 32) {
+      const float2 ml = ml_s[vh * NS + s];
+      const float w = ml.x == -INFINITY ? 0.0f : expf(ml.x - mx);
+      w_s[vh * NS + s] = w;
+      lsum = fmaf(ml.y, w, lsum);
+    }
+    lsum = warp_sum(lsum);
+    if (lane == 0) l_run[vh] = lsum;
+  }
+  __syncthreads();
+  // weighted sum of the partial outputs: item = 4 dims of one head; the
+  // splits of an item are shared by `nsub` threads so all loads go out at once
+  const int items = VH * HD / 4;
+  const int nsub = items >= AD_THREADS ? 1 : AD_THREADS / items;
+  const int sub = tid / items < nsub ? tid / items : nsub;  // == nsub: idle
+  float4* red4 = reinterpret_cast<float4*>(red);  // [nsub][items] when nsub > 1
+  for (int it = tid % items; sub < nsub && it < items; it += (nsub > 1 ? items : AD_THREADS)) {
+    const int vh = (it * 4) / HD;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 8
+    for (int s = sub; s < NS; s += nsub) {
+      const float w = w_s[vh * NS + s];
+      const float4 po = __ldcg(reinterpret_cast<const float4*>(a.part_o + (hb + (size_t)s * VH) * HD) + it);
+      acc.x = fmaf(po.x, w, acc.x);
+      acc.y = fmaf(po.y, w, acc.y);
+      acc.z = fmaf(po.z, w, acc.z);
+      acc.w = fmaf(po.w, w, acc.w);
+    }
+    if (nsub > 1) {
+      red4[sub * items + it] = acc;
+    } else {
+      const int d = it * 4 - vh * HD, row = vh / group, head = kvh * group + vh % group;
+      const float inv = 1.0f / l_run[vh];
+      float* o = a.out + (size_t)(row0 + row) * q_stride + head * HD + d;
+      *reinterpret_cast<float4*>(o) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    }
+  }
+  if (nsub > 1) {
+    __syncthreads();
+    for (int it = tid; it < items; it += AD_THREADS) {
+      const int vh = (it * 4) / HD, d = it * 4 - vh * HD, row = vh / group, head = kvh * group + vh % group;
+      float4 acc = red4[it];
+      for (int s = 1; s < nsub; s++) {
+        const float4 t = red4[s * items + it];
+        acc.x += t.x;
+        acc.y += t.y;
+        acc.z += t.z;
+        acc.w += t.w;
+      }
+      const float inv = 1.0f / l_run[vh];
+      float* o = a.out + (size_t)(row0 + row) * q_stride + head * HD + d;
+      *reinterpret_cast<float4*>(o) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    }
+  }
+  if (tid == 0) a.counters[kvh] = 0u;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const AttnArgs a, int row0, int n_rows) {
+  using S = AdSmem<HD>;
+  constexpr int ROW = S::ROW, CPR = HD / 8, HP = HD / 2, NPART = AD_THREADS / HP;
+  static_assert(NPART * AD_VG * HD <= S::RED, "P.V slice buffer");
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __half* k_s = reinterpret_cast<__half*>(smem_raw);
+  __half* v_s = k_s + AD_C * ROW;
+  float* q_s = reinterpret_cast<float*>(v_s + AD_C * ROW);
   const int group = a.n_heads / a.n_kv, VH = n_rows * group;
-  pdl_wait();
+  float* o_s = q_s + VH * HD;
+  float* s_s = o_s + VH * HD;
+  float* red = s_s + VH * AD_C;
+  float* m_run = red + S::RED;
+  float* l_run = m_run + VH;
+  float* alpha = l_run + VH;
+  const int kvh = blockIdx.y, split = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wi = tid >> 5;
+  const int kv_stride = a.n_kv * HD, q_stride = a.n_heads * HD;
+  const float scale = 1.0f / sqrtf((float)HD);
+
+  // the position counter of a graph-driven step was advanced before the
+  // previous step's kernels finished, so it is safe to read before the wait
   const int pos0 = a.pos_dev ? *a.pos_dev : a.pos0;
   const int L = pos0 + row0 + n_rows;  // positions 0..L-1 are visible to some row
   int per = (L + a.n_splits - 1) / a.n_splits;
-  per = (per + AT_TT - 1) / AT_TT * AT_TT;
-  const int t_begin = split * per, t_end = min(L, t_begin + per);
-  float acc[NP][2];
-  float *m_row, *l_row;
-  attn_body<HD, false>(a.q, a.n_heads * HD, a.kc, a.vc, a.n_kv * HD, kvh, group, row0, n_rows, pos0,
-                       t_begin, t_end, sm, acc, m_row, l_row);
-  pdl_trigger();
-  const int tid = threadIdx.x;
-  const int q_stride = a.n_heads * HD;
-  __shared__ unsigned ticket;
-  if (a.n_splits == 1) {
-#pragma unroll
-    for (int i = 0; i < NP; i++) {
-      const int pi = tid + i * AT_THREADS;
-      if (pi * 2 >= VH * HD) break;
-      const int vh = (pi * 2) / HD, d = (pi * 2) % HD;
-      const int row = vh / group, head = kvh * group + vh % group;
-      const float inv = 1.0f / l_row[vh];
-      float* o = a.out + (size_t)(row0 + row) * q_stride + head * HD + d;
-      o[0] = acc[i][0] * inv;
-      o[1] = acc[i][1] * inv;
-    }
-  } else {
-    attn_merge_splits<HD>(a, kvh, split, row0, VH, group, q_stride, acc, m_row, l_row, &ticket);
-    if (ticket != (unsigned)a.n_splits - 1) return;
-  }
-  // every kv head of these rows finished: quantize the rows for the wo projection
-  if (a.out_q) {
-    __shared__ float red[8 * (AT_THREADS / 32)];
-    __shared__ float inv_s[8];
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) ticket = atomicAdd(a.counters + a.n_kv, 1u);
-    __syncthreads();
-    if (ticket != (unsigned)a.n_kv - 1) return;
-    __threadfence();
-    block_quantize_rows(a.out + (size_t)row0 * q_stride, nullptr, 0.0f, n_rows, q_stride,
-                        a.out_q + (size_t)row0 * q_stride, a.out_s + (size_t)row0 * (q_stride / 32),
-                        a.out_sum + (size_t)row0 * (q_stride / 32), red, inv_s, AT_THREADS, 1);
-    if (tid == 0) a.counters[a.n_kv] = 0u;
-  }
-}
+  per = (per + 15) / 16 * 16;
+  const int t_begin = min(L, split * per), t_end = min(L, t_begin + per);
 
-// Publish this split's (max, sum, o) and, in the last split CTA of the kv head
-// to finish, merge all splits into the output.  `ticket` tells the caller
-// whether this CTA merged (== n_splits - 1).
-template <int HD>
-__device__ void attn_merge_splits(const AttnArgs& a, int kvh, int split, int row0, int VH, int group, int q_stride,
-                                  float (&acc)[(AT_MAX_VHD / 2 + AT_THREADS - 1) / AT_THREADS][2], const float* m_row,
-                                  const float* l_row, unsigned* ticket) {
-  constexpr int NP = (AT_MAX_VHD / 2 + AT_THREADS - 1) / AT_THREADS;
-  const int tid = threadIdx.x;
-  const size_t base = ((size_t)kvh * a.n_splits + split) * VH;
-  for (int vh = tid; vh < VH; vh += AT_THREADS) {
-    a.part_ml[(base + vh) * 2] = m_row[vh];
-    a.part_ml[(base + vh) * 2 + 1] = l_row[vh];
-  }
-#pragma unroll
-  for (int i = 0; i < NP; i++) {
-    const int pi = tid + i * AT_THREADS;
-    if (pi * 2 >= VH * HD) break;
-    const int vh = (pi * 2) / HD, d = (pi * 2) % HD;
-    *reinterpret_cast<float2*>(a.part_o + (base + vh) * HD + d) = make_float2(acc[i][0], acc[i][1]);
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) *ticket = atomicAdd(a.counters + kvh, 1u);
-  __syncthreads();
-  if (*ticket != (unsigned)a.n_splits - 1) return;
-  __threadfence();
-  // last CTA of this kv head: merge all splits
-#pragma unroll
-  for (int i = 0; i < NP; i++) {
-    const int pi = tid + i * AT_THREADS;
-    if (pi * 2 >= VH * HD) break;
-    const int vh = (pi * 2) / HD, d = (pi * 2) % HD;
-    float mx = -INFINITY;
-    for (int s = 0; s < a.n_splits; s++)
-      mx = fmaxf(mx, __ldcg(a.part_ml + (((size_t)kvh * a.n_splits + s) * VH + vh) * 2));
-    float lsum = 0.0f, o0 = 0.0f, o1 = 0.0f;
-    for (int s = 0; s < a.n_splits; s++) {
-      const size_t pb = ((size_t)kvh * a.n_splits + s) * VH + vh;
-      const float ms = __ldcg(a.part_ml + pb * 2);
-      if (ms == -INFINITY) continue;
-      const float w = expf(ms - mx);
-      lsum = fmaf(__ldcg(a.part_ml + pb * 2 + 1), w, lsum);
-      const float2 po = __ldcg(reinterpret_cast<const float2*>(a.part_o + pb * HD + d));
-      o0 = fmaf(po.x, w, o0);
-      o1 = fmaf(po.y, w, o1);
+  auto request = [&](int t0, int n, int lo, int hi) {  // rows t0 + [0, n) with lo <= t < hi
+    for (int c = tid; c < 2 * AD_C * CPR; c += AD_THREADS) {
+      const int which = c / (AD_C * CPR), r = (c / CPR) % AD_C, ch = c % CPR;
+      const int t = t0 + r;
+      if (r >= n || t < lo || t >= hi) continue;
+      const __half* src = (which ? a.vc : a.kc) + (size_t)t * kv_stride + kvh * HD + ch * 8;
+      cp_async16((which ? v_s : k_s) + r * ROW + ch * 8, src);
     }
-    const float inv = 1.0f / lsum;
+  };
+
+  const int n0 = min(AD_C, t_end - t_begin);
+  if (n0 > 0) request(t_begin, n0, 0, pos0);
+  cp_async_commit();
+  pdl_wait();
+  if (n0 > 0) request(t_begin, n0, pos0, INT_MAX);
+  cp_async_commit();
+  for (int i = tid; i < VH * HD; i += AD_THREADS) {
+    const int vh = i / HD, d = i - vh * HD;
     const int row = vh / group, head = kvh * group + vh % group;
-    float* o = a.out + (size_t)(row0 + row) * q_stride + head * HD + d;
-    o[0] = o0 * inv;
-    o[1] = o1 * inv;
+    q_s[i] = a.q[(size_t)(row0 + row) * q_stride + head * HD + d];
+    o_s[i] = 0.0f;
   }
-  if (tid == 0) a.counters[kvh] = 0u;
+  for (int i = tid; i < VH; i += AD_THREADS) {
+    m_run[i] = -INFINITY;
+    l_run[i] = 0.0f;
+  }
+  pdl_trigger();
+
+  for (int t0 = t_begin; t0 < t_end; t0 += AD_C) {
+    const int n = min(AD_C, t_end - t0);
+    if (t0 != t_begin) {
+      request(t0, n, 0, INT_MAX);
+      cp_async_commit();
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    // ---- scores: thread -> (position p, half h of the dims), AD_VG heads at a time
+    {
+      const int p = tid >> 1, h = tid & 1;
+      for (int v0 = 0; v0 < VH; v0 += AD_VG) {
+        float d0[AD_VG], d1[AD_VG];
+#pragma unroll
+        for (int g = 0; g < AD_VG; g++) d0[g] = d1[g] = 0.0f;
+        if (p < n) {
+          const __half* kr = k_s + p * ROW + h * HP;
+#pragma unroll 4
+          for (int dd = 0; dd < HP; dd += 8) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(kr + dd);
+            const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+            const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]);
+            const float2 f2 = __half22float2(h2[2]), f3 = __half22float2(h2[3]);
+#pragma unroll
+            for (int g = 0; g < AD_VG; g++) {
+              if (v0 + g < VH) {
+                const float* qv = q_s + (v0 + g) * HD + h * HP + dd;
+                const float4 qa = *reinterpret_cast<const float4*>(qv);
+                const float4 qb = *reinterpret_cast<const float4*>(qv + 4);
+                d0[g] = fmaf(qa.x, f0.x, d0[g]);
+                d1[g] = fmaf(qa.y, f0.y, d1[g]);
+                d0[g] = fmaf(qa.z, f1.x, d0[g]);
+                d1[g] = fmaf(qa.w, f1.y, d1[g]);
+                d0[g] = fmaf(qb.x, f2.x, d0[g]);
+                d1[g] = fmaf(qb.y, f2.y, d1[g]);
+                d0[g] = fmaf(qb.z, f3.x, d0[g]);
+                d1[g] = fmaf(qb.w, f3.y, d1[g]);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < AD_VG; g++) {
+          float d = d0[g] + d1[g];
+          d += __shfl_xor_sync(0xffffffffu, d, 1);
+          const int vh = v0 + g;
+          if (h == 0 && p < n && vh < VH)
+            s_s[vh * AD_C + p] = (t0 + p <= pos0 + row0 + vh / group) ? __fmul_rn(d, scale) : -INFINITY;
+        }
+      }
+    }
+    __syncthreads();
+    // ---- online softmax: one warp per head
+    for (int vh = wi; vh < VH; vh += AD_THREADS / 32) {
+      float mx = -INFINITY;
+      for (int r = lane; r < n; r += 32) mx = fmaxf(mx, s_s[vh * AD_C + r]);
+      mx = warp_max(mx);
+      const float m_old = m_run[vh], m_new = fmaxf(m_old, mx);
+      float sum = 0.0f;
+      for (int r = lane; r < n; r += 32) {
+        const float s = s_s[vh * AD_C + r];
+        const float pr = (s == -INFINITY) ? 0.0f : expf(s - m_new);
+        s_s[vh * AD_C + r] = pr;
+        sum += pr;
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) {
+        const float al = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
+        m_run[vh] = m_new;
+        l_run[vh] = fmaf(l_run[vh], al, sum);
+        alpha[vh] = al;
+      }
+    }
+    __syncthreads();
+    // ---- P.V: thread -> (dim pair dp, slice of the positions), AD_VG heads at a time
+    {
+      const int dp = tid % HP, part = tid / HP;  // part == NPART: idle (HD/2 does not divide the block)
+      const int per_part = (n + NPART - 1) / NPART;
+      const int r_lo = part < NPART ? min(n, part * per_part) : n, r_hi = min(n, r_lo + per_part);
+      for (int v0 = 0; v0 < VH; v0 += AD_VG) {
+        float o0[AD_VG], o1[AD_VG];
+#pragma unroll
+        for (int g = 0; g < AD_VG; g++) o0[g] = o1[g] = 0.0f;
+#pragma unroll 4
+        for (int r = r_lo; r < r_hi; r++) {
+          const float2 v = __half22float2(*reinterpret_cast<const __half2*>(v_s + r * ROW + 2 * dp));
+#pragma unroll
+          for (int g = 0; g < AD_VG; g++) {
+            if (v0 + g < VH) {
+              const float pr = s_s[(v0 + g) * AD_C + r];
+              o0[g] = fmaf(pr, v.x, o0[g]);
+              o1[g] = fmaf(pr, v.y, o1[g]);
+            }
+          }
+        }
+        if (part < NPART) {
+#pragma unroll
+          for (int g = 0; g < AD_VG; g++)
+            *reinterpret_cast<float2*>(red + (part * AD_VG + g) * HD + 2 * dp) = make_float2(o0[g], o1[g]);
+        }
+        __syncthreads();
+        for (int e = tid; e < AD_VG * HD; e += AD_THREADS) {
+          const int g = e / HD, d = e - g * HD, vh = v0 + g;
+          if (vh >= VH) continue;
+          float s = 0.0f;
+#pragma unroll 4
+          for (int pp = 0; pp < NPART; pp++) s += red[(pp * AD_VG + g) * HD + d];
+          o_s[vh * HD + d] = fmaf(o_s[vh * HD + d], alpha[vh], s);
+        }
+        __syncthreads();
+      }
+    }
+  }
+
+  attn_finish<HD>(a, kvh, split, row0, VH, group, o_s, m_run, l_run, smem_raw, red);
 }
 
 template <int HD>
@@ -327,24 +541,292 @@ __global__ void __launch_bounds__(AT_THREADS) attn_prefill_kernel(const PrefillA
   }
 }
 
+// ---------------------------------------------------------------- tensor-core decode (head_dim 64 / 128)
+//
+// Same split / pass / merge structure as attn_decode_kernel, with Q.K^T and
+// P.V on the tensor cores (mma.sync m16n8k16, f16 inputs, f32 accumulate).
+// A CTA's pass holds AM_C = 128 positions; warp w owns positions 16w..16w+15
+// of the pass and keeps its own online-softmax state (m, l, O) for up to 16
+// virtual heads (the rows of the MMA tile).  f32 operands reach f16 as a
+// hi + lo pair (x = hi + lo to ~2^-22 relative), two MMAs each, so scores and
+// outputs carry f32-level accuracy: the K/V cache is f16 already and every
+// f16 x f16 product is exact in the f32 accumulator.
+constexpr int AM_C = 128;  // positions per pass (8 warps x 16)
+constexpr int AM_ROWS = 16;  // virtual heads per CTA (MMA rows)
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// (x0, x1) -> f16 hi pair and f16 lo pair (lo = x - hi), low half = x0
+__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+  const __half l0 = __float2half_rn(x0 - __half2float(h0)), l1 = __float2half_rn(x1 - __half2float(h1));
+  hi = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+  lo = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+}
+
 template <int HD>
+struct AmSmem {
+  static constexpr int ROW = HD + 8;  // halves; 16 bytes of padding per row (conflict-free ldmatrix)
+  static constexpr size_t KV = 2 * sizeof(__half) * (size_t)AM_C * ROW;
+  static constexpr size_t Q = 2 * sizeof(__half) * (size_t)AM_ROWS * ROW;  // hi, lo
+  static constexpr size_t O = sizeof(float) * (size_t)AM_ROWS * HD;
+  static constexpr size_t RED = 4096;
+  static constexpr size_t bytes = KV + Q + O + RED + sizeof(float) * 2 * AM_ROWS;
+  // the warps' (m, l, O) meet in the K/V buffers after the last pass
+  static_assert(sizeof(float) * 8 * AM_ROWS * (HD + 2) <= KV, "warp merge buffer");
+};
+
+template <int HD>
+__global__ void __launch_bounds__(256) attn_decode_mma(const AttnArgs a, int row0, int n_rows) {
+  using S = AmSmem<HD>;
+  constexpr int ROW = S::ROW, CPR = HD / 8, KS = HD / 16, NT = HD / 8;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __half* k_s = reinterpret_cast<__half*>(smem_raw);
+  __half* v_s = k_s + AM_C * ROW;
+  __half* qh_s = v_s + AM_C * ROW;
+  __half* ql_s = qh_s + AM_ROWS * ROW;
+  float* o_s = reinterpret_cast<float*>(ql_s + AM_ROWS * ROW);
+  float* red = o_s + AM_ROWS * HD;
+  float* m_run = red + S::RED / sizeof(float);
+  float* l_run = m_run + AM_ROWS;
+  const int group = a.n_heads / a.n_kv, VH = n_rows * group;  // VH <= 16
+  const int kvh = blockIdx.y, split = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wi = tid >> 5;
+  const int g = lane >> 2, tig = lane & 3;
+  const int kv_stride = a.n_kv * HD, q_stride = a.n_heads * HD;
+  const float scale = 1.0f / sqrtf((float)HD);
+
+  // the position counter of a graph-driven step was advanced before the
+  // previous step's kernels finished, so it is safe to read before the wait
+  const int pos0 = a.pos_dev ? *a.pos_dev : a.pos0;
+  const int L = pos0 + row0 + n_rows;
+  int per = (L + a.n_splits - 1) / a.n_splits;
+  per = (per + 15) / 16 * 16;
+  const int t_begin = min(L, split * per), t_end = min(L, t_begin + per);
+
+  // thread -> 16-byte chunk `ch` of pass rows r_first, r_first + RSTEP, ... of K and V
+  constexpr int RSTEP = 256 / CPR;
+  const int ch = tid % CPR, r_first = tid / CPR;
+  auto request = [&](int t0, int r_lo, int r_hi) {  // pass rows [r_lo, r_hi)
+    int r = r_first;
+    if (r < r_lo) r += (r_lo - r + RSTEP - 1) / RSTEP * RSTEP;
+    const size_t src0 = (size_t)(t0 + r) * kv_stride + kvh * HD + ch * 8;
+    const __half* ks = a.kc + src0;
+    const __half* vs = a.vc + src0;
+    for (; r < r_hi; r += RSTEP, ks += (size_t)RSTEP * kv_stride, vs += (size_t)RSTEP * kv_stride) {
+      cp_async16(k_s + r * ROW + ch * 8, ks);
+      cp_async16(v_s + r * ROW + ch * 8, vs);
+    }
+  };
+  // V rows past the end of a short pass enter the P.V MMA with P = 0; zero
+  // them so stale shared memory cannot inject NaN (0 x NaN)
+  auto zero_tail = [&](int n) {
+    const int n16 = min(AM_C, (n + 15) / 16 * 16);
+    for (int c = tid; c < (n16 - n) * CPR; c += 256) {
+      const int r = n + c / CPR, ch = c % CPR;
+      *reinterpret_cast<uint4*>(v_s + r * ROW + ch * 8) = make_uint4(0, 0, 0, 0);
+    }
+  };
+
+  __shared__ int q_off[AM_ROWS];  // where virtual head vh's q row starts (-1: padding row)
+  if (tid < AM_ROWS) q_off[tid] = tid < VH ? (row0 + tid / group) * q_stride + (kvh * group + tid % group) * HD : -1;
+  const int n0 = min(AM_C, t_end - t_begin);
+  const int split_at = min(n0, max(0, pos0 - t_begin));  // rows before it were written by earlier steps
+  if (split_at > 0) request(t_begin, 0, split_at);
+  cp_async_commit();
+  pdl_wait();
+  if (n0 > split_at) request(t_begin, split_at, n0);
+  if (n0 > 0) zero_tail(n0);
+  cp_async_commit();
+  __syncthreads();
+  // q rows of the virtual heads as f16 hi/lo tiles; rows >= VH are zero
+  for (int i = tid; i < AM_ROWS * HD; i += 256) {
+    const int vh = i / HD, d = i - vh * HD;
+    const int off = q_off[vh];
+    const float x = off >= 0 ? a.q[off + d] : 0.0f;
+    const __half h = __float2half_rn(x);
+    qh_s[vh * ROW + d] = h;
+    ql_s[vh * ROW + d] = __float2half_rn(x - __half2float(h));
+  }
+  pdl_trigger();
+
+  // per-warp online softmax state: rows g and g + 8 of the MMA tile
+  float m_w[2] = {-INFINITY, -INFINITY}, l_w[2] = {0.0f, 0.0f};
+  float o[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+  const int lr = lane & 7, lj = lane >> 3;  // ldmatrix: row within matrix, matrix index
+
+  for (int t0 = t_begin; t0 < t_end; t0 += AM_C) {
+    const int n = min(AM_C, t_end - t0);
+    if (t0 != t_begin) {
+      request(t0, 0, n);
+      zero_tail(n);
+      cp_async_commit();
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    const int p0 = wi * 16;  // this warp's first position in the pass
+    if (p0 < n) {
+      // ---- S[16 x 16] = Q . K^T over HD (hi and lo halves of Q)
+      float sc[2][4];
+#pragma unroll
+      for (int i = 0; i < 2; i++) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.0f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ks++) {
+        uint32_t ah[4], al[4], kb[4];
+        const int qoff = ((lj & 1) * 8 + lr) * ROW + ks * 16 + (lj >> 1) * 8;
+        ldsm_x4(ah, qh_s + qoff);
+        ldsm_x4(al, ql_s + qoff);
+        ldsm_x4(kb, k_s + (p0 + (lj >> 1) * 8 + lr) * ROW + ks * 16 + (lj & 1) * 8);
+        mma_f16(sc[0], ah, kb[0], kb[1]);
+        mma_f16(sc[0], al, kb[0], kb[1]);
+        mma_f16(sc[1], ah, kb[2], kb[3]);
+        mma_f16(sc[1], al, kb[2], kb[3]);
+      }
+      // ---- mask, scale, online softmax per row (a row's 16 values live in one lane quad)
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const int row = g + (c >> 1) * 8, p = p0 + nt * 8 + tig * 2 + (c & 1);
+          const bool ok = row < VH && p < n && t0 + p <= pos0 + row0 + row / group;
+          sc[nt][c] = ok ? __fmul_rn(sc[nt][c], scale) : -INFINITY;
+          mx[c >> 1] = fmaxf(mx[c >> 1], sc[nt][c]);
+        }
+      float alpha[2], sum[2] = {0.0f, 0.0f};
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+        const float m_new = fmaxf(m_w[h], mx[h]);
+        alpha[h] = (m_w[h] == -INFINITY) ? 0.0f : expf(m_w[h] - m_new);
+        m_w[h] = m_new;
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const float s = sc[nt][c];
+          const float pr = (s == -INFINITY) ? 0.0f : expf(s - m_w[c >> 1]);
+          sc[nt][c] = pr;
+          sum[c >> 1] += pr;
+        }
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 1);
+        sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 2);
+        l_w[h] = fmaf(l_w[h], alpha[h], sum[h]);
+      }
+#pragma unroll
+      for (int i = 0; i < NT; i++) {
+        o[i][0] *= alpha[0];
+        o[i][1] *= alpha[0];
+        o[i][2] *= alpha[1];
+        o[i][3] *= alpha[1];
+      }
+      // ---- O += P . V: the two S tiles are exactly the A fragment of P (16 x 16)
+      uint32_t ph[4], pl[4];
+      split_pair(sc[0][0], sc[0][1], ph[0], pl[0]);
+      split_pair(sc[0][2], sc[0][3], ph[1], pl[1]);
+      split_pair(sc[1][0], sc[1][1], ph[2], pl[2]);
+      split_pair(sc[1][2], sc[1][3], ph[3], pl[3]);
+#pragma unroll
+      for (int dt = 0; dt < NT; dt += 2) {
+        uint32_t vb[4];
+        ldsm_x4_t(vb, v_s + (p0 + (lj & 1) * 8 + lr) * ROW + dt * 8 + (lj >> 1) * 8);
+        mma_f16(o[dt], ph, vb[0], vb[1]);
+        mma_f16(o[dt], pl, vb[0], vb[1]);
+        mma_f16(o[dt + 1], ph, vb[2], vb[3]);
+        mma_f16(o[dt + 1], pl, vb[2], vb[3]);
+      }
+    }
+    __syncthreads();  // the next pass overwrites K and V
+  }
+
+  // ---- the warps' states meet in the K/V buffers: wm/wl [8][16], wo [8][VH][HD]
+  float* wm = reinterpret_cast<float*>(smem_raw);
+  float* wl = wm + 8 * AM_ROWS;
+  float* wo = wl + 8 * AM_ROWS;
+  if (tig == 0) {
+    wm[wi * AM_ROWS + g] = m_w[0];
+    wl[wi * AM_ROWS + g] = l_w[0];
+    wm[wi * AM_ROWS + g + 8] = m_w[1];
+    wl[wi * AM_ROWS + g + 8] = l_w[1];
+  }
+#pragma unroll
+  for (int i = 0; i < NT; i++) {
+    const int d = i * 8 + tig * 2;
+    if (g < VH) *reinterpret_cast<float2*>(wo + (wi * AM_ROWS + g) * HD + d) = make_float2(o[i][0], o[i][1]);
+    if (g + 8 < VH) *reinterpret_cast<float2*>(wo + (wi * AM_ROWS + g + 8) * HD + d) = make_float2(o[i][2], o[i][3]);
+  }
+  __syncthreads();
+  if (tid < VH) {
+    float mx = -INFINITY;
+    for (int w = 0; w < 8; w++) mx = fmaxf(mx, wm[w * AM_ROWS + tid]);
+    float l = 0.0f;
+    for (int w = 0; w < 8; w++) {
+      const float mw = wm[w * AM_ROWS + tid];
+      const float sw = mw == -INFINITY ? 0.0f : expf(mw - mx);
+      wm[w * AM_ROWS + tid] = sw;  // the warp's weight from here on
+      l = fmaf(wl[w * AM_ROWS + tid], sw, l);
+    }
+    m_run[tid] = mx;
+    l_run[tid] = l;
+  }
+  __syncthreads();
+  for (int e = tid; e < VH * HD; e += 256) {
+    const int vh = e / HD;
+    float acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) acc = fmaf(wo[(w * AM_ROWS + vh) * HD + (e - vh * HD)], wm[w * AM_ROWS + vh], acc);
+    o_s[e] = acc;
+  }
+  __syncthreads();
+  attn_finish<HD>(a, kvh, split, row0, VH, group, o_s, m_run, l_run, smem_raw, red);
+}
+
+template <int HD, bool MMA>
 static cudaError_t decode_go(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const int group = a.n_heads / a.n_kv;
-  const int max_rows = AT_MAX_VHD / (HD * group);
+  const int max_rows = MMA ? AM_ROWS / group : AT_MAX_VHD / (HD * group);
   if (max_rows < 1) return cudaErrorInvalidValue;
   for (int row0 = 0; row0 < a.m; row0 += max_rows) {
     const int n_rows = min(max_rows, a.m - row0);
-    const size_t smem = AttnSmem<HD, false>::bytes(n_rows * group);
-    auto k = attn_decode_kernel<HD>;
+    size_t smem;
+    const void* k;
+    if constexpr (MMA) {
+      smem = AmSmem<HD>::bytes;
+      k = (const void*)attn_decode_mma<HD>;
+    } else {
+      smem = AdSmem<HD>::bytes(n_rows * group);
+      k = (const void*)attn_decode_kernel<HD>;
+    }
     if (smem > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
     }
     AttnArgs aa = a;
     void* args[] = {&aa, (void*)&row0, (void*)&n_rows};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_splits, a.n_kv);
-    cfg.blockDim = dim3(AT_THREADS);
+    cfg.blockDim = dim3(AD_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -354,7 +836,7 @@ static cudaError_t decode_go(const AttnArgs& a, cudaStream_t st, bool pdl) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
     }
-    cudaError_t e = cudaLaunchKernelExC(&cfg, (const void*)k, args);
+    cudaError_t e = cudaLaunchKernelExC(&cfg, k, args);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -362,13 +844,15 @@ static cudaError_t decode_go(const AttnArgs& a, cudaStream_t st, bool pdl) {
 
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   if (a.n_kv <= 0 || a.n_heads % a.n_kv || a.m < 1 || a.n_splits < 1) return cudaErrorInvalidValue;
+  // tensor-core path for the common head sizes while a kv head's query heads fit one MMA tile
+  const bool mma = a.n_heads / a.n_kv <= AM_ROWS;
   switch (a.hd) {
-    case 32: return decode_go<32>(a, st, pdl);
-    case 48: return decode_go<48>(a, st, pdl);
-    case 64: return decode_go<64>(a, st, pdl);
-    case 96: return decode_go<96>(a, st, pdl);
-    case 128: return decode_go<128>(a, st, pdl);
-    case 256: return decode_go<256>(a, st, pdl);
+    case 32: return decode_go<32, false>(a, st, pdl);
+    case 48: return decode_go<48, false>(a, st, pdl);
+    case 64: return mma ? decode_go<64, true>(a, st, pdl) : decode_go<64, false>(a, st, pdl);
+    case 96: return decode_go<96, false>(a, st, pdl);
+    case 128: return mma ? decode_go<128, true>(a, st, pdl) : decode_go<128, false>(a, st, pdl);
+    case 256: return decode_go<256, false>(a, st, pdl);
   }
   return cudaErrorInvalidValue;
 }

@@ -379,6 +379,7 @@ static int matmul_common(prana_ctx* c, const prana_weight* w, const float* a, co
   for (size_t t0 = 0; t0 < n_tokens; t0 += 8) {
     const int m = (int)(n_tokens - t0 < 8 ? n_tokens - t0 : 8);
     StreamArgs sa{};
+    sa.w = w->dw;
     sa.K = (int)K;
     sa.N = w->dw.rows;
     sa.m = m;
@@ -387,10 +388,7 @@ static int matmul_common(prana_ctx* c, const prana_weight* w, const float* a, co
     sa.asum = sum + t0 * G;
     sa.out = out + t0 * w->dw.rows;
     sa.err = c->err;
-    const int mt = m <= 1 ? 1 : (m <= 2 ? 2 : (m <= 4 ? 4 : 8));
-    if (!plan_tiles(w->dw, mt, STREAM_SMEM_BUDGET, 1, sa.plan))
-      return fail(PRANA_E_UNSUPPORTED, "no tile plan for a [%d x %d] weight", w->dw.rows, w->dw.cols);
-    PRANA_CK(launch_stream(sa, w->dw.type, EPI_STORE, PRO_Q, c->stream, false));
+    PRANA_CK(launch_stream(sa, EPI_STORE, PRO_Q, c->stream, false));
   }
   return PRANA_OK;
 }
@@ -502,12 +500,6 @@ int prana_f16_kv_write(prana_ctx* c, uint16_t* cache, size_t first_row, size_t k
 
 // Splits for one attention launch: enough CTAs to cover the SMs twice,
 // at least 32 positions each.
-static int pick_splits(prana_ctx* c, size_t positions, size_t n_kv) {
-  const int by_len = (int)((positions + 31) / 32);
-  const int by_sm = (int)((2 * c->sm_count + n_kv - 1) / n_kv);
-  int s = by_len < by_sm ? by_len : by_sm;
-  return s < 1 ? 1 : s;
-}
 
 static int attn_common(prana_ctx* c, const float* q, const uint16_t* kc, const uint16_t* vc, size_t pos0, size_t m,
                        size_t nh, size_t nkv, size_t hd, float* out) {
@@ -517,11 +509,11 @@ static int attn_common(prana_ctx* c, const float* q, const uint16_t* kc, const u
   NEED(hd * (nh / nkv) <= 4096, "head_dim x group exceeds 4096");
   if (!m) return PRANA_OK;
   DevScope ds(c->device);
-  const int splits = pick_splits(c, pos0 + m, nkv);
+  const int splits = attn_splits((int)(pos0 + m), (int)nkv, (int)hd, c->sm_count);
   const int group = (int)(nh / nkv);
   const int rows_per_cta = 4096 / (int)(hd * group);
   const size_t vh = (size_t)(rows_per_cta < (int)m ? rows_per_cta : (int)m) * group;
-  const size_t ml = nkv * splits * vh * 2, po = nkv * splits * vh * hd;
+  const size_t ml = (nkv * splits * vh * 2 + 3) / 4 * 4, po = nkv * splits * vh * hd;  // part_o 16-byte aligned
   void* sp;
   int rc = ctx_scratch(c, (ml + po) * 4, &sp);
   if (rc) return rc;

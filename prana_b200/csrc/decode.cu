@@ -1,335 +1,355 @@
-// decode.cu -- the streaming quantized GEMV that carries the decode step.
+// decode.cu -- the quantized GEMV that carries the decode step.
 //
-// Persistent CTAs, one producer thread + 8 consumer warps.  The producer
-// streams contiguous row tiles of the packed weight planes global -> shared
-// through a ring of `stages` bulk copies (cp.async.bulk + mbarrier), issuing
-// the first stages before waiting on the predecessor kernel (weights do not
-// depend on it), so the weight stream starts while the previous kernel drains.
-// Consumer warps stage the int8 activations once per CTA, then compute
-// per-block dp4a dots from shared memory (exactly the reference's per-block
-// integers, see gemv.cuh) and run the epilogue for each finished row:
+// Each warp owns RPW = 2 consecutive weight rows and streams them from HBM with
+// 128-bit loads straight into registers (no shared-memory staging: at batch 1
+// every weight byte is used once).  Rows longer than one chunk of loads are
+// split across KS warps of the same CTA whose partial sums meet in shared
+// memory.  The first chunk of weights is loaded before the kernel waits on its
+// predecessor (programmatic dependent launch): weights never depend on it, so
+// their DRAM latency overlaps the previous kernel's tail.  Lanes also
+// bulk-prefetch the warp's next rows into L2 while it computes.
+//
+// Activation rows are staged in shared memory by the prologue:
+//   PRO_Q     copy already-quantized int8 rows
+//   PRO_F32   per-32 quantization of f32 rows            (matmul.rs:105-127)
+//   PRO_NORM  rmsnorm, then per-32 quantization          (norms.rs:9-23)
+// The per-block integer dots are exactly the reference's (gemv.cuh); each
+// finished row goes through an epilogue:
 //   EPI_STORE   out = W.x (+ bias)                      (Linear::apply)
 //   EPI_RESID   out += W.x                              (x += wo.attn, x += w2.h)
 //   EPI_ARGMAX  logits + first-max argmax               (Model::logits + argmax)
 //   EPI_QKV     bias + RoPE + q / f16 K,V cache writes  (infer.rs:164-178)
 //   EPI_SWIGLU  h = silu(gate) * up                     (infer.rs:192-199)
-// and the last CTA to finish runs a "finisher" that prepares the next kernel's
-// input once for everyone: rmsnorm + per-32 quantization of the residual
-// stream (FIN_NORM_Q) or plain quantization (FIN_Q).
 #include <climits>
+#include <map>
+#include <mutex>
 
 #include "finish.cuh"
 #include "gemv.cuh"
 #include "internal.h"
-#include "tma.cuh"
+#include "mbar.cuh"
 
 namespace prana {
 
-constexpr int SW_CONSUMERS = 8;                     // consumer warps
-constexpr int SW_THREADS = (SW_CONSUMERS + 1) * 32;  // + one producer warp
-constexpr int SW_CT = SW_CONSUMERS * 32;
+constexpr int DG_WARPS = 8;
+constexpr int DG_THREADS = DG_WARPS * 32;
+constexpr int DG_RPW = 2;  // rows per warp; even, so RoPE and gate/up pairs never straddle warps
 
-// ---------------------------------------------------------------- units from shared memory
+// Units a lane loads per chunk: enough 128-bit loads in flight per lane
+// without spilling (a Q4_0 unit is 18 bytes, Q8_0 34, Q4_K 48, Q6_K 58).
+template <int T> constexpr int chunk_units() { return T == T_Q4_0 ? 4 : 2; }
+int gemv_chunk_units(int type) { return type == T_Q4_0 ? 4 : 2; }
 
-struct StageView {
-  const uint8_t* p[4];  // plane bases inside the stage
-  int rb[4];            // bytes per row of each plane
-};
-
-template <int T> __device__ __forceinline__ Unit<T> load_unit_s(const StageView& v, int lr, int u);
-
-template <> __device__ __forceinline__ Unit<T_Q8_0> load_unit_s<T_Q8_0>(const StageView& v, int lr, int u) {
-  Unit<T_Q8_0> x;
-  const uint8_t* q = v.p[0] + lr * v.rb[0] + u * 32;
-  x.a = *reinterpret_cast<const uint4*>(q);
-  x.b = *reinterpret_cast<const uint4*>(q + 16);
-  x.d = *reinterpret_cast<const unsigned short*>(v.p[1] + lr * v.rb[1] + u * 2);
-  return x;
+// Byte offset of the f32 staging row in a CTA's shared memory: after the int8
+// rows, scales, sums and partial sums, rounded up to 16 bytes.
+__host__ __device__ __forceinline__ size_t gemv_staging_offset(int M, int K) {
+  const size_t b = (size_t)M * K + (size_t)M * (K / 32) * 8 + (size_t)DG_WARPS * DG_RPW * M * 4;
+  return (b + 15) & ~(size_t)15;
 }
-template <> __device__ __forceinline__ Unit<T_Q4_0> load_unit_s<T_Q4_0>(const StageView& v, int lr, int u) {
-  Unit<T_Q4_0> x;
-  x.q = *reinterpret_cast<const uint4*>(v.p[0] + lr * v.rb[0] + u * 16);
-  x.d = *reinterpret_cast<const unsigned short*>(v.p[1] + lr * v.rb[1] + u * 2);
-  return x;
+
+// ---------------------------------------------------------------- epilogue of one finished row group
+
+// Lane m (< g.m) holds v[r] = row (r0 + r) . activation row m.
+template <int EPI>
+__device__ __forceinline__ void finish_rows(const StreamArgs& g, int r0, int m, const float (&v)[DG_RPW], float& run_v,
+                                            int& run_i) {
+  const int N = g.N;
+  if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_ARGMAX) {
+#pragma unroll
+    for (int r = 0; r < DG_RPW; r++) {
+      const int row = r0 + r;
+      if (row >= N) break;
+      if constexpr (EPI == EPI_STORE) {
+        float o = v[r];
+        if (g.bias) o = __fadd_rn(o, g.bias[row]);
+        g.out[(size_t)m * N + row] = o;
+      } else if constexpr (EPI == EPI_RESID) {
+        float* o = g.out + (size_t)m * N + row;
+        *o = __fadd_rn(*o, v[r]);
+      } else {
+        if (g.out) g.out[(size_t)m * N + row] = v[r];
+        if (v[r] > run_v || (v[r] == run_v && row < run_i)) {
+          run_v = v[r];
+          run_i = row;
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    // stored rows 2j (gate) and 2j+1 (up): silu(g)*u exactly as norms.rs:27-31, infer.rs:197-199
+#pragma unroll
+    for (int r = 0; r < DG_RPW; r += 2) {
+      const int row = r0 + r;
+      if (row >= N) break;
+      const float gv = v[r];
+      const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+      g.out[(size_t)m * (N / 2) + row / 2] = __fmul_rn(__fmul_rn(gv, sg), v[r + 1]);
+    }
+  } else {  // EPI_QKV
+    const QkvMap& qm = g.qkv;
+#pragma unroll
+    for (int r = 0; r < DG_RPW; r += 2) {
+      const int row = r0 + r;
+      if (row >= N) break;
+      int s = 0;
+      while (s + 1 < qm.nseg && row >= qm.seg_start[s + 1]) s++;
+      const int kind = qm.kind[s];
+      const int p = (row - qm.seg_start[s]) / 2;  // pair index inside the projection
+      const int half = qm.hd / 2;
+      int ra, rb;
+      if (kind != 2 && qm.neox) {
+        ra = (p / half) * qm.hd + p % half;
+        rb = ra + half;
+      } else {
+        ra = 2 * p;
+        rb = ra + 1;
+      }
+      const int j = p % half;
+      float va = v[r], vb = v[r + 1];
+      if (qm.bias[s]) {
+        va = __fadd_rn(va, qm.bias[s][ra]);
+        vb = __fadd_rn(vb, qm.bias[s][rb]);
+      }
+      const int pos = (qm.pos_dev ? *qm.pos_dev : qm.pos0) + m;
+      if (kind != 2) {
+        const float c = qm.cos_t[(size_t)pos * half + j], sn = qm.sin_t[(size_t)pos * half + j];
+        const float a0 = va, b0 = vb;
+        va = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(b0, sn));
+        vb = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(b0, c));
+      }
+      if (kind == 0) {
+        qm.q_out[(size_t)m * qm.q_dim + ra] = va;
+        qm.q_out[(size_t)m * qm.q_dim + rb] = vb;
+      } else {
+        __half* cache = kind == 1 ? qm.kc : qm.vc;
+        if (pos < qm.cap) {
+          cache[(size_t)pos * qm.kv_dim + ra] = __float2half_rn(va);
+          cache[(size_t)pos * qm.kv_dim + rb] = __float2half_rn(vb);
+        }
+        float* win = kind == 1 ? qm.k_f32 : qm.v_f32;
+        if (win) {
+          win[(size_t)m * qm.kv_dim + ra] = va;
+          win[(size_t)m * qm.kv_dim + rb] = vb;
+        }
+      }
+    }
+  }
 }
-template <> __device__ __forceinline__ Unit<T_Q4_K> load_unit_s<T_Q4_K>(const StageView& v, int lr, int u) {
-  Unit<T_Q4_K> x;
-  const uint8_t* sb = v.p[0] + lr * v.rb[0] + (u >> 2) * 144;
-  x.a = *reinterpret_cast<const uint4*>(sb + 16 + (u & 3) * 32);
-  x.b = *reinterpret_cast<const uint4*>(sb + 32 + (u & 3) * 32);
-  x.meta = *reinterpret_cast<const uint4*>(sb);
-  return x;
-}
-template <> __device__ __forceinline__ Unit<T_Q6_K> load_unit_s<T_Q6_K>(const StageView& v, int lr, int u) {
-  Unit<T_Q6_K> x;
-  const int b = u >> 2, h = (u >> 1) & 1, l0 = (u & 1) * 16;
-  const uint8_t* ql = v.p[0] + lr * v.rb[0] + b * 128 + h * 64 + l0;
-  x.lo = *reinterpret_cast<const uint4*>(ql);
-  x.hi = *reinterpret_cast<const uint4*>(ql + 32);
-  x.qh = *reinterpret_cast<const uint4*>(v.p[1] + lr * v.rb[1] + b * 64 + h * 32 + l0);
-  x.sc = *reinterpret_cast<const uint2*>(v.p[2] + lr * v.rb[2] + b * 16 + h * 8);
-  x.d = *reinterpret_cast<const unsigned short*>(v.p[3] + lr * v.rb[3] + b * 2);
-  return x;
+
+// Bulk-prefetch toward L2 the unit range [u0, u1) of rows [r0, r0 + RPW) of
+// every plane; lane i < RPW * 4 issues at most one range.
+template <int T>
+__device__ __forceinline__ void prefetch_group(const DevWeight& w, int r0, int u0, int u1, int lane) {
+  const int r = lane % DG_RPW, p = lane / DG_RPW;
+  const int row = r0 + r;
+  if (row >= w.rows || u0 >= u1) return;
+  const size_t K = (size_t)w.cols;
+  const size_t n = (size_t)(u1 - u0);
+  if constexpr (T == T_Q8_0) {
+    if (p == 0) prefetch_span(w.qs, row * K + (size_t)u0 * 32, n * 32);
+    if (p == 1) prefetch_span(w.d, row * (K / 16) + (size_t)u0 * 2, n * 2);
+  } else if constexpr (T == T_Q4_0) {
+    if (p == 0) prefetch_span(w.qs, row * (K / 2) + (size_t)u0 * 16, n * 16);
+    if (p == 1) prefetch_span(w.d, row * (K / 16) + (size_t)u0 * 2, n * 2);
+  } else if constexpr (T == T_Q4_K) {  // units are 64-weight pairs, 4 per 144-byte super-block
+    const size_t b0 = u0 / 4, b1 = (u1 + 3) / 4;
+    if (p == 0) prefetch_span(w.qs, row * (K / 256) * 144 + b0 * 144, (b1 - b0) * 144);
+  } else {  // Q6_K: 4 units per 256-weight super-block
+    const size_t b0 = u0 / 4, b1 = (u1 + 3) / 4;
+    if (p == 0) prefetch_span(w.qs, row * (K / 2) + b0 * 128, (b1 - b0) * 128);
+    if (p == 1) prefetch_span(w.qh, row * (K / 4) + b0 * 64, (b1 - b0) * 64);
+    if (p == 2) prefetch_span(w.sc, row * (K / 16) + b0 * 16, (b1 - b0) * 16);
+    if (p == 3) prefetch_span(w.d, row * (K / 128) + b0 * 2, (b1 - b0) * 2);
+  }
 }
 
 // ---------------------------------------------------------------- the kernel
 
-// PRO selects how the consumers stage the activation rows while the producer's
-// first weight tiles are already in flight: PRO_Q copies int8 rows, PRO_F32
-// quantizes f32 rows, PRO_NORM applies rmsnorm then quantizes.
 template <int T, int M, int EPI, int PRO>
-__global__ void __launch_bounds__(SW_THREADS, 1) stream_gemv(const StreamArgs g) {
-  extern __shared__ __align__(128) uint8_t smem[];
+__global__ void __launch_bounds__(DG_THREADS) stream_gemv(const StreamArgs g) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int CH = chunk_units<T>();
+  const DevWeight& w = g.w;
   const int K = g.K, G = K / 32, N = g.N;
-  const TilePlan& tp = g.plan;
-  const int R = tp.R, wpr = tp.wpr, S = tp.stages;
-  const int ntiles = ceil_div(N, R);
-  const int n_my = (int)blockIdx.x < ntiles ? ceil_div(ntiles - (int)blockIdx.x, (int)gridDim.x) : 0;
-  // shared layout: [stages x stage_bytes][acts][partials][barriers]
-  uint8_t* stage0 = smem;
-  int8_t* sq = reinterpret_cast<int8_t*>(smem + (size_t)S * tp.stage_bytes);
+  const int U = units_per_row(T, K);
+  const int ks = g.ks, gpc = DG_WARPS / ks;  // warps per row group, row groups per CTA
+  const int P = ceil_div(U, ks);             // units per K part
+  const int n_groups = ceil_div(N, DG_RPW);
+  const int n_tiles = ceil_div(n_groups, gpc);
+  // shared layout: [int8 rows][scales][sums][partials][f32 row staging][norm weight][barriers]
+  int8_t* sq = reinterpret_cast<int8_t*>(smem);
   float* ss = reinterpret_cast<float*>(sq + (size_t)M * K);
   int32_t* ssum = reinterpret_cast<int32_t*>(ss + M * G);
-  float* part = reinterpret_cast<float*>(ssum + M * G);  // [R][wpr][M]
-  uint64_t* full = reinterpret_cast<uint64_t*>(
-      (reinterpret_cast<uintptr_t>(part + R * wpr * M) + 7) & ~(uintptr_t)7);
-  uint64_t* empty = full + S;
-  __shared__ float red[8 * SW_CONSUMERS];
+  float* part = reinterpret_cast<float*>(ssum + M * G);  // [warp][RPW][M]
+  // bulk-copy destinations start on 16 bytes (M * K + 8 * M * G bytes need not be a multiple of 16)
+  float* xs = reinterpret_cast<float*>(smem + gemv_staging_offset(M, K));  // PRO_F32 / PRO_NORM: one f32 row
+  float* ws = xs + (PRO == PRO_Q ? 0 : K);                                  // PRO_NORM: the rmsnorm weight
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ws + (PRO == PRO_NORM ? K : 0));  // [0]: rows, [1]: weight
+  __shared__ float red[8 * DG_WARPS];
   __shared__ float inv_s[8];
   __shared__ int flag;
-  __shared__ float wbest[SW_CONSUMERS][8];
-  __shared__ int widx[SW_CONSUMERS][8];
+  __shared__ float wbest[DG_WARPS][8];
+  __shared__ int widx[DG_WARPS][8];
 
   const int tid = threadIdx.x, wi = tid >> 5, lane = tid & 31;
-  if (tid == 0) {
-    for (int s = 0; s < S; s++) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
+  const int gs = wi / ks, kp = wi - gs * ks;
+  const int u_lo = kp * P, u_hi = min(U, u_lo + P);
+  if (PRO != PRO_Q && tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
     fence_barrier_init();
+    if (PRO == PRO_NORM) {  // the norm weight is constant: fetch it before the wait
+      mbar_arrive_expect_tx(&bars[1], (uint32_t)K * 4);
+      bulk_g2s(ws, g.norm_w, (uint32_t)K * 4, &bars[1]);
+    }
   }
-  __syncthreads();
 
-  if (wi == SW_CONSUMERS) {
-    // ------------------------------------------------ producer
-    if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
-      for (int i = 0; i < n_my; i++) {
-        const int st = i % S;
-        if (i >= S && !mbar_wait(&empty[st], ((i / S) - 1) & 1)) {
-          atomicExch(g.err, ERR_TIMEOUT);
-          break;
-        }
-        const int t = blockIdx.x + i * gridDim.x;
-        const int r0 = t * R, rows = min(R, N - r0);
-        uint32_t bytes[4], total = 0;
-        for (int p = 0; p < tp.nplanes; p++) {
-          bytes[p] = (uint32_t)(((size_t)rows * tp.row_bytes[p] + 15) & ~(size_t)15);
-          total += bytes[p];
-        }
-        mbar_arrive_expect_tx(&full[st], total);
-        uint8_t* dst = stage0 + (size_t)st * tp.stage_bytes;
-        for (int p = 0; p < tp.nplanes; p++)
-          bulk_g2s(dst + tp.smem_off[p], tp.plane[p] + (size_t)r0 * tp.row_bytes[p], bytes[p], &full[st], pol);
+  Unit<T> buf[DG_RPW][CH];
+  auto load = [&](int r0, int c0) {
+#pragma unroll
+    for (int r = 0; r < DG_RPW; r++) {
+      const int row = min(r0 + r, N - 1);
+#pragma unroll
+      for (int j = 0; j < CH; j++) {
+        const int u = c0 + lane + 32 * j;
+        if (u < u_hi) buf[r][j] = load_unit<T>(w, row, u);
       }
     }
-    return;
-  }
+  };
 
-  // -------------------------------------------------- consumers
+  // weights first: they do not depend on the previous kernel
+  int t = blockIdx.x;
+  if (t < n_tiles && t * gpc + gs < n_groups) {
+    const int r0 = (t * gpc + gs) * DG_RPW;
+    if (lane < DG_RPW * 4 && u_hi - u_lo > 32 * CH) prefetch_group<T>(w, r0, u_lo + 32 * CH, u_hi, lane);
+    load(r0, u_lo);
+  }
+  __syncthreads();  // barrier initialization is visible to every waiting thread
   pdl_wait();
-  if constexpr (PRO == PRO_Q) {  // stage already-quantized activation rows
+  if constexpr (PRO == PRO_Q) {
     const int nb = g.m * K / 16;
-    for (int i = tid; i < nb; i += SW_CT) reinterpret_cast<uint4*>(sq)[i] = __ldcg(reinterpret_cast<const uint4*>(g.aq) + i);
-    for (int i = tid; i < g.m * G; i += SW_CT) {
+    for (int i = tid; i < nb; i += DG_THREADS)
+      reinterpret_cast<uint4*>(sq)[i] = __ldcg(reinterpret_cast<const uint4*>(g.aq) + i);
+    for (int i = tid; i < g.m * G; i += DG_THREADS) {
       ss[i] = __ldcg(g.as + i);
       ssum[i] = __ldcg(g.asum + i);
     }
-  } else {  // (rmsnorm +) per-32 quantization, one group per thread
-    block_quantize_rows(g.x, PRO == PRO_NORM ? g.norm_w : nullptr, g.eps, g.m, K, sq, ss, ssum, red, inv_s, SW_CT, 1);
+  } else {
+    // each f32 row arrives in shared memory with one bulk copy, then is
+    // (normalized and) quantized from there
+    bool ok = PRO != PRO_NORM || mbar_wait(&bars[1], 0);
+    for (int m = 0; m < g.m; m++) {
+      if (tid == 0) {
+        mbar_arrive_expect_tx(&bars[0], (uint32_t)K * 4);
+        bulk_g2s(xs, g.x + (size_t)m * K, (uint32_t)K * 4, &bars[0]);
+      }
+      ok = mbar_wait(&bars[0], m & 1) && ok;
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0 && g.err) atomicExch(g.err, ERR_TIMEOUT);
+        return;
+      }
+      block_quantize_smem(xs, PRO == PRO_NORM ? ws : nullptr, g.eps, K, sq + (size_t)m * K, ss + m * G, ssum + m * G,
+                          red, inv_s);
+      __syncthreads();  // the next row's copy overwrites the staging row
+    }
   }
-  consumer_sync(SW_CT);
+  __syncthreads();
   if (g.trace_q && blockIdx.x == 0) {
-    for (int i = tid; i < g.m * K; i += SW_CT) g.trace_q[i] = sq[i];
-    for (int i = tid; i < g.m * G; i += SW_CT) g.trace_s[i] = ss[i];
+    for (int i = tid; i < g.m * K; i += DG_THREADS) g.trace_q[i] = sq[i];
+    for (int i = tid; i < g.m * G; i += DG_THREADS) g.trace_s[i] = ss[i];
   }
   pdl_trigger();
-  const Acts a{sq, ss, ssum, K, G};
-  const int U = units_per_row(T, K);
-  float run_v[M];
-  int run_i[M];
-#pragma unroll
-  for (int m = 0; m < M; m++) {
-    run_v[m] = -INFINITY;
-    run_i[m] = INT_MAX;
-  }
-  bool ok = true;
-  for (int i = 0; i < n_my; i++) {
-    const int st = i % S;
-    if (tid == 0) flag = mbar_wait(&full[st], (i / S) & 1) ? 1 : 0;
-    consumer_sync(SW_CT);
-    if (!flag) {
-      if (tid == 0) atomicExch(g.err, ERR_TIMEOUT);
-      ok = false;
-      break;
-    }
-    const int t = blockIdx.x + i * gridDim.x;
-    const int r0 = t * R, rows = min(R, N - r0);
-    StageView v;
-    const uint8_t* sb = stage0 + (size_t)st * tp.stage_bytes;
-#pragma unroll
-    for (int p = 0; p < 4; p++) {
-      v.p[p] = sb + tp.smem_off[p];
-      v.rb[p] = tp.row_bytes[p];
-    }
-    // work items: (row, K-segment); a warp takes items wi, wi + 8, ...
-    const int items = rows * wpr;
-    for (int it = wi; it < items; it += SW_CONSUMERS) {
-      const int lr = it / wpr, ks = it - lr * wpr;
-      const int u0 = ks * U / wpr, u1 = (ks + 1) * U / wpr;
-      float acc[M];
-#pragma unroll
-      for (int m = 0; m < M; m++) acc[m] = 0.0f;
-      int u = u0 + lane;
-      for (; u + 32 < u1; u += 64) {
-        const Unit<T> x0 = load_unit_s<T>(v, lr, u);
-        const Unit<T> x1 = load_unit_s<T>(v, lr, u + 32);
-        accum_unit<M>(x0, u, a, g.m, acc);
-        accum_unit<M>(x1, u + 32, a, g.m, acc);
-      }
-      if (u < u1) accum_unit<M>(load_unit_s<T>(v, lr, u), u, a, g.m, acc);
-#pragma unroll
-      for (int m = 0; m < M; m++) acc[m] = warp_sum(acc[m]);
-      if (lane < M) {
-        float mine = acc[0];
-#pragma unroll
-        for (int m = 1; m < M; m++)
-          if (lane == m) mine = acc[m];
-        part[(lr * wpr + ks) * M + lane] = mine;
-      }
-    }
-    consumer_sync(SW_CT);
-    if (tid == 0) mbar_arrive(&empty[st]);  // the stage's bytes are no longer read
-    // ---- epilogue: one thread per (output, activation row)
-    const int pairs = (EPI == EPI_QKV || EPI == EPI_SWIGLU) ? 2 : 1;
-    const int outs = rows / pairs;
-    for (int o = tid; o < outs * g.m; o += SW_CT) {
-      const int oi = o / g.m, m = o - oi * g.m;
-      float val[2] = {0.0f, 0.0f};
-      for (int pp = 0; pp < pairs; pp++)
-        for (int ks = 0; ks < wpr; ks++) val[pp] += part[((oi * pairs + pp) * wpr + ks) * M + m];
-      const int row = r0 + oi * pairs;  // stored row (first of the pair)
-      if constexpr (EPI == EPI_STORE) {
-        float r = val[0];
-        if (g.bias) r = __fadd_rn(r, g.bias[row]);
-        g.out[(size_t)m * N + row] = r;
-      } else if constexpr (EPI == EPI_RESID) {
-        float* o_ = g.out + (size_t)m * N + row;
-        *o_ = __fadd_rn(*o_, val[0]);
-      } else if constexpr (EPI == EPI_ARGMAX) {
-        if (g.out) g.out[(size_t)m * N + row] = val[0];
-        // per-thread running max over the rows it finalizes
-        if (val[0] > run_v[m < M ? m : 0] || (val[0] == run_v[m < M ? m : 0] && row < run_i[m < M ? m : 0])) {
-          run_v[m < M ? m : 0] = val[0];
-          run_i[m < M ? m : 0] = row;
-        }
-      } else if constexpr (EPI == EPI_SWIGLU) {
-        // stored rows 2j (gate) and 2j+1 (up): silu(g)*u exactly as norms.rs:27-31, infer.rs:197-199
-        const float gv = val[0];
-        const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
-        g.out[(size_t)m * (N / 2) + row / 2] = __fmul_rn(__fmul_rn(gv, sg), val[1]);
-      } else {  // EPI_QKV
-        const QkvMap& qm = g.qkv;
-        int s = 0;
-        while (s + 1 < qm.nseg && row >= qm.seg_start[s + 1]) s++;
-        const int kind = qm.kind[s];
-        const int p = (row - qm.seg_start[s]) / 2;  // pair index inside the projection
-        const int half = qm.hd / 2;
-        int ra, rb, j;
-        if (kind != 2 && qm.neox) {
-          ra = (p / half) * qm.hd + p % half;
-          rb = ra + half;
-          j = p % half;
-        } else {
-          ra = 2 * p;
-          rb = ra + 1;
-          j = p % half;
-        }
-        float va = val[0], vb = val[1];
-        if (qm.bias[s]) {
-          va = __fadd_rn(va, qm.bias[s][ra]);
-          vb = __fadd_rn(vb, qm.bias[s][rb]);
-        }
-        const int pos = (qm.pos_dev ? *qm.pos_dev : qm.pos0) + m;
-        if (kind != 2) {
-          const float c = qm.cos_t[(size_t)pos * half + j], sn = qm.sin_t[(size_t)pos * half + j];
-          const float a0 = va, b0 = vb;
-          va = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(b0, sn));
-          vb = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(b0, c));
-        }
-        if (kind == 0) {
-          qm.q_out[(size_t)m * qm.q_dim + ra] = va;
-          qm.q_out[(size_t)m * qm.q_dim + rb] = vb;
-        } else {
-          __half* cache = kind == 1 ? qm.kc : qm.vc;
-          if (pos < qm.cap) {
-            cache[(size_t)pos * qm.kv_dim + ra] = __float2half_rn(va);
-            cache[(size_t)pos * qm.kv_dim + rb] = __float2half_rn(vb);
-          }
-          float* win = kind == 1 ? qm.k_f32 : qm.v_f32;
-          if (win) {
-            win[(size_t)m * qm.kv_dim + ra] = va;
-            win[(size_t)m * qm.kv_dim + rb] = vb;
-          }
-        }
-      }
-    }
-    consumer_sync(SW_CT);  // `part` is rewritten by the next tile
-  }
-  if (!ok) return;
 
-  // -------------------------------------------------- cross-CTA completion
-  if constexpr (EPI == EPI_ARGMAX) {
-    // reduce the per-thread running maxima of this CTA, per activation row
-    for (int m = 0; m < g.m && m < M; m++) {
-      float bv = run_v[m];
-      int bi = run_i[m];
+  const Acts a{sq, ss, ssum, K, G};
+  float run_v = -INFINITY;
+  int run_i = INT_MAX;
+  bool first = true;
+  for (; t < n_tiles; t += gridDim.x) {
+    const int grp = t * gpc + gs;
+    const bool live = grp < n_groups;
+    const int r0 = grp * DG_RPW;
+    // the next tile's rows toward L2 while this one computes
+    if (lane < DG_RPW * 4) {
+      const int nt = t + gridDim.x;
+      if (nt < n_tiles && nt * gpc + gs < n_groups) prefetch_group<T>(w, (nt * gpc + gs) * DG_RPW, u_lo, u_hi, lane);
+    }
+    float acc[DG_RPW][M];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      if (lane == 0) {
-        wbest[wi][m] = bv;
-        widx[wi][m] = bi;
+    for (int r = 0; r < DG_RPW; r++)
+#pragma unroll
+      for (int m = 0; m < M; m++) acc[r][m] = 0.0f;
+    if (live) {
+      for (int c0 = u_lo; c0 < u_hi; c0 += 32 * CH) {
+        if (!first) load(r0, c0);
+        first = false;
+#pragma unroll
+        for (int r = 0; r < DG_RPW; r++)
+#pragma unroll
+          for (int j = 0; j < CH; j++) {
+            const int u = c0 + lane + 32 * j;
+            if (u < u_hi) accum_unit<M>(buf[r][j], u, a, g.m, acc[r]);
+          }
       }
     }
-    consumer_sync(SW_CT);
+    first = false;
+#pragma unroll
+    for (int r = 0; r < DG_RPW; r++)
+#pragma unroll
+      for (int m = 0; m < M; m++) acc[r][m] = warp_sum(acc[r][m]);
+    // lane m keeps activation row m's sums
+    float v[DG_RPW];
+#pragma unroll
+    for (int r = 0; r < DG_RPW; r++) {
+      v[r] = acc[r][0];
+#pragma unroll
+      for (int m = 1; m < M; m++)
+        if (lane == m) v[r] = acc[r][m];
+    }
+    if (ks > 1) {  // K parts of a row group meet in shared memory; the part-0 warp finishes
+      if (lane < M) {
+#pragma unroll
+        for (int r = 0; r < DG_RPW; r++) part[(wi * DG_RPW + r) * M + lane] = v[r];
+      }
+      __syncthreads();
+      if (kp == 0 && lane < g.m) {
+#pragma unroll
+        for (int r = 0; r < DG_RPW; r++) {
+          float s = 0.0f;
+          for (int k = 0; k < ks; k++) s += part[((wi + k) * DG_RPW + r) * M + lane];
+          v[r] = s;
+        }
+        if (live) finish_rows<EPI>(g, r0, lane, v, run_v, run_i);
+      }
+      __syncthreads();
+    } else if (live && lane < g.m) {
+      finish_rows<EPI>(g, r0, lane, v, run_v, run_i);
+    }
+  }
+
+  // -------------------------------------------------- cross-CTA argmax (Model::argmax: first maximum)
+  if constexpr (EPI == EPI_ARGMAX) {
+    if (lane < 8) {
+      wbest[wi][lane] = run_v;
+      widx[wi][lane] = run_i;
+    }
+    __syncthreads();
     if (tid < g.m) {
       float bv = -INFINITY;
       int bi = INT_MAX;
-      for (int w = 0; w < SW_CONSUMERS; w++)
-        if (wbest[w][tid] > bv || (wbest[w][tid] == bv && widx[w][tid] < bi)) {
-          bv = wbest[w][tid];
-          bi = widx[w][tid];
+      for (int q = 0; q < DG_WARPS; q++)
+        if (wbest[q][tid] > bv || (wbest[q][tid] == bv && widx[q][tid] < bi)) {
+          bv = wbest[q][tid];
+          bi = widx[q][tid];
         }
       g.part_val[(size_t)tid * gridDim.x + blockIdx.x] = bv;
       g.part_idx[(size_t)tid * gridDim.x + blockIdx.x] = bi;
     }
-  }
-  if (g.counter == nullptr) return;
-  __threadfence();
-  consumer_sync(SW_CT);
-  if (tid == 0) flag = atomicAdd(g.counter, 1u) == gridDim.x - 1;
-  consumer_sync(SW_CT);
-  if (!flag) return;
-  __threadfence();
-  if constexpr (EPI == EPI_ARGMAX) {
-    for (int m = wi; m < g.m; m += SW_CONSUMERS) {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) flag = atomicAdd(g.counter, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!flag) return;
+    __threadfence();
+    for (int m = wi; m < g.m; m += DG_WARPS) {
       float bv = -INFINITY;
       int bi = INT_MAX;
       for (int b = lane; b < (int)gridDim.x; b += 32) {
@@ -355,10 +375,8 @@ __global__ void __launch_bounds__(SW_THREADS, 1) stream_gemv(const StreamArgs g)
         if (m == 0 && g.token_next) *g.token_next = (int)tok;
       }
     }
+    if (tid == 0) *g.counter = 0u;
   }
-  if (g.fin_x)
-    block_quantize_rows(g.fin_x, g.fin_norm, g.fin_eps, g.m, g.fin_n, g.fin_q, g.fin_s, g.fin_sum, red, inv_s, SW_CT, 1);
-  if (tid == 0) *g.counter = 0u;
 }
 
 // ---------------------------------------------------------------- launch
@@ -372,83 +390,56 @@ static int sw_sm_count() {
   return n[dev];
 }
 
-int row_plane_bytes(int type, int K, int* rb) {
-  switch (type) {
-    case T_Q8_0: rb[0] = K; rb[1] = K / 16; return 2;
-    case T_Q4_0: rb[0] = K / 2; rb[1] = K / 16; return 2;
-    case T_Q4_K: rb[0] = K / 256 * 144; return 1;
-    case T_Q6_K: rb[0] = K / 2; rb[1] = K / 4; rb[2] = K / 16; rb[3] = K / 128; return 4;
-  }
-  return 0;
+// Warps per row group.  A warp streams its rows chunk after chunk (the rest of
+// its rows already on the way to L2), so K is split across warps only when the
+// matrix has too few rows to give every SM a CTA.
+int gemv_split_k(int type, int K, int N, int sm_count) {
+  const int need = ceil_div(units_per_row(type, K), 32 * gemv_chunk_units(type));
+  int ks = 1;
+  while (ks < need && ks < DG_WARPS && ceil_div(ceil_div(N, DG_RPW), DG_WARPS / ks) < sm_count) ks *= 2;
+  return ks;
 }
 
-static size_t acts_bytes(int M, int K) { return (size_t)M * K + (size_t)M * (K / 32) * 8; }
-
-// Tile plan for a weight: rows per tile, warps per row, ring depth.
-// Budget: SMEM_BUDGET bytes per CTA (one CTA per SM).
-bool plan_tiles(const DevWeight& w, int M, int budget, int min_rows_multiple, TilePlan& tp) {
-  int rb[4] = {0, 0, 0, 0};
-  const int np = row_plane_bytes(w.type, w.cols, rb);
-  if (!np) return false;
-  int row = 0;
-  bool aligned = true;
-  for (int p = 0; p < np; p++) {
-    row += rb[p];
-    if (rb[p] % 16) aligned = false;
-  }
-  const size_t acts = acts_bytes(M, w.cols);
-  const int cand[] = {64, 48, 32, 24, 16, 8, 4, 2, 1};
-  // largest tile that still leaves >= 3 stages in flight, else >= 2
-  for (int pass = 0; pass < 2; pass++)
-  for (int R : cand) {
-    if (R % min_rows_multiple) continue;
-    if (R < 8 && !aligned) continue;
-    const int wpr = R >= SW_CONSUMERS ? 1 : SW_CONSUMERS / R;
-    size_t stage = 0;
-    for (int p = 0; p < np; p++) stage += ((size_t)R * rb[p] + 15) & ~(size_t)15;
-    stage = (stage + 127) & ~(size_t)127;
-    const size_t fixed = acts + (size_t)R * wpr * M * 4 + 64 + 16 * 8;
-    if ((size_t)budget <= fixed) continue;
-    const int S = (int)std::min<size_t>(6, ((size_t)budget - fixed) / stage);
-    if (S < (pass == 0 ? 3 : 2) || stage > 48 * 1024) continue;
-    tp.R = R;
-    tp.wpr = wpr;
-    tp.stages = S;
-    tp.stage_bytes = (int)stage;
-    tp.nplanes = np;
-    int off = 0;
-    const uint8_t* base[4] = {w.qs, w.type == T_Q6_K ? w.qh : reinterpret_cast<const uint8_t*>(w.d),
-                              reinterpret_cast<const uint8_t*>(w.sc), reinterpret_cast<const uint8_t*>(w.d)};
-    for (int p = 0; p < 4; p++) {
-      tp.row_bytes[p] = p < np ? rb[p] : 0;
-      tp.plane[p] = p < np ? base[p] : nullptr;
-      tp.smem_off[p] = off;
-      if (p < np) off += (int)(((size_t)R * rb[p] + 15) & ~(size_t)15);
-    }
-    return true;
-  }
-  return false;
+size_t gemv_smem_bytes(int M, int K, int pro) {
+  const size_t staging = pro == PRO_Q ? 0 : (size_t)K * 4 * (pro == PRO_NORM ? 2 : 1);
+  return gemv_staging_offset(M, K) + staging + 16;
 }
 
-size_t stream_smem_bytes(const TilePlan& tp, int M, int K) {
-  return (size_t)tp.stages * tp.stage_bytes + acts_bytes(M, K) + (size_t)tp.R * tp.wpr * M * 4 + 8 + 16 * tp.stages;
+// Resident CTAs per SM of one kernel instance at a given shared-memory size
+// (cached: the decode step asks on every launch).
+static int resident_ctas(const void* k, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, size_t>, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({k, smem});
+  if (it != cache.end()) return it->second;
+  int b = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k, DG_THREADS, smem) != cudaSuccess || b < 1) {
+    cudaGetLastError();
+    b = 1;
+  }
+  cache[{k, smem}] = b;
+  return b;
 }
 
 template <int T, int M, int EPI, int PRO>
-static cudaError_t stream_go(const StreamArgs& g, cudaStream_t st, bool pdl, int ctas_per_sm) {
-  const size_t smem = stream_smem_bytes(g.plan, M, g.K);
+static cudaError_t stream_go(const StreamArgs& g, cudaStream_t st, bool pdl) {
+  const size_t smem = gemv_smem_bytes(M, g.K, PRO);
   auto k = stream_gemv<T, M, EPI, PRO>;
-  cudaError_t e = cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  const int ntiles = ceil_div(g.N, g.plan.R);
-  int grid = sw_sm_count() * ctas_per_sm;
-  if (grid > ntiles) grid = ntiles;
-  if (EPI == EPI_ARGMAX && g.n_parts < grid) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
   StreamArgs a = g;
+  a.ks = gemv_split_k(T, g.K, g.N, sw_sm_count());
+  const int n_tiles = ceil_div(ceil_div(g.N, DG_RPW), DG_WARPS / a.ks);
+  int grid = sw_sm_count() * resident_ctas((const void*)k, smem);
+  if (grid > n_tiles) grid = n_tiles;
+  if (EPI == EPI_ARGMAX && (g.n_parts < grid || g.counter == nullptr)) return cudaErrorInvalidValue;
   void* args[] = {&a};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(SW_THREADS);
+  cfg.blockDim = dim3(DG_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -462,20 +453,20 @@ static cudaError_t stream_go(const StreamArgs& g, cudaStream_t st, bool pdl, int
 }
 
 template <int T, int EPI, int PRO>
-static cudaError_t stream_m(const StreamArgs& g, cudaStream_t st, bool pdl, int cps) {
-  if (g.m <= 1) return stream_go<T, 1, EPI, PRO>(g, st, pdl, cps);
-  if (g.m <= 2) return stream_go<T, 2, EPI, PRO>(g, st, pdl, cps);
-  if (g.m <= 4) return stream_go<T, 4, EPI, PRO>(g, st, pdl, cps);
-  return stream_go<T, 8, EPI, PRO>(g, st, pdl, cps);
+static cudaError_t stream_m(const StreamArgs& g, cudaStream_t st, bool pdl) {
+  if (g.m <= 1) return stream_go<T, 1, EPI, PRO>(g, st, pdl);
+  if (g.m <= 2) return stream_go<T, 2, EPI, PRO>(g, st, pdl);
+  if (g.m <= 4) return stream_go<T, 4, EPI, PRO>(g, st, pdl);
+  return stream_go<T, 8, EPI, PRO>(g, st, pdl);
 }
 
 template <int EPI, int PRO>
-static cudaError_t stream_t(const StreamArgs& g, int type, cudaStream_t st, bool pdl, int cps) {
-  switch (type) {
-    case T_Q8_0: return stream_m<T_Q8_0, EPI, PRO>(g, st, pdl, cps);
-    case T_Q4_0: return stream_m<T_Q4_0, EPI, PRO>(g, st, pdl, cps);
-    case T_Q4_K: return stream_m<T_Q4_K, EPI, PRO>(g, st, pdl, cps);
-    case T_Q6_K: return stream_m<T_Q6_K, EPI, PRO>(g, st, pdl, cps);
+static cudaError_t stream_t(const StreamArgs& g, cudaStream_t st, bool pdl) {
+  switch (g.w.type) {
+    case T_Q8_0: return stream_m<T_Q8_0, EPI, PRO>(g, st, pdl);
+    case T_Q4_0: return stream_m<T_Q4_0, EPI, PRO>(g, st, pdl);
+    case T_Q4_K: return stream_m<T_Q4_K, EPI, PRO>(g, st, pdl);
+    case T_Q6_K: return stream_m<T_Q6_K, EPI, PRO>(g, st, pdl);
   }
   return cudaErrorInvalidValue;
 }
@@ -484,58 +475,19 @@ static cudaError_t stream_t(const StreamArgs& g, int type, cudaStream_t st, bool
 //   Q|K|V, gate|up, LM head:  rmsnorm + quantize the residual stream in the prologue
 //   wo, ffn_down:             quantize the attention output / silu(g)*u, residual epilogue
 //   kernel-level matmuls:     pre-quantized rows, plain store (or rmsnorm'd for unfused gate/up)
-cudaError_t launch_stream(const StreamArgs& g, int type, int epi, int pro, cudaStream_t st, bool pdl) {
-  if (g.m < 1 || g.m > 8) return cudaErrorInvalidValue;
-  static int cps = -1;
-  if (cps < 0) {
-    const char* e = getenv("PRANA_STREAM_CTAS_PER_SM");
-    cps = e ? atoi(e) : 1;
-    if (cps < 1) cps = 1;
-  }
-  if (epi == EPI_QKV && pro == PRO_NORM) return stream_t<EPI_QKV, PRO_NORM>(g, type, st, pdl, cps);
-  if (epi == EPI_SWIGLU && pro == PRO_NORM) return stream_t<EPI_SWIGLU, PRO_NORM>(g, type, st, pdl, cps);
-  if (epi == EPI_ARGMAX && pro == PRO_NORM) return stream_t<EPI_ARGMAX, PRO_NORM>(g, type, st, pdl, cps);
-  if (epi == EPI_RESID && pro == PRO_F32) return stream_t<EPI_RESID, PRO_F32>(g, type, st, pdl, cps);
-  if (epi == EPI_STORE && pro == PRO_Q) return stream_t<EPI_STORE, PRO_Q>(g, type, st, pdl, cps);
-  if (epi == EPI_STORE && pro == PRO_NORM) return stream_t<EPI_STORE, PRO_NORM>(g, type, st, pdl, cps);
+cudaError_t launch_stream(const StreamArgs& g, int epi, int pro, cudaStream_t st, bool pdl) {
+  if (g.m < 1 || g.m > 8 || g.K != g.w.cols || g.N != g.w.rows || g.K % 32) return cudaErrorInvalidValue;
+  // bulk copies of f32 rows need 16-byte aligned sources
+  if (pro != PRO_Q && ((reinterpret_cast<uintptr_t>(g.x) | reinterpret_cast<uintptr_t>(g.norm_w)) & 15))
+    return cudaErrorInvalidValue;
+  if ((epi == EPI_QKV || epi == EPI_SWIGLU) && g.N % 2) return cudaErrorInvalidValue;
+  if (epi == EPI_QKV && pro == PRO_NORM) return stream_t<EPI_QKV, PRO_NORM>(g, st, pdl);
+  if (epi == EPI_SWIGLU && pro == PRO_NORM) return stream_t<EPI_SWIGLU, PRO_NORM>(g, st, pdl);
+  if (epi == EPI_ARGMAX && pro == PRO_NORM) return stream_t<EPI_ARGMAX, PRO_NORM>(g, st, pdl);
+  if (epi == EPI_RESID && pro == PRO_F32) return stream_t<EPI_RESID, PRO_F32>(g, st, pdl);
+  if (epi == EPI_STORE && pro == PRO_Q) return stream_t<EPI_STORE, PRO_Q>(g, st, pdl);
+  if (epi == EPI_STORE && pro == PRO_NORM) return stream_t<EPI_STORE, PRO_NORM>(g, st, pdl);
   return cudaErrorInvalidValue;
-}
-
-// One CTA per token row: the embedding row (checkpoint.rs:169-174) into x, then
-// the first layer's rmsnorm + quantization of that row for the Q|K|V stream.
-__global__ void __launch_bounds__(256) embed_norm_kernel(const DevWeight w, const uint32_t* toks, const int* tok_single,
-                                                         float* x, const float* norm_w, float eps, int8_t* q, float* s,
-                                                         int32_t* sum) {
-  __shared__ float red[8 * 8];
-  __shared__ float inv_s[8];
-  const int m = blockIdx.x, dim = w.cols;
-  pdl_wait();
-  const uint32_t tok = tok_single ? (uint32_t)*tok_single : toks[m];
-  float* xr = x + (size_t)m * dim;
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) xr[i] = embed_value(w, tok, i);
-  __syncthreads();
-  pdl_trigger();
-  block_quantize_rows(xr, norm_w, eps, 1, dim, q + (size_t)m * dim, s + (size_t)m * (dim / 32),
-                      sum + (size_t)m * (dim / 32), red, inv_s, 256, 1);
-}
-
-cudaError_t launch_embed_norm(const DevWeight& emb, const uint32_t* toks, const int* tok_single, int m, float* x,
-                              const float* norm_w, float eps, int8_t* q, float* s, int32_t* sum, cudaStream_t st,
-                              bool pdl) {
-  DevWeight w = emb;
-  void* args[] = {&w, (void*)&toks, (void*)&tok_single, &x, (void*)&norm_w, &eps, &q, &s, &sum};
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(m);
-  cfg.blockDim = dim3(256);
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  if (pdl) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-  }
-  return cudaLaunchKernelExC(&cfg, (const void*)embed_norm_kernel, args);
 }
 
 }  // namespace prana

@@ -51,13 +51,9 @@ struct AttnArgs {
   int n_heads, n_kv, hd;
   int n_splits;
   float* part_ml;        // [n_kv][n_splits][m*group][2]
-  float* part_o;         // [n_kv][n_splits][m*group][hd]
-  unsigned* counters;    // [n_kv + 1], zero between launches
+  float* part_o;         // [n_kv][n_splits][m*group][hd], 16-byte aligned
+  unsigned* counters;    // [n_kv], zero between launches
   float* out;            // [m][n_heads*hd]
-  // optional finisher: quantize the whole output rows for the next projection
-  int8_t* out_q;
-  float* out_s;
-  int32_t* out_sum;
 };
 
 struct PrefillAttnArgs {
@@ -70,16 +66,6 @@ struct PrefillAttnArgs {
 
 // ---------------------------------------------------------------- streaming GEMV (decode.cu)
 enum : int { EPI_QKV = 3, EPI_SWIGLU = 4 };
-
-// How a weight streams through shared memory: R rows per tile (a tile is
-// R contiguous rows of every plane), wpr warps per row (K split when R < 8),
-// `stages` tiles in flight.
-struct TilePlan {
-  int R, wpr, stages, stage_bytes, nplanes;
-  const uint8_t* plane[4];
-  int row_bytes[4];
-  int smem_off[4];
-};
 
 // Q|K|V epilogue: the stored matrix concatenates projections of one weight
 // type; RoPE partners are adjacent stored rows (NeoX rows permuted at upload).
@@ -102,8 +88,9 @@ struct QkvMap {
 };
 
 struct StreamArgs {
+  DevWeight w;
   int K, N, m;
-  TilePlan plan;
+  int ks;  // warps per row group (K split), set by the launcher
   const int8_t* aq;  // PRO_Q: quantized activation rows [m][K] (+ scales, sums [m][K/32])
   const float* as;
   const int32_t* asum;
@@ -121,30 +108,14 @@ struct StreamArgs {
   int n_parts;
   uint32_t* token_out;
   int* token_next;
-  // last-CTA completion: argmax merge and/or finisher; counter is zero between launches
+  // last-CTA argmax merge; the counter is zero between launches
   unsigned* counter;
-  const float* fin_x;     // rows [m][fin_n] to (normalize and) quantize
-  const float* fin_norm;  // rmsnorm weight, or null for plain quantization
-  float fin_eps;
-  int fin_n;
-  int8_t* fin_q;
-  float* fin_s;
-  int32_t* fin_sum;
   QkvMap qkv;
 };
 
-// Shared-memory budget of one streaming-GEMV CTA: small enough that the next
-// kernel's CTA fits on the same SM, so under programmatic dependent launch its
-// producer starts streaming weights while this kernel drains.
-constexpr int STREAM_SMEM_BUDGET = 112 * 1024;
-
-bool plan_tiles(const DevWeight& w, int M, int budget, int min_rows_multiple, TilePlan& tp);
-int row_plane_bytes(int type, int K, int* rb);
-cudaError_t launch_stream(const StreamArgs& g, int type, int epi, int pro, cudaStream_t st, bool pdl);
-// embedding rows -> x, then rmsnorm + quantize into (q, s, sum) for the first projection
-cudaError_t launch_embed_norm(const DevWeight& emb, const uint32_t* toks, const int* tok_single, int m, float* x,
-                              const float* norm_w, float eps, int8_t* q, float* s, int32_t* sum, cudaStream_t st,
-                              bool pdl);
+cudaError_t launch_stream(const StreamArgs& g, int epi, int pro, cudaStream_t st, bool pdl);
+int gemv_split_k(int type, int K, int N, int sm_count);
+size_t gemv_smem_bytes(int M, int K, int pro);
 
 cudaError_t launch_gemv(const GemvArgs& g, int pro, int epi, cudaStream_t st, bool pdl);
 cudaError_t launch_quantize_acts(const float* x, int rows, int k, int8_t* q, float* s, int32_t* sum, cudaStream_t st);
@@ -164,6 +135,8 @@ cudaError_t launch_advance(int* tok, int* pos, uint32_t* ring, int ring_cap, int
 
 // attention.cu
 int attn_max_rows_per_cta(int hd);
+// attention splits for a cache of `positions` rows (scratch is sized by it)
+int attn_splits(int positions, int n_kv, int hd, int sm_count);
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_attn_prefill(const PrefillAttnArgs& a, cudaStream_t st);
 

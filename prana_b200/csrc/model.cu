@@ -178,22 +178,10 @@ using namespace prana;
 
 namespace {
 
-// A weight that streams through stream_gemv, with a tile plan per activation-row bucket.
+// A weight that streams through stream_gemv (the head may alias the embedding).
 struct StreamW {
   prana_weight w;
   bool owns = true;
-  TilePlan plan[4];  // M buckets 1, 2, 4, 8
-  bool planned[4] = {false, false, false, false};
-  int pair_rows = 1;  // tiles must hold whole (q/k rope, gate/up) pairs
-  int bucket(int m) const { return m <= 1 ? 0 : (m <= 2 ? 1 : (m <= 4 ? 2 : 3)); }
-  const TilePlan* plan_for(int m) {
-    const int b = bucket(m);
-    if (!planned[b]) {
-      if (!plan_tiles(w.dw, 1 << b, STREAM_SMEM_BUDGET, pair_rows, plan[b])) return nullptr;
-      planned[b] = true;
-    }
-    return &plan[b];
-  }
 };
 
 struct QkvPart {
@@ -312,9 +300,7 @@ int linear_raw(const Gguf& g, const std::string& name, size_t rows, size_t cols,
 
 size_t gguf_row_bytes(uint32_t type, size_t cols) { return type_size(type, cols); }
 
-int upload_stream(prana_model* m, uint32_t type, size_t rows, size_t cols, const uint8_t* bytes, int pair_rows,
-                  StreamW* sw) {
-  sw->pair_rows = pair_rows;
+int upload_stream(prana_model* m, uint32_t type, size_t rows, size_t cols, const uint8_t* bytes, StreamW* sw) {
   return upload_weight(m->ctx, (int)type, rows, cols, bytes, &sw->w);
 }
 
@@ -386,6 +372,7 @@ struct Trace {
 
 StreamArgs stream_args(prana_model* m, StreamW& w, int mrows, const float* x, const float* norm_w) {
   StreamArgs a{};
+  a.w = w.w.dw;
   a.K = w.w.dw.cols;
   a.N = w.w.dw.rows;
   a.m = mrows;
@@ -396,12 +383,8 @@ StreamArgs stream_args(prana_model* m, StreamW& w, int mrows, const float* x, co
   return a;
 }
 
-int run_stream(prana_model* m, StreamW& w, StreamArgs& a, int epi, int pro, bool pdl) {
-  const TilePlan* tp = w.plan_for(a.m);
-  if (!tp) return fail(PRANA_E_UNSUPPORTED, "no tile plan for a [%d x %d] weight of type %d", w.w.dw.rows, w.w.dw.cols,
-                       w.w.dw.type);
-  a.plan = *tp;
-  PRANA_CK(launch_stream(a, w.w.dw.type, epi, pro, m->ctx->own, pdl));
+int run_stream(prana_model* m, StreamArgs& a, int epi, int pro, bool pdl) {
+  PRANA_CK(launch_stream(a, epi, pro, m->ctx->own, pdl));
   return PRANA_OK;
 }
 
@@ -455,7 +438,7 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
           q.k_f32 = b.kf + (size_t)c0 * kv_dim;
           q.v_f32 = b.vf + (size_t)c0 * kv_dim;
         }
-        if ((rc = run_stream(m, part.sw, a, EPI_QKV, PRO_NORM, pdl))) return rc;
+        if ((rc = run_stream(m, a, EPI_QKV, PRO_NORM, pdl))) return rc;
       }
       first_part = false;
     }
@@ -487,7 +470,7 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       StreamArgs a = stream_args(m, L.wo, mc, b.att + (size_t)c0 * q_dim, nullptr);
       if (tr) tr->site(a, q_dim);
       a.out = b.x + (size_t)c0 * dim;
-      if ((rc = run_stream(m, L.wo, a, EPI_RESID, PRO_F32, pdl))) return rc;
+      if ((rc = run_stream(m, a, EPI_RESID, PRO_F32, pdl))) return rc;
     }
     // --- rmsnorm -> gate|up -> silu(gate) * up
     for (int c0 = 0; c0 < n; c0 += 8) {
@@ -496,15 +479,15 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
         StreamArgs a = stream_args(m, L.gu, mc, b.x + (size_t)c0 * dim, L.rms_ffn);
         if (tr) tr->site(a, dim);
         a.out = b.h + (size_t)c0 * hid;
-        if ((rc = run_stream(m, L.gu, a, EPI_SWIGLU, PRO_NORM, pdl))) return rc;
+        if ((rc = run_stream(m, a, EPI_SWIGLU, PRO_NORM, pdl))) return rc;
       } else {
         StreamArgs a = stream_args(m, L.w1, mc, b.x + (size_t)c0 * dim, L.rms_ffn);
         if (tr) tr->site(a, dim);
         a.out = b.h + (size_t)c0 * hid;
-        if ((rc = run_stream(m, L.w1, a, EPI_STORE, PRO_NORM, pdl))) return rc;
+        if ((rc = run_stream(m, a, EPI_STORE, PRO_NORM, pdl))) return rc;
         StreamArgs u = stream_args(m, L.w3, mc, b.x + (size_t)c0 * dim, L.rms_ffn);
         u.out = b.u + (size_t)c0 * hid;
-        if ((rc = run_stream(m, L.w3, u, EPI_STORE, PRO_NORM, pdl))) return rc;
+        if ((rc = run_stream(m, u, EPI_STORE, PRO_NORM, pdl))) return rc;
         PRANA_CK(launch_silu_mul(b.h + (size_t)c0 * hid, b.u + (size_t)c0 * hid, (size_t)mc * hid, st));
       }
     }
@@ -514,7 +497,7 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       StreamArgs a = stream_args(m, L.w2, mc, b.h + (size_t)c0 * hid, nullptr);
       if (tr) tr->site(a, hid);
       a.out = b.x + (size_t)c0 * dim;
-      if ((rc = run_stream(m, L.w2, a, EPI_RESID, PRO_F32, pdl))) return rc;
+      if ((rc = run_stream(m, a, EPI_RESID, PRO_F32, pdl))) return rc;
     }
   }
   if (!head) return PRANA_OK;
@@ -530,7 +513,7 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
     a.counter = m->ctr;
     a.token_out = b.tok_out + c0;
     a.token_next = (n == 1 && tok_dev) ? const_cast<int*>(tok_dev) : nullptr;
-    if ((rc = run_stream(m, m->head, a, EPI_ARGMAX, PRO_NORM, pdl))) return rc;
+    if ((rc = run_stream(m, a, EPI_ARGMAX, PRO_NORM, pdl))) return rc;
   }
   return PRANA_OK;
 }
@@ -744,13 +727,13 @@ int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
       }
       part.seg_start[part.nseg] = (int)at;
       L.qkv.push_back(part);
-      if ((rc = upload_stream(m.get(), types[s0], total_rows, dim, buf.data(), 2, &L.qkv.back().sw))) return rc;
+      if ((rc = upload_stream(m.get(), types[s0], total_rows, dim, buf.data(), &L.qkv.back().sw))) return rc;
       s0 = s1;
     }
     uint32_t ty;
     const uint8_t* raw;
     if ((rc = linear_raw(g, p + "attn_output.weight", dim, q_dim, &ty, &raw)) ||
-        (rc = upload_stream(m.get(), ty, dim, q_dim, raw, 1, &L.wo)))
+        (rc = upload_stream(m.get(), ty, dim, q_dim, raw, &L.wo)))
       return rc;
     // gate|up: interleave rows (gate j, up j) when both have one type
     uint32_t t1, t3;
@@ -766,14 +749,14 @@ int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
         memcpy(&buf[(2 * j + 1) * rb], r3 + j * rb, rb);
       }
       L.fused_gu = true;
-      if ((rc = upload_stream(m.get(), t1, 2 * hid, dim, buf.data(), 2, &L.gu))) return rc;
+      if ((rc = upload_stream(m.get(), t1, 2 * hid, dim, buf.data(), &L.gu))) return rc;
     } else {
-      if ((rc = upload_stream(m.get(), t1, hid, dim, r1, 1, &L.w1)) ||
-          (rc = upload_stream(m.get(), t3, hid, dim, r3, 1, &L.w3)))
+      if ((rc = upload_stream(m.get(), t1, hid, dim, r1, &L.w1)) ||
+          (rc = upload_stream(m.get(), t3, hid, dim, r3, &L.w3)))
         return rc;
     }
     if ((rc = linear_raw(g, p + "ffn_down.weight", dim, hid, &ty, &raw)) ||
-        (rc = upload_stream(m.get(), ty, dim, hid, raw, 1, &L.w2)))
+        (rc = upload_stream(m.get(), ty, dim, hid, raw, &L.w2)))
       return rc;
     // gguf.rs:388-394: each bias optional
     const char* bn[3] = {"attn_q.bias", "attn_k.bias", "attn_v.bias"};
@@ -793,7 +776,7 @@ int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
     uint32_t ty;
     const uint8_t* raw;
     if ((rc = linear_raw(g, "output.weight", (size_t)c.vocab_size, dim, &ty, &raw)) ||
-        (rc = upload_stream(m.get(), ty, (size_t)c.vocab_size, dim, raw, 1, &m->head)))
+        (rc = upload_stream(m.get(), ty, (size_t)c.vocab_size, dim, raw, &m->head)))
       return rc;
   } else {
     // tied classifier over a packed table runs the quantized kernel (checkpoint.rs:246)
@@ -868,14 +851,12 @@ int prana_kv_create(prana_model* m, size_t positions, prana_kv** out) {
   }
   PRANA_CK(cudaMemset(kv->k, 0, per * 2));
   PRANA_CK(cudaMemset(kv->v, 0, per * 2));
-  // attention splits for this capacity: >= 2 CTAs per SM at full length
-  const int by_len = (int)((positions + 31) / 32);
-  const int by_sm = (int)((2 * m->ctx->sm_count + c.n_kv_heads - 1) / c.n_kv_heads);
-  kv->n_splits = std::max(1, std::min(by_len, by_sm));
+  // attention splits for this capacity (the decode graph keeps them as the cache fills)
+  kv->n_splits = attn_splits((int)positions, (int)c.n_kv_heads, (int)c.head_dim, m->ctx->sm_count);
   const int group = (int)(c.n_heads / c.n_kv_heads);
   const int rows_cta = std::max(1, 4096 / (int)(c.head_dim * group));
   const size_t vh = (size_t)rows_cta * group;  // largest row chunk one attention CTA takes
-  const size_t ml = (size_t)c.n_kv_heads * kv->n_splits * vh * 2;
+  const size_t ml = ((size_t)c.n_kv_heads * kv->n_splits * vh * 2 + 3) / 4 * 4;  // part_o 16-byte aligned
   const size_t po = (size_t)c.n_kv_heads * kv->n_splits * vh * c.head_dim;
   PRANA_CK(cudaMalloc(&kv->part_ml, (ml + po) * 4));
   kv->part_o = kv->part_ml + ml;

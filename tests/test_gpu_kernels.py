@@ -168,8 +168,10 @@ def _cache(seed, rows, kv_dim):
     return np.array([[0]], np.uint16) if rows == 0 else f.astype(np.float16).view(np.uint16)
 
 
+# tensor-core path: hd 64/128 with <= 16 query heads per kv head; CUDA-core path otherwise
 @pytest.mark.parametrize("nh,nkv,hd,pos", [(6, 6, 48, 0), (6, 6, 48, 255), (14, 2, 64, 2047), (32, 8, 128, 700),
-                                           (12, 2, 128, 1023)])
+                                           (12, 2, 128, 1023), (32, 8, 128, 4095), (8, 1, 64, 5), (4, 4, 64, 16),
+                                           (4, 4, 64, 129), (64, 2, 128, 300), (16, 16, 32, 77)])
 def test_attention_decode(gpu, oracle, nh, nkv, hd, pos):
     kc = _cache(1, pos + 1, nkv * hd)
     vc = _cache(2, pos + 1, nkv * hd)
@@ -180,9 +182,10 @@ def test_attention_decode(gpu, oracle, nh, nkv, hd, pos):
     assert rel(got, ref) < 2e-5
 
 
-@pytest.mark.parametrize("nh,nkv,hd", [(6, 6, 48), (14, 2, 64), (12, 2, 128)])
-def test_attention_verify(gpu, oracle, nh, nkv, hd):
-    pos0, seq = 300, 5
+@pytest.mark.parametrize("nh,nkv,hd,seq", [(6, 6, 48, 5), (14, 2, 64, 5), (12, 2, 128, 5), (32, 8, 128, 8),
+                                           (8, 1, 64, 3)])
+def test_attention_verify(gpu, oracle, nh, nkv, hd, seq):
+    pos0 = 300
     kc = _cache(4, pos0 + seq, nkv * hd)
     vc = _cache(5, pos0 + seq, nkv * hd)
     q = np.random.default_rng(6).standard_normal((seq, nh * hd)).astype(np.float32)
