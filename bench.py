@@ -203,14 +203,14 @@ def reference_arm(args):
 
 
 def gemv_roofline(torch, peak_gbs, iters=64):
-    """Q4_0 GEMV [14336 x 4096] at batch 1 (the FFN gate/up/down shape family)."""
+    """Q4_0 GEMV [28672 x 4096] at batch 1: the shape of the fused gate|up weight, the step's largest GEMV."""
     from prana_b200 import kernels as K
     from prana_b200 import synth
     from prana_b200._ffi import TYPE_Q4_0
 
-    rows, cols = 14336, 4096
+    rows, cols = 28672, 4096
     raw = synth.matrix(TYPE_Q4_0, rows, cols, seed=77)
-    copies = [K.QuantMatrix(TYPE_Q4_0, rows, cols, raw) for _ in range(8)]  # 8 x 33 MB > 2 x L2
+    copies = [K.QuantMatrix(TYPE_Q4_0, rows, cols, raw) for _ in range(6)]  # 6 x 66 MB > 3 x L2
     acts = K.quantize_acts(torch.randn(1, cols, device="cuda"))  # int8 rows, as a decode step feeds them
     side = torch.cuda.Stream()
     with torch.cuda.stream(side):
@@ -234,7 +234,7 @@ def gemv_roofline(torch, peak_gbs, iters=64):
     alg = rows * cols // 32 * 18 + cols * 4 + rows * 4  # GGUF weight bytes + f32 in + f32 out
     gbs = alg / (us * 1e-6) / 1e9
     return {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak_gbs, "unit": "GB/s",
-            "frac": round(gbs / peak_gbs, 4), "traffic": None, "kernel": "gemv Q4_0 [14336 x 4096] M=1",
+            "frac": round(gbs / peak_gbs, 4), "traffic": None, "kernel": "stream_gemv Q4_0 [28672 x 4096] M=1",
             "us_per_launch": round(us, 2), "algorithmic_bytes": alg}
 
 

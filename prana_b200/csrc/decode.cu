@@ -165,7 +165,7 @@ __device__ __forceinline__ void prefetch_group(const DevWeight& w, int r0, int u
 // ---------------------------------------------------------------- the kernel
 
 template <int T, int M, int EPI, int PRO>
-__global__ void __launch_bounds__(DG_THREADS) stream_gemv(const StreamArgs g) {
+__global__ void __launch_bounds__(DG_THREADS, 2) stream_gemv(const StreamArgs g) {
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int CH = chunk_units<T>();
   const DevWeight& w = g.w;
@@ -204,22 +204,28 @@ __global__ void __launch_bounds__(DG_THREADS) stream_gemv(const StreamArgs g) {
   }
 
   Unit<T> buf[DG_RPW][CH];
-  auto load = [&](int r0, int c0) {
+  auto load_into = [&](Unit<T>(&b)[DG_RPW][CH], int r0, int c0) {
 #pragma unroll
     for (int r = 0; r < DG_RPW; r++) {
       const int row = min(r0 + r, N - 1);
 #pragma unroll
       for (int j = 0; j < CH; j++) {
         const int u = c0 + lane + 32 * j;
-        if (u < u_hi) buf[r][j] = load_unit<T>(w, row, u);
+        if (u < u_hi) b[r][j] = load_unit<T>(w, row, u);
       }
     }
   };
+  auto load = [&](int r0, int c0) { load_into(buf, r0, c0); };
 
+  // Row groups: with whole rows per warp (ks == 1) the groups are dealt to the
+  // warps of all CTAs in turn (group (k * 8 + warp) * grid + cta), so every SM
+  // streams the same share of rows; with K split, CTA tiles of gpc groups.
+  const int gstride = DG_WARPS * (int)gridDim.x;
+  const int g_first = ks == 1 ? wi * (int)gridDim.x + (int)blockIdx.x : (int)blockIdx.x * gpc + gs;
   // weights first: they do not depend on the previous kernel
   int t = blockIdx.x;
-  if (t < n_tiles && t * gpc + gs < n_groups) {
-    const int r0 = (t * gpc + gs) * DG_RPW;
+  if ((ks == 1 || t < n_tiles) && g_first < n_groups) {
+    const int r0 = g_first * DG_RPW;
     if (lane < DG_RPW * 4 && u_hi - u_lo > 32 * CH) prefetch_group<T>(w, r0, u_lo + 32 * CH, u_hi, lane);
     load(r0, u_lo);
   }
@@ -263,15 +269,75 @@ __global__ void __launch_bounds__(DG_THREADS) stream_gemv(const StreamArgs g) {
   float run_v = -INFINITY;
   int run_i = INT_MAX;
   bool first = true;
-  for (; t < n_tiles; t += gridDim.x) {
-    const int grp = t * gpc + gs;
+  // Batch 1 with whole rows per warp: a flat sequence of (row group, chunk)
+  // items with the next item's weights in flight while the current one computes.
+  constexpr bool kPipe = M == 1 && (T == T_Q4_0 || T == T_Q8_0);
+  if (kPipe && ks == 1) {
+    Unit<T> nb[DG_RPW][CH];
+    int c0 = u_lo, gcur = g_first;
+    bool have = gcur < n_groups;
+    float accv[DG_RPW];
+#pragma unroll
+    for (int r = 0; r < DG_RPW; r++) accv[r] = 0.0f;
+    auto step = [&](Unit<T>(&cur)[DG_RPW][CH], Unit<T>(&nxt)[DG_RPW][CH]) {
+      int ng = gcur, nc = c0 + 32 * CH;
+      if (nc >= u_hi) {
+        nc = u_lo;
+        ng = gcur + gstride;
+      }
+      const bool nhave = ng < n_groups;
+      if (nhave) {
+        load_into(nxt, ng * DG_RPW, nc);
+        // the group after that toward L2 when a new group starts
+        const int pg = ng + gstride;
+        if (nc == u_lo && lane < DG_RPW * 4 && pg < n_groups) prefetch_group<T>(w, pg * DG_RPW, u_lo, u_hi, lane);
+      }
+#pragma unroll
+      for (int j = 0; j < CH; j++) {
+        const int u = c0 + lane + 32 * j;
+        if (u < u_hi) {
+          const ActU<T> au = load_act<T>(a, u);
+#pragma unroll
+          for (int r = 0; r < DG_RPW; r++) accum_r(cur[r][j], au, u, accv[r]);
+        }
+      }
+      if (c0 + 32 * CH >= u_hi) {  // last chunk of the group: finish its rows
+        float v[DG_RPW];
+#pragma unroll
+        for (int r = 0; r < DG_RPW; r++) {
+          v[r] = warp_sum(accv[r]);
+          accv[r] = 0.0f;
+        }
+        if (lane == 0) finish_rows<EPI>(g, gcur * DG_RPW, 0, v, run_v, run_i);
+      }
+      gcur = ng;
+      c0 = nc;
+      have = nhave;
+    };
+    while (have) {
+      step(buf, nb);
+      if (!have) break;
+      step(nb, buf);
+    }
+  }
+  for (int it = 0; !(kPipe && ks == 1); it++) {
+    // ks == 1: this warp's it-th group (warps leave independently); ks > 1: the
+    // CTA's it-th tile, every warp stays for the tile's barriers
+    int grp, nxt;
+    if (ks == 1) {
+      grp = g_first + it * gstride;
+      if (grp >= n_groups) break;
+      nxt = grp + gstride;
+    } else {
+      t = blockIdx.x + it * gridDim.x;
+      if (t >= n_tiles) break;
+      grp = t * gpc + gs;
+      nxt = t + (int)gridDim.x < n_tiles ? (t + gridDim.x) * gpc + gs : n_groups;
+    }
     const bool live = grp < n_groups;
     const int r0 = grp * DG_RPW;
-    // the next tile's rows toward L2 while this one computes
-    if (lane < DG_RPW * 4) {
-      const int nt = t + gridDim.x;
-      if (nt < n_tiles && nt * gpc + gs < n_groups) prefetch_group<T>(w, (nt * gpc + gs) * DG_RPW, u_lo, u_hi, lane);
-    }
+    // the next group's rows toward L2 while this one computes
+    if (lane < DG_RPW * 4 && nxt < n_groups) prefetch_group<T>(w, nxt * DG_RPW, u_lo, u_hi, lane);
     float acc[DG_RPW][M];
 #pragma unroll
     for (int r = 0; r < DG_RPW; r++)
@@ -281,13 +347,25 @@ __global__ void __launch_bounds__(DG_THREADS) stream_gemv(const StreamArgs g) {
       for (int c0 = u_lo; c0 < u_hi; c0 += 32 * CH) {
         if (!first) load(r0, c0);
         first = false;
-#pragma unroll
-        for (int r = 0; r < DG_RPW; r++)
+        if constexpr (M == 1) {  // activations once per chunk, reused by every row
 #pragma unroll
           for (int j = 0; j < CH; j++) {
             const int u = c0 + lane + 32 * j;
-            if (u < u_hi) accum_unit<M>(buf[r][j], u, a, g.m, acc[r]);
+            if (u < u_hi) {
+              const ActU<T> au = load_act<T>(a, u);
+#pragma unroll
+              for (int r = 0; r < DG_RPW; r++) accum_r(buf[r][j], au, u, acc[r][0]);
+            }
           }
+        } else {
+#pragma unroll
+          for (int r = 0; r < DG_RPW; r++)
+#pragma unroll
+            for (int j = 0; j < CH; j++) {
+              const int u = c0 + lane + 32 * j;
+              if (u < u_hi) accum_unit<M>(buf[r][j], u, a, g.m, acc[r]);
+            }
+        }
       }
     }
     first = false;
@@ -432,9 +510,11 @@ static cudaError_t stream_go(const StreamArgs& g, cudaStream_t st, bool pdl) {
   }
   StreamArgs a = g;
   a.ks = gemv_split_k(T, g.K, g.N, sw_sm_count());
-  const int n_tiles = ceil_div(ceil_div(g.N, DG_RPW), DG_WARPS / a.ks);
+  const int n_groups = ceil_div(g.N, DG_RPW);
+  const int n_tiles = ceil_div(n_groups, DG_WARPS / a.ks);
   int grid = sw_sm_count() * resident_ctas((const void*)k, smem);
-  if (grid > n_tiles) grid = n_tiles;
+  // K split: one CTA per tile at most; whole rows: every resident CTA takes a share
+  if (grid > (a.ks == 1 ? n_groups : n_tiles)) grid = a.ks == 1 ? n_groups : n_tiles;
   if (EPI == EPI_ARGMAX && (g.n_parts < grid || g.counter == nullptr)) return cudaErrorInvalidValue;
   void* args[] = {&a};
   cudaLaunchConfig_t cfg = {};

@@ -245,6 +245,123 @@ __device__ __forceinline__ void accum_unit(const Unit<T_Q6_K>& x, int u, const A
     }
 }
 
+// ---- one activation row held in registers (the batch-1 decode path) ----
+// A lane loads the activation data of its unit once per chunk and reuses it
+// for every weight row the warp streams; the arithmetic is accum_unit's with
+// a single activation row, operation for operation.
+template <int T> struct ActU;
+template <> struct ActU<T_Q8_0> { int4 a0, a1; float s; };
+template <> struct ActU<T_Q4_0> { int4 a0, a1; float s; int sum8; };
+template <> struct ActU<T_Q4_K> { int4 l0, l1, h0, h1; float s1, s2; int sum1, sum2; };
+template <> struct ActU<T_Q6_K> { int4 a[4]; float s[4]; };
+
+template <int T> __device__ __forceinline__ ActU<T> load_act(const Acts& a, int u);
+template <> __device__ __forceinline__ ActU<T_Q8_0> load_act<T_Q8_0>(const Acts& a, int u) {
+  ActU<T_Q8_0> r;
+  r.a0 = *reinterpret_cast<const int4*>(a.q + u * 32);
+  r.a1 = *reinterpret_cast<const int4*>(a.q + u * 32 + 16);
+  r.s = a.s[u];
+  return r;
+}
+template <> __device__ __forceinline__ ActU<T_Q4_0> load_act<T_Q4_0>(const Acts& a, int u) {
+  ActU<T_Q4_0> r;
+  r.a0 = *reinterpret_cast<const int4*>(a.q + u * 32);
+  r.a1 = *reinterpret_cast<const int4*>(a.q + u * 32 + 16);
+  r.s = a.s[u];
+  r.sum8 = 8 * a.sum[u];
+  return r;
+}
+template <> __device__ __forceinline__ ActU<T_Q4_K> load_act<T_Q4_K>(const Acts& a, int u) {
+  ActU<T_Q4_K> r;
+  const int g_lo = (u >> 2) * 8 + 2 * (u & 3);
+  const int8_t* q = a.q + g_lo * 32;
+  r.l0 = *reinterpret_cast<const int4*>(q);
+  r.l1 = *reinterpret_cast<const int4*>(q + 16);
+  r.h0 = *reinterpret_cast<const int4*>(q + 32);
+  r.h1 = *reinterpret_cast<const int4*>(q + 48);
+  r.s1 = a.s[g_lo];
+  r.s2 = a.s[g_lo + 1];
+  r.sum1 = a.sum[g_lo];
+  r.sum2 = a.sum[g_lo + 1];
+  return r;
+}
+template <> __device__ __forceinline__ ActU<T_Q6_K> load_act<T_Q6_K>(const Acts& a, int u) {
+  ActU<T_Q6_K> r;
+  const int b = u >> 2, h = (u >> 1) & 1, half16 = u & 1;
+  const int8_t* q = a.q + b * 256 + h * 128 + half16 * 16;
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    r.a[g] = *reinterpret_cast<const int4*>(q + g * 32);
+    r.s[g] = a.s[b * 8 + h * 4 + g];
+  }
+  return r;
+}
+
+__device__ __forceinline__ void accum_r(const Unit<T_Q8_0>& x, const ActU<T_Q8_0>& a, int, float& acc) {
+  int s = dp4(x.a.x, a.a0.x, 0);
+  s = dp4(x.a.y, a.a0.y, s); s = dp4(x.a.z, a.a0.z, s); s = dp4(x.a.w, a.a0.w, s);
+  s = dp4(x.b.x, a.a1.x, s); s = dp4(x.b.y, a.a1.y, s); s = dp4(x.b.z, a.a1.z, s); s = dp4(x.b.w, a.a1.w, s);
+  acc = fmaf(__fmul_rn(h2f(x.d), a.s), (float)s, acc);
+}
+__device__ __forceinline__ void accum_r(const Unit<T_Q4_0>& x, const ActU<T_Q4_0>& a, int, float& acc) {
+  const unsigned m = 0x0F0F0F0Fu;
+  int s = dp4(x.q.x & m, a.a0.x, 0);
+  s = dp4(x.q.y & m, a.a0.y, s); s = dp4(x.q.z & m, a.a0.z, s); s = dp4(x.q.w & m, a.a0.w, s);
+  s = dp4((x.q.x >> 4) & m, a.a1.x, s); s = dp4((x.q.y >> 4) & m, a.a1.y, s);
+  s = dp4((x.q.z >> 4) & m, a.a1.z, s); s = dp4((x.q.w >> 4) & m, a.a1.w, s);
+  acc = fmaf(__fmul_rn(h2f(x.d), a.s), (float)(s - a.sum8), acc);
+}
+__device__ __forceinline__ void accum_r(const Unit<T_Q4_K>& x, const ActU<T_Q4_K>& a, int u, float& acc) {
+  const float d = h2f((unsigned short)(x.meta.x & 0xffffu)), dmin = h2f((unsigned short)(x.meta.x >> 16));
+  uint8_t sb[12];
+  *reinterpret_cast<unsigned*>(sb) = x.meta.y;
+  *reinterpret_cast<unsigned*>(sb + 4) = x.meta.z;
+  *reinterpret_cast<unsigned*>(sb + 8) = x.meta.w;
+  const int p = u & 3;
+  int sc1, m1, sc2, m2;
+  q4k_scale_min(2 * p, sb, sc1, m1);
+  q4k_scale_min(2 * p + 1, sb, sc2, m2);
+  const float dsc1 = __fmul_rn(d, (float)sc1), dm1 = __fmul_rn(dmin, (float)m1);
+  const float dsc2 = __fmul_rn(d, (float)sc2), dm2 = __fmul_rn(dmin, (float)m2);
+  const unsigned m = 0x0F0F0F0Fu;
+  int s1 = dp4(x.a.x & m, a.l0.x, 0);
+  s1 = dp4(x.a.y & m, a.l0.y, s1); s1 = dp4(x.a.z & m, a.l0.z, s1); s1 = dp4(x.a.w & m, a.l0.w, s1);
+  s1 = dp4(x.b.x & m, a.l1.x, s1); s1 = dp4(x.b.y & m, a.l1.y, s1); s1 = dp4(x.b.z & m, a.l1.z, s1);
+  s1 = dp4(x.b.w & m, a.l1.w, s1);
+  int s2 = dp4((x.a.x >> 4) & m, a.h0.x, 0);
+  s2 = dp4((x.a.y >> 4) & m, a.h0.y, s2); s2 = dp4((x.a.z >> 4) & m, a.h0.z, s2); s2 = dp4((x.a.w >> 4) & m, a.h0.w, s2);
+  s2 = dp4((x.b.x >> 4) & m, a.h1.x, s2); s2 = dp4((x.b.y >> 4) & m, a.h1.y, s2);
+  s2 = dp4((x.b.z >> 4) & m, a.h1.z, s2); s2 = dp4((x.b.w >> 4) & m, a.h1.w, s2);
+  const float t1 = __fsub_rn(__fmul_rn(dsc1, (float)s1), __fmul_rn(dm1, (float)a.sum1));
+  const float t2 = __fsub_rn(__fmul_rn(dsc2, (float)s2), __fmul_rn(dm2, (float)a.sum2));
+  acc = fmaf(a.s1, t1, acc);
+  acc = fmaf(a.s2, t2, acc);
+}
+__device__ __forceinline__ void accum_r(const Unit<T_Q6_K>& x, const ActU<T_Q6_K>& a, int u, float& acc) {
+  const float d = h2f(x.d);
+  const int half16 = u & 1;
+  const unsigned lo[4] = {x.lo.x, x.lo.y, x.lo.z, x.lo.w}, hi[4] = {x.hi.x, x.hi.y, x.hi.z, x.hi.w},
+                 qh[4] = {x.qh.x, x.qh.y, x.qh.z, x.qh.w};
+  int s[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    unsigned q[4];
+    q6_words(lo[k], hi[k], qh[k], q);
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+      const int aw = k == 0 ? a.a[g].x : (k == 1 ? a.a[g].y : (k == 2 ? a.a[g].z : a.a[g].w));
+      s[g] = dp4(q[g], aw, s[g]);
+    }
+  }
+  // sub-block scales of this quarter: int8 at byte 2g + half16 of x.sc
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    const unsigned word = g < 2 ? x.sc.x : x.sc.y;
+    const int sc = (int)(int8_t)((word >> (8 * ((g * 2 + half16) & 3))) & 0xffu);
+    acc = fmaf(__fmul_rn(__fmul_rn(d, a.s[g]), (float)sc), (float)s[g], acc);
+  }
+}
+
 // Warp computes NR rows (rows[r] < 0 = idle) x up to M activation rows.
 // UNR units per lane are loaded before any is consumed, so NR*UNR 128-bit
 // loads per lane are in flight.

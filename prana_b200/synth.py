@@ -120,6 +120,9 @@ QWEN2_0P5B_MIX = ModelSpec("qwen2", 896, 4864, 24, 14, 2, 64, 151936, 4096, 1e6,
 # C4: Llama-3-8B shape (Q4_0 and Q8_0 variants)
 LLAMA3_8B_Q4_0 = ModelSpec("llama", 4096, 14336, 32, 32, 8, 128, 128256, 8192, 5e5, 1e-5).with_types(TYPE_Q4_0)
 LLAMA3_8B_Q8_0 = LLAMA3_8B_Q4_0.with_types(TYPE_Q8_0)
+# Profiling case: the 8B layer shapes with 4 layers (~0.8 GB of weights, still
+# far larger than L2), for captures that must hold little device memory.
+LLAMA3_8B_Q4_0_L4 = replace(LLAMA3_8B_Q4_0, n_layers=4)
 
 # C5: Qwen2 shapes for speculative decode (Q8_0)
 QWEN2_0P5B_Q8 = replace(QWEN2_0P5B_MIX.with_types(TYPE_Q8_0), ctx=4096)
@@ -130,6 +133,7 @@ PRESETS = {
     "qwen2_0p5b_mix": QWEN2_0P5B_MIX,
     "llama3_8b_q4_0": LLAMA3_8B_Q4_0,
     "llama3_8b_q8_0": LLAMA3_8B_Q8_0,
+    "llama3_8b_q4_0_l4": LLAMA3_8B_Q4_0_L4,
     "qwen2_0p5b_q8_0": QWEN2_0P5B_Q8,
     "qwen2_1p5b_q8_0": QWEN2_1P5B_Q8,
 }
