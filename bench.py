@@ -202,6 +202,13 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+# DRAM bytes (read + write) per launch of the roofline kernel, from one ncu --set full
+# capture of this same launch (mean of launches 1 and 2: 66.91 and 66.62 MB); the
+# command and the figures are in profiles/stream_gemv_q4_0_llama3_8b.txt.
+ROOFLINE_TRAFFIC = 66_764_000
+ROOFLINE_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/stream_gemv_q4_0_llama3_8b.txt"
+
+
 def gemv_roofline(torch, peak_gbs, iters=64):
     """Q4_0 GEMV [28672 x 4096] at batch 1: the shape of the fused gate|up weight, the step's largest GEMV."""
     from prana_b200 import kernels as K
@@ -234,7 +241,8 @@ def gemv_roofline(torch, peak_gbs, iters=64):
     alg = rows * cols // 32 * 18 + cols * 4 + rows * 4  # GGUF weight bytes + f32 in + f32 out
     gbs = alg / (us * 1e-6) / 1e9
     return {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak_gbs, "unit": "GB/s",
-            "frac": round(gbs / peak_gbs, 4), "traffic": None, "kernel": "stream_gemv Q4_0 [28672 x 4096] M=1",
+            "frac": round(gbs / peak_gbs, 4), "traffic": ROOFLINE_TRAFFIC, "traffic_source": ROOFLINE_TRAFFIC_SOURCE,
+            "kernel": "stream_gemv Q4_0 [28672 x 4096] M=1",
             "us_per_launch": round(us, 2), "algorithmic_bytes": alg}
 
 
