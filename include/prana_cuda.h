@@ -110,6 +110,21 @@ int prana_f16_kv_write(prana_ctx *ctx, uint16_t *cache, size_t first_row, size_t
 /* attention_decode (attention.rs:129-160) */
 int prana_attention_decode(prana_ctx *ctx, const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
                            size_t pos, size_t n_heads, size_t n_kv_heads, size_t head_dim, float *out);
+/* attention_decode without allocation.  No counterpart in the reference: it
+ * is for callers that cannot allocate device memory on the call path (a host
+ * that reserved all device memory for its own pool, a loop that must never
+ * block on cudaMalloc/cudaFree).  Same kernels and results as
+ * prana_attention_decode, but the split partials live in a fixed 4 MiB static
+ * device array (1,048,576 floats; at most 1024 kv heads); a shape that needs
+ * more returns PRANA_E_INVALID and names the limit.  It never allocates.
+ * The first call on a device looks up the array's address (set-up); make that
+ * first call before any stream capture.  The array is shared by every context
+ * of the process on that device: calls that overlap in time (other streams,
+ * other threads) race on it and must be serialized by the caller.  Its ticket
+ * counters must be zero between calls; they start at zero and every call
+ * leaves them at zero. */
+int prana_attention_decode_noalloc(prana_ctx *ctx, const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                                   size_t pos, size_t n_heads, size_t n_kv_heads, size_t head_dim, float *out);
 /* attention_verify (attention.rs:296-333) */
 int prana_attention_verify(prana_ctx *ctx, const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
                            size_t pos0, size_t seq, size_t n_heads, size_t n_kv_heads, size_t head_dim,

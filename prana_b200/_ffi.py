@@ -70,6 +70,7 @@ SIGNATURES = {
     "prana_rope_neox": [P, P, SZ, SZ, SZ, SZ, C.c_float],
     "prana_f16_kv_write": [P, P, SZ, SZ, P, SZ],
     "prana_attention_decode": [P, P, P, P, SZ, SZ, SZ, SZ, P],
+    "prana_attention_decode_noalloc": [P, P, P, P, SZ, SZ, SZ, SZ, P],
     "prana_attention_verify": [P, P, P, P, SZ, SZ, SZ, SZ, SZ, P],
     "prana_attention": [P, P, P, P, SZ, SZ, SZ, SZ, P],
     "prana_argmax": [P, P, SZ, SZ, P],

@@ -19,7 +19,7 @@ CSRC = PKG / "csrc"
 LIB = PKG / "_lib"
 ROOT = PKG.parent
 
-CUDA_SOURCES = ["kernels.cu", "attention.cu", "decode.cu", "ctx.cu", "model.cu"]
+CUDA_SOURCES = ["kernels.cu", "attention.cu", "decode.cu", "ctx.cu", "model.cu", "noalloc.cu"]
 CUDA_HEADERS = ["common.cuh", "gemv.cuh", "finish.cuh", "mbar.cuh", "internal.h", "host.h"]
 NVCC_FLAGS = [
     "-O3",

@@ -228,6 +228,21 @@ def attention_decode(q, k_cache, v_cache, pos, n_heads, n_kv_heads, head_dim) ->
     return out
 
 
+def attention_decode_noalloc(q, k_cache, v_cache, pos, n_heads, n_kv_heads, head_dim, out=None) -> torch.Tensor:
+    """attention_decode on the library's static split scratch: the call itself
+    allocates no device memory (pass `out` to avoid the output allocation too).
+    Calls that overlap in time share that scratch and must be serialized."""
+    if n_kv_heads <= 0 or n_heads % n_kv_heads:
+        raise ValueError("n_heads must be a multiple of n_kv_heads")
+    if k_cache.numel() < (pos + 1) * n_kv_heads * head_dim:
+        raise ValueError("k_cache not filled to pos")
+    if out is None:
+        out = torch.empty(n_heads * head_dim, dtype=torch.float32, device=q.device)
+    call("prana_attention_decode_noalloc", context(q.device.index), _ptr(q), _ptr(k_cache), _ptr(v_cache), pos,
+         n_heads, n_kv_heads, head_dim, _ptr(out))
+    return out
+
+
 def attention_verify(q, k_cache, v_cache, pos0, seq, n_heads, n_kv_heads, head_dim) -> torch.Tensor:
     """attention_verify (attention.rs:296-333): seq query rows at pos0.."""
     if k_cache.numel() < (pos0 + seq) * n_kv_heads * head_dim:
