@@ -12,9 +12,16 @@
 // per (query-row chunk, kv head), no split.
 #include <climits>
 
+#include <cooperative_groups.h>
+
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 #include "internal.h"
+#include "mbar.cuh"
 
 namespace prana {
 
@@ -802,6 +809,289 @@ __global__ void __launch_bounds__(256) attn_decode_mma(const AttnArgs a, int row
   attn_finish<HD>(a, kvh, split, row0, VH, group, o_s, m_run, l_run, smem_raw, red);
 }
 
+// ---------------------------------------------------------------- cluster decode (head_dim 64 / 128)
+//
+// The C (<= 16) splits of a kv head form one thread-block cluster.  Each CTA
+// streams its ~1/C of the positions through two shared-memory stages of AC_C
+// rows.  A stage is filled by tensor-map (TMA) copies of 64-dim x 128-position
+// boxes of K and V, 128-byte swizzled so the ldmatrix reads below hit every
+// bank once; boxes that hold only rows of earlier steps are requested before
+// the programmatic-launch wait.  Each pass runs the tensor-core QK^T / online
+// softmax / P.V of attn_decode_mma; the 8 warps then merge, and the splits
+// meet through distributed shared memory: after a cluster barrier, CTA r
+// combines its share of the head's outputs from all C CTAs' (max, sum, o).
+// No global scratch, atomics or fences; a second cluster barrier keeps every
+// CTA's shared memory alive until the others have read it.
+constexpr int AC_MAX = 16;  // largest cluster (splits per kv head)
+constexpr int AC_C = 128;   // positions per pass (8 warps x 16)
+constexpr int AC_BOX = 64;  // dims per TMA box: 64 halves = one 128-byte swizzle line
+
+template <int HD>
+struct AcSmem {
+  static constexpr int NB = HD / AC_BOX;                             // boxes per row of K (or V)
+  static constexpr size_t BOX = (size_t)AC_C * AC_BOX * 2;            // 16 KB
+  static constexpr size_t STAGE = 2 * NB * BOX;                       // K and V
+  static constexpr int QROW = HD + 8;                                 // padded q tile rows (halves)
+  static constexpr size_t Q = 2 * sizeof(__half) * (size_t)AM_ROWS * QROW;
+  static constexpr size_t O = sizeof(float) * (size_t)AM_ROWS * HD;
+  static constexpr size_t ML = sizeof(float) * (4 * AM_ROWS + AM_ROWS * AC_MAX);
+  static constexpr size_t bytes = 1024 + 2 * STAGE + Q + O + ML + 16;  // + alignment slack
+  static_assert(sizeof(float) * 8 * AM_ROWS * (HD + 2) <= 2 * STAGE, "warp merge buffer (both stages)");
+};
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// byte offset of the 16-byte chunk `chunk` (of 8 halves) of position row r in a
+// 128-byte-swizzled box
+__device__ __forceinline__ int swz(int r, int chunk) { return r * 128 + ((chunk ^ (r & 7)) << 4); }
+
+template <int HD>
+__global__ void __launch_bounds__(256, 1) attn_decode_cluster(const __grid_constant__ AttnArgs a, int row0, int n_rows) {
+  using S = AcSmem<HD>;
+  constexpr int NB = S::NB, QROW = S::QROW, KS = HD / 16, NT = HD / 8;
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  // stages start on 1024 bytes, as 128-byte swizzled TMA boxes require
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~(uintptr_t)1023);
+  uint8_t* stage0 = base;
+  __half* qh_s = reinterpret_cast<__half*>(base + 2 * S::STAGE);
+  __half* ql_s = qh_s + AM_ROWS * QROW;
+  float* o_s = reinterpret_cast<float*>(ql_s + AM_ROWS * QROW);
+  float* m_run = o_s + AM_ROWS * HD;
+  float* l_run = m_run + AM_ROWS;
+  float* l_tot = l_run + AM_ROWS;
+  float* w_s = l_tot + 2 * AM_ROWS;  // [AM_ROWS][AC_MAX]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(w_s + AM_ROWS * AC_MAX);
+  const int group = a.n_heads / a.n_kv, VH = n_rows * group;  // VH <= 16
+  const int C = (int)cluster.num_blocks(), split = (int)cluster.block_rank();
+  const int kvh = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, wi = tid >> 5;
+  const int g = lane >> 2, tig = lane & 3;
+  const int q_stride = a.n_heads * HD;
+  const float scale = 1.0f / sqrtf((float)HD);
+
+  // the position counter of a graph-driven step was advanced before the
+  // previous step's kernels finished, so it is safe to read before the wait
+  const int pos0 = a.pos_dev ? *a.pos_dev : a.pos0;
+  const int L = pos0 + row0 + n_rows;
+  int per = (L + C - 1) / C;
+  per = (per + 15) / 16 * 16;
+  const int t_begin = min(L, split * per), t_end = min(L, t_begin + per);
+  const int n_pass = (t_end - t_begin + AC_C - 1) / AC_C;
+
+  auto kbox = [&](int st, int b) { return stage0 + st * S::STAGE + b * S::BOX; };
+  auto vbox = [&](int st, int b) { return stage0 + st * S::STAGE + (NB + b) * S::BOX; };
+  // pass p -> stage p & 1: every box of K and V from position t_begin + p * AC_C
+  auto issue = [&](int p) {
+    const int st = p & 1, t0 = t_begin + p * AC_C;
+    mbar_arrive_expect_tx(&bars[st], (uint32_t)(2 * NB * S::BOX));
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+      tma_load_3d(kbox(st, b), &a.tm_k, b * AC_BOX, kvh, t0, &bars[st]);
+      tma_load_3d(vbox(st, b), &a.tm_v, b * AC_BOX, kvh, t0, &bars[st]);
+    }
+  };
+  // a pass holding only rows written by earlier steps may load before the wait
+  auto early = [&](int p) { return t_begin + p * AC_C + AC_C <= pos0; };
+
+  __shared__ int q_off[AM_ROWS];
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_barrier_init();
+    for (int p = 0; p < 2 && p < n_pass; p++)
+      if (early(p)) issue(p);
+  }
+  if (tid < AM_ROWS) q_off[tid] = tid < VH ? (row0 + tid / group) * q_stride + (kvh * group + tid % group) * HD : -1;
+  pdl_wait();
+  if (tid == 0)
+    for (int p = 0; p < 2 && p < n_pass; p++)
+      if (!early(p)) issue(p);
+  __syncthreads();
+  for (int i = tid; i < AM_ROWS * HD; i += 256) {
+    const int vh = i / HD, d = i - vh * HD;
+    const int off = q_off[vh];
+    const float x = off >= 0 ? a.q[off + d] : 0.0f;
+    const __half h = __float2half_rn(x);
+    qh_s[vh * QROW + d] = h;
+    ql_s[vh * QROW + d] = __float2half_rn(x - __half2float(h));
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  float m_w[2] = {-INFINITY, -INFINITY}, l_w[2] = {0.0f, 0.0f};
+  float o[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+  const int lr = lane & 7, lj = lane >> 3;
+  bool ok = true;
+  for (int p = 0; p < n_pass; p++) {
+    const int st = p & 1, t0 = t_begin + p * AC_C, n = min(AC_C, t_end - t0);
+    ok = mbar_wait(&bars[st], (p >> 1) & 1) && ok;
+    const int p0 = wi * 16;
+    if (p0 < n) {
+      float sc[2][4];
+#pragma unroll
+      for (int i = 0; i < 2; i++) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.0f;
+      const int kr = p0 + (lj >> 1) * 8 + lr;  // K row this lane addresses
+#pragma unroll
+      for (int ks = 0; ks < KS; ks++) {
+        uint32_t ah[4], al[4], kb[4];
+        const int qoff = ((lj & 1) * 8 + lr) * QROW + ks * 16 + (lj >> 1) * 8;
+        ldsm_x4(ah, qh_s + qoff);
+        ldsm_x4(al, ql_s + qoff);
+        const int c = ks * 2 + (lj & 1);  // 8-dim chunk along the head
+        ldsm_x4(kb, kbox(st, c / 8) + swz(kr, c % 8));
+        mma_f16(sc[0], ah, kb[0], kb[1]);
+        mma_f16(sc[0], al, kb[0], kb[1]);
+        mma_f16(sc[1], ah, kb[2], kb[3]);
+        mma_f16(sc[1], al, kb[2], kb[3]);
+      }
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) {
+          const int row = g + (cc >> 1) * 8, pp = p0 + nt * 8 + tig * 2 + (cc & 1);
+          const bool vis = row < VH && pp < n && t0 + pp <= pos0 + row0 + row / group;
+          sc[nt][cc] = vis ? __fmul_rn(sc[nt][cc], scale) : -INFINITY;
+          mx[cc >> 1] = fmaxf(mx[cc >> 1], sc[nt][cc]);
+        }
+      float alpha[2], sum[2] = {0.0f, 0.0f};
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+        const float m_new = fmaxf(m_w[h], mx[h]);
+        alpha[h] = (m_w[h] == -INFINITY) ? 0.0f : expf(m_w[h] - m_new);
+        m_w[h] = m_new;
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) {
+          const float sv = sc[nt][cc];
+          const float pr = (sv == -INFINITY) ? 0.0f : expf(sv - m_w[cc >> 1]);
+          sc[nt][cc] = pr;
+          sum[cc >> 1] += pr;
+        }
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 1);
+        sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 2);
+        l_w[h] = fmaf(l_w[h], alpha[h], sum[h]);
+      }
+#pragma unroll
+      for (int i = 0; i < NT; i++) {
+        o[i][0] *= alpha[0];
+        o[i][1] *= alpha[0];
+        o[i][2] *= alpha[1];
+        o[i][3] *= alpha[1];
+      }
+      uint32_t ph[4], pl[4];
+      split_pair(sc[0][0], sc[0][1], ph[0], pl[0]);
+      split_pair(sc[0][2], sc[0][3], ph[1], pl[1]);
+      split_pair(sc[1][0], sc[1][1], ph[2], pl[2]);
+      split_pair(sc[1][2], sc[1][3], ph[3], pl[3]);
+      const int vr = p0 + (lj & 1) * 8 + lr;  // V row this lane addresses
+#pragma unroll
+      for (int dt = 0; dt < NT; dt += 2) {
+        uint32_t vb[4];
+        const int c = dt + (lj >> 1);
+        ldsm_x4_t(vb, vbox(st, c / 8) + swz(vr, c % 8));
+        mma_f16(o[dt], ph, vb[0], vb[1]);
+        mma_f16(o[dt], pl, vb[0], vb[1]);
+        mma_f16(o[dt + 1], ph, vb[2], vb[3]);
+        mma_f16(o[dt + 1], pl, vb[2], vb[3]);
+      }
+    }
+    __syncthreads();  // the stage is free again
+    if (tid == 0 && p + 2 < n_pass) issue(p + 2);
+  }
+  if (!ok && tid == 0 && a.err) atomicExch(a.err, 1u);
+
+  // ---- this CTA's warps meet in the (now idle) stages: wm/wl [8][16], wo [8][VH][HD]
+  float* wm = reinterpret_cast<float*>(stage0);
+  float* wl = wm + 8 * AM_ROWS;
+  float* wo = wl + 8 * AM_ROWS;
+  if (tig == 0) {
+    wm[wi * AM_ROWS + g] = m_w[0];
+    wl[wi * AM_ROWS + g] = l_w[0];
+    wm[wi * AM_ROWS + g + 8] = m_w[1];
+    wl[wi * AM_ROWS + g + 8] = l_w[1];
+  }
+#pragma unroll
+  for (int i = 0; i < NT; i++) {
+    const int d = i * 8 + tig * 2;
+    if (g < VH) *reinterpret_cast<float2*>(wo + (wi * AM_ROWS + g) * HD + d) = make_float2(o[i][0], o[i][1]);
+    if (g + 8 < VH) *reinterpret_cast<float2*>(wo + (wi * AM_ROWS + g + 8) * HD + d) = make_float2(o[i][2], o[i][3]);
+  }
+  __syncthreads();
+  if (tid < VH) {
+    float mx = -INFINITY;
+    for (int w = 0; w < 8; w++) mx = fmaxf(mx, wm[w * AM_ROWS + tid]);
+    float l = 0.0f;
+    for (int w = 0; w < 8; w++) {
+      const float mw = wm[w * AM_ROWS + tid];
+      const float sw = mw == -INFINITY ? 0.0f : expf(mw - mx);
+      wm[w * AM_ROWS + tid] = sw;
+      l = fmaf(wl[w * AM_ROWS + tid], sw, l);
+    }
+    m_run[tid] = mx;
+    l_run[tid] = l;
+  }
+  __syncthreads();
+  for (int e = tid; e < VH * HD; e += 256) {
+    const int vh = e / HD;
+    float acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) acc = fmaf(wo[(w * AM_ROWS + vh) * HD + (e - vh * HD)], wm[w * AM_ROWS + vh], acc);
+    o_s[e] = acc;
+  }
+
+  // ---- the C splits meet through distributed shared memory
+  cluster.sync();
+  const int n_w = VH * AC_MAX;  // weight of split j for virtual head vh: 16 lanes per head
+  if (tid < ((n_w + 31) & ~31)) {  // whole warps, so every shuffle sees all its lanes
+    const int vh = tid / AC_MAX, j = tid % AC_MAX;
+    const bool act = tid < n_w && j < C;
+    float mj = -INFINITY, lj_ = 0.0f;
+    if (act) {
+      mj = *cluster.map_shared_rank(m_run + vh, j);
+      lj_ = *cluster.map_shared_rank(l_run + vh, j);
+    }
+    float mx = mj;
+#pragma unroll
+    for (int o_ = AC_MAX / 2; o_ > 0; o_ >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o_));
+    const float w = mj == -INFINITY ? 0.0f : expf(mj - mx);
+    float lw = w * lj_;
+#pragma unroll
+    for (int o_ = AC_MAX / 2; o_ > 0; o_ >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o_);
+    if (tid < n_w) {
+      w_s[vh * AC_MAX + j] = w;
+      if (j == 0) l_tot[vh] = lw;
+    }
+  }
+  __syncthreads();
+  const int E = VH * HD, chunk = (E + C - 1) / C;
+  const int e_end = min(E, (split + 1) * chunk);
+  for (int e = split * chunk + tid; e < e_end; e += 256) {
+    const int vh = e / HD, d = e - vh * HD;
+    float acc = 0.0f;
+    for (int j = 0; j < C; j++) acc = fmaf(*cluster.map_shared_rank(o_s + e, j), w_s[vh * AC_MAX + j], acc);
+    const int row = vh / group, head = kvh * group + vh % group;
+    a.out[(size_t)(row0 + row) * q_stride + head * HD + d] = acc / l_tot[vh];
+  }
+  cluster.sync();  // every CTA's shared memory stays alive until the others have read it
+}
+
 template <int HD, bool MMA>
 static cudaError_t decode_go(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const int group = a.n_heads / a.n_kv;
@@ -842,16 +1132,132 @@ static cudaError_t decode_go(const AttnArgs& a, cudaStream_t st, bool pdl) {
   return cudaSuccess;
 }
 
+// ---- tensor maps of the f16 cache (driver entry point, looked up once)
+using EncodeTiledFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// {hd, n_kv, positions} view of one layer's K or V cache; a box is 64 dims x
+// 1 head x 128 positions, 128-byte swizzled; rows past `positions` read as 0
+static bool encode_cache_map(CUtensorMap* m, const __half* base, int positions, int n_kv, int hd) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn || positions < 1 || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)n_kv, (cuuint64_t)positions};
+  const cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)n_kv * hd * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)AC_BOX, 1, (cuuint32_t)AC_C};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+void attn_make_maps(AttnArgs& a, int positions) {
+  a.has_tm = 0;
+  if (a.hd != 64 && a.hd != 128) return;
+  if (encode_cache_map(&a.tm_k, a.kc, positions, a.n_kv, a.hd) && encode_cache_map(&a.tm_v, a.vc, positions, a.n_kv, a.hd))
+    a.has_tm = 1;
+}
+
+// Cluster size for n_kv kv heads: the largest C <= 16 such that all n_kv
+// clusters of C CTAs are resident at once (asked once per device and n_kv);
+// 0 when none fits.
+template <int HD>
+static int cluster_size(int n_kv) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({dev, n_kv});
+  if (it != cache.end()) return it->second;
+  auto k = attn_decode_cluster<HD>;
+  int best = 0;
+  if (cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AcSmem<HD>::bytes) ==
+          cudaSuccess &&
+      cudaFuncSetAttribute((const void*)k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+    for (int c = AC_MAX; c >= 2 && !best; c -= 2) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(c, n_kv);
+      cfg.blockDim = dim3(256);
+      cfg.dynamicSmemBytes = AcSmem<HD>::bytes;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = c;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, (const void*)k, &cfg) == cudaSuccess && n >= n_kv) best = c;
+    }
+  }
+  cudaGetLastError();
+  cache[{dev, n_kv}] = best;
+  return best;
+}
+
+template <int HD>
+static cudaError_t cluster_go(const AttnArgs& a, int c, cudaStream_t st, bool pdl) {
+  const int group = a.n_heads / a.n_kv;
+  const int max_rows = AM_ROWS / group;
+  for (int row0 = 0; row0 < a.m; row0 += max_rows) {
+    const int n_rows = min(max_rows, a.m - row0);
+    void* args[] = {const_cast<AttnArgs*>(&a), (void*)&row0, (void*)&n_rows};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c, a.n_kv);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = AcSmem<HD>::bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = c;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    int na = 1;
+    if (pdl && row0 == 0) {
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
+      na = 2;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    cudaError_t e = cudaLaunchKernelExC(&cfg, (const void*)attn_decode_cluster<HD>, args);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   if (a.n_kv <= 0 || a.n_heads % a.n_kv || a.m < 1 || a.n_splits < 1) return cudaErrorInvalidValue;
-  // tensor-core path for the common head sizes while a kv head's query heads fit one MMA tile
+  // tensor cores for the common head sizes while a kv head's query heads fit one MMA tile;
+  // the cluster kernel (no global merge) when the cache has tensor maps and the clusters fit
   const bool mma = a.n_heads / a.n_kv <= AM_ROWS;
   switch (a.hd) {
     case 32: return decode_go<32, false>(a, st, pdl);
     case 48: return decode_go<48, false>(a, st, pdl);
-    case 64: return mma ? decode_go<64, true>(a, st, pdl) : decode_go<64, false>(a, st, pdl);
+    case 64: {
+      if (!mma) return decode_go<64, false>(a, st, pdl);
+      const int c = a.has_tm ? cluster_size<64>(a.n_kv) : 0;
+      return c ? cluster_go<64>(a, c, st, pdl) : decode_go<64, true>(a, st, pdl);
+    }
     case 96: return decode_go<96, false>(a, st, pdl);
-    case 128: return mma ? decode_go<128, true>(a, st, pdl) : decode_go<128, false>(a, st, pdl);
+    case 128: {
+      if (!mma) return decode_go<128, false>(a, st, pdl);
+      const int c = a.has_tm ? cluster_size<128>(a.n_kv) : 0;
+      return c ? cluster_go<128>(a, c, st, pdl) : decode_go<128, true>(a, st, pdl);
+    }
     case 256: return decode_go<256, false>(a, st, pdl);
   }
   return cudaErrorInvalidValue;

@@ -532,6 +532,8 @@ static int attn_common(prana_ctx* c, const float* q, const uint16_t* kc, const u
   a.part_o = static_cast<float*>(sp) + ml;
   a.counters = c->counters;
   a.out = out;
+  a.err = c->err;
+  attn_make_maps(a, (int)(pos0 + m));
   cudaError_t e = launch_attn_decode(a, c->stream, false);
   if (e == cudaErrorInvalidValue) return fail(PRANA_E_UNSUPPORTED, "attention: head_dim %zu not built", hd);
   PRANA_CK(e);

@@ -1,6 +1,7 @@
 // internal.h -- argument blocks and launcher entry points shared between the
 // kernel translation units and the host engine.  Not part of the public ABI.
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -42,6 +43,11 @@ struct GemvArgs {
 };
 
 struct AttnArgs {
+  // TMA views of this layer's K and V cache ({hd, n_kv, positions}, 128-byte
+  // swizzled boxes of 64 x 1 x 128); has_tm = 0 when they could not be made
+  CUtensorMap tm_k;
+  CUtensorMap tm_v;
+  int has_tm;
   const float* q;        // [m][n_heads*hd]
   const __half* kc;      // [positions][n_kv*hd]
   const __half* vc;
@@ -54,6 +60,7 @@ struct AttnArgs {
   float* part_o;         // [n_kv][n_splits][m*group][hd], 16-byte aligned
   unsigned* counters;    // [n_kv], zero between launches
   float* out;            // [m][n_heads*hd]
+  unsigned* err;         // device error flag for bounded waits (nullable)
 };
 
 struct PrefillAttnArgs {
@@ -137,6 +144,9 @@ cudaError_t launch_advance(int* tok, int* pos, uint32_t* ring, int ring_cap, int
 int attn_max_rows_per_cta(int hd);
 // attention splits for a cache of `positions` rows (scratch is sized by it)
 int attn_splits(int positions, int n_kv, int hd, int sm_count);
+// Fill a.tm_k / a.tm_v for caches of `positions` rows (a.kc, a.vc, a.n_kv,
+// a.hd set); leaves has_tm = 0 for head sizes the TMA kernel does not take.
+void attn_make_maps(AttnArgs& a, int positions);
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_attn_prefill(const PrefillAttnArgs& a, cudaStream_t st);
 

@@ -251,6 +251,7 @@ struct prana_kv {
   size_t positions = 0;
   __half* k = nullptr;
   __half* v = nullptr;
+  std::vector<prana::AttnArgs> maps;  // per layer: the K / V tensor maps (tm_k, tm_v, has_tm)
   int n_splits = 1;
   float* part_ml = nullptr;
   float* part_o = nullptr;
@@ -462,6 +463,12 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       a.part_o = kv->part_o;
       a.counters = kv->counters;
       a.out = b.att;
+      a.err = m->err;
+      if ((size_t)l < kv->maps.size()) {
+        a.tm_k = kv->maps[l].tm_k;
+        a.tm_v = kv->maps[l].tm_v;
+        a.has_tm = kv->maps[l].has_tm;
+      }
       PRANA_CK(launch_attn_decode(a, st, pdl));
     }
     // --- quantize(attn) -> wo -> residual
@@ -851,6 +858,16 @@ int prana_kv_create(prana_model* m, size_t positions, prana_kv** out) {
   }
   PRANA_CK(cudaMemset(kv->k, 0, per * 2));
   PRANA_CK(cudaMemset(kv->v, 0, per * 2));
+  // TMA views of every layer's K and V cache for the decode attention
+  kv->maps.resize(c.n_layers);
+  for (size_t l = 0; l < c.n_layers; l++) {
+    AttnArgs& t = kv->maps[l];
+    t.kc = kv->k + l * positions * kv_dim;
+    t.vc = kv->v + l * positions * kv_dim;
+    t.n_kv = (int)c.n_kv_heads;
+    t.hd = (int)c.head_dim;
+    attn_make_maps(t, (int)positions);
+  }
   // attention splits for this capacity (the decode graph keeps them as the cache fills)
   kv->n_splits = attn_splits((int)positions, (int)c.n_kv_heads, (int)c.head_dim, m->ctx->sm_count);
   const int group = (int)(c.n_heads / c.n_kv_heads);

@@ -94,6 +94,7 @@ extern "C" int prana_attention_decode_noalloc(prana_ctx* c, const float* q, cons
     a.part_o = slot->scratch + ml;
     a.counters = slot->counters;
     a.out = out;
+    attn_make_maps(a, (int)(pos + 1));
     const cudaError_t e = launch_attn_decode(a, c->stream, false);
     if (e == cudaErrorInvalidValue) return fail(PRANA_E_UNSUPPORTED, "attention: head_dim %zu not built", hd);
     PRANA_CK(e);
