@@ -10,8 +10,8 @@ token.  Weights stream from HBM every step (4.2 GB >> the 126 MB L2).
           replayed back to back, sampled id fed back on the device)
   e2e     tok/s through the C ABI per token: host token id in (H2D), sampled
           id out (D2H), prana_forward per step
-  roofline  the Q4_0 GEMV at the FFN shape [14336 x 4096], rotating weight
-          copies larger than L2, timed with CUDA events on its stream
+  roofline  the Q4_0 GEMV at the gate|up shape [28672 x 4096], rotating weight
+          copies larger than L2, timed in a CUDA graph with events on its stream
   cpu_baseline  the CPU oracle (C restatement of Prana's AVX2/VNNI path and
           worker pool) decoding the same model from the same KV contents
 
@@ -19,8 +19,10 @@ Both arms start from the same seeded KV contents (4096 rows of N(0, 0.5) f16
 per layer) instead of a 4096-token prefill, so the CPU arm finishes in minutes;
 the bytes a decode step reads are the same either way.
 
---gpus N > 1 (under torchrun): N independent replicas, one sequence per GPU
-(weak scaling); value is the sum of the per-rank tok/s.
+--gpus N > 1 (under torchrun): the model is tensor-parallel over the N GPUs
+(column-split Q/K/V and gate|up, row-split wo and ffn_down, vocabulary-split
+LM head; an NCCL all-reduce after wo and after ffn_down), one sequence, so the
+work per token is fixed (strong scaling); value is that sequence's tok/s.
 --impl reference: the CPU oracle alone on the host cores (rank 0).
 """
 from __future__ import annotations
@@ -85,12 +87,18 @@ def seeded_kv_rows(layer, is_v, rows, kv_dim, seed=4242):
     return (rng.standard_normal((rows, kv_dim), dtype=np.float32) * 0.5).astype(np.float16).view(np.uint16)
 
 
-def launches_per_step(spec) -> int:
+def launches_per_step(spec, world=1, peer=False) -> int:
+    """Kernels of this library per decode step (NCCL's own kernels not counted;
+    the peer-memory exchange adds 2 all-reduces per layer and the argmax
+    all-gather)."""
     types = [spec.type_q, spec.type_k, spec.type_v]
     qkv = 1 + sum(1 for i in range(1, 3) if types[i] != types[i - 1])
     swiglu = 1 if spec.type_gate == spec.type_up else 4
-    # embed + per layer (qkv, attention, wo, ffn, down) + lm head + advance
-    return 1 + spec.n_layers * (qkv + 1 + 1 + swiglu + 1) + 1 + 1
+    # embed + per layer (qkv, attention, wo, ffn, down) + lm head (+ the cross-rank argmax) + advance
+    n = 1 + spec.n_layers * (qkv + 1 + 1 + swiglu + 1) + 1 + (1 if world > 1 else 0) + 1
+    if world > 1 and peer:
+        n += 2 * spec.n_layers + 1
+    return n
 
 
 class Clocks:
@@ -263,19 +271,26 @@ def prana_arm(args):
     from prana_b200 import model as pm
 
     spec, path = model_path(args, rank)
+    tp = None
     if dist:
         dist.barrier()
+        # tensor parallel over the ranks: rank 0's NCCL id reaches every rank
+        uid = [pm.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        tp = (world, rank, uid[0])
     peak, peak_kind = peaks()
     t_load = time.perf_counter()
-    model = pm.Model.load(str(path), local)
+    model = pm.Model.load(str(path), local, tp=tp)
     t_load = time.perf_counter() - t_load
     c = model.config
     kv_dim = c.kv_dim()
+    kv_l = model.local_kv_dim()  # this rank's kv heads
     cap = args.ctx + 2 * (args.warmup + args.steps) + 16
     kv = pm.KvCache(model, cap)
     for layer in range(c.n_layers):
         for is_v in (False, True):
-            kv.write(layer, is_v, seeded_kv_rows(layer, is_v, args.ctx, kv_dim))
+            rows = seeded_kv_rows(layer, is_v, args.ctx, kv_dim)
+            kv.write(layer, is_v, rows[:, rank * kv_l:(rank + 1) * kv_l] if world > 1 else rows)
     stream = torch.cuda.ExternalStream(model.stream())
 
     def barrier():
@@ -330,19 +345,20 @@ def prana_arm(args):
         bytes_tok = spec.weight_bytes_per_token() + 2 * c.n_layers * (args.ctx + args.warmup + args.steps // 2) * kv_dim * 2
         step_gbs = bytes_tok * (1000.0 / ms) / 1e9
         line = {
-            "metric": METRIC, "value": round(world * 1000.0 / ms, 3), "unit": UNIT, "n_gpus": world,
+            "metric": METRIC, "value": round(1000.0 / ms, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 / f32 (Q4_0 weights, f16 KV)",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> int32 / f32 (Q4_0 weights, f16 KV)",
             "data": "synthetic", "impl": "prana",
             "config": {"workload": args.workload, "ctx": args.ctx, "batch": 1,
-                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "parallelism": f"tp{world}" if world > 1 else "single",
+                       "exchange": ("peer memory" if model.peer_exchange else "nccl") if world > 1 else None,
                        "l2": "inputs larger than L2 (4.2 GB weights per step)"},
-            "e2e": {"value": round(world * 1000.0 / ms_e2e, 3), "unit": UNIT, "h2d_bytes_per_step": 8,
+            "e2e": {"value": round(1000.0 / ms_e2e, 3), "unit": UNIT, "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4},
             "roofline": roof, "peak_kind": peak_kind,
             "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": round(step_gbs, 1),
                               "frac": round(step_gbs / peak, 4)},
-            "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches_per_step(spec) * args.steps,
+            "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches_per_step(spec, world, model.peer_exchange) * args.steps,
             "load_s": round(t_load, 1),
         }
         print(json.dumps(line), flush=True)

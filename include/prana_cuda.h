@@ -145,6 +145,21 @@ typedef struct prana_model_config {
 
 /* gguf::load (gguf.rs:338-460) for llama / qwen2 into the device arena */
 int prana_model_load_gguf(prana_ctx *ctx, const char *path, prana_model **out);
+/* Tensor parallelism over `world` GPUs, one process (or context) per rank
+ * (the Megatron-style split of the survey: column-split Q/K/V by heads and
+ * gate/up by FFN rows, row-split wo and ffn_down by input columns, vocabulary
+ * split LM head; one all-reduce after wo and one after ffn_down).  Rank 0 calls
+ * prana_tp_unique_id and hands the NCCL_UNIQUE_ID_BYTES (128) id to every
+ * rank, which loads its shard with prana_model_load_gguf_tp; from there every
+ * model-level call runs on all ranks together (same tokens, same order) and
+ * returns the full result on each.  KV caches hold the rank's kv heads
+ * (prana_kv_read/write move [rows, n_kv_heads / world * head_dim]). */
+int prana_tp_unique_id(void *id_out);
+int prana_model_load_gguf_tp(prana_ctx *ctx, const char *path, int world, int rank, const void *nccl_id,
+                             prana_model **out);
+/* peer_exchange (may be NULL): 1 when the decode-sized all-reduces and the argmax
+   all-gather run over mapped peer memory, 0 when NCCL carries every exchange */
+int prana_model_tp_get(const prana_model *m, int *world, int *rank, int *peer_exchange);
 int prana_model_free(prana_model *m); /* also frees the model's remaining KV caches */
 int prana_model_config_get(const prana_model *m, prana_model_config *out);
 /* KvCache::with_len (infer.rs:37-45): f16 K/V for `positions` rows per layer */

@@ -75,6 +75,9 @@ SIGNATURES = {
     "prana_attention": [P, P, P, P, SZ, SZ, SZ, SZ, P],
     "prana_argmax": [P, P, SZ, SZ, P],
     "prana_model_load_gguf": [P, C.c_char_p, C.POINTER(P)],
+    "prana_model_load_gguf_tp": [P, C.c_char_p, I, I, P, C.POINTER(P)],
+    "prana_tp_unique_id": [P],
+    "prana_model_tp_get": [P, C.POINTER(I), C.POINTER(I), C.POINTER(I)],
     "prana_model_free": [P],
     "prana_model_config_get": [P, C.POINTER(ModelConfig)],
     "prana_kv_create": [P, SZ, C.POINTER(P)],

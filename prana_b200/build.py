@@ -19,8 +19,8 @@ CSRC = PKG / "csrc"
 LIB = PKG / "_lib"
 ROOT = PKG.parent
 
-CUDA_SOURCES = ["kernels.cu", "attention.cu", "decode.cu", "ctx.cu", "model.cu", "noalloc.cu"]
-CUDA_HEADERS = ["common.cuh", "gemv.cuh", "finish.cuh", "mbar.cuh", "internal.h", "host.h"]
+CUDA_SOURCES = ["kernels.cu", "attention.cu", "decode.cu", "ctx.cu", "model.cu", "noalloc.cu", "comm.cu"]
+CUDA_HEADERS = ["common.cuh", "gemv.cuh", "finish.cuh", "mbar.cuh", "comm.h", "internal.h", "host.h"]
 NVCC_FLAGS = [
     "-O3",
     "-std=c++17",
@@ -76,7 +76,7 @@ def build_cuda(force: bool = False, verbose: bool = False) -> Path:
 
     with ThreadPoolExecutor(max_workers=len(CUDA_SOURCES)) as ex:
         list(ex.map(_run, cmds))
-    _run([_nvcc(), "-shared", "-cudart", "static", "-o", str(out), *map(str, objs)])
+    _run([_nvcc(), "-shared", "-cudart", "static", "-o", str(out), *map(str, objs), "-ldl"])
     return out
 
 

@@ -1,0 +1,48 @@
+// comm.h -- the NCCL calls of the tensor-parallel decode step, resolved at run
+// time.  The process may already hold a libnccl.so.2 (PyTorch ships one); the
+// library binds to that copy when it is loaded, else opens one itself, so two
+// NCCL builds never meet in one process.
+#pragma once
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+namespace prana {
+
+struct Nccl {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+// The resolved entry points, or nullptr (with *why set) when NCCL is unavailable.
+const Nccl* nccl(const char** why);
+
+// One-shot all-reduce over NVLink peer memory.  Every rank owns a receive
+// area of 2 (alternating calls) x world slots of `cap` floats plus 2 x world
+// flags, mapped into every other rank's address space.  A call pushes this
+// rank's values into its slot on every rank, raises its flag there to the
+// call's epoch, waits (bounded) until every rank's flag carries the epoch, and
+// sums the world slots in rank order, so every rank computes identical bits.
+constexpr int kTpMaxWorld = 8;
+struct TpPeers {
+  int world = 1, rank = 0;
+  size_t cap = 0;                      // floats per slot
+  float* buf[kTpMaxWorld] = {};        // each rank's receive area (this process's mapping)
+  unsigned* flag[kTpMaxWorld] = {};    // each rank's flags [2][world]
+  unsigned* epoch = nullptr;           // this rank's call counter (device)
+};
+// Map every rank's receive area (exchanged with an NCCL all-gather of IPC
+// handles); false when peer access is unavailable.
+bool tp_peers_setup(ncclComm_t comm, int world, int rank, size_t cap, cudaStream_t st, TpPeers* out,
+                    void** own_mem);
+void tp_peers_release(TpPeers* p, void* own_mem);
+// x[0..n) = sum over ranks of every rank's x[0..n); err is raised when a wait gives up.
+cudaError_t launch_tp_allreduce(const TpPeers& p, float* x, int n, unsigned* err, cudaStream_t st);
+// dst[r * n .. r * n + n) = rank r's src[0..n); the two calls share the epoch sequence.
+cudaError_t launch_tp_allgather(const TpPeers& p, const float* src, int n, float* dst, unsigned* err,
+                                cudaStream_t st);
+
+}  // namespace prana

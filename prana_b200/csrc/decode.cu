@@ -448,8 +448,9 @@ __global__ void __launch_bounds__(DG_THREADS, 2) stream_gemv(const StreamArgs g)
         }
       }
       if (lane == 0) {
-        const uint32_t tok = bi == INT_MAX ? 0u : (uint32_t)bi;
+        const uint32_t tok = bi == INT_MAX ? 0u : (uint32_t)(bi + g.idx_offset);
         g.token_out[m] = tok;
+        if (g.best_val) g.best_val[m] = bv;
         if (m == 0 && g.token_next) *g.token_next = (int)tok;
       }
     }
@@ -555,6 +556,7 @@ static cudaError_t stream_t(const StreamArgs& g, cudaStream_t st, bool pdl) {
 //   Q|K|V, gate|up, LM head:  rmsnorm + quantize the residual stream in the prologue
 //   wo, ffn_down:             quantize the attention output / silu(g)*u, residual epilogue
 //   kernel-level matmuls:     pre-quantized rows, plain store (or rmsnorm'd for unfused gate/up)
+//   tensor-parallel wo / ffn_down on ranks > 0: f32 rows, plain store of the partial product
 cudaError_t launch_stream(const StreamArgs& g, int epi, int pro, cudaStream_t st, bool pdl) {
   if (g.m < 1 || g.m > 8 || g.K != g.w.cols || g.N != g.w.rows || g.K % 32) return cudaErrorInvalidValue;
   // bulk copies of f32 rows need 16-byte aligned sources
@@ -567,6 +569,7 @@ cudaError_t launch_stream(const StreamArgs& g, int epi, int pro, cudaStream_t st
   if (epi == EPI_RESID && pro == PRO_F32) return stream_t<EPI_RESID, PRO_F32>(g, st, pdl);
   if (epi == EPI_STORE && pro == PRO_Q) return stream_t<EPI_STORE, PRO_Q>(g, st, pdl);
   if (epi == EPI_STORE && pro == PRO_NORM) return stream_t<EPI_STORE, PRO_NORM>(g, st, pdl);
+  if (epi == EPI_STORE && pro == PRO_F32) return stream_t<EPI_STORE, PRO_F32>(g, st, pdl);  // tensor-parallel partials
   return cudaErrorInvalidValue;
 }
 

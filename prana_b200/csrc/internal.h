@@ -117,6 +117,8 @@ struct StreamArgs {
   int* token_next;
   // last-CTA argmax merge; the counter is zero between launches
   unsigned* counter;
+  int idx_offset;      // ARGMAX: global index of this matrix's row 0 (vocab shard start)
+  float* best_val;     // ARGMAX: the maximum itself per activation row (nullable)
   QkvMap qkv;
 };
 
@@ -139,6 +141,8 @@ cudaError_t launch_argmax(const float* x, int rows, int n, uint32_t* out, cudaSt
 cudaError_t launch_block_dots(const DevWeight& w, int row, const int8_t* aq, const int32_t* asum, int32_t* out,
                               cudaStream_t st);
 cudaError_t launch_advance(int* tok, int* pos, uint32_t* ring, int ring_cap, int* ring_n, cudaStream_t st, bool pdl);
+// first maximum over ranks: all = [world][16] (8 best values, then 8 index bit patterns)
+cudaError_t launch_tp_argmax(const float* all, int world, int m, uint32_t* tok_out, int* tok_next, cudaStream_t st);
 
 // attention.cu
 int attn_max_rows_per_cta(int hd);

@@ -354,4 +354,32 @@ cudaError_t launch_advance(int* tok, int* pos, uint32_t* ring, int ring_cap, int
   return launch((const void*)advance_kernel, dim3(1), dim3(1), 0, st, args, pdl);
 }
 
+
+// ---------------------------------------------------------------- tensor-parallel argmax
+// Each rank's LM-head shard reported (max, global index) per row; the first
+// maximum over the ranks (larger value, or equal value at the smaller index)
+// is the token, as Model::argmax picks the first maximum (infer.rs:560-568).
+__global__ void tp_argmax_kernel(const float* all, int world, int m, uint32_t* tok_out, int* tok_next) {
+  const int i = threadIdx.x;
+  if (i >= m) return;
+  float bv = -INFINITY;
+  uint32_t bi = 0xffffffffu;
+  for (int r = 0; r < world; r++) {
+    const float v = all[r * 16 + i];
+    const uint32_t idx = __float_as_uint(all[r * 16 + 8 + i]);
+    if (v > bv || (v == bv && idx < bi)) {
+      bv = v;
+      bi = idx;
+    }
+  }
+  if (bi == 0xffffffffu) bi = 0;
+  tok_out[i] = bi;
+  if (i == 0 && tok_next) *tok_next = (int)bi;
+}
+
+cudaError_t launch_tp_argmax(const float* all, int world, int m, uint32_t* tok_out, int* tok_next, cudaStream_t st) {
+  tp_argmax_kernel<<<1, 32, 0, st>>>(all, world, m, tok_out, tok_next);
+  return cudaGetLastError();
+}
+
 }  // namespace prana

@@ -15,6 +15,7 @@
 #include <memory>
 #include <new>
 
+#include "comm.h"
 #include "host.h"
 
 namespace prana {
@@ -203,6 +204,7 @@ struct Bufs {
   size_t rows = 0;
   float *x = nullptr, *q = nullptr, *att = nullptr, *kf = nullptr, *vf = nullptr, *h = nullptr, *u = nullptr;
   float* logits = nullptr;
+  float* logits_l = nullptr;  // tensor parallel: this rank's vocabulary slice
   uint32_t* toks = nullptr;     // input ids [rows]
   uint32_t* tok_out = nullptr;  // argmax per row [rows]
   std::vector<void*> owned;
@@ -244,6 +246,16 @@ struct prana_model {
   uint32_t* h_tok = nullptr;
   bool pdl = true;
   std::vector<prana_kv*> caches;  // live KV caches (freed with the model)
+  // tensor parallelism: this rank's share of heads, FFN rows and vocabulary
+  // (the whole model when tp_world == 1)
+  int tp_world = 1, tp_rank = 0;
+  ncclComm_t comm = nullptr;
+  int64_t heads_l = 0, kv_heads_l = 0, hid_l = 0, vocab_l = 0, vocab_off = 0;
+  float* tp_local = nullptr;  // [16]: per row the best logit, then its index bits
+  float* tp_all = nullptr;    // [world][16]
+  prana::TpPeers peers;       // one-shot all-reduce over peer memory (world == 1: unused)
+  void* peers_mem = nullptr;
+  bool peers_ok = false;
 };
 
 struct prana_kv {
@@ -301,6 +313,18 @@ int linear_raw(const Gguf& g, const std::string& name, size_t rows, size_t cols,
 
 size_t gguf_row_bytes(uint32_t type, size_t cols) { return type_size(type, cols); }
 
+// Columns [c0, c1) of every row of a [rows, cols] GGUF tensor (whole blocks).
+int slice_cols(uint32_t type, size_t rows, size_t cols, const uint8_t* raw, size_t c0, size_t c1,
+               std::vector<uint8_t>& out) {
+  const size_t blk = (type == T_Q4_K || type == T_Q6_K) ? 256 : (type == T_Q8_0 || type == T_Q4_0) ? 32 : 1;
+  if (c0 % blk || c1 % blk || c1 > cols || c0 >= c1)
+    return fail(PRANA_E_UNSUPPORTED, "column shard [%zu, %zu) does not fall on %zu-value blocks", c0, c1, blk);
+  const size_t rb = gguf_row_bytes(type, cols), sb = gguf_row_bytes(type, c1 - c0), off = gguf_row_bytes(type, c0);
+  out.resize(rows * sb);
+  for (size_t r = 0; r < rows; r++) memcpy(out.data() + r * sb, raw + r * rb + off, sb);
+  return PRANA_OK;
+}
+
 int upload_stream(prana_model* m, uint32_t type, size_t rows, size_t cols, const uint8_t* bytes, StreamW* sw) {
   return upload_weight(m->ctx, (int)type, rows, cols, bytes, &sw->w);
 }
@@ -328,13 +352,18 @@ void free_model(prana_model* m) {
   }
   for (void* p : m->owned) cudaFree(p);
   m->dec.reset();
+  if (m->peers_ok) tp_peers_release(&m->peers, m->peers_mem);
+  if (m->comm) {
+    const Nccl* api = nccl(nullptr);
+    if (api) api->comm_destroy(m->comm);
+  }
   if (m->h_io) cudaFreeHost(m->h_io);
   delete m;
 }
 
 int make_bufs(prana_model* m, size_t rows, bool window, Bufs& b) {
   const auto& c = m->cfg;
-  const size_t q_dim = c.n_heads * c.head_dim, kv_dim = c.n_kv_heads * c.head_dim, dim = c.dim, hid = c.hidden_dim;
+  const size_t q_dim = m->heads_l * c.head_dim, kv_dim = m->kv_heads_l * c.head_dim, dim = c.dim, hid = m->hid_l;
   b.rows = rows;
   int rc = 0;
   rc |= b.alloc(b.x, rows * dim);
@@ -349,6 +378,7 @@ int make_bufs(prana_model* m, size_t rows, bool window, Bufs& b) {
     rc |= b.alloc(b.vf, rows * kv_dim);
   } else {
     rc |= b.alloc(b.logits, rows * c.vocab_size);
+    if (m->tp_world > 1) rc |= b.alloc(b.logits_l, rows * m->vocab_l);
   }
   return rc ? PRANA_E_OOM : PRANA_OK;
 }
@@ -395,12 +425,46 @@ int run_stream(prana_model* m, StreamArgs& a, int epi, int pro, bool pdl) {
 // f32 in-window K/V (prefill); MODE_CACHE over the f16 cache (decode, verify).
 // Every projection's kernel normalizes / quantizes its own input rows in its
 // prologue while its first weight tiles are already streaming in.
+// Tensor parallel (tp_world > 1): each rank holds its heads, FFN rows and
+// vocabulary slice.  wo and ffn_down are split by input columns: rank 0 adds
+// its partial product to x (residual epilogue), the other ranks store theirs
+// into x, and one in-place all-reduce (sum) leaves x + sum of partials on every
+// rank.  The LM head reports each shard's (max, index); an all-gather and the
+// first maximum over ranks give the token.  gather_logits also assembles the
+// full logits rows.
+int tp_sum_rows(prana_model* m, float* x, size_t n, cudaStream_t st) {
+  if (m->peers_ok && n <= m->peers.cap) {  // small (decode / verify) rows: one-shot over peer memory
+    PRANA_CK(launch_tp_allreduce(m->peers, x, (int)n, m->err, st));
+    return PRANA_OK;
+  }
+  const char* why = nullptr;
+  const Nccl* api = nccl(&why);
+  if (!api) return fail(PRANA_E_COMM, "%s", why);
+  const ncclResult_t r = api->all_reduce(x, x, n, ncclFloat, ncclSum, m->comm, st);
+  if (r != ncclSuccess) return fail(PRANA_E_COMM, "ncclAllReduce: %s", api->error_string(r));
+  return PRANA_OK;
+}
+
+int tp_gather(prana_model* m, const float* src, float* dst, size_t n, cudaStream_t st) {
+  if (m->peers_ok && n <= m->peers.cap) {
+    PRANA_CK(launch_tp_allgather(m->peers, src, (int)n, dst, m->err, st));
+    return PRANA_OK;
+  }
+  const char* why = nullptr;
+  const Nccl* api = nccl(&why);
+  if (!api) return fail(PRANA_E_COMM, "%s", why);
+  const ncclResult_t r = api->all_gather(src, dst, n, ncclFloat, m->comm, st);
+  if (r != ncclSuccess) return fail(PRANA_E_COMM, "ncclAllGather: %s", api->error_string(r));
+  return PRANA_OK;
+}
+
 int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* toks_dev, const int* tok_dev, int pos0,
-                 const int* pos_dev, int mode, bool head, bool pdl, Trace* tr = nullptr) {
+                 const int* pos_dev, int mode, bool head, bool pdl, Trace* tr = nullptr, bool gather_logits = true) {
   const auto& c = m->cfg;
   cudaStream_t st = m->ctx->own;
-  const int dim = (int)c.dim, hd = (int)c.head_dim, hid = (int)c.hidden_dim;
-  const int q_dim = (int)(c.n_heads * c.head_dim), kv_dim = (int)(c.n_kv_heads * c.head_dim);
+  const bool tp = m->tp_world > 1;
+  const int dim = (int)c.dim, hd = (int)c.head_dim, hid = (int)m->hid_l;
+  const int q_dim = (int)(m->heads_l * c.head_dim), kv_dim = (int)(m->kv_heads_l * c.head_dim);
   const size_t lstride = kv->positions * (size_t)kv_dim;
   int rc;
   PRANA_CK(launch_embed(m->emb.dw, toks_dev, tok_dev, n, b.x, st, pdl));
@@ -445,7 +509,7 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
     }
     // --- attention
     if (mode == MODE_WINDOW) {
-      PrefillAttnArgs a{b.q, b.kf, b.vf, n, (int)c.n_heads, (int)c.n_kv_heads, hd, b.att};
+      PrefillAttnArgs a{b.q, b.kf, b.vf, n, (int)m->heads_l, (int)m->kv_heads_l, hd, b.att};
       PRANA_CK(launch_attn_prefill(a, st));
     } else {
       AttnArgs a{};
@@ -455,8 +519,8 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       a.m = n;
       a.pos0 = pos0;
       a.pos_dev = pos_dev;
-      a.n_heads = (int)c.n_heads;
-      a.n_kv = (int)c.n_kv_heads;
+      a.n_heads = (int)m->heads_l;
+      a.n_kv = (int)m->kv_heads_l;
       a.hd = hd;
       a.n_splits = kv->n_splits;
       a.part_ml = kv->part_ml;
@@ -477,8 +541,9 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       StreamArgs a = stream_args(m, L.wo, mc, b.att + (size_t)c0 * q_dim, nullptr);
       if (tr) tr->site(a, q_dim);
       a.out = b.x + (size_t)c0 * dim;
-      if ((rc = run_stream(m, a, EPI_RESID, PRO_F32, pdl))) return rc;
+      if ((rc = run_stream(m, a, tp && m->tp_rank ? EPI_STORE : EPI_RESID, PRO_F32, pdl))) return rc;
     }
+    if (tp && (rc = tp_sum_rows(m, b.x, (size_t)n * dim, st))) return rc;
     // --- rmsnorm -> gate|up -> silu(gate) * up
     for (int c0 = 0; c0 < n; c0 += 8) {
       const int mc = std::min(8, n - c0);
@@ -504,8 +569,9 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       StreamArgs a = stream_args(m, L.w2, mc, b.h + (size_t)c0 * hid, nullptr);
       if (tr) tr->site(a, hid);
       a.out = b.x + (size_t)c0 * dim;
-      if ((rc = run_stream(m, a, EPI_RESID, PRO_F32, pdl))) return rc;
+      if ((rc = run_stream(m, a, tp && m->tp_rank ? EPI_STORE : EPI_RESID, PRO_F32, pdl))) return rc;
     }
+    if (tp && (rc = tp_sum_rows(m, b.x, (size_t)n * dim, st))) return rc;
   }
   if (!head) return PRANA_OK;
   // --- final rmsnorm -> LM head -> argmax (Model::logits, checkpoint.rs:239-248; infer.rs:560-568)
@@ -513,14 +579,30 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
     const int mc = std::min(8, n - c0);
     StreamArgs a = stream_args(m, m->head, mc, b.x + (size_t)c0 * dim, m->rms_final);
     if (tr) tr->site(a, dim);
-    a.out = b.logits + (size_t)c0 * c.vocab_size;
     a.part_val = m->part_val;
     a.part_idx = m->part_idx;
     a.n_parts = m->n_parts;
     a.counter = m->ctr;
-    a.token_out = b.tok_out + c0;
-    a.token_next = (n == 1 && tok_dev) ? const_cast<int*>(tok_dev) : nullptr;
+    if (!tp) {
+      a.out = b.logits + (size_t)c0 * c.vocab_size;
+      a.token_out = b.tok_out + c0;
+      a.token_next = (n == 1 && tok_dev) ? const_cast<int*>(tok_dev) : nullptr;
+      if ((rc = run_stream(m, a, EPI_ARGMAX, PRO_NORM, pdl))) return rc;
+      continue;
+    }
+    a.out = b.logits_l + (size_t)c0 * m->vocab_l;
+    a.idx_offset = (int)m->vocab_off;
+    a.best_val = m->tp_local;
+    a.token_out = reinterpret_cast<uint32_t*>(m->tp_local + 8);
     if ((rc = run_stream(m, a, EPI_ARGMAX, PRO_NORM, pdl))) return rc;
+    if ((rc = tp_gather(m, m->tp_local, m->tp_all, 16, st))) return rc;
+    PRANA_CK(launch_tp_argmax(m->tp_all, m->tp_world, mc, b.tok_out + c0,
+                              (n == 1 && tok_dev) ? const_cast<int*>(tok_dev) : nullptr, st));
+    if (gather_logits)
+      for (int i = 0; i < mc; i++)
+        if ((rc = tp_gather(m, b.logits_l + (size_t)(c0 + i) * m->vocab_l, b.logits + (size_t)(c0 + i) * c.vocab_size,
+                            (size_t)m->vocab_l, st)))
+          return rc;
   }
   return PRANA_OK;
 }
@@ -542,7 +624,8 @@ int capture(prana_model* m, prana_kv* kv, bool loop, cudaGraphExec_t* out) {
     const bool pdl = m->pdl && attempt == 0;
     cudaGraph_t graph = nullptr;
     PRANA_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
-    int rc = enqueue_rows(m, kv, *m->dec, 1, nullptr, m->d_tokpos, 0, m->d_tokpos + 1, MODE_CACHE, true, pdl);
+    int rc = enqueue_rows(m, kv, *m->dec, 1, nullptr, m->d_tokpos, 0, m->d_tokpos + 1, MODE_CACHE, true, pdl, nullptr,
+                          !loop);
     if (!rc && loop) {
       cudaError_t e = launch_advance(m->d_tokpos, m->d_tokpos + 1, kv->ring, (int)kv->positions, kv->ring_n, st, pdl);
       if (e != cudaSuccess) rc = fail(PRANA_E_CUDA, "advance launch: %s", cudaGetErrorString(e));
@@ -616,9 +699,15 @@ struct RowSrc {
 
 extern "C" {
 
-int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
+// Load a GGUF model, or one tensor-parallel shard of it (world > 1): this
+// rank's query / kv heads, FFN rows and vocabulary rows; wo and ffn_down keep
+// this rank's input columns.  nccl_id (NCCL_UNIQUE_ID_BYTES) names the
+// communicator every rank joins.
+static int load_model(prana_ctx* ctx, const char* path, int world, int rank, const void* nccl_id, prana_model** out) {
   API_BEGIN
   NEED(ctx && path && out, "null argument");
+  NEED(world >= 1 && rank >= 0 && rank < world && (world == 1 || nccl_id), "bad tensor-parallel rank %d of %d", rank,
+       world);
   *out = nullptr;
   DevScope ds(ctx->device);
   const int fd = open(path, O_RDONLY);
@@ -680,6 +769,17 @@ int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
   const size_t dim = (size_t)c.dim, hid = (size_t)c.hidden_dim, q_dim = (size_t)(c.n_heads * c.head_dim),
                kv_dim = (size_t)(c.n_kv_heads * c.head_dim);
   NEED(q_dim % 32 == 0, "q_dim must be a multiple of 32");
+  NEED(world == 1 || (c.n_kv_heads % world == 0 && c.hidden_dim % world == 0 && c.vocab_size % world == 0),
+       "tensor parallel over %d ranks needs kv heads, FFN width and vocabulary divisible by it", world);
+  m->tp_world = world;
+  m->tp_rank = rank;
+  m->heads_l = c.n_heads / world;
+  m->kv_heads_l = c.n_kv_heads / world;
+  m->hid_l = c.hidden_dim / world;
+  m->vocab_l = c.vocab_size / world;
+  m->vocab_off = (int64_t)rank * m->vocab_l;
+  const size_t q_dim_l = (size_t)(m->heads_l * c.head_dim), kv_dim_l = (size_t)(m->kv_heads_l * c.head_dim),
+               hid_l = (size_t)m->hid_l;
 
   // token embedding (gguf.rs:309-326)
   {
@@ -703,11 +803,14 @@ int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
     if ((rc = vec_f32(g, p + "ffn_norm.weight", dim, v)) || (rc = dev_vec(m.get(), v, &L.rms_ffn))) return rc;
     // Q|K|V: concatenate runs of one weight type; RoPE partners become adjacent rows
     const char* names[3] = {"attn_q.weight", "attn_k.weight", "attn_v.weight"};
-    const size_t seg_rows[3] = {q_dim, kv_dim, kv_dim};
+    const size_t full_rows[3] = {q_dim, kv_dim, kv_dim};
+    const size_t seg_rows[3] = {q_dim_l, kv_dim_l, kv_dim_l};  // this rank's heads
     uint32_t types[3];
     const uint8_t* raws[3];
-    for (int s = 0; s < 3; s++)
-      if ((rc = linear_raw(g, p + names[s], seg_rows[s], dim, &types[s], &raws[s]))) return rc;
+    for (int s = 0; s < 3; s++) {
+      if ((rc = linear_raw(g, p + names[s], full_rows[s], dim, &types[s], &raws[s]))) return rc;
+      raws[s] += (size_t)rank * seg_rows[s] * gguf_row_bytes(types[s], dim);
+    }
     for (int s0 = 0; s0 < 3;) {
       int s1 = s0 + 1;
       while (s1 < 3 && types[s1] == types[s0]) s1++;
@@ -739,8 +842,10 @@ int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
     }
     uint32_t ty;
     const uint8_t* raw;
+    std::vector<uint8_t> cols;
     if ((rc = linear_raw(g, p + "attn_output.weight", dim, q_dim, &ty, &raw)) ||
-        (rc = upload_stream(m.get(), ty, dim, q_dim, raw, &L.wo)))
+        (rc = slice_cols(ty, dim, q_dim, raw, rank * q_dim_l, (rank + 1) * q_dim_l, cols)) ||
+        (rc = upload_stream(m.get(), ty, dim, q_dim_l, cols.data(), &L.wo)))
       return rc;
     // gate|up: interleave rows (gate j, up j) when both have one type
     uint32_t t1, t3;
@@ -748,30 +853,35 @@ int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
     if ((rc = linear_raw(g, p + "ffn_gate.weight", hid, dim, &t1, &r1)) ||
         (rc = linear_raw(g, p + "ffn_up.weight", hid, dim, &t3, &r3)))
       return rc;
+    r1 += (size_t)rank * hid_l * gguf_row_bytes(t1, dim);  // this rank's FFN rows
+    r3 += (size_t)rank * hid_l * gguf_row_bytes(t3, dim);
     if (t1 == t3) {
       const size_t rb = gguf_row_bytes(t1, dim);
-      std::vector<uint8_t> buf(2 * hid * rb);
-      for (size_t j = 0; j < hid; j++) {
+      std::vector<uint8_t> buf(2 * hid_l * rb);
+      for (size_t j = 0; j < hid_l; j++) {
         memcpy(&buf[(2 * j) * rb], r1 + j * rb, rb);
         memcpy(&buf[(2 * j + 1) * rb], r3 + j * rb, rb);
       }
       L.fused_gu = true;
-      if ((rc = upload_stream(m.get(), t1, 2 * hid, dim, buf.data(), &L.gu))) return rc;
+      if ((rc = upload_stream(m.get(), t1, 2 * hid_l, dim, buf.data(), &L.gu))) return rc;
     } else {
-      if ((rc = upload_stream(m.get(), t1, hid, dim, r1, &L.w1)) ||
-          (rc = upload_stream(m.get(), t3, hid, dim, r3, &L.w3)))
+      if ((rc = upload_stream(m.get(), t1, hid_l, dim, r1, &L.w1)) ||
+          (rc = upload_stream(m.get(), t3, hid_l, dim, r3, &L.w3)))
         return rc;
     }
     if ((rc = linear_raw(g, p + "ffn_down.weight", dim, hid, &ty, &raw)) ||
-        (rc = upload_stream(m.get(), ty, dim, hid, raw, &L.w2)))
+        (rc = slice_cols(ty, dim, hid, raw, rank * hid_l, (rank + 1) * hid_l, cols)) ||
+        (rc = upload_stream(m.get(), ty, dim, hid_l, cols.data(), &L.w2)))
       return rc;
     // gguf.rs:388-394: each bias optional
     const char* bn[3] = {"attn_q.bias", "attn_k.bias", "attn_v.bias"};
     float** bd[3] = {&L.bq, &L.bk, &L.bv};
-    const size_t bl[3] = {q_dim, kv_dim, kv_dim};
+    const size_t bl[3] = {q_dim, kv_dim, kv_dim}, bl_l[3] = {q_dim_l, kv_dim_l, kv_dim_l};
     for (int j = 0; j < 3; j++)
       if (g.tensors.count(p + bn[j])) {
-        if ((rc = vec_f32(g, p + bn[j], bl[j], v)) || (rc = dev_vec(m.get(), v, bd[j]))) return rc;
+        if ((rc = vec_f32(g, p + bn[j], bl[j], v))) return rc;
+        std::vector<float> local(v.begin() + (size_t)rank * bl_l[j], v.begin() + (size_t)(rank + 1) * bl_l[j]);
+        if ((rc = dev_vec(m.get(), local, bd[j]))) return rc;
         c.has_bias = 1;
       }
   }
@@ -782,17 +892,25 @@ int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
   if (g.tensors.count("output.weight")) {
     uint32_t ty;
     const uint8_t* raw;
-    if ((rc = linear_raw(g, "output.weight", (size_t)c.vocab_size, dim, &ty, &raw)) ||
-        (rc = upload_stream(m.get(), ty, (size_t)c.vocab_size, dim, raw, &m->head)))
-      return rc;
+    if ((rc = linear_raw(g, "output.weight", (size_t)c.vocab_size, dim, &ty, &raw))) return rc;
+    raw += (size_t)m->vocab_off * gguf_row_bytes(ty, dim);  // this rank's vocabulary rows
+    if ((rc = upload_stream(m.get(), ty, (size_t)m->vocab_l, dim, raw, &m->head))) return rc;
   } else {
     // tied classifier over a packed table runs the quantized kernel (checkpoint.rs:246)
     c.shared_classifier = 1;
     const int et = m->emb.dw.type;
     if (et != T_Q4_0 && et != T_Q4_K && et != T_Q6_K)
       return fail(PRANA_E_UNSUPPORTED, "tied classifier over a dense table is not built");
-    m->head.w = m->emb;
-    m->head.owns = false;
+    if (world == 1) {
+      m->head.w = m->emb;
+      m->head.owns = false;
+    } else {
+      const GgufTensor* t;
+      const uint8_t* raw;
+      if ((rc = tensor_raw(g, "token_embd.weight", &t, &raw))) return rc;
+      raw += (size_t)m->vocab_off * gguf_row_bytes(t->type, dim);
+      if ((rc = upload_stream(m.get(), t->type, (size_t)m->vocab_l, dim, raw, &m->head))) return rc;
+    }
   }
   // weight bytes on the device
   size_t wb = m->emb.bytes + (m->head.owns ? m->head.w.bytes : 0);
@@ -821,11 +939,57 @@ int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
   m->d_tokpos = reinterpret_cast<int*>(static_cast<uint8_t*>(p) + 64);
   PRANA_CK(cudaHostAlloc((void**)&m->h_io, 64, cudaHostAllocDefault));
   m->h_tok = reinterpret_cast<uint32_t*>(m->h_io + 4);
+  if (world > 1) {
+    PRANA_CK(cudaMalloc(&p, (size_t)(world + 1) * 16 * 4));
+    m->owned.push_back(p);
+    m->tp_local = static_cast<float*>(p);
+    m->tp_all = m->tp_local + 16;
+    const char* why = nullptr;
+    const Nccl* api = nccl(&why);
+    if (!api) return fail(PRANA_E_COMM, "%s", why);
+    ncclUniqueId id;
+    memcpy(&id, nccl_id, sizeof(id));
+    const ncclResult_t r = api->comm_init_rank(&m->comm, world, id, rank);
+    if (r != ncclSuccess) return fail(PRANA_E_COMM, "ncclCommInitRank: %s", api->error_string(r));
+    // peer-memory all-reduce for up to 8 rows of the residual stream (NCCL otherwise)
+    const char* mode = getenv("PRANA_TP_ALLREDUCE");
+    if (!(mode && !strcmp(mode, "nccl")))
+      m->peers_ok = tp_peers_setup(m->comm, world, rank, 8 * dim, ctx->own, &m->peers, &m->peers_mem);
+  }
   const char* e = getenv("PRANA_PDL");
   m->pdl = !(e && e[0] == '0');
   *out = m.release();
   return PRANA_OK;
   API_END
+}
+
+int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
+  return load_model(ctx, path, 1, 0, nullptr, out);
+}
+
+int prana_model_load_gguf_tp(prana_ctx* ctx, const char* path, int world, int rank, const void* nccl_id,
+                             prana_model** out) {
+  return load_model(ctx, path, world, rank, nccl_id, out);
+}
+
+int prana_tp_unique_id(void* out) {
+  NEED(out, "null argument");
+  const char* why = nullptr;
+  const Nccl* api = nccl(&why);
+  if (!api) return fail(PRANA_E_COMM, "%s", why);
+  ncclUniqueId id;
+  const ncclResult_t r = api->get_unique_id(&id);
+  if (r != ncclSuccess) return fail(PRANA_E_COMM, "ncclGetUniqueId: %s", api->error_string(r));
+  memcpy(out, &id, sizeof(id));
+  return PRANA_OK;
+}
+
+int prana_model_tp_get(const prana_model* m, int* world, int* rank, int* peer_exchange) {
+  NEED(m && world && rank, "null argument");
+  *world = m->tp_world;
+  *rank = m->tp_rank;
+  if (peer_exchange) *peer_exchange = m->peers_ok ? 1 : 0;
+  return PRANA_OK;
 }
 
 int prana_model_free(prana_model* m) {
@@ -850,7 +1014,7 @@ int prana_kv_create(prana_model* m, size_t positions, prana_kv** out) {
   std::unique_ptr<prana_kv, void (*)(prana_kv*)> kv(new prana_kv(), destroy_kv);
   kv->m = m;
   kv->positions = positions;
-  const size_t kv_dim = (size_t)(c.n_kv_heads * c.head_dim);
+  const size_t kv_dim = (size_t)(m->kv_heads_l * c.head_dim);
   const size_t per = (size_t)c.n_layers * positions * kv_dim;
   if (cudaMalloc(&kv->k, per * 2) != cudaSuccess || cudaMalloc(&kv->v, per * 2) != cudaSuccess) {
     cudaGetLastError();
@@ -864,17 +1028,17 @@ int prana_kv_create(prana_model* m, size_t positions, prana_kv** out) {
     AttnArgs& t = kv->maps[l];
     t.kc = kv->k + l * positions * kv_dim;
     t.vc = kv->v + l * positions * kv_dim;
-    t.n_kv = (int)c.n_kv_heads;
+    t.n_kv = (int)m->kv_heads_l;
     t.hd = (int)c.head_dim;
     attn_make_maps(t, (int)positions);
   }
   // attention splits for this capacity (the decode graph keeps them as the cache fills)
-  kv->n_splits = attn_splits((int)positions, (int)c.n_kv_heads, (int)c.head_dim, m->ctx->sm_count);
+  kv->n_splits = attn_splits((int)positions, (int)m->kv_heads_l, (int)c.head_dim, m->ctx->sm_count);
   const int group = (int)(c.n_heads / c.n_kv_heads);
   const int rows_cta = std::max(1, 4096 / (int)(c.head_dim * group));
   const size_t vh = (size_t)rows_cta * group;  // largest row chunk one attention CTA takes
-  const size_t ml = ((size_t)c.n_kv_heads * kv->n_splits * vh * 2 + 3) / 4 * 4;  // part_o 16-byte aligned
-  const size_t po = (size_t)c.n_kv_heads * kv->n_splits * vh * c.head_dim;
+  const size_t ml = ((size_t)m->kv_heads_l * kv->n_splits * vh * 2 + 3) / 4 * 4;  // part_o 16-byte aligned
+  const size_t po = (size_t)m->kv_heads_l * kv->n_splits * vh * c.head_dim;
   PRANA_CK(cudaMalloc(&kv->part_ml, (ml + po) * 4));
   kv->part_o = kv->part_ml + ml;
   PRANA_CK(cudaMalloc(&kv->counters, 1024 * sizeof(unsigned)));
@@ -897,7 +1061,7 @@ int prana_kv_read(prana_kv* kv, size_t layer, int is_v, size_t rows, uint16_t* h
   const auto& c = kv->m->cfg;
   NEED(layer < (size_t)c.n_layers && rows <= kv->positions, "layer/rows out of range");
   DevScope ds(kv->m->ctx->device);
-  const size_t kv_dim = (size_t)(c.n_kv_heads * c.head_dim);
+  const size_t kv_dim = (size_t)(kv->m->kv_heads_l * c.head_dim);  // this rank's kv heads
   const __half* base = (is_v ? kv->v : kv->k) + layer * kv->positions * kv_dim;
   PRANA_CK(cudaStreamSynchronize(kv->m->ctx->own));
   PRANA_CK(cudaMemcpy(host, base, rows * kv_dim * 2, cudaMemcpyDeviceToHost));
@@ -935,6 +1099,7 @@ int prana_forward_trace(prana_model* m, prana_kv* kv, uint32_t token, size_t pos
   const auto& c = m->cfg;
   const size_t need = (size_t)c.n_layers * (2 * c.dim + c.n_heads * c.head_dim + c.hidden_dim) + c.dim;
   NEED(cap >= need, "trace buffer holds %zu values, %zu needed", cap, need);
+  NEED(m->tp_world == 1, "forward_trace runs on a single-GPU model");
   DevScope ds(m->ctx->device);
   cudaStream_t st = m->ctx->own;
   Trace tr;
@@ -966,7 +1131,7 @@ int prana_kv_write(prana_kv* kv, size_t layer, int is_v, size_t rows, const uint
   const auto& c = kv->m->cfg;
   NEED(layer < (size_t)c.n_layers && rows <= kv->positions, "layer/rows out of range");
   DevScope ds(kv->m->ctx->device);
-  const size_t kv_dim = (size_t)(c.n_kv_heads * c.head_dim);
+  const size_t kv_dim = (size_t)(kv->m->kv_heads_l * c.head_dim);  // this rank's kv heads
   __half* base = (is_v ? kv->v : kv->k) + layer * kv->positions * kv_dim;
   PRANA_CK(cudaStreamSynchronize(kv->m->ctx->own));
   PRANA_CK(cudaMemcpy(base, host, rows * kv_dim * 2, cudaMemcpyHostToDevice));
@@ -1011,7 +1176,8 @@ int prana_forward_batch(prana_model* m, prana_kv* kv, const uint32_t* tokens, si
     b = tmp.get();
   }
   PRANA_CK(cudaMemcpyAsync(b->toks, tokens, n * 4, cudaMemcpyHostToDevice, st));
-  int rc = enqueue_rows(m, kv, *b, (int)n, b->toks, nullptr, (int)pos0, nullptr, MODE_CACHE, true, false);
+  int rc = enqueue_rows(m, kv, *b, (int)n, b->toks, nullptr, (int)pos0, nullptr, MODE_CACHE, true, false, nullptr,
+                        logits != nullptr);
   if (rc) return rc;
   if (logits) PRANA_CK(cudaMemcpyAsync(logits, b->logits, n * (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, st));
   if (argmax) PRANA_CK(cudaMemcpyAsync(argmax, b->tok_out, n * 4, cudaMemcpyDeviceToHost, st));

@@ -49,6 +49,13 @@ class Config:
         return self.n_heads * self.head_dim
 
 
+def tp_unique_id() -> bytes:
+    """NCCL unique id (128 bytes) that rank 0 shares with every tensor-parallel rank."""
+    buf = C.create_string_buffer(128)
+    call("prana_tp_unique_id", buf)
+    return buf.raw
+
+
 class Model:
     def __init__(self, handle: C.c_void_p, device: int):
         self._h = handle
@@ -59,12 +66,28 @@ class Model:
         self.config = Config(c.dim, c.hidden_dim, c.n_layers, c.n_heads, c.n_kv_heads, c.vocab_size, c.seq_len,
                              c.head_dim, c.rope_theta, c.norm_eps, bool(c.rope_neox), bool(c.has_bias),
                              bool(c.shared_classifier), c.weight_bytes)
+        world, rank, peer = C.c_int(), C.c_int(), C.c_int()
+        call("prana_model_tp_get", handle, C.byref(world), C.byref(rank), C.byref(peer))
+        self.world, self.rank = world.value, rank.value
+        self.peer_exchange = bool(peer.value)
 
     @classmethod
-    def load(cls, path: str, device: int = 0) -> "Model":
+    def load(cls, path: str, device: int = 0, tp: "tuple[int, int, bytes] | None" = None) -> "Model":
+        """Load a GGUF model; tp = (world, rank, unique_id) loads this rank's
+        tensor-parallel shard (every rank then calls the same model methods in
+        the same order)."""
         h = C.c_void_p()
-        call("prana_model_load_gguf", context(device), str(path).encode(), C.byref(h))
+        if tp is None or tp[0] == 1:
+            call("prana_model_load_gguf", context(device), str(path).encode(), C.byref(h))
+        else:
+            world, rank, uid = tp
+            buf = C.create_string_buffer(bytes(uid), 128)
+            call("prana_model_load_gguf_tp", context(device), str(path).encode(), world, rank, buf, C.byref(h))
         return cls(h, device)
+
+    def local_kv_dim(self) -> int:
+        """Width of this rank's KV-cache rows (its kv heads)."""
+        return self.config.n_kv_heads // self.world * self.config.head_dim
 
     @property
     def handle(self) -> C.c_void_p:
@@ -106,7 +129,7 @@ class KvCache:
         return self._h
 
     def read(self, layer: int, is_v: bool, rows: int) -> np.ndarray:
-        out = np.empty((rows, self.model.config.kv_dim()), dtype=np.uint16)
+        out = np.empty((rows, self.model.local_kv_dim()), dtype=np.uint16)
         call("prana_kv_read", self._h, layer, int(is_v), rows, out.ctypes.data_as(C.c_void_p))
         return out
 
