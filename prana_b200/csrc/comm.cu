@@ -42,96 +42,170 @@ const Nccl* nccl(const char** why) {
 
 namespace {
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Every element travels as one 8-byte word: the value's bits in the low half,
+// the call's epoch in the high half.  An aligned 8-byte store is single-copy
+// atomic, so a reader that sees the epoch also sees the value: no fence and no
+// separate flag, one NVLink crossing per call.
+__device__ __forceinline__ void st_word(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
+constexpr int kExThreads = 512;
+constexpr int kExMaxCtas = 64;
+
 // GATHER == false: x[i] = sum over ranks (all-reduce, in place).
 // GATHER == true:  dst[r * n + i] = rank r's x[i] (all-gather).
-template <bool GATHER>
-__global__ void __launch_bounds__(1024) tp_exchange_kernel(const TpPeers p, float* x, int n, float* dst,
-                                                           unsigned* err) {
-  __shared__ int ok_all;
+// W ranks; each thread moves E elements per round, all of whose words are in
+// flight together (the waits overlap instead of following one another).
+// Each CTA keeps its own epoch (p.epoch[blockIdx.x]): every rank launches the
+// same grids in the same order, so CTA b's counter agrees on every rank.
+template <bool GATHER, int W, int E>
+__global__ void __launch_bounds__(kExThreads) tp_exchange_kernel(const TpPeers p, float* x, int n, float* dst,
+                                                                 unsigned* err) {
+  // the next kernel may start streaming its weights while this one waits
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // x is final
+  __shared__ int timed_out;
   const int tid = threadIdx.x;
-  const unsigned e = *p.epoch + 1;  // this call's epoch (every rank counts in lockstep)
-  const int par = (int)(e & 1);
+  if (tid == 0) timed_out = 0;
+  unsigned* epoch = p.epoch + blockIdx.x;
+  const unsigned e = *epoch + 1;  // this call's epoch
+  const size_t area = (size_t)(e & 1) * W * p.cap;  // alternate halves on consecutive calls
+  const uint64_t tag = (uint64_t)e << 32;
+  const int per_cta = (int)((n + gridDim.x - 1) / gridDim.x);
+  const int lo = blockIdx.x * per_cta, hi = min(n, lo + per_cta);
+  uint32_t budget = 1u << 22;
+  bool late = false;
   // push: this rank's values into its slot on every rank
-  for (int r = 0; r < p.world; r++) {
-    float* dst = p.buf[r] + ((size_t)par * p.world + p.rank) * p.cap;
-    for (int i = tid; i < n; i += blockDim.x) dst[i] = x[i];
+  for (int b = lo; b < hi; b += kExThreads * E) {
+    float v[E];
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+      const int i = b + j * kExThreads + tid;
+      v[j] = i < hi ? x[i] : 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < W; r++) {
+      uint64_t* slot = p.buf[r] + area + (size_t)p.rank * p.cap;
+#pragma unroll
+      for (int j = 0; j < E; j++) {
+        const int i = b + j * kExThreads + tid;
+        if (i < hi) st_word(slot + i, tag | __float_as_uint(v[j]));
+      }
+    }
   }
-  __syncthreads();
-  // announce: the stores above happen before the flags (release at system scope)
-  if (tid < p.world) {
-    __threadfence_system();
-    st_release_sys(p.flag[tid] + par * p.world + p.rank, e);
-  }
-  if (tid == 0) ok_all = 1;
-  __syncthreads();
-  // wait for every rank's values in this rank's area (bounded)
-  if (tid < p.world) {
-    const unsigned* f = p.flag[p.rank] + par * p.world + tid;
-    bool ok = false;
-    for (uint32_t i = 0; i < (1u << 24); i++) {
-      if (ld_acquire_sys(f) == e) {
-        ok = true;
+  // receive: every rank's word carries this epoch once it has landed (bounded wait)
+  const uint64_t* own = p.buf[p.rank] + area;
+  for (int b = lo; b < hi; b += kExThreads * E) {
+    uint64_t w[E][W];
+#pragma unroll
+    for (int j = 0; j < E; j++)
+#pragma unroll
+      for (int r = 0; r < W; r++) {
+        const int i = b + j * kExThreads + tid;
+        w[j][r] = i < hi ? ld_word(own + (size_t)r * p.cap + i) : tag;
+      }
+    for (;;) {
+      bool ready = true;
+#pragma unroll
+      for (int j = 0; j < E; j++)
+#pragma unroll
+        for (int r = 0; r < W; r++) ready &= (uint32_t)(w[j][r] >> 32) == e;
+      if (ready || !budget) {
+        late |= !ready;
         break;
       }
-      __nanosleep(32);
+      budget--;
+      __nanosleep(20);
+#pragma unroll
+      for (int j = 0; j < E; j++)
+#pragma unroll
+        for (int r = 0; r < W; r++) {
+          const int i = b + j * kExThreads + tid;
+          if ((uint32_t)(w[j][r] >> 32) != e) w[j][r] = ld_word(own + (size_t)r * p.cap + i);
+        }
     }
-    if (!ok) {
-      ok_all = 0;
-      if (err) atomicExch(err, 1u);
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+      const int i = b + j * kExThreads + tid;
+      if (i >= hi) continue;
+      if (GATHER) {
+#pragma unroll
+        for (int r = 0; r < W; r++) dst[(size_t)r * n + i] = __uint_as_float((uint32_t)w[j][r]);
+      } else {
+        float s = __uint_as_float((uint32_t)w[j][0]);
+#pragma unroll
+        for (int r = 1; r < W; r++) s += __uint_as_float((uint32_t)w[j][r]);  // rank order on every rank
+        x[i] = s;
+      }
     }
   }
+  if (late) timed_out = 1;
   __syncthreads();
-  // reduce in rank order (or lay the slots out side by side)
-  const float* own = p.buf[p.rank] + (size_t)par * p.world * p.cap;
-  if (GATHER) {
-    if (ok_all)
-      for (int r = 0; r < p.world; r++)
-        for (int i = tid; i < n; i += blockDim.x) dst[(size_t)r * n + i] = own[(size_t)r * p.cap + i];
-  } else if (ok_all)
-    for (int i = tid; i < n; i += blockDim.x) {
-      float s = own[i];
-      for (int r = 1; r < p.world; r++) s += own[(size_t)r * p.cap + i];
-      x[i] = s;
-    }
-  __syncthreads();
-  if (tid == 0) *p.epoch = e;
+  if (tid == 0) {
+    if (timed_out && err) atomicExch(err, 1u);
+    *epoch = e;
+  }
+}
+
+template <bool GATHER, int W>
+cudaError_t exchange_w(const TpPeers& p, float* x, int n, float* dst, unsigned* err, cudaLaunchConfig_t& cfg) {
+  constexpr int E = 16 / W;
+  // as many CTAs as keep each thread at one round or more, up to kExMaxCtas
+  int grid = (n + kExThreads * E - 1) / (kExThreads * E);
+  if (grid > kExMaxCtas) grid = kExMaxCtas;
+  cfg.gridDim = dim3(grid);
+  return cudaLaunchKernelEx(&cfg, tp_exchange_kernel<GATHER, W, E>, p, x, n, dst, err);
+}
+
+cudaError_t launch_exchange(const TpPeers& p, bool gather, float* x, int n, float* dst, unsigned* err,
+                            cudaStream_t st, bool pdl) {
+  if (n <= 0 || (size_t)n > p.cap) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kExThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  switch (p.world) {
+    case 2: return gather ? exchange_w<true, 2>(p, x, n, dst, err, cfg) : exchange_w<false, 2>(p, x, n, dst, err, cfg);
+    case 4: return gather ? exchange_w<true, 4>(p, x, n, dst, err, cfg) : exchange_w<false, 4>(p, x, n, dst, err, cfg);
+    case 8: return gather ? exchange_w<true, 8>(p, x, n, dst, err, cfg) : exchange_w<false, 8>(p, x, n, dst, err, cfg);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace
 
-cudaError_t launch_tp_allreduce(const TpPeers& p, float* x, int n, unsigned* err, cudaStream_t st) {
-  if (n <= 0 || (size_t)n > p.cap || p.world < 2) return cudaErrorInvalidValue;
-  tp_exchange_kernel<false><<<1, 1024, 0, st>>>(p, x, n, nullptr, err);
-  return cudaGetLastError();
+cudaError_t launch_tp_allreduce(const TpPeers& p, float* x, int n, unsigned* err, cudaStream_t st, bool pdl) {
+  return launch_exchange(p, false, x, n, nullptr, err, st, pdl);
 }
 
 cudaError_t launch_tp_allgather(const TpPeers& p, const float* src, int n, float* dst, unsigned* err,
-                                cudaStream_t st) {
-  if (n <= 0 || (size_t)n > p.cap || p.world < 2) return cudaErrorInvalidValue;
-  tp_exchange_kernel<true><<<1, 1024, 0, st>>>(p, const_cast<float*>(src), n, dst, err);
-  return cudaGetLastError();
+                                cudaStream_t st, bool pdl) {
+  return launch_exchange(p, true, const_cast<float*>(src), n, dst, err, st, pdl);
 }
 
 bool tp_peers_setup(ncclComm_t comm, int world, int rank, size_t cap, cudaStream_t st, TpPeers* out,
                     void** own_mem) {
   const Nccl* api = nccl(nullptr);
-  if (!api || world < 2 || world > kTpMaxWorld) return false;
+  if (!api || !(world == 2 || world == 4 || world == 8)) return false;
   TpPeers p;
   p.world = world;
   p.rank = rank;
   p.cap = cap;
-  // [2][world][cap] floats, then [2][world] flags, then the epoch counter
-  const size_t buf_bytes = 2 * (size_t)world * cap * sizeof(float);
-  const size_t bytes = buf_bytes + 2 * world * sizeof(unsigned) + 256;
+  // [2][world][cap] words, then one epoch counter per exchange CTA
+  const size_t buf_bytes = 2 * (size_t)world * cap * sizeof(uint64_t);
+  const size_t bytes = buf_bytes + kExMaxCtas * sizeof(unsigned);
   void* mem = nullptr;
   if (cudaMalloc(&mem, bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -157,12 +231,9 @@ bool tp_peers_setup(ncclComm_t comm, int world, int rank, size_t cap, cudaStream
     if (r != rank &&
         cudaIpcOpenMemHandle(&base, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
       ok = false;
-    if (ok) {
-      p.buf[r] = static_cast<float*>(base);
-      p.flag[r] = reinterpret_cast<unsigned*>(static_cast<char*>(base) + buf_bytes);
-    }
+    if (ok) p.buf[r] = static_cast<uint64_t*>(base);
   }
-  p.epoch = reinterpret_cast<unsigned*>(static_cast<char*>(mem) + buf_bytes + 2 * world * sizeof(unsigned));
+  p.epoch = reinterpret_cast<unsigned*>(static_cast<char*>(mem) + buf_bytes);
   if (!ok) {
     cudaGetLastError();
     tp_peers_release(&p, mem);

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <cstdint>
+
 namespace prana {
 
 struct Nccl {
@@ -21,28 +23,28 @@ struct Nccl {
 const Nccl* nccl(const char** why);
 
 // One-shot all-reduce over NVLink peer memory.  Every rank owns a receive
-// area of 2 (alternating calls) x world slots of `cap` floats plus 2 x world
-// flags, mapped into every other rank's address space.  A call pushes this
-// rank's values into its slot on every rank, raises its flag there to the
-// call's epoch, waits (bounded) until every rank's flag carries the epoch, and
-// sums the world slots in rank order, so every rank computes identical bits.
+// area of 2 (alternating calls) x world slots of `cap` 8-byte words, mapped
+// into every other rank's address space.  A call stores each of this rank's
+// values, tagged with the call's epoch, into its slot on every rank, waits
+// (bounded) until every slot of its own area carries the epoch, and sums the
+// slots in rank order, so every rank computes identical bits.
 constexpr int kTpMaxWorld = 8;
 struct TpPeers {
   int world = 1, rank = 0;
-  size_t cap = 0;                      // floats per slot
-  float* buf[kTpMaxWorld] = {};        // each rank's receive area (this process's mapping)
-  unsigned* flag[kTpMaxWorld] = {};    // each rank's flags [2][world]
-  unsigned* epoch = nullptr;           // this rank's call counter (device)
+  size_t cap = 0;                      // words per slot
+  uint64_t* buf[kTpMaxWorld] = {};     // each rank's receive area (this process's mapping)
+  unsigned* epoch = nullptr;           // this rank's call counters, one per exchange CTA (device)
 };
 // Map every rank's receive area (exchanged with an NCCL all-gather of IPC
-// handles); false when peer access is unavailable.
+// handles); false when peer access is unavailable or world is not 2, 4 or 8.
 bool tp_peers_setup(ncclComm_t comm, int world, int rank, size_t cap, cudaStream_t st, TpPeers* out,
                     void** own_mem);
 void tp_peers_release(TpPeers* p, void* own_mem);
-// x[0..n) = sum over ranks of every rank's x[0..n); err is raised when a wait gives up.
-cudaError_t launch_tp_allreduce(const TpPeers& p, float* x, int n, unsigned* err, cudaStream_t st);
+// x[0..n) = sum over ranks of every rank's x[0..n); err is raised when a wait
+// gives up.  pdl: launched as a programmatic dependent of the kernel before it.
+cudaError_t launch_tp_allreduce(const TpPeers& p, float* x, int n, unsigned* err, cudaStream_t st, bool pdl);
 // dst[r * n .. r * n + n) = rank r's src[0..n); the two calls share the epoch sequence.
 cudaError_t launch_tp_allgather(const TpPeers& p, const float* src, int n, float* dst, unsigned* err,
-                                cudaStream_t st);
+                                cudaStream_t st, bool pdl);
 
 }  // namespace prana

@@ -432,9 +432,9 @@ int run_stream(prana_model* m, StreamArgs& a, int epi, int pro, bool pdl) {
 // rank.  The LM head reports each shard's (max, index); an all-gather and the
 // first maximum over ranks give the token.  gather_logits also assembles the
 // full logits rows.
-int tp_sum_rows(prana_model* m, float* x, size_t n, cudaStream_t st) {
+int tp_sum_rows(prana_model* m, float* x, size_t n, cudaStream_t st, bool pdl) {
   if (m->peers_ok && n <= m->peers.cap) {  // small (decode / verify) rows: one-shot over peer memory
-    PRANA_CK(launch_tp_allreduce(m->peers, x, (int)n, m->err, st));
+    PRANA_CK(launch_tp_allreduce(m->peers, x, (int)n, m->err, st, pdl));
     return PRANA_OK;
   }
   const char* why = nullptr;
@@ -445,9 +445,9 @@ int tp_sum_rows(prana_model* m, float* x, size_t n, cudaStream_t st) {
   return PRANA_OK;
 }
 
-int tp_gather(prana_model* m, const float* src, float* dst, size_t n, cudaStream_t st) {
+int tp_gather(prana_model* m, const float* src, float* dst, size_t n, cudaStream_t st, bool pdl) {
   if (m->peers_ok && n <= m->peers.cap) {
-    PRANA_CK(launch_tp_allgather(m->peers, src, (int)n, dst, m->err, st));
+    PRANA_CK(launch_tp_allgather(m->peers, src, (int)n, dst, m->err, st, pdl));
     return PRANA_OK;
   }
   const char* why = nullptr;
@@ -543,7 +543,7 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       a.out = b.x + (size_t)c0 * dim;
       if ((rc = run_stream(m, a, tp && m->tp_rank ? EPI_STORE : EPI_RESID, PRO_F32, pdl))) return rc;
     }
-    if (tp && (rc = tp_sum_rows(m, b.x, (size_t)n * dim, st))) return rc;
+    if (tp && (rc = tp_sum_rows(m, b.x, (size_t)n * dim, st, pdl))) return rc;
     // --- rmsnorm -> gate|up -> silu(gate) * up
     for (int c0 = 0; c0 < n; c0 += 8) {
       const int mc = std::min(8, n - c0);
@@ -571,7 +571,7 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       a.out = b.x + (size_t)c0 * dim;
       if ((rc = run_stream(m, a, tp && m->tp_rank ? EPI_STORE : EPI_RESID, PRO_F32, pdl))) return rc;
     }
-    if (tp && (rc = tp_sum_rows(m, b.x, (size_t)n * dim, st))) return rc;
+    if (tp && (rc = tp_sum_rows(m, b.x, (size_t)n * dim, st, pdl))) return rc;
   }
   if (!head) return PRANA_OK;
   // --- final rmsnorm -> LM head -> argmax (Model::logits, checkpoint.rs:239-248; infer.rs:560-568)
@@ -595,13 +595,13 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
     a.best_val = m->tp_local;
     a.token_out = reinterpret_cast<uint32_t*>(m->tp_local + 8);
     if ((rc = run_stream(m, a, EPI_ARGMAX, PRO_NORM, pdl))) return rc;
-    if ((rc = tp_gather(m, m->tp_local, m->tp_all, 16, st))) return rc;
+    if ((rc = tp_gather(m, m->tp_local, m->tp_all, 16, st, pdl))) return rc;
     PRANA_CK(launch_tp_argmax(m->tp_all, m->tp_world, mc, b.tok_out + c0,
                               (n == 1 && tok_dev) ? const_cast<int*>(tok_dev) : nullptr, st));
     if (gather_logits)
       for (int i = 0; i < mc; i++)
         if ((rc = tp_gather(m, b.logits_l + (size_t)(c0 + i) * m->vocab_l, b.logits + (size_t)(c0 + i) * c.vocab_size,
-                            (size_t)m->vocab_l, st)))
+                            (size_t)m->vocab_l, st, false)))
           return rc;
   }
   return PRANA_OK;
