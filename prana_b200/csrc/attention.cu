@@ -852,7 +852,7 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 __device__ __forceinline__ int swz(int r, int chunk) { return r * 128 + ((chunk ^ (r & 7)) << 4); }
 
 template <int HD>
-__global__ void __launch_bounds__(256, 1) attn_decode_cluster(const __grid_constant__ AttnArgs a, int row0, int n_rows) {
+__global__ void __launch_bounds__(256, 2) attn_decode_cluster(const __grid_constant__ AttnArgs a, int row0, int n_rows) {
   using S = AcSmem<HD>;
   constexpr int NB = S::NB, QROW = S::QROW, KS = HD / 16, NT = HD / 8;
   namespace cg = cooperative_groups;

@@ -229,6 +229,18 @@ __global__ void __launch_bounds__(DG_THREADS, 2) stream_gemv(const StreamArgs g)
     if (lane < DG_RPW * 4 && u_hi - u_lo > 32 * CH) prefetch_group<T>(w, r0, u_lo + 32 * CH, u_hi, lane);
     load(r0, u_lo);
   }
+  // Batch-1 residual epilogue: the residual rows of the warp's first group are
+  // read before the wait too.  The residual stream is never written by the
+  // kernel this one waits on (attention before wo, gate|up before ffn_down):
+  // its last writer finished before that kernel passed its own wait, which it
+  // does before letting this kernel launch.
+  float pre[DG_RPW] = {};
+  constexpr bool kPre = EPI == EPI_RESID && M == 1;
+  if (kPre && ks == 1 && lane == 0 && g_first < n_groups) {
+#pragma unroll
+    for (int r = 0; r < DG_RPW; r++)
+      if (g_first * DG_RPW + r < N) pre[r] = __ldcg(g.out + g_first * DG_RPW + r);
+  }
   __syncthreads();  // barrier initialization is visible to every waiting thread
   pdl_wait();
   if constexpr (PRO == PRO_Q) {
@@ -308,7 +320,15 @@ __global__ void __launch_bounds__(DG_THREADS, 2) stream_gemv(const StreamArgs g)
           v[r] = warp_sum(accv[r]);
           accv[r] = 0.0f;
         }
-        if (lane == 0) finish_rows<EPI>(g, gcur * DG_RPW, 0, v, run_v, run_i);
+        if (lane == 0) {
+          if (kPre && gcur == g_first) {
+#pragma unroll
+            for (int r = 0; r < DG_RPW; r++)
+              if (gcur * DG_RPW + r < N) g.out[gcur * DG_RPW + r] = __fadd_rn(pre[r], v[r]);
+          } else {
+            finish_rows<EPI>(g, gcur * DG_RPW, 0, v, run_v, run_i);
+          }
+        }
       }
       gcur = ng;
       c0 = nc;
