@@ -1187,7 +1187,7 @@ static int cluster_size(int n_kv) {
   if (cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AcSmem<HD>::bytes) ==
           cudaSuccess &&
       cudaFuncSetAttribute((const void*)k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
-    for (int c = AC_MAX; c >= 2 && !best; c -= 2) {
+    for (int c = AC_MAX; c >= 2 && !best; c--) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(c, n_kv);
       cfg.blockDim = dim3(256);

@@ -423,6 +423,16 @@ __global__ void __launch_bounds__(DG_THREADS, 2) stream_gemv(const StreamArgs g)
     }
   }
 
+  // -------------------------------------------------- the next weights toward L2
+  // A warp done with its rows spends the kernel's tail starting the next
+  // matrix's first rows, so DRAM stays busy while the last rows finish and
+  // the next kernel's first loads find L2.
+  if (g.pf_rows > 0 && lane == 0) {
+    const int nw = (int)gridDim.x * DG_WARPS, gw = (int)blockIdx.x * DG_WARPS + wi;
+    const int rp = (g.pf_rows + nw - 1) / nw, r0 = gw * rp;
+    if (r0 < g.pf_rows) prefetch_rows(g.pf_w, r0, min(rp, g.pf_rows - r0));
+  }
+
   // -------------------------------------------------- cross-CTA argmax (Model::argmax: first maximum)
   if constexpr (EPI == EPI_ARGMAX) {
     if (lane < 8) {

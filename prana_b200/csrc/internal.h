@@ -120,6 +120,10 @@ struct StreamArgs {
   int idx_offset;      // ARGMAX: global index of this matrix's row 0 (vocab shard start)
   float* best_val;     // ARGMAX: the maximum itself per activation row (nullable)
   QkvMap qkv;
+  // rows [0, pf_rows) of the next kernel's weights are prefetched toward L2 by
+  // warps that have finished their own rows (pf_rows == 0: none)
+  DevWeight pf_w;
+  int pf_rows;
 };
 
 cudaError_t launch_stream(const StreamArgs& g, int epi, int pro, cudaStream_t st, bool pdl);

@@ -414,6 +414,27 @@ StreamArgs stream_args(prana_model* m, StreamW& w, int mrows, const float* x, co
   return a;
 }
 
+// The next matrix's first rows (up to kPrefetchBytes) for a kernel's tail:
+// wo -> gate|up, gate|up -> down, down -> the next layer's Q|K|V (or the LM
+// head).  Q|K|V prefetches nothing: attention follows it and streams the
+// cache, and wo's rows fetched then measured slower.
+constexpr size_t kPrefetchBytes = size_t(16) << 20;
+void set_prefetch(StreamArgs& a, const StreamW* next) {
+  if (!next || next->w.dw.rows <= 0) return;
+  const DevWeight& w = next->w.dw;
+  size_t row_bytes;
+  switch (w.type) {
+    case T_Q8_0: row_bytes = (size_t)w.cols * 34 / 32; break;
+    case T_Q4_0: row_bytes = (size_t)w.cols * 18 / 32; break;
+    case T_Q4_K: row_bytes = (size_t)w.cols / 256 * 144; break;
+    case T_Q6_K: row_bytes = (size_t)w.cols / 256 * 210; break;
+    default: return;
+  }
+  const size_t rows = kPrefetchBytes / (row_bytes ? row_bytes : 1);
+  a.pf_w = w;
+  a.pf_rows = (int)std::min<size_t>(rows, (size_t)w.rows);
+}
+
 int run_stream(prana_model* m, StreamArgs& a, int epi, int pro, bool pdl) {
   PRANA_CK(launch_stream(a, epi, pro, m->ctx->own, pdl));
   return PRANA_OK;
@@ -541,6 +562,7 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       StreamArgs a = stream_args(m, L.wo, mc, b.att + (size_t)c0 * q_dim, nullptr);
       if (tr) tr->site(a, q_dim);
       a.out = b.x + (size_t)c0 * dim;
+      if (n <= 8) set_prefetch(a, L.fused_gu ? &L.gu : &L.w1);
       if ((rc = run_stream(m, a, tp && m->tp_rank ? EPI_STORE : EPI_RESID, PRO_F32, pdl))) return rc;
     }
     if (tp && (rc = tp_sum_rows(m, b.x, (size_t)n * dim, st, pdl))) return rc;
@@ -551,6 +573,7 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
         StreamArgs a = stream_args(m, L.gu, mc, b.x + (size_t)c0 * dim, L.rms_ffn);
         if (tr) tr->site(a, dim);
         a.out = b.h + (size_t)c0 * hid;
+        if (n <= 8) set_prefetch(a, &L.w2);
         if ((rc = run_stream(m, a, EPI_SWIGLU, PRO_NORM, pdl))) return rc;
       } else {
         StreamArgs a = stream_args(m, L.w1, mc, b.x + (size_t)c0 * dim, L.rms_ffn);
@@ -569,6 +592,12 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       StreamArgs a = stream_args(m, L.w2, mc, b.h + (size_t)c0 * hid, nullptr);
       if (tr) tr->site(a, hid);
       a.out = b.x + (size_t)c0 * dim;
+      if (n <= 8) {
+        if (l + 1 < m->layers.size())
+          set_prefetch(a, &m->layers[l + 1].qkv.front().sw);
+        else if (head)
+          set_prefetch(a, &m->head);
+      }
       if ((rc = run_stream(m, a, tp && m->tp_rank ? EPI_STORE : EPI_RESID, PRO_F32, pdl))) return rc;
     }
     if (tp && (rc = tp_sum_rows(m, b.x, (size_t)n * dim, st, pdl))) return rc;
