@@ -18,6 +18,7 @@
 
 #include <algorithm>
 #include <map>
+#include <tuple>
 #include <mutex>
 
 #include "internal.h"
@@ -871,6 +872,8 @@ __global__ void __launch_bounds__(256, 2) attn_decode_cluster(const __grid_const
   uint64_t* bars = reinterpret_cast<uint64_t*>(w_s + AM_ROWS * AC_MAX);
   const int group = a.n_heads / a.n_kv, VH = n_rows * group;  // VH <= 16
   const int C = (int)cluster.num_blocks(), split = (int)cluster.block_rank();
+  // K clusters per kv head: the positions are split over all K * C CTAs
+  const int K = (int)gridDim.x / C, cq = (int)blockIdx.x / C, gsplit = (int)blockIdx.x;
   const int kvh = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, wi = tid >> 5;
   const int g = lane >> 2, tig = lane & 3;
@@ -881,9 +884,9 @@ __global__ void __launch_bounds__(256, 2) attn_decode_cluster(const __grid_const
   // previous step's kernels finished, so it is safe to read before the wait
   const int pos0 = a.pos_dev ? *a.pos_dev : a.pos0;
   const int L = pos0 + row0 + n_rows;
-  int per = (L + C - 1) / C;
+  int per = (L + K * C - 1) / (K * C);
   per = (per + 15) / 16 * 16;
-  const int t_begin = min(L, split * per), t_end = min(L, t_begin + per);
+  const int t_begin = min(L, gsplit * per), t_end = min(L, t_begin + per);
   const int n_pass = (t_end - t_begin + AC_C - 1) / AC_C;
 
   auto kbox = [&](int st, int b) { return stage0 + st * S::STAGE + b * S::BOX; };
@@ -1076,20 +1079,62 @@ __global__ void __launch_bounds__(256, 2) attn_decode_cluster(const __grid_const
     for (int o_ = AC_MAX / 2; o_ > 0; o_ >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o_);
     if (tid < n_w) {
       w_s[vh * AC_MAX + j] = w;
-      if (j == 0) l_tot[vh] = lw;
+      if (j == 0) {
+        l_tot[vh] = lw;
+        l_tot[AM_ROWS + vh] = mx;  // the cluster's running max
+      }
     }
   }
   __syncthreads();
   const int E = VH * HD, chunk = (E + C - 1) / C;
   const int e_end = min(E, (split + 1) * chunk);
+  // one cluster: final rows; K clusters: this cluster's unnormalized partial
+  // (attn_finish's partial layout, with the K clusters as the splits)
+  const size_t pbase = ((size_t)kvh * K + cq) * VH;
   for (int e = split * chunk + tid; e < e_end; e += 256) {
     const int vh = e / HD, d = e - vh * HD;
     float acc = 0.0f;
     for (int j = 0; j < C; j++) acc = fmaf(*cluster.map_shared_rank(o_s + e, j), w_s[vh * AC_MAX + j], acc);
-    const int row = vh / group, head = kvh * group + vh % group;
+    if (K == 1) {
+      const int row = vh / group, head = kvh * group + vh % group;
+      a.out[(size_t)(row0 + row) * q_stride + head * HD + d] = acc / l_tot[vh];
+    } else {
+      a.part_o[pbase * HD + e] = acc;
+    }
+  }
+  if (K > 1 && split == 0 && tid < VH)
+    reinterpret_cast<float2*>(a.part_ml)[pbase + tid] = make_float2(l_tot[AM_ROWS + tid], l_tot[tid]);
+  cluster.sync();  // every CTA's shared memory stays alive until the others have read it
+  if (K == 1) return;
+
+  // ---- the last of the kv head's K * C CTAs merges the K cluster partials
+  __shared__ unsigned ticket;
+  __syncthreads();
+  if (tid == 0) ticket = ticket_acq_rel(a.counters + kvh);
+  __syncthreads();
+  if (ticket != (unsigned)(K * C) - 1) return;
+  const size_t hb = (size_t)kvh * K * VH;
+  if (tid < VH) {
+    float mx = -INFINITY;
+    for (int q = 0; q < K; q++) mx = fmaxf(mx, __ldcg(reinterpret_cast<const float2*>(a.part_ml) + hb + q * VH + tid).x);
+    float l = 0.0f;
+    for (int q = 0; q < K; q++) {
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + hb + q * VH + tid);
+      const float wq = ml.x == -INFINITY ? 0.0f : expf(ml.x - mx);
+      w_s[tid * AC_MAX + q] = wq;
+      l = fmaf(ml.y, wq, l);
+    }
+    l_tot[tid] = l;
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += 256) {
+    const int vh = e / HD;
+    float acc = 0.0f;
+    for (int q = 0; q < K; q++) acc = fmaf(__ldcg(a.part_o + (hb + (size_t)q * VH) * HD + e), w_s[vh * AC_MAX + q], acc);
+    const int row = vh / group, head = kvh * group + vh % group, d = e - vh * HD;
     a.out[(size_t)(row0 + row) * q_stride + head * HD + d] = acc / l_tot[vh];
   }
-  cluster.sync();  // every CTA's shared memory stays alive until the others have read it
+  if (tid == 0) a.counters[kvh] = 0u;
 }
 
 template <int HD, bool MMA>
@@ -1170,24 +1215,32 @@ void attn_make_maps(AttnArgs& a, int positions) {
     a.has_tm = 1;
 }
 
-// Cluster size for n_kv kv heads: the largest C <= 16 such that all n_kv
-// clusters of C CTAs are resident at once (asked once per device and n_kv);
-// 0 when none fits.
+// Cluster shape for n_kv kv heads: C CTAs per cluster (the largest C <= 16
+// for which all n_kv clusters are resident at once) and, when C reaches 16
+// with room to spare (few kv heads: a tensor-parallel shard), K clusters per
+// kv head whose partials meet through global memory; K is capped by the split
+// scratch (max_k) and by AC_MAX.  Asked once per device, n_kv and max_k.
+// C == 0: no cluster fits.
+struct ClusterPlan {
+  int c = 0, k = 1;
+};
 template <int HD>
-static int cluster_size(int n_kv) {
+static ClusterPlan cluster_plan(int n_kv, int max_k) {
   static std::mutex mu;
-  static std::map<std::pair<int, int>, int> cache;
+  static std::map<std::tuple<int, int, int>, ClusterPlan> cache;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return {};
+  if (max_k > AC_MAX) max_k = AC_MAX;
+  if (max_k < 1) max_k = 1;
   std::lock_guard<std::mutex> lock(mu);
-  auto it = cache.find({dev, n_kv});
+  auto it = cache.find({dev, n_kv, max_k});
   if (it != cache.end()) return it->second;
   auto k = attn_decode_cluster<HD>;
-  int best = 0;
+  ClusterPlan best;
   if (cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AcSmem<HD>::bytes) ==
           cudaSuccess &&
       cudaFuncSetAttribute((const void*)k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
-    for (int c = AC_MAX; c >= 2 && !best; c--) {
+    for (int c = AC_MAX; c >= 2 && !best.c; c--) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(c, n_kv);
       cfg.blockDim = dim3(256);
@@ -1200,23 +1253,29 @@ static int cluster_size(int n_kv) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, (const void*)k, &cfg) == cudaSuccess && n >= n_kv) best = c;
+      if (cudaOccupancyMaxActiveClusters(&n, (const void*)k, &cfg) == cudaSuccess && n >= n_kv) {
+        best.c = c;
+        // several clusters per kv head only at full cluster size: below it the
+        // global merge costs more than the extra CTAs gain
+        if (c == AC_MAX) best.k = std::min(max_k, n / n_kv);
+      }
     }
   }
   cudaGetLastError();
-  cache[{dev, n_kv}] = best;
+  cache[{dev, n_kv, max_k}] = best;
   return best;
 }
 
 template <int HD>
-static cudaError_t cluster_go(const AttnArgs& a, int c, cudaStream_t st, bool pdl) {
+static cudaError_t cluster_go(const AttnArgs& a, ClusterPlan pl, cudaStream_t st, bool pdl) {
+  const int c = pl.c;
   const int group = a.n_heads / a.n_kv;
   const int max_rows = AM_ROWS / group;
   for (int row0 = 0; row0 < a.m; row0 += max_rows) {
     const int n_rows = min(max_rows, a.m - row0);
     void* args[] = {const_cast<AttnArgs*>(&a), (void*)&row0, (void*)&n_rows};
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(c, a.n_kv);
+    cfg.gridDim = dim3(c * pl.k, a.n_kv);
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = AcSmem<HD>::bytes;
     cfg.stream = st;
@@ -1249,14 +1308,14 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
     case 48: return decode_go<48, false>(a, st, pdl);
     case 64: {
       if (!mma) return decode_go<64, false>(a, st, pdl);
-      const int c = a.has_tm ? cluster_size<64>(a.n_kv) : 0;
-      return c ? cluster_go<64>(a, c, st, pdl) : decode_go<64, true>(a, st, pdl);
+      const ClusterPlan pl = a.has_tm ? cluster_plan<64>(a.n_kv, a.n_splits) : ClusterPlan{};
+      return pl.c ? cluster_go<64>(a, pl, st, pdl) : decode_go<64, true>(a, st, pdl);
     }
     case 96: return decode_go<96, false>(a, st, pdl);
     case 128: {
       if (!mma) return decode_go<128, false>(a, st, pdl);
-      const int c = a.has_tm ? cluster_size<128>(a.n_kv) : 0;
-      return c ? cluster_go<128>(a, c, st, pdl) : decode_go<128, true>(a, st, pdl);
+      const ClusterPlan pl = a.has_tm ? cluster_plan<128>(a.n_kv, a.n_splits) : ClusterPlan{};
+      return pl.c ? cluster_go<128>(a, pl, st, pdl) : decode_go<128, true>(a, st, pdl);
     }
     case 256: return decode_go<256, false>(a, st, pdl);
   }
