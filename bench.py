@@ -14,6 +14,9 @@ token.  Weights stream from HBM every step (4.2 GB >> the 126 MB L2).
           copies larger than L2, timed in a CUDA graph with events on its stream
   cpu_baseline  the CPU oracle (C restatement of Prana's AVX2/VNNI path and
           worker pool) decoding the same model from the same KV contents
+  batch_decode  (one GPU) batch 16: 16 independent sequences with their own KV
+          caches at the same context, one token each per prana_forward_multi
+          call, host ids in and out (the BASELINE config's bs 16)
 
 Both arms start from the same seeded KV contents (4096 rows of N(0, 0.5) f16
 per layer) instead of a 4096-token prefill, so the CPU arm finishes in minutes;
@@ -21,8 +24,9 @@ the bytes a decode step reads are the same either way.
 
 --gpus N > 1 (under torchrun): the model is tensor-parallel over the N GPUs
 (column-split Q/K/V and gate|up, row-split wo and ffn_down, vocabulary-split
-LM head; an NCCL all-reduce after wo and after ffn_down), one sequence, so the
-work per token is fixed (strong scaling); value is that sequence's tok/s.
+LM head; a one-shot all-reduce over NVLink peer memory after wo and after
+ffn_down), one sequence, so the work per token is fixed (strong scaling);
+value is that sequence's tok/s.
 --impl reference: the CPU oracle alone on the host cores (rank 0).
 """
 from __future__ import annotations
@@ -57,6 +61,8 @@ def parse():
     p.add_argument("--model-dir", default=os.environ.get("PRANA_BENCH_DIR", "/dev/shm/prana_bench"))
     p.add_argument("--cpu-seconds", type=float, default=20.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--batch-seqs", type=int, default=16,
+                   help="also time this many independent sequences per step (0: skip; single GPU only)")
     return p.parse_args()
 
 
@@ -254,6 +260,43 @@ def gemv_roofline(torch, peak_gbs, iters=64):
             "us_per_launch": round(us, 2), "algorithmic_bytes": alg}
 
 
+def batch_decode(torch, model, args, stream, steps=24, warmup=3):
+    """Decode at batch B = args.batch_seqs: B independent sequences, each with its
+    own KV cache at the same context, one token each per prana_forward_multi
+    call (host token ids in, host argmax out).  The reference has no
+    multi-sequence batch; its equivalent is B forward calls per step."""
+    from prana_b200 import model as pm
+
+    c, n = model.config, args.batch_seqs
+    caches = [pm.KvCache(model, args.ctx + steps + warmup + 8) for _ in range(n)]
+    try:
+        for layer in range(c.n_layers):
+            for is_v in (False, True):
+                rows = seeded_kv_rows(layer, is_v, args.ctx, c.kv_dim())
+                for kv in caches:
+                    kv.write(layer, is_v, rows)
+        toks = (np.arange(n, dtype=np.uint32) * 7919 + 17) % c.vocab_size
+        pos = args.ctx
+        for _ in range(warmup):
+            _, toks = pm.forward_multi(model, caches, toks, [pos] * n, want_logits=False)
+            pos += 1
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            _, toks = pm.forward_multi(model, caches, toks, [pos] * n, want_logits=False)
+            pos += 1
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        return {"value": round(n * 1000.0 / ms, 2), "unit": "tok/s", "sequences": n, "ms_per_step": round(ms, 3),
+                "steps": steps, "ctx": args.ctx, "h2d_bytes_per_step": 4 * n + 8 * n, "d2h_bytes_per_step": 4 * n,
+                "path": "prana_forward_multi: GEMV rows in chunks of 8, attention per sequence"}
+    finally:
+        for kv in caches:
+            kv.close()
+
+
 def prana_arm(args):
     import torch
 
@@ -334,6 +377,7 @@ def prana_arm(args):
         t = torch.tensor([ms, ms_e2e], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, ms_e2e = float(t[0]), float(t[1])
+    batch = batch_decode(torch, model, args, stream) if world == 1 and args.batch_seqs > 0 else None
     roof = gemv_roofline(torch, peak) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -358,7 +402,7 @@ def prana_arm(args):
             "roofline": roof, "peak_kind": peak_kind,
             "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": round(step_gbs, 1),
                               "frac": round(step_gbs / peak, 4)},
-            "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches_per_step(spec, world, model.peer_exchange) * args.steps,
+            "cpu_baseline": cpu, "batch_decode": batch, "clocks": clk, "gpu_launches": launches_per_step(spec, world, model.peer_exchange) * args.steps,
             "load_s": round(t_load, 1),
         }
         print(json.dumps(line), flush=True)

@@ -188,6 +188,13 @@ int prana_prefill(prana_model *m, prana_kv *kv, const uint32_t *tokens, size_t n
  * and per-row argmax (may be NULL) */
 int prana_forward_batch(prana_model *m, prana_kv *kv, const uint32_t *tokens, size_t n, size_t pos0,
                         float *logits, uint32_t *argmax);
+/* n independent sequences, one token each: row i is forward_impl (infer.rs:142-211)
+ * for tokens[i] at positions[i] over caches[i] (n distinct caches of this model),
+ * with the weights streamed once per 8 rows.  The reference has no such batch:
+ * its equivalent is n forward calls.  logits [n, vocab] and argmax [n] may be NULL.
+ * Single-GPU models only. */
+int prana_forward_multi(prana_model *m, prana_kv *const *caches, size_t n, const uint32_t *tokens,
+                        const size_t *positions, float *logits, uint32_t *argmax);
 /* generate (infer.rs:696-771), greedy, over token ids; stop_id < 0 disables stopping.
  * out must hold `steps` ids; *n_out receives the count. */
 int prana_generate(prana_model *m, const uint32_t *prompt, size_t p, size_t steps, int64_t stop_id,

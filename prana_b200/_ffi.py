@@ -88,6 +88,7 @@ SIGNATURES = {
     "prana_kv_write": [P, SZ, I, SZ, P],
     "prana_prefill": [P, P, P, SZ],
     "prana_forward_batch": [P, P, P, SZ, SZ, P, P],
+    "prana_forward_multi": [P, P, SZ, P, P, P, P],
     "prana_generate": [P, P, SZ, SZ, C.c_int64, P, C.POINTER(SZ)],
     "prana_generate_speculative": [P, P, P, SZ, SZ, SZ, C.c_int64, P, C.POINTER(SZ), P],
     "prana_decode_begin": [P, P, C.c_uint32, SZ],

@@ -109,7 +109,8 @@ __device__ __forceinline__ void finish_rows(const StreamArgs& g, int r0, int m, 
         va = __fadd_rn(va, qm.bias[s][ra]);
         vb = __fadd_rn(vb, qm.bias[s][rb]);
       }
-      const int pos = (qm.pos_dev ? *qm.pos_dev : qm.pos0) + m;
+      const SeqRow* sr = qm.rows ? qm.rows + m : nullptr;
+      const int pos = sr ? sr->pos : (qm.pos_dev ? *qm.pos_dev : qm.pos0) + m;
       if (kind != 2) {
         const float c = qm.cos_t[(size_t)pos * half + j], sn = qm.sin_t[(size_t)pos * half + j];
         const float a0 = va, b0 = vb;
@@ -120,8 +121,8 @@ __device__ __forceinline__ void finish_rows(const StreamArgs& g, int r0, int m, 
         qm.q_out[(size_t)m * qm.q_dim + ra] = va;
         qm.q_out[(size_t)m * qm.q_dim + rb] = vb;
       } else {
-        __half* cache = kind == 1 ? qm.kc : qm.vc;
-        if (pos < qm.cap) {
+        __half* cache = sr ? (kind == 1 ? sr->k : sr->v) + (size_t)qm.layer * sr->lstride : (kind == 1 ? qm.kc : qm.vc);
+        if (pos < (sr ? sr->cap : qm.cap)) {
           cache[(size_t)pos * qm.kv_dim + ra] = __float2half_rn(va);
           cache[(size_t)pos * qm.kv_dim + rb] = __float2half_rn(vb);
         }

@@ -76,6 +76,16 @@ enum : int { EPI_QKV = 3, EPI_SWIGLU = 4 };
 
 // Q|K|V epilogue: the stored matrix concatenates projections of one weight
 // type; RoPE partners are adjacent stored rows (NeoX rows permuted at upload).
+// One independent sequence of a multi-sequence decode pass: its KV cache
+// (layer-0 base and per-layer stride, in halves), capacity and position.
+struct SeqRow {
+  __half* k;
+  __half* v;
+  size_t lstride;
+  int pos;
+  int cap;
+};
+
 struct QkvMap {
   int nseg;
   int seg_start[4];  // stored-row offsets of each projection (+ end)
@@ -92,6 +102,8 @@ struct QkvMap {
   __half* vc;
   float* k_f32;
   float* v_f32;
+  const SeqRow* rows;  // non-null: activation row m belongs to sequence rows[m] (cache, position)
+  int layer;           // with rows: the layer whose cache rows are written
 };
 
 struct StreamArgs {

@@ -479,8 +479,17 @@ int tp_gather(prana_model* m, const float* src, float* dst, size_t n, cudaStream
   return PRANA_OK;
 }
 
+// Rows of independent sequences (prana_forward_multi): row i decodes one token
+// of sequence i at its own position with its own KV cache.
+struct Multi {
+  const SeqRow* rows_dev;    // [n] device: cache bases, strides, positions
+  prana_kv* const* kvs;      // [n] the caches (attention runs per sequence)
+  const size_t* pos;         // [n] host copy of the positions
+};
+
 int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* toks_dev, const int* tok_dev, int pos0,
-                 const int* pos_dev, int mode, bool head, bool pdl, Trace* tr = nullptr, bool gather_logits = true) {
+                 const int* pos_dev, int mode, bool head, bool pdl, Trace* tr = nullptr, bool gather_logits = true,
+                 const Multi* mu = nullptr) {
   const auto& c = m->cfg;
   cudaStream_t st = m->ctx->own;
   const bool tp = m->tp_world > 1;
@@ -524,6 +533,10 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
           q.k_f32 = b.kf + (size_t)c0 * kv_dim;
           q.v_f32 = b.vf + (size_t)c0 * kv_dim;
         }
+        if (mu) {
+          q.rows = mu->rows_dev + c0;
+          q.layer = (int)l;
+        }
         if ((rc = run_stream(m, a, EPI_QKV, PRO_NORM, pdl))) return rc;
       }
       first_part = false;
@@ -533,28 +546,33 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       PrefillAttnArgs a{b.q, b.kf, b.vf, n, (int)m->heads_l, (int)m->kv_heads_l, hd, b.att};
       PRANA_CK(launch_attn_prefill(a, st));
     } else {
-      AttnArgs a{};
-      a.q = b.q;
-      a.kc = kc;
-      a.vc = vc;
-      a.m = n;
-      a.pos0 = pos0;
-      a.pos_dev = pos_dev;
-      a.n_heads = (int)m->heads_l;
-      a.n_kv = (int)m->kv_heads_l;
-      a.hd = hd;
-      a.n_splits = kv->n_splits;
-      a.part_ml = kv->part_ml;
-      a.part_o = kv->part_o;
-      a.counters = kv->counters;
-      a.out = b.att;
-      a.err = m->err;
-      if ((size_t)l < kv->maps.size()) {
-        a.tm_k = kv->maps[l].tm_k;
-        a.tm_v = kv->maps[l].tm_v;
-        a.has_tm = kv->maps[l].has_tm;
+      // one launch over the rows of one cache, or one per sequence
+      for (int s0 = 0; s0 < (mu ? n : 1); s0++) {
+        prana_kv* kq = mu ? mu->kvs[s0] : kv;
+        const size_t ls = kq->positions * (size_t)kv_dim;
+        AttnArgs a{};
+        a.q = b.q + (size_t)s0 * q_dim;
+        a.kc = mu ? kq->k + l * ls : kc;
+        a.vc = mu ? kq->v + l * ls : vc;
+        a.m = mu ? 1 : n;
+        a.pos0 = mu ? (int)mu->pos[s0] : pos0;
+        a.pos_dev = mu ? nullptr : pos_dev;
+        a.n_heads = (int)m->heads_l;
+        a.n_kv = (int)m->kv_heads_l;
+        a.hd = hd;
+        a.n_splits = kq->n_splits;
+        a.part_ml = kq->part_ml;
+        a.part_o = kq->part_o;
+        a.counters = kq->counters;
+        a.out = b.att + (size_t)s0 * q_dim;
+        a.err = m->err;
+        if ((size_t)l < kq->maps.size()) {
+          a.tm_k = kq->maps[l].tm_k;
+          a.tm_v = kq->maps[l].tm_v;
+          a.has_tm = kq->maps[l].has_tm;
+        }
+        PRANA_CK(launch_attn_decode(a, st, pdl));
       }
-      PRANA_CK(launch_attn_decode(a, st, pdl));
     }
     // --- quantize(attn) -> wo -> residual
     for (int c0 = 0; c0 < n; c0 += 8) {
@@ -1212,6 +1230,49 @@ int prana_forward_batch(prana_model* m, prana_kv* kv, const uint32_t* tokens, si
   if (argmax) PRANA_CK(cudaMemcpyAsync(argmax, b->tok_out, n * 4, cudaMemcpyDeviceToHost, st));
   PRANA_CK(cudaStreamSynchronize(st));
   kv->loop_active = false;
+  return check_err(m);
+  API_END
+}
+
+int prana_forward_multi(prana_model* m, prana_kv* const* kvs, size_t n, const uint32_t* tokens,
+                        const size_t* positions, float* logits, uint32_t* argmax) {
+  API_BEGIN
+  NEED(m && kvs && tokens && positions, "null argument");
+  if (!n) return PRANA_OK;
+  NEED(m->tp_world == 1, "multi-sequence decode runs on a single-GPU model");
+  const size_t kv_dim = (size_t)(m->kv_heads_l * m->cfg.head_dim);
+  std::vector<SeqRow> rows(n);
+  for (size_t i = 0; i < n; i++) {
+    NEED(kvs[i] && kvs[i]->m == m, "cache %zu is null or of another model", i);
+    NEED(positions[i] < kvs[i]->positions, "sequence %zu: position %zu beyond kv capacity %zu", i, positions[i],
+         kvs[i]->positions);
+    NEED(tokens[i] < (uint64_t)m->cfg.vocab_size, "token out of vocabulary");
+    for (size_t j = 0; j < i; j++) NEED(kvs[j] != kvs[i], "sequences %zu and %zu share a cache", j, i);
+    rows[i] = SeqRow{kvs[i]->k, kvs[i]->v, kvs[i]->positions * kv_dim, (int)positions[i], (int)kvs[i]->positions};
+  }
+  DevScope ds(m->ctx->device);
+  cudaStream_t st = m->ctx->own;
+  std::unique_ptr<Bufs> tmp;
+  Bufs* b = m->dec.get();
+  if (n > b->rows) {
+    tmp.reset(new Bufs());
+    int rc = make_bufs(m, n, false, *tmp);
+    if (rc) return rc;
+    b = tmp.get();
+  }
+  SeqRow* rows_dev = nullptr;
+  Bufs scratch;
+  if (int rc = scratch.alloc(rows_dev, n)) return rc;
+  PRANA_CK(cudaMemcpyAsync(b->toks, tokens, n * 4, cudaMemcpyHostToDevice, st));
+  PRANA_CK(cudaMemcpyAsync(rows_dev, rows.data(), n * sizeof(SeqRow), cudaMemcpyHostToDevice, st));
+  const Multi mu{rows_dev, kvs, positions};
+  int rc = enqueue_rows(m, kvs[0], *b, (int)n, b->toks, nullptr, 0, nullptr, MODE_CACHE, true, false, nullptr,
+                        logits != nullptr, &mu);
+  if (rc) return rc;
+  if (logits) PRANA_CK(cudaMemcpyAsync(logits, b->logits, n * (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, st));
+  if (argmax) PRANA_CK(cudaMemcpyAsync(argmax, b->tok_out, n * 4, cudaMemcpyDeviceToHost, st));
+  PRANA_CK(cudaStreamSynchronize(st));
+  for (size_t i = 0; i < n; i++) kvs[i]->loop_active = false;
   return check_err(m);
   API_END
 }

@@ -189,6 +189,22 @@ def forward_batch(model: Model, cache: KvCache, tokens, pos0: int, want_logits: 
     return logits, am
 
 
+def forward_multi(model: Model, caches, tokens, positions, want_logits: bool = True):
+    """One token for each of len(caches) independent sequences (row i: tokens[i]
+    at positions[i] over caches[i]); returns (logits [n, vocab] or None, argmax [n]).
+    The reference's equivalent is one forward (infer.rs:142-211) per sequence."""
+    t = _u32(tokens)
+    n = t.size
+    assert len(caches) == n and len(positions) == n
+    handles = (C.c_void_p * n)(*[c.handle.value for c in caches])
+    pos = np.ascontiguousarray(positions, dtype=np.uint64)
+    logits = np.empty((n, model.config.vocab_size), dtype=np.float32) if want_logits else None
+    am = np.empty(n, dtype=np.uint32)
+    call("prana_forward_multi", model.handle, handles, n, t.ctypes.data_as(C.c_void_p), pos.ctypes.data_as(C.c_void_p),
+         logits.ctypes.data_as(C.c_void_p) if logits is not None else None, am.ctypes.data_as(C.c_void_p))
+    return logits, am
+
+
 def generate(model: Model, prompt, steps: int, stop_id: int = -1) -> np.ndarray:
     """generate (infer.rs:696-771), greedy, over token ids."""
     p = _u32(prompt)
