@@ -879,10 +879,19 @@ __global__ void __launch_bounds__(256, 2) attn_decode_cluster(const __grid_const
   const int g = lane >> 2, tig = lane & 3;
   const int q_stride = a.n_heads * HD;
   const float scale = 1.0f / sqrtf((float)HD);
+  // several sequences: this CTA's one (its cache views, position, scratch, q / out row)
+  const AttnSeq* sq = a.seqs ? a.seqs + blockIdx.z : nullptr;
+  const CUtensorMap* tm_k = sq ? &sq->tm_k : &a.tm_k;
+  const CUtensorMap* tm_v = sq ? &sq->tm_v : &a.tm_v;
+  const float* qz = a.q + (sq ? (size_t)blockIdx.z * q_stride : 0);
+  float* outz = a.out + (sq ? (size_t)blockIdx.z * q_stride : 0);
+  float* part_ml = sq ? sq->part_ml : a.part_ml;
+  float* part_o = sq ? sq->part_o : a.part_o;
+  unsigned* counters = sq ? sq->counters : a.counters;
 
   // the position counter of a graph-driven step was advanced before the
   // previous step's kernels finished, so it is safe to read before the wait
-  const int pos0 = a.pos_dev ? *a.pos_dev : a.pos0;
+  const int pos0 = sq ? sq->pos0 : (a.pos_dev ? *a.pos_dev : a.pos0);
   const int L = pos0 + row0 + n_rows;
   int per = (L + K * C - 1) / (K * C);
   per = (per + 15) / 16 * 16;
@@ -897,8 +906,8 @@ __global__ void __launch_bounds__(256, 2) attn_decode_cluster(const __grid_const
     mbar_arrive_expect_tx(&bars[st], (uint32_t)(2 * NB * S::BOX));
 #pragma unroll
     for (int b = 0; b < NB; b++) {
-      tma_load_3d(kbox(st, b), &a.tm_k, b * AC_BOX, kvh, t0, &bars[st]);
-      tma_load_3d(vbox(st, b), &a.tm_v, b * AC_BOX, kvh, t0, &bars[st]);
+      tma_load_3d(kbox(st, b), tm_k, b * AC_BOX, kvh, t0, &bars[st]);
+      tma_load_3d(vbox(st, b), tm_v, b * AC_BOX, kvh, t0, &bars[st]);
     }
   };
   // a pass holding only rows written by earlier steps may load before the wait
@@ -921,7 +930,7 @@ __global__ void __launch_bounds__(256, 2) attn_decode_cluster(const __grid_const
   for (int i = tid; i < AM_ROWS * HD; i += 256) {
     const int vh = i / HD, d = i - vh * HD;
     const int off = q_off[vh];
-    const float x = off >= 0 ? a.q[off + d] : 0.0f;
+    const float x = off >= 0 ? qz[off + d] : 0.0f;
     const __half h = __float2half_rn(x);
     qh_s[vh * QROW + d] = h;
     ql_s[vh * QROW + d] = __float2half_rn(x - __half2float(h));
@@ -1097,29 +1106,29 @@ __global__ void __launch_bounds__(256, 2) attn_decode_cluster(const __grid_const
     for (int j = 0; j < C; j++) acc = fmaf(*cluster.map_shared_rank(o_s + e, j), w_s[vh * AC_MAX + j], acc);
     if (K == 1) {
       const int row = vh / group, head = kvh * group + vh % group;
-      a.out[(size_t)(row0 + row) * q_stride + head * HD + d] = acc / l_tot[vh];
+      outz[(size_t)(row0 + row) * q_stride + head * HD + d] = acc / l_tot[vh];
     } else {
-      a.part_o[pbase * HD + e] = acc;
+      part_o[pbase * HD + e] = acc;
     }
   }
   if (K > 1 && split == 0 && tid < VH)
-    reinterpret_cast<float2*>(a.part_ml)[pbase + tid] = make_float2(l_tot[AM_ROWS + tid], l_tot[tid]);
+    reinterpret_cast<float2*>(part_ml)[pbase + tid] = make_float2(l_tot[AM_ROWS + tid], l_tot[tid]);
   cluster.sync();  // every CTA's shared memory stays alive until the others have read it
   if (K == 1) return;
 
   // ---- the last of the kv head's K * C CTAs merges the K cluster partials
   __shared__ unsigned ticket;
   __syncthreads();
-  if (tid == 0) ticket = ticket_acq_rel(a.counters + kvh);
+  if (tid == 0) ticket = ticket_acq_rel(counters + kvh);
   __syncthreads();
   if (ticket != (unsigned)(K * C) - 1) return;
   const size_t hb = (size_t)kvh * K * VH;
   if (tid < VH) {
     float mx = -INFINITY;
-    for (int q = 0; q < K; q++) mx = fmaxf(mx, __ldcg(reinterpret_cast<const float2*>(a.part_ml) + hb + q * VH + tid).x);
+    for (int q = 0; q < K; q++) mx = fmaxf(mx, __ldcg(reinterpret_cast<const float2*>(part_ml) + hb + q * VH + tid).x);
     float l = 0.0f;
     for (int q = 0; q < K; q++) {
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + hb + q * VH + tid);
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(part_ml) + hb + q * VH + tid);
       const float wq = ml.x == -INFINITY ? 0.0f : expf(ml.x - mx);
       w_s[tid * AC_MAX + q] = wq;
       l = fmaf(ml.y, wq, l);
@@ -1130,11 +1139,11 @@ __global__ void __launch_bounds__(256, 2) attn_decode_cluster(const __grid_const
   for (int e = tid; e < E; e += 256) {
     const int vh = e / HD;
     float acc = 0.0f;
-    for (int q = 0; q < K; q++) acc = fmaf(__ldcg(a.part_o + (hb + (size_t)q * VH) * HD + e), w_s[vh * AC_MAX + q], acc);
+    for (int q = 0; q < K; q++) acc = fmaf(__ldcg(part_o + (hb + (size_t)q * VH) * HD + e), w_s[vh * AC_MAX + q], acc);
     const int row = vh / group, head = kvh * group + vh % group, d = e - vh * HD;
-    a.out[(size_t)(row0 + row) * q_stride + head * HD + d] = acc / l_tot[vh];
+    outz[(size_t)(row0 + row) * q_stride + head * HD + d] = acc / l_tot[vh];
   }
-  if (tid == 0) a.counters[kvh] = 0u;
+  if (tid == 0) counters[kvh] = 0u;
 }
 
 template <int HD, bool MMA>
@@ -1267,7 +1276,7 @@ static ClusterPlan cluster_plan(int n_kv, int max_k) {
 }
 
 template <int HD>
-static cudaError_t cluster_go(const AttnArgs& a, ClusterPlan pl, cudaStream_t st, bool pdl) {
+static cudaError_t cluster_go(const AttnArgs& a, ClusterPlan pl, cudaStream_t st, bool pdl, int n_seq = 1) {
   const int c = pl.c;
   const int group = a.n_heads / a.n_kv;
   const int max_rows = AM_ROWS / group;
@@ -1275,7 +1284,7 @@ static cudaError_t cluster_go(const AttnArgs& a, ClusterPlan pl, cudaStream_t st
     const int n_rows = min(max_rows, a.m - row0);
     void* args[] = {const_cast<AttnArgs*>(&a), (void*)&row0, (void*)&n_rows};
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(c * pl.k, a.n_kv);
+    cfg.gridDim = dim3(c * pl.k, a.n_kv, n_seq);
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = AcSmem<HD>::bytes;
     cfg.stream = st;
@@ -1320,6 +1329,16 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
     case 256: return decode_go<256, false>(a, st, pdl);
   }
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_attn_decode_seqs(const AttnArgs& a, int n_seq, cudaStream_t st, bool pdl) {
+  if (!a.seqs || a.m != 1 || n_seq < 1 || a.n_kv <= 0 || a.n_heads % a.n_kv || a.n_splits < 1)
+    return cudaErrorInvalidValue;
+  if (a.n_heads / a.n_kv > AM_ROWS || !a.has_tm || !(a.hd == 64 || a.hd == 128) || n_seq > 65535)
+    return cudaErrorNotSupported;
+  const ClusterPlan pl = a.hd == 64 ? cluster_plan<64>(a.n_kv, a.n_splits) : cluster_plan<128>(a.n_kv, a.n_splits);
+  if (!pl.c) return cudaErrorNotSupported;
+  return a.hd == 64 ? cluster_go<64>(a, pl, st, pdl, n_seq) : cluster_go<128>(a, pl, st, pdl, n_seq);
 }
 
 template <int HD>

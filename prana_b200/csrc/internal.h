@@ -42,6 +42,19 @@ struct GemvArgs {
   float* trace_s;   // [m][K/32]
 };
 
+// One sequence of a decode-attention launch over several independent
+// sequences (blockIdx.z): its cache views, position and split scratch.
+struct AttnSeq {
+  CUtensorMap tm_k;  // first: 64-byte aligned in the device array
+  CUtensorMap tm_v;
+  const __half* kc;
+  const __half* vc;
+  float* part_ml;
+  float* part_o;
+  unsigned* counters;
+  int pos0;
+};
+
 struct AttnArgs {
   // TMA views of this layer's K and V cache ({hd, n_kv, positions}, 128-byte
   // swizzled boxes of 64 x 1 x 128); has_tm = 0 when they could not be made
@@ -61,6 +74,9 @@ struct AttnArgs {
   unsigned* counters;    // [n_kv], zero between launches
   float* out;            // [m][n_heads*hd]
   unsigned* err;         // device error flag for bounded waits (nullable)
+  // non-null: gridDim.z sequences, sequence z = seqs[z] (one query row each,
+  // at q / out row z); seqs replaces tm_*, kc, vc, pos0, part_*, counters
+  const AttnSeq* seqs;
 };
 
 struct PrefillAttnArgs {
@@ -168,6 +184,9 @@ int attn_splits(int positions, int n_kv, int hd, int sm_count);
 // a.hd set); leaves has_tm = 0 for head sizes the TMA kernel does not take.
 void attn_make_maps(AttnArgs& a, int positions);
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
+// a.seqs set, a.m == 1: n_seq sequences in one launch (head dims 64 / 128 with
+// tensor maps); cudaErrorNotSupported when the shape needs per-sequence launches
+cudaError_t launch_attn_decode_seqs(const AttnArgs& a, int n_seq, cudaStream_t st, bool pdl);
 cudaError_t launch_attn_prefill(const PrefillAttnArgs& a, cudaStream_t st);
 
 }  // namespace prana

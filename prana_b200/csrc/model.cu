@@ -483,8 +483,11 @@ int tp_gather(prana_model* m, const float* src, float* dst, size_t n, cudaStream
 // of sequence i at its own position with its own KV cache.
 struct Multi {
   const SeqRow* rows_dev;    // [n] device: cache bases, strides, positions
-  prana_kv* const* kvs;      // [n] the caches (attention runs per sequence)
+  prana_kv* const* kvs;      // [n] the caches
   const size_t* pos;         // [n] host copy of the positions
+  const AttnSeq* attn_dev;   // [layers][n] device: per-sequence attention views (one launch per layer)
+  int min_splits;            // the smallest split scratch among the caches
+  bool all_tm;               // every cache has tensor maps for every layer
 };
 
 int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* toks_dev, const int* tok_dev, int pos0,
@@ -546,8 +549,24 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       PrefillAttnArgs a{b.q, b.kf, b.vf, n, (int)m->heads_l, (int)m->kv_heads_l, hd, b.att};
       PRANA_CK(launch_attn_prefill(a, st));
     } else {
-      // one launch over the rows of one cache, or one per sequence
-      for (int s0 = 0; s0 < (mu ? n : 1); s0++) {
+      // one launch over the rows of one cache, over all sequences, or one per sequence
+      cudaError_t es = cudaErrorNotSupported;
+      if (mu) {
+        AttnArgs a{};
+        a.q = b.q;
+        a.out = b.att;
+        a.m = 1;
+        a.n_heads = (int)m->heads_l;
+        a.n_kv = (int)m->kv_heads_l;
+        a.hd = hd;
+        a.n_splits = mu->min_splits;
+        a.has_tm = mu->all_tm ? 1 : 0;
+        a.err = m->err;
+        a.seqs = mu->attn_dev + l * (size_t)n;
+        es = launch_attn_decode_seqs(a, n, st, pdl);
+        if (es != cudaErrorNotSupported) PRANA_CK(es);
+      }
+      for (int s0 = 0; es == cudaErrorNotSupported && s0 < (mu ? n : 1); s0++) {
         prana_kv* kq = mu ? mu->kvs[s0] : kv;
         const size_t ls = kq->positions * (size_t)kv_dim;
         AttnArgs a{};
@@ -1260,13 +1279,42 @@ int prana_forward_multi(prana_model* m, prana_kv* const* kvs, size_t n, const ui
     if (rc) return rc;
     b = tmp.get();
   }
+  // per layer and sequence: the cache's tensor maps, scratch and position
+  const size_t nl = m->layers.size();
+  std::vector<AttnSeq> att(nl * n);
+  int min_splits = INT_MAX;
+  bool all_tm = true;
+  for (size_t i = 0; i < n; i++) {
+    prana_kv* kq = kvs[i];
+    min_splits = std::min(min_splits, kq->n_splits);
+    for (size_t l = 0; l < nl; l++) {
+      AttnSeq& q = att[l * n + i];
+      q = AttnSeq{};
+      const size_t ls = kq->positions * kv_dim;
+      q.kc = kq->k + l * ls;
+      q.vc = kq->v + l * ls;
+      q.part_ml = kq->part_ml;
+      q.part_o = kq->part_o;
+      q.counters = kq->counters;
+      q.pos0 = (int)positions[i];
+      if (l < kq->maps.size() && kq->maps[l].has_tm) {
+        q.tm_k = kq->maps[l].tm_k;
+        q.tm_v = kq->maps[l].tm_v;
+      } else {
+        all_tm = false;
+      }
+    }
+  }
   SeqRow* rows_dev = nullptr;
+  AttnSeq* att_dev = nullptr;
   Bufs scratch;
   if (int rc = scratch.alloc(rows_dev, n)) return rc;
+  if (int rc = scratch.alloc(att_dev, att.size())) return rc;
   PRANA_CK(cudaMemcpyAsync(b->toks, tokens, n * 4, cudaMemcpyHostToDevice, st));
   PRANA_CK(cudaMemcpyAsync(rows_dev, rows.data(), n * sizeof(SeqRow), cudaMemcpyHostToDevice, st));
-  const Multi mu{rows_dev, kvs, positions};
-  int rc = enqueue_rows(m, kvs[0], *b, (int)n, b->toks, nullptr, 0, nullptr, MODE_CACHE, true, false, nullptr,
+  PRANA_CK(cudaMemcpyAsync(att_dev, att.data(), att.size() * sizeof(AttnSeq), cudaMemcpyHostToDevice, st));
+  const Multi mu{rows_dev, kvs, positions, att_dev, min_splits, all_tm};
+  int rc = enqueue_rows(m, kvs[0], *b, (int)n, b->toks, nullptr, 0, nullptr, MODE_CACHE, true, true, nullptr,
                         logits != nullptr, &mu);
   if (rc) return rc;
   if (logits) PRANA_CK(cudaMemcpyAsync(logits, b->logits, n * (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, st));
