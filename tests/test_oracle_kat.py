@@ -1,7 +1,7 @@
 """The CPU oracle against the reference's own known-answer tests (CPU only).
 
 Each test restates one test of the Prana workspace with the same inputs and
-the same assertions, so the oracle that judges the CUDA library is itself
+the same assertions, so the oracle that checks the CUDA library is itself
 pinned to the reference's published behaviour:
 
   f16 conversions      crates/prana-kernels/src/lib.rs:119-154, crates/prana-model/src/gguf.rs:887-897
