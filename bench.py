@@ -209,7 +209,7 @@ def reference_arm(args):
               f"{threads} threads, {tier} tier, {el:.1f} s; C restatement of Prana's CPU path (Rust toolchain absent)")
     line = {"metric": METRIC, "value": round(tps, 4), "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
             "steps": steps, "warmup": 1, "ms_per_step": round(1000.0 / tps, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 / f32", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> int32 / f32", "data": "synthetic",
             "config": {"workload": args.workload, "ctx": args.ctx, "batch": 1},
             "cpu_baseline": {"value": round(tps, 4), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": round(tps, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
