@@ -212,6 +212,38 @@ int prana_decode_begin(prana_model *m, prana_kv *kv, uint32_t token, size_t pos)
 int prana_decode_run(prana_model *m, prana_kv *kv, size_t n_steps);
 int prana_decode_tokens(prana_model *m, prana_kv *kv, uint32_t *out, size_t max, size_t *n_out);
 
+/* ---- tokenizers (host only; no device is touched) ----
+ * Text is bytes; invalid UTF-8 is first replaced as Rust's String::from_utf8_lossy
+ * does.  Calls that fill a caller buffer set *n_out to the size needed and return
+ * PRANA_E_INVALID when cap is smaller. */
+typedef struct prana_tokenizer prana_tokenizer;
+/* load_tokenizer (gguf.rs:462-537): "llama" (SentencePiece pieces, U+2581 read as
+ * a space) or "gpt2" (byte-level BPE with tokenizer.ggml.merges; token types 3 and
+ * 4 encode verbatim) from a GGUF file's tokenizer.ggml.* metadata */
+int prana_tokenizer_load_gguf(const char *path, prana_tokenizer **out);
+/* Tokenizer::from_parts + with_special (tokenizer.rs:51-67): n pieces of lens[i] bytes */
+int prana_tokenizer_spm(size_t n, const char *const *pieces, const size_t *lens, const float *scores,
+                        uint32_t bos, uint32_t eos, int add_bos, prana_tokenizer **out);
+/* BpeTokenizer::new + with_specials (bpe.rs:57-84): merges are "left right" strings
+ * in rank order; bos / eos < 0: none */
+int prana_tokenizer_bpe(size_t n, const char *const *pieces, const size_t *lens, size_t n_merges,
+                        const char *const *merges, const size_t *merge_lens, size_t n_specials,
+                        const uint32_t *special_ids, int64_t bos, int64_t eos, int add_bos,
+                        prana_tokenizer **out);
+int prana_tokenizer_free(prana_tokenizer *t);
+int prana_tokenizer_vocab_size(const prana_tokenizer *t, size_t *out);
+/* encode_prompt (Tokenize::encode_prompt, tokenizer.rs / bpe.rs:166-192) with bos = -1
+ * and eos = 0; SentencePiece also takes Tokenizer::encode's explicit bos / eos (0 or 1,
+ * tokenizer.rs:89-140) */
+int prana_tokenize(const prana_tokenizer *t, const char *text, size_t len, int bos, int eos, uint32_t *ids,
+                   size_t cap, size_t *n_out);
+/* Tokenize::decode (tokenizer.rs:144-160, bpe.rs:194-199): the bytes of one token
+ * given the previous one */
+int prana_detokenize(const prana_tokenizer *t, uint32_t prev, uint32_t token, char *out, size_t cap,
+                     size_t *n_out);
+/* Tokenize::is_stop: the EOS or BOS id */
+int prana_tokenizer_is_stop(const prana_tokenizer *t, uint32_t token, int *out);
+
 #ifdef __cplusplus
 }
 #endif

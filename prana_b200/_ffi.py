@@ -89,6 +89,14 @@ SIGNATURES = {
     "prana_prefill": [P, P, P, SZ],
     "prana_forward_batch": [P, P, P, SZ, SZ, P, P],
     "prana_forward_multi": [P, P, SZ, P, P, P, P],
+    "prana_tokenizer_load_gguf": [C.c_char_p, C.POINTER(P)],
+    "prana_tokenizer_spm": [SZ, P, P, P, C.c_uint32, C.c_uint32, I, C.POINTER(P)],
+    "prana_tokenizer_bpe": [SZ, P, P, SZ, P, P, SZ, P, C.c_int64, C.c_int64, I, C.POINTER(P)],
+    "prana_tokenizer_free": [P],
+    "prana_tokenizer_vocab_size": [P, C.POINTER(SZ)],
+    "prana_tokenize": [P, C.c_char_p, SZ, I, I, P, SZ, C.POINTER(SZ)],
+    "prana_detokenize": [P, C.c_uint32, C.c_uint32, P, SZ, C.POINTER(SZ)],
+    "prana_tokenizer_is_stop": [P, C.c_uint32, C.POINTER(I)],
     "prana_generate": [P, P, SZ, SZ, C.c_int64, P, C.POINTER(SZ)],
     "prana_generate_speculative": [P, P, P, SZ, SZ, SZ, C.c_int64, P, C.POINTER(SZ), P],
     "prana_decode_begin": [P, P, C.c_uint32, SZ],
