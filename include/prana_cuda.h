@@ -244,6 +244,18 @@ int prana_detokenize(const prana_tokenizer *t, uint32_t prev, uint32_t token, ch
 /* Tokenize::is_stop: the EOS or BOS id */
 int prana_tokenizer_is_stop(const prana_tokenizer *t, uint32_t token, int *out);
 
+/* ---- sampling (host only) ----
+ * Sampler::new (sampler.rs:13-20): greedy when temperature <= 0, else temperature
+ * sampling driven by xorshift64* from seed (0 reads as 1) */
+typedef struct prana_sampler prana_sampler;
+int prana_sampler_create(float temperature, uint64_t seed, prana_sampler **out);
+int prana_sampler_free(prana_sampler *s);
+/* Sampler::sample (sampler.rs:22-37) over n host logits: softmax(logits / temperature)
+ * (norms.rs:44-56), then the first id where the running draw drops to <= 0 */
+int prana_sample(prana_sampler *s, const float *logits, size_t n, uint32_t *token);
+/* XorShift::next_f32 (sampler.rs:67-70): the stream's next uniform draw in [0, 1) */
+int prana_sampler_next_f32(prana_sampler *s, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -97,6 +97,10 @@ SIGNATURES = {
     "prana_tokenize": [P, C.c_char_p, SZ, I, I, P, SZ, C.POINTER(SZ)],
     "prana_detokenize": [P, C.c_uint32, C.c_uint32, P, SZ, C.POINTER(SZ)],
     "prana_tokenizer_is_stop": [P, C.c_uint32, C.POINTER(I)],
+    "prana_sampler_create": [C.c_float, C.c_uint64, C.POINTER(P)],
+    "prana_sampler_free": [P],
+    "prana_sample": [P, P, SZ, C.POINTER(C.c_uint32)],
+    "prana_sampler_next_f32": [P, C.POINTER(C.c_float)],
     "prana_generate": [P, P, SZ, SZ, C.c_int64, P, C.POINTER(SZ)],
     "prana_generate_speculative": [P, P, P, SZ, SZ, SZ, C.c_int64, P, C.POINTER(SZ), P],
     "prana_decode_begin": [P, P, C.c_uint32, SZ],
