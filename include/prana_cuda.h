@@ -53,9 +53,21 @@ int prana_ctx_destroy(prana_ctx *ctx); /* idempotent on NULL */
 /* run kernel-level calls on a caller-owned cudaStream_t (NULL = the context's own
  * stream; pass cudaStreamLegacy, 0x1, for the legacy default stream) */
 int prana_ctx_set_stream(prana_ctx *ctx, void *cuda_stream);
+/* Wait for the context's kernel-level calls; a bounded device wait that gave
+ * up in one of them (including prana_attention_decode_noalloc on this device)
+ * returns PRANA_E_TIMEOUT here, once, and the context stays usable. */
 int prana_ctx_synchronize(prana_ctx *ctx);
 /* the context's own stream (model-level work always runs there), for event timing */
 int prana_ctx_stream(prana_ctx *ctx, void **cuda_stream);
+
+/* Diagnostic, no reference counterpart: make one bounded device wait run out
+ * on data that never arrives, and report it the way the kernel-level calls do.
+ * which = 0: an mbarrier wait that no copy completes; which = 1: the peer
+ * exchange's receive wait, run on this GPU alone with a second local buffer
+ * standing in for a rank that never stores.  polls bounds the wait.  Returns
+ * PRANA_E_TIMEOUT when the wait gave up (the expected outcome); no fault is
+ * raised and the context stays usable. */
+int prana_debug_wait_timeout(prana_ctx *ctx, int which, unsigned polls);
 
 /* ---------------------------------------------------------------- weights
  * Upload one [rows, cols] tensor given in its GGUF byte layout and repack it
@@ -182,6 +194,16 @@ int prana_forward(prana_model *m, prana_kv *kv, uint32_t token, size_t pos, floa
  * (hidden); then the final-norm input (dim) -- with their per-32 scales. */
 int prana_forward_trace(prana_model *m, prana_kv *kv, uint32_t token, size_t pos, float *logits, int8_t *q_out,
                         float *scales_out, size_t capacity, size_t *n_out);
+/* Diagnostic batch form of prana_forward_trace: prefill (prefill = 1; positions
+ * 0..n, pos0 ignored) or forward_batch (prefill = 0; positions pos0..) of n
+ * tokens, run eagerly, additionally returning the quantized activation rows of
+ * every site in CPU-path order -- per layer the n rows of the attention-norm
+ * input, the attention output, the ffn-norm input and silu(gate)*up; then the
+ * n final-norm rows (forward_batch only) -- with their per-32 scales.
+ * logits [n, vocab] (forward_batch only; may be NULL). */
+int prana_forward_batch_trace(prana_model *m, prana_kv *kv, const uint32_t *tokens, size_t n, size_t pos0,
+                              int prefill, float *logits, int8_t *q_out, float *scales_out, size_t capacity,
+                              size_t *n_out);
 /* prefill (infer.rs:220-286): tokens at positions 0..n, no logits */
 int prana_prefill(prana_model *m, prana_kv *kv, const uint32_t *tokens, size_t n);
 /* forward_batch (infer.rs:296-374): n tokens at pos0.., logits [n, vocab] (may be NULL)
@@ -195,6 +217,13 @@ int prana_forward_batch(prana_model *m, prana_kv *kv, const uint32_t *tokens, si
  * Single-GPU models only. */
 int prana_forward_multi(prana_model *m, prana_kv *const *caches, size_t n, const uint32_t *tokens,
                         const size_t *positions, float *logits, uint32_t *argmax);
+/* Diagnostic form of prana_forward_multi (eager, no logits gather shortcut):
+ * additionally returns the quantized activation rows in the layout of
+ * prana_forward_batch_trace (per layer the n rows of each site, then the n
+ * final-norm rows). */
+int prana_forward_multi_trace(prana_model *m, prana_kv *const *caches, size_t n, const uint32_t *tokens,
+                              const size_t *positions, float *logits, int8_t *q_out, float *scales_out,
+                              size_t capacity, size_t *n_out);
 /* generate (infer.rs:696-771), greedy, over token ids; stop_id < 0 disables stopping.
  * out must hold `steps` ids; *n_out receives the count. */
 int prana_generate(prana_model *m, const uint32_t *prompt, size_t p, size_t steps, int64_t stop_id,

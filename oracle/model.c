@@ -509,8 +509,19 @@ static void rope_row(const or_config *c, float *x, size_t n, size_t pos) {
 /* Embedding::row (checkpoint.rs:169-174) */
 static void emb_row(const or_model *m, uint32_t tok, float *x) { or_matrix_dequant_row(&m->emb, tok, x); }
 
-/* Linear::apply (checkpoint.rs:94-100) */
+/* Linear::apply (checkpoint.rs:94-100); in forced trace mode a quantized
+ * matrix takes the current site's given row through matmul_q8_prefill /
+ * matmul_kquant_prefill, whose per-element dot is the decode GEMV's. */
+static int forced_rows(size_t n, size_t k, const int8_t **q, const float **s, int32_t **sums);
 static void apply(const or_model *m, const or_matrix *w, const float *x, float *y) {
+  const int8_t *fq;
+  const float *fs;
+  int32_t *fsum;
+  if (w->kind != OR_GGML_F32 && forced_rows(1, w->cols, &fq, &fs, &fsum)) {
+    or_matmul_prefill(m->tier, w, fq, fs, fsum, 1, y);
+    free(fsum);
+    return;
+  }
   or_matmul(m->tier, w, x, 1, y);
 }
 
@@ -521,18 +532,48 @@ static void logits(const or_model *m, const float *x, float *out) {
 }
 
 /* Diagnostic trace of the quantized activation rows a forward pass feeds its
- * integer dots (the same quantize_acts the matmuls run internally). */
+ * integer dots (the same quantize_acts the matmuls run internally).
+ *
+ * Forced mode (test instrumentation): when tr_fq is set, the rows quantized at
+ * each site are recorded as usual, but the matmuls that consume the site take
+ * the given rows (tr_fq / tr_fs at the same offsets) instead.  A comparison
+ * that first proves every difference between the given rows and the recorded
+ * ones is a rounding tie can then follow the given rows through the rest of
+ * the pass: the next site's values differ from the other side's only by f32
+ * summation order. */
 static __thread int8_t *tr_q;
 static __thread float *tr_s, *tr_v;
 static __thread size_t tr_nq, tr_cap;
+static __thread const int8_t *tr_fq;
+static __thread const float *tr_fs;
+static __thread size_t tr_site_off;
+static __thread int tr_site_forced;
 
 static void trace_site(const float *x, size_t n) {
+  tr_site_forced = 0;
   if (!tr_q || tr_nq + n > tr_cap) return;
   int32_t *sums = malloc(sizeof(int32_t) * (n / 32));
   or_quantize_acts(x, n, tr_q + tr_nq, tr_s + tr_nq / 32, sums);
   if (tr_v) memcpy(tr_v + tr_nq, x, n * sizeof(float));
   free(sums);
+  tr_site_off = tr_nq;
+  tr_site_forced = tr_fq != NULL;
   tr_nq += n;
+}
+
+/* n rows of k quantized values of the current site, taken from the forced rows */
+static int forced_rows(size_t n, size_t k, const int8_t **q, const float **s, int32_t **sums) {
+  if (!tr_site_forced) return 0;
+  *q = tr_fq + tr_site_off;
+  *s = tr_fs + tr_site_off / 32;
+  size_t g = n * k / 32;
+  *sums = malloc(sizeof(int32_t) * g);
+  for (size_t i = 0; i < g; i++) {
+    int32_t t = 0;
+    for (int j = 0; j < 32; j++) t += (*q)[i * 32 + j];
+    (*sums)[i] = t;
+  }
+  return 1;
 }
 
 /* infer.rs:142-211 forward_impl */
@@ -583,24 +624,53 @@ void or_forward(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float 
   free(x); free(xb); free(q); free(k); free(v); free(att); free(o); free(g); free(u); free(dn);
 }
 
-size_t or_forward_trace(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float *logits, int8_t *q,
-                        float *s, float *vals, size_t cap) {
+static void trace_begin(int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq, const float *fs) {
   tr_q = q;
   tr_s = s;
   tr_v = vals;
   tr_nq = 0;
   tr_cap = cap;
-  or_forward(m, kv, token, pos, logits);
+  tr_fq = fq;
+  tr_fs = fs;
+  tr_site_forced = 0;
+}
+static size_t trace_end(void) {
   size_t n = tr_nq;
   tr_q = NULL;
   tr_s = NULL;
+  tr_v = NULL;
+  tr_fq = NULL;
+  tr_fs = NULL;
+  tr_site_forced = 0;
   return n;
+}
+
+size_t or_forward_trace(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float *logits, int8_t *q,
+                        float *s, float *vals, size_t cap) {
+  trace_begin(q, s, vals, cap, NULL, NULL);
+  or_forward(m, kv, token, pos, logits);
+  return trace_end();
+}
+
+size_t or_forward_trace_forced(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float *logits,
+                               int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq, const float *fs) {
+  trace_begin(q, s, vals, cap, fq, fs);
+  or_forward(m, kv, token, pos, logits);
+  return trace_end();
 }
 
 /* Linear::apply_prefill (checkpoint.rs:140-146) for n rows */
 static void apply_prefill(const or_model *m, const or_matrix *w, const float *xs, size_t n, float *y) {
   if (w->kind == OR_GGML_F32) {
     or_matmul(m->tier, w, xs, n, y);
+    return;
+  }
+  const int8_t *fq;
+  const float *fs;
+  int32_t *fsum;
+  if (forced_rows(n, w->cols, &fq, &fs, &fsum)) {
+    or_matmul_prefill(m->tier, w, fq, fs, fsum, n, y);
+    free(fsum);
     return;
   }
   size_t k = w->cols, g = k / 32;
@@ -631,6 +701,7 @@ static void batch_body(const or_model *m, or_kv *kv, const uint32_t *toks, size_
   for (size_t l = 0; l < c->n_layers; l++) {
     layer *L = &m->layers[l];
     or_rmsnorm(x, L->rms_att, n, dim, c->norm_eps, xb);
+    trace_site(xb, n * dim);
     apply_prefill(m, &L->wq, xb, n, q);
     apply_prefill(m, &L->wk, xb, n, k);
     apply_prefill(m, &L->wv, xb, n, v);
@@ -646,19 +717,23 @@ static void batch_body(const or_model *m, or_kv *kv, const uint32_t *toks, size_
     or_f16_kv_write(vc, pos0, kv_dim, v, n * kv_dim);
     if (verify) or_attention_verify(q, kc, vc, pos0, n, c->n_heads, c->n_kv_heads, hd, att);
     else or_attention(q, k, v, n, c->n_heads, c->n_kv_heads, hd, att);
+    trace_site(att, n * q_dim);
     apply_prefill(m, &L->wo, att, n, o);
     for (size_t i = 0; i < n * dim; i++) x[i] += o[i];
     or_rmsnorm(x, L->rms_ffn, n, dim, c->norm_eps, xb);
+    trace_site(xb, n * dim);
     apply_prefill(m, &L->w1, xb, n, g);
     apply_prefill(m, &L->w3, xb, n, u);
     or_silu(g, n * hid);
     for (size_t i = 0; i < n * hid; i++) g[i] *= u[i];
+    trace_site(g, n * hid);
     apply_prefill(m, &L->w2, g, n, dn);
     for (size_t i = 0; i < n * dim; i++) x[i] += dn[i];
   }
   if (verify && out_logits) {
     /* Model::logits_batch (checkpoint.rs:256-265) */
     or_rmsnorm(x, m->rms_final, n, dim, c->norm_eps, xb);
+    trace_site(xb, n * dim);
     apply_prefill(m, m->has_wcls ? &m->wcls : &m->emb, xb, n, out_logits);
   }
   free(x); free(xb); free(q); free(k); free(v); free(att); free(o); free(g); free(u); free(dn);
@@ -671,6 +746,18 @@ void or_prefill(const or_model *m, or_kv *kv, const uint32_t *tokens, size_t n) 
 void or_forward_batch(const or_model *m, or_kv *kv, const uint32_t *tokens, size_t n, size_t pos0,
                       float *logits_out) {
   batch_body(m, kv, tokens, n, pos0, 1, logits_out);
+}
+
+/* prefill (verify == 0, positions 0..n) or forward_batch (verify == 1) with
+ * the activation trace of or_forward_trace_forced: per layer the n rows of
+ * each site, then the final-norm rows (verify only); fq / fs (or NULL) force
+ * the rows the matmuls take. */
+size_t or_batch_trace(const or_model *m, or_kv *kv, const uint32_t *tokens, size_t n, size_t pos0, int verify,
+                      float *logits_out, int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq,
+                      const float *fs) {
+  trace_begin(q, s, vals, cap, fq, fs);
+  batch_body(m, kv, tokens, n, verify ? pos0 : 0, verify, logits_out);
+  return trace_end();
 }
 
 /* infer.rs:696-771 generate, greedy, over ids */

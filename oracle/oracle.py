@@ -92,6 +92,8 @@ def lib() -> C.CDLL:
             "or_kv_layer": ([P, C.c_int, C.c_int], P),
             "or_forward": ([P, P, C.c_uint32, SZ, P], None),
             "or_forward_trace": ([P, P, C.c_uint32, SZ, P, P, P, P, SZ], SZ),
+            "or_forward_trace_forced": ([P, P, C.c_uint32, SZ, P, P, P, P, SZ, P, P], SZ),
+            "or_batch_trace": ([P, P, P, SZ, SZ, C.c_int, P, P, P, P, SZ, P, P], SZ),
             "or_prefill": ([P, P, P, SZ], None),
             "or_forward_batch": ([P, P, P, SZ, SZ, P], None),
             "or_generate": ([P, P, SZ, SZ, C.c_int64, P], SZ),
@@ -197,15 +199,53 @@ class OModel:
         c = self.c
         return c.n_layers * (2 * c.dim + c.n_heads * c.head_dim + c.hidden_dim) + c.dim
 
-    def forward_trace(self, kv: "OKv", token: int, pos: int, with_values: bool = False):
-        """(logits, int8 activation rows, scales[, the f32 values quantized]) in forward order."""
+    def forward_trace(self, kv: "OKv", token: int, pos: int, with_values: bool = False, force=None):
+        """(logits, int8 activation rows, scales[, the f32 values quantized]) in forward order.
+
+        force = (q, scales) of another pass's trace: the oracle still records
+        its own quantized rows, but every matmul takes the given rows instead
+        (test instrumentation; see or_forward_trace_forced)."""
         n = self.trace_len()
         q = np.empty(n, np.int8)
         s = np.empty(n // 32, np.float32)
         v = np.empty(n, np.float32) if with_values else None
         lg = np.empty(self.c.vocab_size, np.float32)
-        got = lib().or_forward_trace(self.h, kv.h, token, pos, ptr(lg), ptr(q), ptr(s),
-                                     ptr(v) if v is not None else None, n)
+        if force is None:
+            got = lib().or_forward_trace(self.h, kv.h, token, pos, ptr(lg), ptr(q), ptr(s),
+                                         ptr(v) if v is not None else None, n)
+        else:
+            fq = np.ascontiguousarray(force[0], np.int8)
+            fs = np.ascontiguousarray(force[1], np.float32)
+            assert fq.size == n and fs.size == n // 32
+            got = lib().or_forward_trace_forced(self.h, kv.h, token, pos, ptr(lg), ptr(q), ptr(s),
+                                                ptr(v) if v is not None else None, n, ptr(fq), ptr(fs))
+        assert got == n
+        return (lg, q, s, v) if with_values else (lg, q, s)
+
+    def batch_trace_len(self, n: int, verify: bool) -> int:
+        c = self.c
+        return n * (c.n_layers * (2 * c.dim + c.n_heads * c.head_dim + c.hidden_dim) + (c.dim if verify else 0))
+
+    def batch_trace(self, kv: "OKv", tokens, pos0: int, verify: bool, with_values: bool = False, force=None):
+        """prefill (verify False, positions 0..n) or forward_batch (verify True) with
+        the activation trace: per layer the n rows of each site, then the
+        final-norm rows (verify only).  Returns (logits [n, vocab] or None, q,
+        scales[, values]); force as in forward_trace."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        n = self.batch_trace_len(t.size, verify)
+        q = np.empty(n, np.int8)
+        s = np.empty(n // 32, np.float32)
+        v = np.empty(n, np.float32) if with_values else None
+        lg = np.empty((t.size, self.c.vocab_size), np.float32) if verify else None
+        fq = fs = None
+        if force is not None:
+            fq = np.ascontiguousarray(force[0], np.int8)
+            fs = np.ascontiguousarray(force[1], np.float32)
+            assert fq.size == n and fs.size == n // 32
+        got = lib().or_batch_trace(self.h, kv.h, ptr(t), t.size, pos0, int(verify),
+                                   ptr(lg) if lg is not None else None, ptr(q), ptr(s),
+                                   ptr(v) if v is not None else None, n,
+                                   ptr(fq) if fq is not None else None, ptr(fs) if fs is not None else None)
         assert got == n
         return (lg, q, s, v) if with_values else (lg, q, s)
 

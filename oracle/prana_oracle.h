@@ -163,6 +163,11 @@ void or_forward(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float 
  * input, attention output, ffn-norm input, silu(g)*u; then the final-norm input) */
 size_t or_forward_trace(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float *logits, int8_t *q,
                         float *s, float *vals /* f32 values quantized, may be NULL */, size_t cap);
+size_t or_forward_trace_forced(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float *logits,
+                               int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq, const float *fs);
+size_t or_batch_trace(const or_model *m, or_kv *kv, const uint32_t *tokens, size_t n, size_t pos0, int verify,
+                      float *logits_out, int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq,
+                      const float *fs);
 /* batched prompt, no logits (infer.rs:220-286) */
 void or_prefill(const or_model *m, or_kv *kv, const uint32_t *tokens, size_t n);
 /* verify pass: logits [n][vocab] (infer.rs:296-374) */

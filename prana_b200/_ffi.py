@@ -52,6 +52,7 @@ SIGNATURES = {
     "prana_ctx_set_stream": [P, P],
     "prana_ctx_synchronize": [P],
     "prana_ctx_stream": [P, C.POINTER(P)],
+    "prana_debug_wait_timeout": [P, I, C.c_uint],
     "prana_weight_upload": [P, I, SZ, SZ, P, C.POINTER(P)],
     "prana_weight_free": [P],
     "prana_weight_bytes": [P, C.POINTER(SZ)],
@@ -86,9 +87,11 @@ SIGNATURES = {
     "prana_forward": [P, P, C.c_uint32, SZ, P, P],
     "prana_forward_trace": [P, P, C.c_uint32, SZ, P, P, P, SZ, C.POINTER(SZ)],
     "prana_kv_write": [P, SZ, I, SZ, P],
+    "prana_forward_batch_trace": [P, P, P, SZ, SZ, I, P, P, P, SZ, C.POINTER(SZ)],
     "prana_prefill": [P, P, P, SZ],
     "prana_forward_batch": [P, P, P, SZ, SZ, P, P],
     "prana_forward_multi": [P, P, SZ, P, P, P, P],
+    "prana_forward_multi_trace": [P, P, SZ, P, P, P, P, P, SZ, C.POINTER(SZ)],
     "prana_tokenizer_load_gguf": [C.c_char_p, C.POINTER(P)],
     "prana_tokenizer_spm": [SZ, P, P, P, C.c_uint32, C.c_uint32, I, C.POINTER(P)],
     "prana_tokenizer_bpe": [SZ, P, P, SZ, P, P, SZ, P, C.c_int64, C.c_int64, I, C.POINTER(P)],

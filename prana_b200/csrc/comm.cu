@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(kExThreads) tp_exchange_kernel(const TpPeers p
   const uint64_t tag = (uint64_t)e << 32;
   const int per_cta = (int)((n + gridDim.x - 1) / gridDim.x);
   const int lo = blockIdx.x * per_cta, hi = min(n, lo + per_cta);
-  uint32_t budget = 1u << 22;
+  uint32_t budget = p.budget;
   bool late = false;
   // push: this rank's values into its slot on every rank
   for (int b = lo; b < hi; b += kExThreads * E) {

@@ -34,6 +34,7 @@ struct TpPeers {
   size_t cap = 0;                      // words per slot
   uint64_t* buf[kTpMaxWorld] = {};     // each rank's receive area (this process's mapping)
   unsigned* epoch = nullptr;           // this rank's call counters, one per exchange CTA (device)
+  uint32_t budget = 1u << 22;          // polls (20 ns apart at least) before a wait gives up
 };
 // Map every rank's receive area (exchanged with an NCCL all-gather of IPC
 // handles); false when peer access is unavailable or world is not 2, 4 or 8.

@@ -5,6 +5,7 @@
 #include <cstring>
 #include <new>
 
+#include "comm.h"
 #include "host.h"
 
 namespace prana {
@@ -259,14 +260,14 @@ int prana_ctx_create(int device, prana_ctx** out) {
   c->device = device;
   c->sm_count = prop.multiProcessorCount;
   if (cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaMalloc(&c->counters, 4096 * sizeof(unsigned)) != cudaSuccess ||
-      cudaMemset(c->counters, 0, 4096 * sizeof(unsigned)) != cudaSuccess) {
+      cudaMalloc(&c->counters, (4096 + 64) * sizeof(unsigned)) != cudaSuccess ||
+      cudaMemset(c->counters, 0, (4096 + 64) * sizeof(unsigned)) != cudaSuccess) {
     cudaGetLastError();
     delete c;
     return fail(PRANA_E_CUDA, "context setup failed");
   }
   c->stream = c->own;
-  c->err = c->counters + 4095;
+  c->err = c->counters + 4096;  // past every kv head's counter, on its own 256-byte line
   *out = c;
   return PRANA_OK;
   API_END
@@ -300,11 +301,56 @@ int prana_ctx_stream(prana_ctx* c, void** stream) {
   return PRANA_OK;
 }
 
+// Waits for the kernel-level calls on the context's stream, then reports a
+// bounded device wait that gave up in any of them (the context's own error
+// word, and the no-allocation attention word of this device) as
+// PRANA_E_TIMEOUT, clearing the word so the context stays usable.
 int prana_ctx_synchronize(prana_ctx* c) {
   NEED(c, "ctx is null");
   DevScope ds(c->device);
   PRANA_CK(cudaStreamSynchronize(c->stream));
+  unsigned e = 0, e2 = 0;
+  PRANA_CK(cudaMemcpy(&e, c->err, sizeof(unsigned), cudaMemcpyDeviceToHost));
+  if (e) PRANA_CK(cudaMemset(c->err, 0, sizeof(unsigned)));
+  if (int rc = noalloc_take_error(c->device, &e2)) return rc;
+  if (e || e2)
+    return fail(PRANA_E_TIMEOUT, "a bounded device-side wait expired in a kernel-level call (%s)",
+                e ? "context" : "no-allocation attention");
   return PRANA_OK;
+}
+
+int prana_debug_wait_timeout(prana_ctx* c, int which, unsigned polls) {
+  NEED(c, "ctx is null");
+  NEED(which == 0 || which == 1, "which must be 0 (mbarrier) or 1 (peer exchange)");
+  NEED(polls > 0, "polls must be positive");
+  DevScope ds(c->device);
+  if (int rc = prana_ctx_synchronize(c)) return rc;  // start from a clear error word
+  if (which == 0) {
+    PRANA_CK(launch_wait_never(polls, c->err, c->stream));
+    return prana_ctx_synchronize(c);
+  }
+  // rank 0 of two, both receive areas on this GPU: rank 1's slot in rank 0's
+  // area is never stored to, so the receive wait runs out
+  constexpr size_t cap = 64;
+  const size_t area = 2 * 2 * cap * sizeof(uint64_t);
+  void* mem = nullptr;
+  PRANA_CK(cudaMalloc(&mem, 2 * area + 64 * sizeof(unsigned) + cap * sizeof(float)));
+  struct Free {
+    void* p;
+    ~Free() { cudaFree(p); }
+  } fr{mem};
+  PRANA_CK(cudaMemset(mem, 0, 2 * area + 64 * sizeof(unsigned) + cap * sizeof(float)));
+  TpPeers p;
+  p.world = 2;
+  p.rank = 0;
+  p.cap = cap;
+  p.buf[0] = static_cast<uint64_t*>(mem);
+  p.buf[1] = reinterpret_cast<uint64_t*>(static_cast<char*>(mem) + area);
+  p.epoch = reinterpret_cast<unsigned*>(static_cast<char*>(mem) + 2 * area);
+  p.budget = polls;
+  float* x = reinterpret_cast<float*>(p.epoch + 64);
+  PRANA_CK(launch_tp_allreduce(p, x, (int)cap, c->err, c->stream, false));
+  return prana_ctx_synchronize(c);
 }
 
 int prana_weight_upload(prana_ctx* c, int type, size_t rows, size_t cols, const void* host, prana_weight** out) {
@@ -507,6 +553,7 @@ static int attn_common(prana_ctx* c, const float* q, const uint16_t* kc, const u
   NEED(nkv > 0 && nh % nkv == 0, "n_heads must be a multiple of n_kv_heads");
   NEED(hd <= 256, "head_dim %zu exceeds 256", hd);
   NEED(hd * (nh / nkv) <= 4096, "head_dim x group exceeds 4096");
+  NEED(nkv <= 4096, "too many kv heads");
   if (!m) return PRANA_OK;
   DevScope ds(c->device);
   const int splits = attn_splits((int)(pos0 + m), (int)nkv, (int)hd, c->sm_count);
@@ -517,7 +564,6 @@ static int attn_common(prana_ctx* c, const float* q, const uint16_t* kc, const u
   void* sp;
   int rc = ctx_scratch(c, (ml + po) * 4, &sp);
   if (rc) return rc;
-  NEED(nkv <= 4096, "too many kv heads");
   AttnArgs a{};
   a.q = q;
   a.kc = reinterpret_cast<const __half*>(kc);

@@ -44,8 +44,8 @@ struct prana_ctx {
   cudaStream_t own = nullptr;
   cudaStream_t stream = nullptr;
   prana::Scratch scratch;
-  unsigned* counters = nullptr;  // 4096 zeroed ticket counters
-  unsigned* err = nullptr;       // device error flag of kernel-level calls (counters + 4095)
+  unsigned* counters = nullptr;  // 4096 zeroed ticket counters (one per kv head of an attention launch)
+  unsigned* err = nullptr;       // device error flag of kernel-level calls (a word of its own after the counters)
   std::map<std::tuple<int, uint32_t, int>, prana::RopeTable> rope;
   std::vector<void*> retired;  // outgrown RoPE tables: captured graphs may still point at them
 };
@@ -65,6 +65,8 @@ int ctx_rope(prana_ctx* ctx, int head_dim, float theta, int neox, int positions,
 // Repack GGUF bytes of a [rows, cols] tensor into device layout.
 int upload_weight(prana_ctx* ctx, int type, size_t rows, size_t cols, const void* host, prana_weight* w);
 void free_weight(prana_weight* w);
+// Read and clear the error word of prana_attention_decode_noalloc on `device`.
+int noalloc_take_error(int device, unsigned* out);
 struct DevScope {
   int prev = -1;
   explicit DevScope(int dev) {

@@ -173,6 +173,8 @@ cudaError_t launch_argmax(const float* x, int rows, int n, uint32_t* out, cudaSt
 cudaError_t launch_block_dots(const DevWeight& w, int row, const int8_t* aq, const int32_t* asum, int32_t* out,
                               cudaStream_t st);
 cudaError_t launch_advance(int* tok, int* pos, uint32_t* ring, int ring_cap, int* ring_n, cudaStream_t st, bool pdl);
+// diagnostic: one bounded mbarrier wait that nothing completes (raises *err)
+cudaError_t launch_wait_never(unsigned polls, unsigned* err, cudaStream_t st);
 // first maximum over ranks: all = [world][16] (8 best values, then 8 index bit patterns)
 cudaError_t launch_tp_argmax(const float* all, int world, int m, uint32_t* tok_out, int* tok_next, cudaStream_t st);
 

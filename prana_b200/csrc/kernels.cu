@@ -13,6 +13,7 @@
 
 #include "gemv.cuh"
 #include "internal.h"
+#include "mbar.cuh"
 
 namespace prana {
 
@@ -379,6 +380,25 @@ __global__ void tp_argmax_kernel(const float* all, int world, int m, uint32_t* t
 
 cudaError_t launch_tp_argmax(const float* all, int world, int m, uint32_t* tok_out, int* tok_next, cudaStream_t st) {
   tp_argmax_kernel<<<1, 32, 0, st>>>(all, world, m, tok_out, tok_next);
+  return cudaGetLastError();
+}
+
+// A bounded mbarrier wait on a barrier nothing arrives at: the wait gives up
+// after `polls` tries and raises the error flag, as every kernel's waits do
+// when a copy never completes.
+__global__ void wait_never_kernel(unsigned polls, unsigned* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(&bar, 0, polls);
+  if (threadIdx.x == 0 && !ok && err) atomicExch(err, ERR_TIMEOUT);
+}
+
+cudaError_t launch_wait_never(unsigned polls, unsigned* err, cudaStream_t st) {
+  wait_never_kernel<<<1, 32, 0, st>>>(polls, err);
   return cudaGetLastError();
 }
 

@@ -33,8 +33,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
 }
 // ~2^22 polls, each of which may itself suspend for a hardware-chosen time:
 // far beyond any healthy copy.  Returns false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
-  for (uint32_t i = 0; i < (1u << 22); i++)
+constexpr uint32_t kMbarPolls = 1u << 22;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_t polls = kMbarPolls) {
+  for (uint32_t i = 0; i < polls; i++)
     if (mbar_try_wait(bar, phase)) return true;
   return false;
 }

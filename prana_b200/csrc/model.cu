@@ -393,11 +393,12 @@ struct Trace {
   int8_t* q = nullptr;
   float* s = nullptr;
   size_t nq = 0, ns = 0;
+  // a launch over a.m rows of k values each appends its rows [a.m][k]
   void site(StreamArgs& a, int k) {
     a.trace_q = q + nq;
     a.trace_s = s + ns;
-    nq += (size_t)k;
-    ns += (size_t)k / 32;
+    nq += (size_t)a.m * k;
+    ns += (size_t)a.m * k / 32;
   }
 };
 
@@ -1192,6 +1193,50 @@ int prana_forward_trace(prana_model* m, prana_kv* kv, uint32_t token, size_t pos
   API_END
 }
 
+int prana_forward_batch_trace(prana_model* m, prana_kv* kv, const uint32_t* tokens, size_t n, size_t pos0,
+                              int prefill, float* logits, int8_t* q_host, float* s_host, size_t cap, size_t* n_out) {
+  API_BEGIN
+  NEED(m && kv && kv->m == m && tokens && q_host && s_host && n_out, "null or mismatched argument");
+  NEED(n > 0, "empty batch");
+  NEED(m->tp_world == 1, "forward_batch_trace runs on a single-GPU model");
+  if (prefill) pos0 = 0;
+  NEED(pos0 + n <= kv->positions, "rows %zu..%zu beyond kv capacity %zu", pos0, pos0 + n, kv->positions);
+  for (size_t i = 0; i < n; i++) NEED(tokens[i] < (uint64_t)m->cfg.vocab_size, "token out of vocabulary");
+  const auto& c = m->cfg;
+  const size_t need =
+      n * ((size_t)c.n_layers * (2 * c.dim + c.n_heads * c.head_dim + c.hidden_dim) + (prefill ? 0 : c.dim));
+  NEED(cap >= need, "trace buffer holds %zu values, %zu needed", cap, need);
+  DevScope ds(m->ctx->device);
+  cudaStream_t st = m->ctx->own;
+  Bufs b;
+  int rc = make_bufs(m, n, prefill != 0, b);
+  if (rc) return rc;
+  Trace tr;
+  PRANA_CK(cudaMalloc(&tr.q, need));
+  PRANA_CK(cudaMalloc(&tr.s, need / 32 * 4 + 4));
+  struct Free {
+    Trace& t;
+    ~Free() {
+      cudaFree(t.q);
+      cudaFree(t.s);
+    }
+  } fr{tr};
+  PRANA_CK(cudaMemcpyAsync(b.toks, tokens, n * 4, cudaMemcpyHostToDevice, st));
+  rc = enqueue_rows(m, kv, b, (int)n, b.toks, nullptr, (int)pos0, nullptr, prefill ? MODE_WINDOW : MODE_CACHE,
+                    !prefill, false, &tr);
+  if (rc) return rc;
+  if (tr.nq != need) return fail(PRANA_E_INVALID, "trace recorded %zu values, expected %zu", tr.nq, need);
+  PRANA_CK(cudaMemcpyAsync(q_host, tr.q, tr.nq, cudaMemcpyDeviceToHost, st));
+  PRANA_CK(cudaMemcpyAsync(s_host, tr.s, tr.ns * 4, cudaMemcpyDeviceToHost, st));
+  if (logits && !prefill)
+    PRANA_CK(cudaMemcpyAsync(logits, b.logits, n * (size_t)c.vocab_size * 4, cudaMemcpyDeviceToHost, st));
+  PRANA_CK(cudaStreamSynchronize(st));
+  *n_out = tr.nq;
+  kv->loop_active = false;
+  return check_err(m);
+  API_END
+}
+
 int prana_kv_write(prana_kv* kv, size_t layer, int is_v, size_t rows, const uint16_t* host) {
   NEED(kv && host, "null argument");
   const auto& c = kv->m->cfg;
@@ -1253,8 +1298,8 @@ int prana_forward_batch(prana_model* m, prana_kv* kv, const uint32_t* tokens, si
   API_END
 }
 
-int prana_forward_multi(prana_model* m, prana_kv* const* kvs, size_t n, const uint32_t* tokens,
-                        const size_t* positions, float* logits, uint32_t* argmax) {
+static int forward_multi_impl(prana_model* m, prana_kv* const* kvs, size_t n, const uint32_t* tokens,
+                              const size_t* positions, float* logits, uint32_t* argmax, Trace* tr) {
   API_BEGIN
   NEED(m && kvs && tokens && positions, "null argument");
   if (!n) return PRANA_OK;
@@ -1314,7 +1359,7 @@ int prana_forward_multi(prana_model* m, prana_kv* const* kvs, size_t n, const ui
   PRANA_CK(cudaMemcpyAsync(rows_dev, rows.data(), n * sizeof(SeqRow), cudaMemcpyHostToDevice, st));
   PRANA_CK(cudaMemcpyAsync(att_dev, att.data(), att.size() * sizeof(AttnSeq), cudaMemcpyHostToDevice, st));
   const Multi mu{rows_dev, kvs, positions, att_dev, min_splits, all_tm};
-  int rc = enqueue_rows(m, kvs[0], *b, (int)n, b->toks, nullptr, 0, nullptr, MODE_CACHE, true, true, nullptr,
+  int rc = enqueue_rows(m, kvs[0], *b, (int)n, b->toks, nullptr, 0, nullptr, MODE_CACHE, true, tr == nullptr, tr,
                         logits != nullptr, &mu);
   if (rc) return rc;
   if (logits) PRANA_CK(cudaMemcpyAsync(logits, b->logits, n * (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, st));
@@ -1322,6 +1367,41 @@ int prana_forward_multi(prana_model* m, prana_kv* const* kvs, size_t n, const ui
   PRANA_CK(cudaStreamSynchronize(st));
   for (size_t i = 0; i < n; i++) kvs[i]->loop_active = false;
   return check_err(m);
+  API_END
+}
+
+int prana_forward_multi(prana_model* m, prana_kv* const* kvs, size_t n, const uint32_t* tokens,
+                        const size_t* positions, float* logits, uint32_t* argmax) {
+  return forward_multi_impl(m, kvs, n, tokens, positions, logits, argmax, nullptr);
+}
+
+int prana_forward_multi_trace(prana_model* m, prana_kv* const* kvs, size_t n, const uint32_t* tokens,
+                              const size_t* positions, float* logits, int8_t* q_host, float* s_host, size_t cap,
+                              size_t* n_out) {
+  API_BEGIN
+  NEED(m && q_host && s_host && n_out, "null argument");
+  NEED(n > 0, "empty batch");
+  const auto& c = m->cfg;
+  const size_t need = n * ((size_t)c.n_layers * (2 * c.dim + c.n_heads * c.head_dim + c.hidden_dim) + c.dim);
+  NEED(cap >= need, "trace buffer holds %zu values, %zu needed", cap, need);
+  DevScope ds(m->ctx->device);
+  Trace tr;
+  PRANA_CK(cudaMalloc(&tr.q, need));
+  PRANA_CK(cudaMalloc(&tr.s, need / 32 * 4 + 4));
+  struct Free {
+    Trace& t;
+    ~Free() {
+      cudaFree(t.q);
+      cudaFree(t.s);
+    }
+  } fr{tr};
+  int rc = forward_multi_impl(m, kvs, n, tokens, positions, logits, nullptr, &tr);
+  if (rc) return rc;
+  if (tr.nq != need) return fail(PRANA_E_INVALID, "trace recorded %zu values, expected %zu", tr.nq, need);
+  PRANA_CK(cudaMemcpy(q_host, tr.q, tr.nq, cudaMemcpyDeviceToHost));
+  PRANA_CK(cudaMemcpy(s_host, tr.s, tr.ns * 4, cudaMemcpyDeviceToHost));
+  *n_out = tr.nq;
+  return PRANA_OK;
   API_END
 }
 

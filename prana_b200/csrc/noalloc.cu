@@ -24,6 +24,9 @@ constexpr int kMaxKvHeads = 1024;  // one ticket counter per kv head
 // clearing between calls.  The partials need no initial value.
 static __device__ __align__(256) float g_scratch[kScratchFloats];
 static __device__ __align__(256) unsigned g_counters[kMaxKvHeads];
+// Raised by a launch whose bounded mbarrier wait gave up (the output of that
+// call is then incomplete); read and cleared by prana_ctx_synchronize.
+static __device__ __align__(256) unsigned g_error;
 
 namespace {
 
@@ -31,6 +34,7 @@ struct Slot {
   bool ready = false;
   float* scratch = nullptr;
   unsigned* counters = nullptr;
+  unsigned* error = nullptr;
 };
 constexpr int kMaxDevices = 64;
 Slot g_slots[kMaxDevices];
@@ -49,6 +53,9 @@ int setup(int device, Slot** out) {
     e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.counters), g_counters);
     if (e != cudaSuccess)
       return prana::fail(PRANA_E_CUDA, "cudaGetSymbolAddress(counters) failed: %s", cudaGetErrorString(e));
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.error), g_error);
+    if (e != cudaSuccess)
+      return prana::fail(PRANA_E_CUDA, "cudaGetSymbolAddress(error) failed: %s", cudaGetErrorString(e));
     s.ready = true;
   }
   *out = &s;
@@ -56,6 +63,28 @@ int setup(int device, Slot** out) {
 }
 
 }  // namespace
+
+namespace prana {
+
+// The no-allocation entry point's error word on `device`: 0 when no call there
+// has reported a timeout since the last look (or the device never ran one);
+// a nonzero word is cleared.  The caller has synchronized the stream the
+// calls ran on.
+int noalloc_take_error(int device, unsigned* out) {
+  *out = 0;
+  if (device < 0 || device >= kMaxDevices) return PRANA_OK;
+  unsigned* word = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_slots[device].ready) word = g_slots[device].error;
+  }
+  if (!word) return PRANA_OK;
+  PRANA_CK(cudaMemcpy(out, word, sizeof(unsigned), cudaMemcpyDeviceToHost));
+  if (*out) PRANA_CK(cudaMemset(word, 0, sizeof(unsigned)));
+  return PRANA_OK;
+}
+
+}  // namespace prana
 
 using namespace prana;
 
@@ -94,6 +123,7 @@ extern "C" int prana_attention_decode_noalloc(prana_ctx* c, const float* q, cons
     a.part_o = slot->scratch + ml;
     a.counters = slot->counters;
     a.out = out;
+    a.err = slot->error;
     attn_make_maps(a, (int)(pos + 1));
     const cudaError_t e = launch_attn_decode(a, c->stream, false);
     if (e == cudaErrorInvalidValue) return fail(PRANA_E_UNSUPPORTED, "attention: head_dim %zu not built", hd);

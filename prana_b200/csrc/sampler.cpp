@@ -66,7 +66,7 @@ int prana_sampler_create(float temperature, uint64_t seed, prana_sampler** out) 
   if (!out) return fail(PRANA_E_INVALID, "null argument");
   prana_sampler* s = new (std::nothrow) prana_sampler();
   if (!s) return fail(PRANA_E_OOM, "host allocation failed");
-  s->greedy = !(temperature > 0.0f);
+  s->greedy = temperature <= 0.0f;  // as Sampler::new: a NaN temperature samples
   s->temp = temperature;
   s->state = seed ? seed : 1;  // XorShift::new: seed.max(1)
   *out = s;

@@ -40,6 +40,19 @@ def context(device: int | None = None) -> C.c_void_p:
     return ctx
 
 
+def synchronize(device: int | None = None) -> None:
+    """Wait for this device's kernel-level calls; raises PranaError
+    (PRANA_E_TIMEOUT) when a bounded device wait gave up in one of them."""
+    call("prana_ctx_synchronize", context(device))
+
+
+def debug_wait_timeout(which: int, polls: int, device: int | None = None) -> int:
+    """Run one bounded device wait on data that never arrives (0: an mbarrier,
+    1: the peer exchange's receive wait on local buffers) and return the status
+    code the library reports (PRANA_E_TIMEOUT, -6, when the wait gave up)."""
+    return int(_ffi.lib().prana_debug_wait_timeout(context(device), which, polls))
+
+
 def _ptr(t: torch.Tensor | None) -> C.c_void_p:
     if t is None:
         return C.c_void_p(0)

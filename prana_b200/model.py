@@ -172,6 +172,25 @@ def forward_trace(model: Model, cache: KvCache, token: int, pos: int):
     return logits, q, s
 
 
+def batch_trace(model: Model, cache: KvCache, tokens, pos0: int, prefill: bool):
+    """Diagnostic prefill (positions 0..n) or forward_batch (positions pos0..):
+    (logits [n, vocab] or None, int8 activation rows, their scales); per layer
+    the n rows of each site, then the final-norm rows (forward_batch only)."""
+    c = model.config
+    t = _u32(tokens)
+    n = t.size
+    total = n * (c.n_layers * (2 * c.dim + c.q_dim() + c.hidden_dim) + (0 if prefill else c.dim))
+    q = np.empty(total, np.int8)
+    s = np.empty(total // 32, np.float32)
+    logits = None if prefill else np.empty((n, c.vocab_size), np.float32)
+    got = C.c_size_t()
+    call("prana_forward_batch_trace", model.handle, cache.handle, t.ctypes.data_as(C.c_void_p), n, pos0,
+         int(prefill), logits.ctypes.data_as(C.c_void_p) if logits is not None else None,
+         q.ctypes.data_as(C.c_void_p), s.ctypes.data_as(C.c_void_p), total, C.byref(got))
+    assert got.value == total
+    return logits, q, s
+
+
 def prefill(model: Model, cache: KvCache, tokens) -> None:
     """prefill (infer.rs:220-286)."""
     t = _u32(tokens)
@@ -203,6 +222,28 @@ def forward_multi(model: Model, caches, tokens, positions, want_logits: bool = T
     call("prana_forward_multi", model.handle, handles, n, t.ctypes.data_as(C.c_void_p), pos.ctypes.data_as(C.c_void_p),
          logits.ctypes.data_as(C.c_void_p) if logits is not None else None, am.ctypes.data_as(C.c_void_p))
     return logits, am
+
+
+def forward_multi_trace(model: Model, caches, tokens, positions):
+    """Diagnostic forward_multi: (logits [n, vocab], int8 activation rows, scales)
+    in the batch-trace layout (per layer the n rows of each site, then the n
+    final-norm rows)."""
+    c = model.config
+    t = _u32(tokens)
+    n = t.size
+    assert len(caches) == n and len(positions) == n
+    handles = (C.c_void_p * n)(*[k.handle.value for k in caches])
+    pos = np.ascontiguousarray(positions, dtype=np.uint64)
+    total = n * (c.n_layers * (2 * c.dim + c.q_dim() + c.hidden_dim) + c.dim)
+    q = np.empty(total, np.int8)
+    s = np.empty(total // 32, np.float32)
+    logits = np.empty((n, c.vocab_size), np.float32)
+    got = C.c_size_t()
+    call("prana_forward_multi_trace", model.handle, handles, n, t.ctypes.data_as(C.c_void_p),
+         pos.ctypes.data_as(C.c_void_p), logits.ctypes.data_as(C.c_void_p), q.ctypes.data_as(C.c_void_p),
+         s.ctypes.data_as(C.c_void_p), total, C.byref(got))
+    assert got.value == total
+    return logits, q, s
 
 
 def generate(model: Model, prompt, steps: int, stop_id: int = -1) -> np.ndarray:

@@ -13,7 +13,7 @@ from ._ffi import call
 class Sampler:
     def __init__(self, temperature: float = 0.0, seed: int = 0):
         """Sampler::new (sampler.rs:13-20): greedy when temperature <= 0."""
-        self.greedy = not temperature > 0.0
+        self.greedy = temperature <= 0.0  # NaN samples, as in the reference
         self._h = C.c_void_p()
         call("prana_sampler_create", float(temperature), int(seed) & (2**64 - 1), C.byref(self._h))
 

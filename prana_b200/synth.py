@@ -123,6 +123,11 @@ LLAMA3_8B_Q8_0 = LLAMA3_8B_Q4_0.with_types(TYPE_Q8_0)
 # Profiling case: the 8B layer shapes with 4 layers (~0.8 GB of weights, still
 # far larger than L2), for captures that must hold little device memory.
 LLAMA3_8B_Q4_0_L4 = replace(LLAMA3_8B_Q4_0, n_layers=4)
+# Parity cases at the benchmarked width: every 8B tensor shape (dim 4096,
+# 32/8 heads, FFN 14336, vocab 128256) with 2 layers, so the CPU oracle keeps
+# up.
+LLAMA3_8B_Q4_0_L2 = replace(LLAMA3_8B_Q4_0, n_layers=2)
+LLAMA3_8B_Q8_0_L2 = replace(LLAMA3_8B_Q8_0, n_layers=2)
 
 # C5: Qwen2 shapes for speculative decode (Q8_0)
 QWEN2_0P5B_Q8 = replace(QWEN2_0P5B_MIX.with_types(TYPE_Q8_0), ctx=4096)
@@ -134,6 +139,8 @@ PRESETS = {
     "llama3_8b_q4_0": LLAMA3_8B_Q4_0,
     "llama3_8b_q8_0": LLAMA3_8B_Q8_0,
     "llama3_8b_q4_0_l4": LLAMA3_8B_Q4_0_L4,
+    "llama3_8b_q4_0_l2": LLAMA3_8B_Q4_0_L2,
+    "llama3_8b_q8_0_l2": LLAMA3_8B_Q8_0_L2,
     "qwen2_0p5b_q8_0": QWEN2_0P5B_Q8,
     "qwen2_1p5b_q8_0": QWEN2_1P5B_Q8,
 }

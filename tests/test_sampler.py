@@ -60,3 +60,14 @@ def test_draws_match_the_restatement_exactly():
                     want = i
                     break
             assert s.sample(logits) == want
+
+
+def test_nan_temperature_samples_like_the_reference():
+    """Sampler::new takes the temperature branch unless temp <= 0 (sampler.rs:14),
+    so a NaN temperature samples: every scaled logit is NaN, no bucket takes the
+    draw and the last id comes back, one draw consumed."""
+    s = Sampler(float("nan"), 5)
+    assert s.sample([1.0, 2.0, 3.0]) == 2
+    ref = XorShift(5)
+    ref.next_f32()
+    assert np.float32(s.next_f32()) == ref.next_f32()
