@@ -548,6 +548,23 @@ static __thread const int8_t *tr_fq;
 static __thread const float *tr_fs;
 static __thread size_t tr_site_off;
 static __thread int tr_site_forced;
+/* K/V rows: the f16 rows this pass computed (and their f32 values) are
+ * recorded per layer [K rows][V rows]; with tr_fkv set, the cache then holds
+ * the given rows instead (the f16 write is a rounding point like the int8
+ * sites). */
+static __thread uint16_t *tr_kv_own;
+static __thread float *tr_kv_val;
+static __thread const uint16_t *tr_fkv;
+static __thread size_t tr_kv_off, tr_kv_cap;
+
+/* n rows of kv_dim K (or V) values just written at cache row `first` */
+static void trace_kv(uint16_t *cache, size_t first, size_t kv_dim, const float *vals, size_t n) {
+  if (!tr_kv_own || tr_kv_off + n * kv_dim > tr_kv_cap) return;
+  memcpy(tr_kv_own + tr_kv_off, cache + first * kv_dim, n * kv_dim * sizeof(uint16_t));
+  memcpy(tr_kv_val + tr_kv_off, vals, n * kv_dim * sizeof(float));
+  if (tr_fkv) memcpy(cache + first * kv_dim, tr_fkv + tr_kv_off, n * kv_dim * sizeof(uint16_t));
+  tr_kv_off += n * kv_dim;
+}
 
 static void trace_site(const float *x, size_t n) {
   tr_site_forced = 0;
@@ -601,6 +618,8 @@ void or_forward(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float 
     rope_row(c, k, kv_dim, pos);
     or_f16_kv_write(or_kv_layer(kv, (int)l, 0), pos, kv_dim, k, kv_dim);
     or_f16_kv_write(or_kv_layer(kv, (int)l, 1), pos, kv_dim, v, kv_dim);
+    trace_kv(or_kv_layer(kv, (int)l, 0), pos, kv_dim, k, 1);
+    trace_kv(or_kv_layer(kv, (int)l, 1), pos, kv_dim, v, 1);
     or_attention_decode(q, or_kv_layer(kv, (int)l, 0), or_kv_layer(kv, (int)l, 1), pos, c->n_heads,
                         c->n_kv_heads, hd, att);
     trace_site(att, q_dim);
@@ -624,6 +643,13 @@ void or_forward(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float 
   free(x); free(xb); free(q); free(k); free(v); free(att); free(o); free(g); free(u); free(dn);
 }
 
+static void trace_kv_begin(uint16_t *own, float *val, const uint16_t *fkv, size_t cap) {
+  tr_kv_own = own;
+  tr_kv_val = val;
+  tr_fkv = fkv;
+  tr_kv_off = 0;
+  tr_kv_cap = cap;
+}
 static void trace_begin(int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq, const float *fs) {
   tr_q = q;
   tr_s = s;
@@ -636,6 +662,9 @@ static void trace_begin(int8_t *q, float *s, float *vals, size_t cap, const int8
 }
 static size_t trace_end(void) {
   size_t n = tr_nq;
+  tr_kv_own = NULL;
+  tr_kv_val = NULL;
+  tr_fkv = NULL;
   tr_q = NULL;
   tr_s = NULL;
   tr_v = NULL;
@@ -653,8 +682,10 @@ size_t or_forward_trace(const or_model *m, or_kv *kv, uint32_t token, size_t pos
 }
 
 size_t or_forward_trace_forced(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float *logits,
-                               int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq, const float *fs) {
+                               int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq, const float *fs,
+                               uint16_t *kv_own, float *kv_val, const uint16_t *fkv, size_t kv_cap) {
   trace_begin(q, s, vals, cap, fq, fs);
+  trace_kv_begin(kv_own, kv_val, fkv, kv_cap);
   or_forward(m, kv, token, pos, logits);
   return trace_end();
 }
@@ -715,6 +746,8 @@ static void batch_body(const or_model *m, or_kv *kv, const uint32_t *toks, size_
     uint16_t *kc = or_kv_layer(kv, (int)l, 0), *vc = or_kv_layer(kv, (int)l, 1);
     or_f16_kv_write(kc, pos0, kv_dim, k, n * kv_dim);
     or_f16_kv_write(vc, pos0, kv_dim, v, n * kv_dim);
+    trace_kv(kc, pos0, kv_dim, k, n);
+    trace_kv(vc, pos0, kv_dim, v, n);
     if (verify) or_attention_verify(q, kc, vc, pos0, n, c->n_heads, c->n_kv_heads, hd, att);
     else or_attention(q, k, v, n, c->n_heads, c->n_kv_heads, hd, att);
     trace_site(att, n * q_dim);
@@ -754,8 +787,9 @@ void or_forward_batch(const or_model *m, or_kv *kv, const uint32_t *tokens, size
  * the rows the matmuls take. */
 size_t or_batch_trace(const or_model *m, or_kv *kv, const uint32_t *tokens, size_t n, size_t pos0, int verify,
                       float *logits_out, int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq,
-                      const float *fs) {
+                      const float *fs, uint16_t *kv_own, float *kv_val, const uint16_t *fkv, size_t kv_cap) {
   trace_begin(q, s, vals, cap, fq, fs);
+  trace_kv_begin(kv_own, kv_val, fkv, kv_cap);
   batch_body(m, kv, tokens, n, verify ? pos0 : 0, verify, logits_out);
   return trace_end();
 }

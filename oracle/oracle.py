@@ -92,8 +92,8 @@ def lib() -> C.CDLL:
             "or_kv_layer": ([P, C.c_int, C.c_int], P),
             "or_forward": ([P, P, C.c_uint32, SZ, P], None),
             "or_forward_trace": ([P, P, C.c_uint32, SZ, P, P, P, P, SZ], SZ),
-            "or_forward_trace_forced": ([P, P, C.c_uint32, SZ, P, P, P, P, SZ, P, P], SZ),
-            "or_batch_trace": ([P, P, P, SZ, SZ, C.c_int, P, P, P, P, SZ, P, P], SZ),
+            "or_forward_trace_forced": ([P, P, C.c_uint32, SZ, P, P, P, P, SZ, P, P, P, P, P, SZ], SZ),
+            "or_batch_trace": ([P, P, P, SZ, SZ, C.c_int, P, P, P, P, SZ, P, P, P, P, P, SZ], SZ),
             "or_prefill": ([P, P, P, SZ], None),
             "or_forward_batch": ([P, P, P, SZ, SZ, P], None),
             "or_generate": ([P, P, SZ, SZ, C.c_int64, P], SZ),
@@ -199,55 +199,87 @@ class OModel:
         c = self.c
         return c.n_layers * (2 * c.dim + c.n_heads * c.head_dim + c.hidden_dim) + c.dim
 
-    def forward_trace(self, kv: "OKv", token: int, pos: int, with_values: bool = False, force=None):
+    def kv_trace_len(self, rows: int = 1) -> int:
+        return self.c.n_layers * 2 * rows * self.c.n_kv_heads * self.c.head_dim
+
+    def forward_trace(self, kv: "OKv", token: int, pos: int, with_values: bool = False, force=None, force_kv=None):
         """(logits, int8 activation rows, scales[, the f32 values quantized]) in forward order.
 
         force = (q, scales) of another pass's trace: the oracle still records
-        its own quantized rows, but every matmul takes the given rows instead
-        (test instrumentation; see or_forward_trace_forced)."""
+        its own quantized rows, but every matmul takes the given rows instead.
+        force_kv = f16 K/V rows of another pass (per layer: the K row, then the
+        V row): the cache keeps those instead of this pass's own; the return
+        value then ends with (own f16 rows, their f32 values).  Test
+        instrumentation (or_forward_trace_forced)."""
         n = self.trace_len()
         q = np.empty(n, np.int8)
         s = np.empty(n // 32, np.float32)
         v = np.empty(n, np.float32) if with_values else None
         lg = np.empty(self.c.vocab_size, np.float32)
-        if force is None:
+        if force is None and force_kv is None:
             got = lib().or_forward_trace(self.h, kv.h, token, pos, ptr(lg), ptr(q), ptr(s),
                                          ptr(v) if v is not None else None, n)
-        else:
+            assert got == n
+            return (lg, q, s, v) if with_values else (lg, q, s)
+        fq = fs = fkv = kv_own = kv_val = None
+        if force is not None:
             fq = np.ascontiguousarray(force[0], np.int8)
             fs = np.ascontiguousarray(force[1], np.float32)
             assert fq.size == n and fs.size == n // 32
-            got = lib().or_forward_trace_forced(self.h, kv.h, token, pos, ptr(lg), ptr(q), ptr(s),
-                                                ptr(v) if v is not None else None, n, ptr(fq), ptr(fs))
+        nkv = self.kv_trace_len(1)
+        if force_kv is not None:
+            fkv = np.ascontiguousarray(force_kv, np.uint16).reshape(-1)
+            assert fkv.size == nkv
+            kv_own = np.empty(nkv, np.uint16)
+            kv_val = np.empty(nkv, np.float32)
+        got = lib().or_forward_trace_forced(self.h, kv.h, token, pos, ptr(lg), ptr(q), ptr(s),
+                                            ptr(v) if v is not None else None, n,
+                                            ptr(fq) if fq is not None else None, ptr(fs) if fs is not None else None,
+                                            ptr(kv_own) if kv_own is not None else None,
+                                            ptr(kv_val) if kv_val is not None else None,
+                                            ptr(fkv) if fkv is not None else None, nkv)
         assert got == n
-        return (lg, q, s, v) if with_values else (lg, q, s)
+        out = (lg, q, s, v) if with_values else (lg, q, s)
+        return out + (kv_own, kv_val) if force_kv is not None else out
 
     def batch_trace_len(self, n: int, verify: bool) -> int:
         c = self.c
         return n * (c.n_layers * (2 * c.dim + c.n_heads * c.head_dim + c.hidden_dim) + (c.dim if verify else 0))
 
-    def batch_trace(self, kv: "OKv", tokens, pos0: int, verify: bool, with_values: bool = False, force=None):
+    def batch_trace(self, kv: "OKv", tokens, pos0: int, verify: bool, with_values: bool = False, force=None,
+                    force_kv=None):
         """prefill (verify False, positions 0..n) or forward_batch (verify True) with
         the activation trace: per layer the n rows of each site, then the
         final-norm rows (verify only).  Returns (logits [n, vocab] or None, q,
-        scales[, values]); force as in forward_trace."""
+        scales[, values][, own K/V rows, their f32 values]); force and force_kv
+        (per layer: n K rows, then n V rows) as in forward_trace."""
         t = np.ascontiguousarray(tokens, np.uint32)
         n = self.batch_trace_len(t.size, verify)
         q = np.empty(n, np.int8)
         s = np.empty(n // 32, np.float32)
         v = np.empty(n, np.float32) if with_values else None
         lg = np.empty((t.size, self.c.vocab_size), np.float32) if verify else None
-        fq = fs = None
+        fq = fs = fkv = kv_own = kv_val = None
         if force is not None:
             fq = np.ascontiguousarray(force[0], np.int8)
             fs = np.ascontiguousarray(force[1], np.float32)
             assert fq.size == n and fs.size == n // 32
+        nkv = self.kv_trace_len(t.size)
+        if force_kv is not None:
+            fkv = np.ascontiguousarray(force_kv, np.uint16).reshape(-1)
+            assert fkv.size == nkv
+            kv_own = np.empty(nkv, np.uint16)
+            kv_val = np.empty(nkv, np.float32)
         got = lib().or_batch_trace(self.h, kv.h, ptr(t), t.size, pos0, int(verify),
                                    ptr(lg) if lg is not None else None, ptr(q), ptr(s),
                                    ptr(v) if v is not None else None, n,
-                                   ptr(fq) if fq is not None else None, ptr(fs) if fs is not None else None)
+                                   ptr(fq) if fq is not None else None, ptr(fs) if fs is not None else None,
+                                   ptr(kv_own) if kv_own is not None else None,
+                                   ptr(kv_val) if kv_val is not None else None,
+                                   ptr(fkv) if fkv is not None else None, nkv)
         assert got == n
-        return (lg, q, s, v) if with_values else (lg, q, s)
+        out = (lg, q, s, v) if with_values else (lg, q, s)
+        return out + (kv_own, kv_val) if force_kv is not None else out
 
     def prefill(self, kv: "OKv", tokens):
         t = np.ascontiguousarray(tokens, np.uint32)

@@ -163,11 +163,17 @@ void or_forward(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float 
  * input, attention output, ffn-norm input, silu(g)*u; then the final-norm input) */
 size_t or_forward_trace(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float *logits, int8_t *q,
                         float *s, float *vals /* f32 values quantized, may be NULL */, size_t cap);
+/* Test instrumentation: or_forward_trace whose matmuls take the given rows
+ * (fq / fs, may be NULL) and whose K/V cache rows become the given f16 rows
+ * (fkv, may be NULL) after the pass's own rows and their f32 values are
+ * recorded in kv_own / kv_val (per layer: K rows, then V rows). */
 size_t or_forward_trace_forced(const or_model *m, or_kv *kv, uint32_t token, size_t pos, float *logits,
-                               int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq, const float *fs);
+                               int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq, const float *fs,
+                               uint16_t *kv_own, float *kv_val, const uint16_t *fkv, size_t kv_cap);
+/* prefill (verify == 0) or forward_batch (verify == 1) with the same trace and forcing */
 size_t or_batch_trace(const or_model *m, or_kv *kv, const uint32_t *tokens, size_t n, size_t pos0, int verify,
                       float *logits_out, int8_t *q, float *s, float *vals, size_t cap, const int8_t *fq,
-                      const float *fs);
+                      const float *fs, uint16_t *kv_own, float *kv_val, const uint16_t *fkv, size_t kv_cap);
 /* batched prompt, no logits (infer.rs:220-286) */
 void or_prefill(const or_model *m, or_kv *kv, const uint32_t *tokens, size_t n);
 /* verify pass: logits [n][vocab] (infer.rs:296-374) */

@@ -13,7 +13,7 @@ KV rows are the benchmark's seeded N(0, 0.5) f16 rows.
 import numpy as np
 import pytest
 
-from parity import Flips, check_logits, check_trace
+from parity import Flips, check_logits, forced_decode
 from prana_b200 import model as pm
 from prana_b200 import synth
 
@@ -52,9 +52,7 @@ def test_full_width_decode_at_ctx_4096(tmp_path, gpu, oracle, preset):
             for layer in range(c.n_layers):
                 for is_v in (False, True):
                     gkv.write(layer, is_v, okv.layer(layer, is_v)[:pos])
-            lg_g, q_g, s_g = pm.forward_trace(gm, gkv, tok, pos)
-            lg_o, q_o, s_o, v_o = om.forward_trace(okv, tok, pos, with_values=True, force=(q_g, s_g))
-            check_trace(c, q_g, s_g, q_o, s_o, v_o, flips, f"{preset} pos {pos}")
+            lg_g, lg_o = forced_decode(om, okv, gm, gkv, tok, pos, flips, f"{preset} pos {pos}")
             gated += check_logits(lg_g, lg_o, f"{preset} pos {pos}")
             # the CUDA-graph decode step computes the traced pass's logits
             lg_p, nxt = pm.forward(gm, gkv, tok, pos)

@@ -11,7 +11,7 @@ margin exceeds 1e-3 -- for single-token decode, prefill, forward_batch
 import numpy as np
 import pytest
 
-from parity import Flips, check_logits, check_trace
+from parity import Flips, check_logits, forced_batch, forced_decode
 from prana_b200 import model as pm
 from prana_b200 import synth
 from prana_b200._ffi import TYPE_Q4_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0
@@ -55,20 +55,6 @@ def copy_cache(okv, gkv, n_layers, rows):
             gkv.write(layer, is_v, okv.layer(layer, is_v)[:rows])
 
 
-def f16_key(bits):
-    """f16 bit patterns on one ordered integer line (+0 and -0 both 0)."""
-    b = np.asarray(bits).astype(np.int32)
-    return np.where(b & 0x8000, -(b & 0x7FFF), b)
-
-
-def check_caches(okv, gkv, n_layers, rows, where):
-    """K/V rows written from the same int8 inputs: f16 values equal or one ulp apart."""
-    for layer in range(n_layers):
-        for is_v in (False, True):
-            d = np.abs(f16_key(gkv.read(layer, is_v, rows)) - f16_key(okv.layer(layer, is_v)[:rows]))
-            assert int(d.max()) <= 1, f"{where}: layer {layer} {'V' if is_v else 'K'} differs by {int(d.max())} ulps"
-
-
 ALL = [n for n in SPECS if n != "qwen2_draft"]
 
 
@@ -86,9 +72,7 @@ def test_forward_teacher_forced(models, name):
     for pos in range(steps):
         copy_cache(okv, gkv, c.n_layers, pos)
         tok = int(rng.integers(c.vocab_size))
-        lg_g, q_g, s_g = pm.forward_trace(gm, gkv, tok, pos)
-        lg_o, q_o, s_o, v_o = om.forward_trace(okv, tok, pos, with_values=True, force=(q_g, s_g))
-        check_trace(c, q_g, s_g, q_o, s_o, v_o, flips, f"{name} pos {pos}")
+        lg_g, lg_o = forced_decode(om, okv, gm, gkv, tok, pos, flips, f"{name} pos {pos}")
         gated += check_logits(lg_g, lg_o, f"{name} pos {pos}")
         # the forward path without the trace gives the same logits
         lg_p, nxt = pm.forward(gm, gkv, tok, pos)
@@ -108,16 +92,11 @@ def test_prefill_then_decode(models, name):
     n = len(toks)
     okv, gkv = om.kv(40), pm.KvCache(gm, 40)
     flips = Flips()
-    _, q_g, s_g = pm.batch_trace(gm, gkv, toks, 0, prefill=True)
-    _, q_o, s_o, v_o = om.batch_trace(okv, toks, 0, verify=False, with_values=True, force=(q_g, s_g))
-    check_trace(c, q_g, s_g, q_o, s_o, v_o, flips, f"{name} prefill", rows=n, final=False)
-    check_caches(okv, gkv, c.n_layers, n, f"{name} prefill")
-    lg_g, q_g, s_g = pm.forward_trace(gm, gkv, 9, n)
-    lg_o, q_o, s_o, v_o = om.forward_trace(okv, 9, n, with_values=True, force=(q_g, s_g))
-    check_trace(c, q_g, s_g, q_o, s_o, v_o, flips, f"{name} decode after prefill")
+    forced_batch(om, okv, gm, gkv, toks, 0, True, flips, f"{name} prefill")
+    lg_g, lg_o = forced_decode(om, okv, gm, gkv, 9, n, flips, f"{name} decode after prefill")
     check_logits(lg_g, lg_o, f"{name} decode after prefill")
     assert flips.bounded()
-    # the prefill entry point is the traced pass
+    # the prefill entry point computes the traced pass's cache rows
     kv2 = pm.KvCache(gm, 40)
     pm.prefill(gm, kv2, toks)
     for layer in range(c.n_layers):
@@ -138,9 +117,7 @@ def test_forward_batch(models, name, n):
     om.prefill(okv, pre)
     copy_cache(okv, gkv, c.n_layers, len(pre))
     flips = Flips()
-    lg_g, q_g, s_g = pm.batch_trace(gm, gkv, toks, len(pre), prefill=False)
-    lg_o, q_o, s_o, v_o = om.batch_trace(okv, toks, len(pre), verify=True, with_values=True, force=(q_g, s_g))
-    check_trace(c, q_g, s_g, q_o, s_o, v_o, flips, f"{name} n={n}", rows=n)
+    lg_g, lg_o = forced_batch(om, okv, gm, gkv, toks, len(pre), False, flips, f"{name} n={n}")
     for i in range(n):
         check_logits(lg_g[i], lg_o[i], f"{name} n={n} row {i}")
     assert flips.bounded()
@@ -168,16 +145,12 @@ def test_generate_greedy_tokens(models, name):
     p = len(prompt)
     okv, gkv = om.kv(p + steps), pm.KvCache(gm, p + steps)
     flips = Flips()
-    _, q_g, s_g = pm.batch_trace(gm, gkv, prompt[:-1], 0, prefill=True)
-    _, q_o, s_o, v_o = om.batch_trace(okv, prompt[:-1], 0, verify=False, with_values=True, force=(q_g, s_g))
-    check_trace(c, q_g, s_g, q_o, s_o, v_o, flips, f"{name} prompt", rows=p - 1, final=False)
+    forced_batch(om, okv, gm, gkv, prompt[:-1], 0, True, flips, f"{name} prompt")
     tok, gated = int(prompt[-1]), 0
     for i in range(len(got)):
         pos = p - 1 + i
-        lg_g, q_g, s_g = pm.forward_trace(gm, gkv, tok, pos)
+        lg_g, lg_o = forced_decode(om, okv, gm, gkv, tok, pos, flips, f"{name} step {i}")
         assert int(np.argmax(lg_g)) == int(got[i]), f"{name}: step {i} of the decode loop differs from the traced pass"
-        lg_o, q_o, s_o, v_o = om.forward_trace(okv, tok, pos, with_values=True, force=(q_g, s_g))
-        check_trace(c, q_g, s_g, q_o, s_o, v_o, flips, f"{name} step {i}")
         gated += check_logits(lg_g, lg_o, f"{name} step {i}")
         tok = int(got[i])
     assert flips.bounded()

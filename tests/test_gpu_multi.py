@@ -13,7 +13,7 @@ K/V rows the first one wrote are exercised by the second.
 import numpy as np
 import pytest
 
-from parity import Flips, check_logits, check_trace, row_trace
+from parity import Flips, check_logits, check_trace, gpu_kv_rows, row_trace
 from prana_b200 import model as pm
 from prana_b200 import synth
 from prana_b200._ffi import TYPE_Q4_0, TYPE_Q6_K, TYPE_Q8_0, PranaError
@@ -65,8 +65,11 @@ def test_forward_multi_matches_oracle(tmp_path, gpu, oracle, name):
             lg, q, s = pm.forward_multi_trace(m, gkvs, toks, pos + step)
             for i in range(N_SEQ):
                 qi, si = row_trace(q, s, c, N_SEQ, i)
-                lo, q_o, s_o, v_o = om.forward_trace(okvs[i], int(toks[i]), int(pos[i]) + step, with_values=True,
-                                                      force=(qi, si))
+                p_i = int(pos[i]) + step
+                kv_g = gpu_kv_rows(gkvs[i], c.n_layers, p_i, 1)
+                lo, q_o, s_o, v_o, kv_o, kv_v = om.forward_trace(okvs[i], int(toks[i]), p_i, with_values=True,
+                                                                  force=(qi, si), force_kv=kv_g)
+                flips.check_kv(kv_g, kv_o, kv_v, f"{name} step {step} seq {i}", c.n_kv_heads * c.head_dim)
                 check_trace(c, qi, si, q_o, s_o, v_o, flips, f"{name} step {step} seq {i}")
                 gated += check_logits(lg[i], lo, f"{name} step {step} seq {i}")
         assert flips.bounded()
