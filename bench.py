@@ -63,6 +63,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--batch-seqs", type=int, default=16,
                    help="also time this many independent sequences per step (0: skip; single GPU only)")
+    p.add_argument("--configs", default=None,
+                   help="comma list of the other BASELINE configs to measure in the same line "
+                        "(c1,c2,c3,c4q8; default: all on one GPU, none under tensor parallelism)")
     return p.parse_args()
 
 
@@ -108,7 +111,7 @@ def launches_per_step(spec, world=1, peer=False) -> int:
 
 
 class Clocks:
-    """nvidia-smi samples (every 100 ms) kept only when they fall inside the timed region."""
+    """nvidia-smi samples (every 20 ms) kept only when they fall inside the timed region."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -124,7 +127,7 @@ class Clocks:
         """Start sampling; returns once the first sample is in, so the region that follows is covered."""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except FileNotFoundError:
             self.proc = None
@@ -168,30 +171,63 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_decode(path, ctx, kv_rows_fn, n_layers, kv_dim, seconds, token=17, max_steps=None):
-    """Time the CPU oracle decoding from `ctx` with the given KV rows; returns (tok/s, steps, threads)."""
+def margin(lg) -> float:
+    """top-2 logit margin relative to the largest magnitude (the greedy-parity gate)."""
+    srt = np.sort(np.asarray(lg, np.float64))
+    return float((srt[-1] - srt[-2]) / max(float(np.max(np.abs(lg))), 1e-30))
+
+
+PARITY_RULE = ("CPU oracle fed the GPU's tokens (same seeded KV, same start); a token counts as gated when the "
+               "oracle's top-2 margin exceeds 1e-3 of the largest logit, and identical when the GPU chose the "
+               "oracle's argmax")
+
+
+def cpu_decode(path, ctx, kv_rows_fn, n_layers, kv_dim, seconds, token=17, max_steps=None, threads=None,
+               follow=None):
+    """Time the CPU oracle decoding from position `ctx` after the given KV rows.
+
+    Starts from (token, ctx) like the GPU loop.  With `follow` (the GPU's tokens
+    from the same start) the oracle is fed those tokens and each of its argmaxes
+    is compared with the GPU's (margin-gated).  Returns (tok/s, steps, threads,
+    tier, seconds, parity or None)."""
     from oracle import oracle as orc
 
-    threads = os.cpu_count() or 1
+    threads = threads or os.cpu_count() or 1
     orc.lib().or_pool_set_threads(threads)
     om = orc.OModel(str(path), orc.TIER_AUTO)
     kv = om.kv(ctx + 64)
     for layer in range(n_layers):
         for is_v in (False, True):
             kv.set_layer(layer, is_v, kv_rows_fn(layer, is_v))
-    om.forward(kv, token, ctx)  # warm the pool and caches
-    t0 = time.perf_counter()
-    steps, pos, tok = 0, ctx + 1, token
+    cmp = gated = same = 0
+    steps, pos, tok = 0, ctx, token
+    t0 = None
     while True:
         lg = om.forward(kv, tok, pos)
-        tok = int(np.argmax(lg))
+        mine = int(np.argmax(lg))
+        if follow is not None and steps < len(follow):
+            cmp += 1
+            if margin(lg) > 1e-3:
+                gated += 1
+                same += int(mine == int(follow[steps]))
+            tok = int(follow[steps])
+        else:
+            tok = mine
         steps += 1
         pos += 1
+        if t0 is None:  # the first step warms the pool and caches
+            t0, steps = time.perf_counter(), 0
+            if follow is not None:
+                follow = follow[1:]
+            continue
         el = time.perf_counter() - t0
         if el >= seconds or (max_steps and steps >= max_steps) or pos >= ctx + 60:
             break
     tier = {1: "scalar", 2: "avx2", 3: "vnni"}[orc.lib().or_default_tier()]
-    return steps / el, steps, threads, tier, el
+    parity = None
+    if follow is not None:
+        parity = {"tokens_compared": cmp, "margin_gated": gated, "identical": same, "rule": PARITY_RULE}
+    return steps / el, steps, threads, tier, el, parity
 
 
 def reference_arm(args):
@@ -203,8 +239,8 @@ def reference_arm(args):
     spec, path = model_path(args, 0)
     kv_dim = spec.n_kv_heads * spec.head_dim
     budget = max(30.0, min(150.0, (args.steps + args.warmup) * 2.0))
-    tps, steps, threads, tier, el = cpu_decode(path, args.ctx, lambda l, v: seeded_kv_rows(l, v, args.ctx, kv_dim),
-                                               spec.n_layers, kv_dim, budget, max_steps=args.steps)
+    tps, steps, threads, tier, el, _ = cpu_decode(path, args.ctx, lambda l, v: seeded_kv_rows(l, v, args.ctx, kv_dim),
+                                                  spec.n_layers, kv_dim, budget, max_steps=args.steps)
     sample = (f"{steps} greedy decode tokens at positions {args.ctx + 1}.. from seeded KV ({args.workload}), "
               f"{threads} threads, {tier} tier, {el:.1f} s; C restatement of Prana's CPU path (Rust toolchain absent)")
     line = {"metric": METRIC, "value": round(tps, 4), "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
@@ -297,6 +333,332 @@ def batch_decode(torch, model, args, stream, steps=24, warmup=3):
             kv.close()
 
 
+# ---------------------------------------------------------------- the other BASELINE configs
+#
+# Each returns one object of the line's "configs": the config's metric measured
+# on this GPU through the same public API (value: device-resident loop; e2e:
+# host ids in and out), its roofline where one applies, and the CPU oracle on
+# a bounded sample of the same workload beside it.
+
+
+def _preset_path(args, name):
+    from prana_b200 import synth
+
+    spec = synth.PRESETS[name]
+    d = Path(args.model_dir)
+    d.mkdir(parents=True, exist_ok=True)
+    path = d / f"{name}_seed{spec.seed}.gguf"
+    if not path.exists():
+        tmp = path.with_suffix(".tmp")
+        synth.write_gguf(spec, tmp)
+        tmp.rename(path)
+    return spec, path
+
+
+def _events(torch):
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def suite_c1(torch, args, peak):
+    """C1: stories15M shape, Q8_0: 8 seeded prompt ids, greedy 248 tokens, bs 1."""
+    from oracle import oracle as orc
+    from prana_b200 import model as pm
+
+    spec, path = _preset_path(args, "stories15m_q8_0")
+    model = pm.Model.load(str(path), 0)
+    try:
+        rng = np.random.default_rng(1234)
+        prompt = rng.integers(spec.vocab, size=8).astype(np.uint32)
+        steps = spec.ctx - len(prompt)  # 248: the context fills exactly
+        stream = torch.cuda.ExternalStream(model.stream())
+        pm.generate(model, prompt, steps)  # warm: graphs captured
+        torch.cuda.synchronize()
+        # e2e: prana_generate (prefill of 7 ids, then the device loop; ids back to the host)
+        reps = 5
+        e0, e1 = _events(torch)
+        e0.record(stream)
+        for _ in range(reps):
+            got = pm.generate(model, prompt, steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_gen = e0.elapsed_time(e1) / reps
+        # value: the device-resident decode loop alone over the same 248 positions
+        kv = pm.KvCache(model, spec.ctx)
+        pm.prefill(model, kv, prompt[:-1])
+        loop = pm.DecodeLoop(model, kv)
+        loop.begin(int(prompt[-1]), len(prompt) - 1)
+        loop.run(4)
+        torch.cuda.synchronize()
+        loop.begin(int(prompt[-1]), len(prompt) - 1)
+        e0, e1 = _events(torch)
+        e0.record(stream)
+        loop.run(steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_loop = e0.elapsed_time(e1) / steps
+        kv.close()
+        # CPU oracle: the same generate
+        orc.lib().or_pool_set_threads(os.cpu_count() or 1)
+        om = orc.OModel(str(path), orc.TIER_AUTO)
+        om.generate(prompt, 8)
+        t0 = time.perf_counter()
+        ref = om.generate(prompt, steps)
+        el = time.perf_counter() - t0
+        # greedy parity: the oracle fed the GPU's tokens, margin-gated
+        okv = om.kv(spec.ctx)
+        om.prefill(okv, prompt[:-1])
+        tok, gated, same = int(prompt[-1]), 0, 0
+        for i in range(len(got)):
+            lg = om.forward(okv, tok, len(prompt) - 1 + i)
+            if margin(lg) > 1e-3:
+                gated += 1
+                same += int(int(np.argmax(lg)) == int(got[i]))
+            tok = int(got[i])
+        agree = int(np.argmax(np.concatenate([got != ref, [True]])))
+        wb = spec.weight_bytes_per_token()
+        return {
+            "metric": "decode tok/s at batch 1 (greedy 248 tokens after an 8-id prompt)", "unit": UNIT,
+            "value": round(1000.0 / ms_loop, 1), "ms_per_step": round(ms_loop, 4),
+            "e2e": {"value": round(steps * 1000.0 / ms_gen, 1), "unit": UNIT, "path": "prana_generate per call",
+                    "h2d_bytes_per_step": round(len(prompt) * 4 / steps, 3), "d2h_bytes_per_step": 4},
+            "step_roofline": {"bytes_per_token": wb, "achieved_gbs": round(wb / ms_loop / 1e6, 1),
+                              "frac": round(wb / ms_loop / 1e6 / peak, 4),
+                              "note": "16 MB per token fits in L2; the step is launch/latency-bound"},
+            "cpu_baseline": {"value": round(steps / el, 1), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"oracle generate, {steps} tokens, {el:.2f} s"},
+            "parity": {"tokens_compared": len(got), "margin_gated": gated, "identical": same,
+                       "free_running_identical_prefix": agree, "rule": PARITY_RULE},
+            "config": {"workload": "stories15m_q8_0", "prompt": len(prompt), "steps": steps, "batch": 1},
+        }
+    finally:
+        model.close()
+
+
+GEMV_SHAPES = (4096, 11008, 14336)
+GEMV_ROWS = (1, 4, 8, 64)
+
+
+def suite_c2(torch, args, peak):
+    """C2: the quantized GEMV/GEMM microbench, K = 4096, weights rotating over
+    copies larger than twice L2, activations quantized per row (matmul_*_prefill)."""
+    from oracle import oracle as orc
+    from prana_b200 import kernels as K
+    from prana_b200 import synth
+    from prana_b200._ffi import TYPE_NAMES, TYPE_Q4_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0
+
+    cols = 4096
+    bpw = {TYPE_Q8_0: 34 / 32, TYPE_Q4_0: 18 / 32, TYPE_Q4_K: 144 / 256, TYPE_Q6_K: 210 / 256}
+    out = {}
+    side = torch.cuda.Stream()
+    cpu = {}
+    orc.lib().or_pool_set_threads(os.cpu_count() or 1)
+    for ty in (TYPE_Q8_0, TYPE_Q4_0, TYPE_Q4_K, TYPE_Q6_K):
+        res = {}
+        for rows in GEMV_SHAPES:
+            raw = synth.matrix(ty, rows, cols, seed=700 + rows)
+            wbytes = rows * cols * bpw[ty]
+            n_copies = max(4, int(np.ceil(2.2 * 126e6 / wbytes)))
+            copies = [K.QuantMatrix(ty, rows, cols, raw) for _ in range(n_copies)]
+            fn = K.matmul_q8_prefill if ty == TYPE_Q8_0 else K.matmul_kquant_prefill
+            per = {}
+            for m in GEMV_ROWS:
+                acts = K.quantize_acts(torch.randn(m, cols, device="cuda"))
+                iters = 2 * n_copies
+                with torch.cuda.stream(side):
+                    for w in copies:
+                        fn(acts, w)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=side, capture_error_mode="relaxed"):
+                    for i in range(iters):
+                        fn(acts, copies[i % n_copies])
+                graph.replay()
+                torch.cuda.synchronize()
+                e0, e1 = _events(torch)
+                e0.record(side)
+                with torch.cuda.stream(side):
+                    graph.replay()
+                e1.record(side)
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1000.0 / iters
+                g = cols // 32
+                alg = wbytes + m * (cols + 8 * g) + m * rows * 4
+                gbs = alg / (us * 1e-6) / 1e9
+                per[str(m)] = {"us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+                del graph
+            res[str(rows)] = per
+            if rows == 4096:  # the CPU reference GEMV at batch 1 (the reference's `prana bench` shape family)
+                om = orc.OMatrix(ty, rows, cols, raw)
+                a = np.random.default_rng(1).standard_normal(cols).astype(np.float32)
+                om.matmul(a)
+                t0 = time.perf_counter()
+                n_it = 0
+                while time.perf_counter() - t0 < 1.0:
+                    om.matmul(a)
+                    n_it += 1
+                el = (time.perf_counter() - t0) / n_it
+                cpu[TYPE_NAMES[ty]] = {"us": round(el * 1e6, 1), "gbs": round(wbytes / el / 1e9, 2)}
+            del copies
+        out[TYPE_NAMES[ty]] = res
+    return {"metric": "quant GEMV HBM GB/s as % of B200 peak", "unit": "GB/s", "peak": peak, "k": cols,
+            "results": out,
+            "algorithmic_bytes": "N*K*bpw (GGUF bytes) + M*(K + 8*K/32) + M*N*4",
+            "l2": "weights rotate over copies totalling > 2.2 x 126 MB",
+            "path": "M <= 8: streaming dp4a GEMV; M > 8: the same, 8 rows per launch",
+            "cpu_baseline": {"results_m1_n4096": cpu, "cores": os.cpu_count(), "kind": "port",
+                             "sample": "oracle matmul at batch 1, 1 s per format"},
+            "config": {"workload": "gemv_microbench", "k": cols, "n": list(GEMV_SHAPES), "m": list(GEMV_ROWS)}}
+
+
+def suite_c3(torch, args, peak):
+    """C3: Qwen2-0.5B shape, Q4_K/Q6_K-style mixture: prefill 2048 seeded ids,
+    then greedy decode 256 over the prefilled cache."""
+    from prana_b200 import model as pm
+
+    spec, path = _preset_path(args, "qwen2_0p5b_mix")
+    model = pm.Model.load(str(path), 0)
+    try:
+        c = model.config
+        rng = np.random.default_rng(2048)
+        prompt = rng.integers(spec.vocab, size=2048).astype(np.uint32)
+        steps = 256
+        stream = torch.cuda.ExternalStream(model.stream())
+        kv = pm.KvCache(model, len(prompt) + steps + 8)
+        pm.prefill(model, kv, prompt[:64])  # warm
+        torch.cuda.synchronize()
+        e0, e1 = _events(torch)
+        e0.record(stream)
+        pm.prefill(model, kv, prompt[:-1])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_prefill = e0.elapsed_time(e1)
+        loop = pm.DecodeLoop(model, kv)
+        loop.begin(int(prompt[-1]), len(prompt) - 1)
+        loop.run(4)
+        torch.cuda.synchronize()
+        loop.begin(int(prompt[-1]), len(prompt) - 1)
+        e0, e1 = _events(torch)
+        e0.record(stream)
+        loop.run(steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        # e2e: prana_forward per token, host id in and out, continuing the sequence
+        toks = loop.tokens(steps)
+        pos, tok = len(prompt) - 1 + steps, int(toks[-1])
+        n_e2e = 64
+        kv2 = pm.KvCache(model, len(prompt) + steps + n_e2e + 8)
+        for layer in range(c.n_layers):
+            for is_v in (False, True):
+                kv2.write(layer, is_v, kv.read(layer, is_v, pos))
+        e0, e1 = _events(torch)
+        e0.record(stream)
+        for _ in range(n_e2e):
+            _, tok = pm.forward(model, kv2, tok, pos, want_logits=False)
+            pos += 1
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_e2e = e0.elapsed_time(e1) / n_e2e
+        kv2.close()
+        kv.close()
+        # CPU oracle and greedy parity from seeded KV at 2048 (the oracle's prefill
+        # of 2048 tokens alone would take minutes)
+        kv_dim = c.kv_dim()
+        ctx = 2048
+        rows_fn = lambda l, v: seeded_kv_rows(l, v, ctx, kv_dim)  # noqa: E731
+        kv3 = pm.KvCache(model, ctx + 64)
+        for layer in range(c.n_layers):
+            for is_v in (False, True):
+                kv3.write(layer, is_v, rows_fn(layer, is_v))
+        loop3 = pm.DecodeLoop(model, kv3)
+        loop3.begin(17, ctx)
+        loop3.run(40)
+        follow = loop3.tokens(40)
+        kv3.close()
+        tps, n_cpu, threads, tier, el, parity = cpu_decode(path, ctx, rows_fn, c.n_layers, kv_dim, 10.0,
+                                                           follow=follow)
+        kv_bytes = 2 * c.n_layers * (len(prompt) + steps // 2) * kv_dim * 2
+        bt = spec.weight_bytes_per_token() + kv_bytes
+        return {
+            "metric": "decode tok/s at batch 1 (after a 2048-token prefill)", "unit": UNIT,
+            "value": round(1000.0 / ms, 1), "ms_per_step": round(ms, 4),
+            "e2e": {"value": round(1000.0 / ms_e2e, 1), "unit": UNIT, "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4},
+            "prefill": {"tokens": len(prompt) - 1, "ms": round(ms_prefill, 2),
+                        "tok_s": round((len(prompt) - 1) * 1000.0 / ms_prefill, 1),
+                        "path": "streaming GEMV, 8 rows per launch; f32 in-window attention"},
+            "step_roofline": {"bytes_per_token": bt, "achieved_gbs": round(bt / ms / 1e6, 1),
+                              "frac": round(bt / ms / 1e6 / peak, 4)},
+            "cpu_baseline": {"value": round(tps, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{n_cpu} greedy tokens at ctx {ctx + 1}.. from seeded KV, {tier} tier, "
+                                       f"{el:.1f} s"},
+            "parity": parity,
+            "config": {"workload": "qwen2_0p5b_mix", "prefill": len(prompt), "steps": steps, "batch": 1,
+                       "types": "Q4_0 (attn q/k/o, ffn gate/up, embedding), Q8_0 (attn v, output), Q6_K (ffn down)"},
+        }
+    finally:
+        model.close()
+
+
+def suite_c4q8(torch, args, peak):
+    """C4, Q8_0 variant: the 8B shape in Q8_0 at ctx 4096, batch 1."""
+    from prana_b200 import model as pm
+
+    spec, path = _preset_path(args, "llama3_8b_q8_0")
+    model = pm.Model.load(str(path), 0)
+    try:
+        c = model.config
+        kv_dim = c.kv_dim()
+        steps, warm = 64, 8
+        kv = pm.KvCache(model, args.ctx + steps + warm + 80)
+        rows_fn = lambda l, v: seeded_kv_rows(l, v, args.ctx, kv_dim)  # noqa: E731
+        for layer in range(c.n_layers):
+            for is_v in (False, True):
+                kv.write(layer, is_v, rows_fn(layer, is_v))
+        stream = torch.cuda.ExternalStream(model.stream())
+        loop = pm.DecodeLoop(model, kv)
+        loop.begin(17, args.ctx)
+        loop.run(warm)
+        torch.cuda.synchronize()
+        e0, e1 = _events(torch)
+        e0.record(stream)
+        loop.run(steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        toks = loop.tokens(warm + steps)
+        pos, tok = args.ctx + warm + steps, int(toks[-1])
+        e0, e1 = _events(torch)
+        e0.record(stream)
+        for _ in range(32):
+            _, tok = pm.forward(model, kv, tok, pos, want_logits=False)
+            pos += 1
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_e2e = e0.elapsed_time(e1) / 32
+        kv.close()
+        tps, n_cpu, threads, tier, el, parity = cpu_decode(path, args.ctx, rows_fn, c.n_layers, kv_dim, 12.0,
+                                                           follow=toks)
+        bt = spec.weight_bytes_per_token() + 2 * c.n_layers * (args.ctx + warm + steps // 2) * kv_dim * 2
+        return {
+            "metric": METRIC, "unit": UNIT, "value": round(1000.0 / ms, 2), "ms_per_step": round(ms, 4),
+            "e2e": {"value": round(1000.0 / ms_e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4},
+            "step_roofline": {"bytes_per_token": bt, "achieved_gbs": round(bt / ms / 1e6, 1),
+                              "frac": round(bt / ms / 1e6 / peak, 4)},
+            "cpu_baseline": {"value": round(tps, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{n_cpu} greedy tokens at ctx {args.ctx + 1}.. from the same seeded KV, fed "
+                                       f"the GPU's tokens, {tier} tier, {el:.1f} s"},
+            "parity": parity,
+            "config": {"workload": "llama3_8b_q8_0", "ctx": args.ctx, "batch": 1},
+        }
+    finally:
+        model.close()
+
+
+SUITE = {"c1": suite_c1, "c2": suite_c2, "c3": suite_c3, "c4q8": suite_c4q8}
+
+
 def prana_arm(args):
     import torch
 
@@ -351,15 +713,20 @@ def prana_arm(args):
     clocks.start()
     t_region = time.monotonic()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        # align the ranks on the device: one more (untimed) step, whose exchanges
+        # finish together on every rank, precedes the start event in stream order
+        loop.run(1)
     e0.record(stream)
     loop.run(args.steps)
     e1.record(stream)
     barrier()
     clk = clocks.stop(t_region, time.monotonic())
     ms = e0.elapsed_time(e1) / args.steps
-    toks = loop.tokens(args.warmup + args.steps)
+    n_loop = args.warmup + args.steps + (1 if dist else 0)
+    toks = loop.tokens(n_loop)
     # ---- e2e: C-ABI call per token with host buffers
-    pos = args.ctx + args.warmup + args.steps
+    pos = args.ctx + n_loop
     tok = int(toks[-1]) if len(toks) else 17
     for _ in range(args.warmup):
         _, tok = pm.forward(model, kv, tok, pos, want_logits=False)
@@ -379,12 +746,32 @@ def prana_arm(args):
         ms, ms_e2e = float(t[0]), float(t[1])
     batch = batch_decode(torch, model, args, stream) if world == 1 and args.batch_seqs > 0 else None
     roof = gemv_roofline(torch, peak) if rank == 0 else None
-    cpu = None
+    cpu = cpu8 = parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tps, steps, threads, tier, el = cpu_decode(path, args.ctx, lambda l, v: seeded_kv_rows(l, v, args.ctx, kv_dim),
-                                                   c.n_layers, kv_dim, args.cpu_seconds)
+        rows_fn = lambda l, v: seeded_kv_rows(l, v, args.ctx, kv_dim)  # noqa: E731
+        tps, steps, threads, tier, el, parity = cpu_decode(path, args.ctx, rows_fn, c.n_layers, kv_dim,
+                                                           args.cpu_seconds, follow=toks)
         cpu = {"value": round(tps, 4), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{steps} greedy tokens at ctx {args.ctx + 1}.. from the same seeded KV, {tier} tier, {el:.1f} s"}
+               "sample": f"{steps} greedy tokens at ctx {args.ctx + 1}.. from the same seeded KV, fed the GPU's "
+                         f"tokens, {tier} tier, {el:.1f} s"}
+        # the reference's default worker count, min(cores, 8) (threading.rs:46-53)
+        t8 = min(os.cpu_count() or 1, 8)
+        tps8, steps8, _, tier8, el8, _ = cpu_decode(path, args.ctx, rows_fn, c.n_layers, kv_dim,
+                                                    args.cpu_seconds / 2, threads=t8)
+        cpu8 = {"value": round(tps8, 4), "unit": UNIT, "cores": t8, "kind": "port",
+                "sample": f"{steps8} greedy tokens at ctx {args.ctx + 1}.., {tier8} tier, {el8:.1f} s"}
+    suite = {}
+    if rank == 0 and world == 1:
+        todo = args.configs.split(",") if args.configs is not None else ["c1", "c2", "c3", "c4q8"]
+        for name in [x.strip() for x in todo if x.strip()]:
+            fn = SUITE.get(name)
+            if fn is None:
+                suite[name] = {"error": "unknown config"}
+                continue
+            try:
+                suite[name] = fn(torch, args, peak)
+            except Exception as e:  # one config's failure is reported, not fatal to the line
+                suite[name] = {"error": f"{type(e).__name__}: {e}"}
     if rank == 0:
         bytes_tok = spec.weight_bytes_per_token() + 2 * c.n_layers * (args.ctx + args.warmup + args.steps // 2) * kv_dim * 2
         step_gbs = bytes_tok * (1000.0 / ms) / 1e9
@@ -402,8 +789,11 @@ def prana_arm(args):
             "roofline": roof, "peak_kind": peak_kind,
             "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": round(step_gbs, 1),
                               "frac": round(step_gbs / peak, 4)},
-            "cpu_baseline": cpu, "batch_decode": batch, "clocks": clk, "gpu_launches": launches_per_step(spec, world, model.peer_exchange) * args.steps,
+            "cpu_baseline": cpu, "cpu_baseline_default_threads": cpu8, "parity": parity,
+            "batch_decode": batch, "clocks": clk,
+            "gpu_launches": launches_per_step(spec, world, model.peer_exchange) * args.steps,
             "load_s": round(t_load, 1),
+            "configs": suite or None,
         }
         print(json.dumps(line), flush=True)
     kv.close()

@@ -27,10 +27,10 @@ SCALE_TOL = 1e-5   # per-32 scales follow the f32 values (a few ulps)
 # (127 x the value difference, with margin).
 ATT_SCALE_TOL = 1e-4
 ATT_TIE_TOL = 1e-2
-# A flipped f16 K/V element's f32 value lies within this fraction of its row's
-# largest magnitude of the midpoint between the two f16 values (the f32
-# values come from sums whose order differs; their error scales with the
-# terms, not with the possibly small result).
+# A GPU f16 K/V value must be the rounding of a value within this fraction of
+# its row's largest magnitude of the oracle's f32 value (the f32 values come
+# from sums whose order differs; their error scales with the terms, not with
+# the possibly small result).
 KV_TIE_TOL = 1e-5
 
 
@@ -86,21 +86,25 @@ class Flips:
         self.flips += int(idx.size)
 
     def check_kv(self, kv_g, kv_o, kv_val, where: str, kv_dim: int) -> None:
-        """f16 K/V rows written from the same int8 inputs: equal, or one f16 ulp
-        apart where the oracle's f32 value sits at the midpoint of the two."""
+        """f16 K/V rows written from the same int8 inputs: every GPU value is the
+        f16 rounding of some value within KV_TIE_TOL x (its row's largest
+        magnitude) of the oracle's f32 value -- one ulp apart at a rounding tie,
+        or a few subnormal-range ulps for values near zero."""
         a, b = f16_key(kv_g), f16_key(kv_o)
         d = np.abs(a - b)
         self.kv_total += d.size
         if not np.any(d):
             return
-        assert int(d.max()) <= 1, f"{where}: K/V rows differ by {int(d.max())} f16 ulps"
         idx = np.nonzero(d)[0]
-        hg = np.asarray(kv_g, np.uint16)[idx].view(np.float16).astype(np.float64)
-        ho = np.asarray(kv_o, np.uint16)[idx].view(np.float16).astype(np.float64)
-        vals = np.asarray(kv_val, np.float64)
+        vals = np.asarray(kv_val, np.float32)
         row_max = np.max(np.abs(vals.reshape(-1, kv_dim)), axis=1)
-        dist = np.abs(vals[idx] - (hg + ho) / 2) / np.maximum(row_max[idx // kv_dim], 1e-30)
-        assert np.all(dist < KV_TIE_TOL), f"{where}: an f16 K/V flip away from a tie ({dist.max():.2e})"
+        tau = (KV_TIE_TOL * row_max[idx // kv_dim]).astype(np.float32)
+        x = vals[idx]
+        lo = f16_key((x - tau).astype(np.float16).view(np.uint16))
+        hi = f16_key((x + tau).astype(np.float16).view(np.uint16))
+        ok = (a[idx] >= lo) & (a[idx] <= hi)
+        assert np.all(ok), (f"{where}: {int((~ok).sum())} f16 K/V values are not roundings of the oracle's "
+                            f"value within {KV_TIE_TOL:g} of the row (max {int(d.max())} ulps)")
         self.kv_flips += int(idx.size)
 
     def bounded(self, frac: float = 0.01, floor: int = 32) -> bool:
