@@ -94,6 +94,18 @@ int prana_matmul_q8_prefill(prana_ctx *ctx, const int8_t *q, const float *scales
                             size_t n_tokens, const prana_weight *w, float *out);
 int prana_matmul_kquant_prefill(prana_ctx *ctx, const int8_t *q, const float *scales, const int32_t *sums,
                                 size_t n_tokens, const prana_weight *w, float *out);
+/* The same products on the tensor cores (tcgen05 kind::i8, one MMA per
+ * 32-value block -- 16 for Q6_K -- into a fresh TMEM accumulator, per-block
+ * scales applied in f32): the path matmul_*_prefill takes above 8 rows,
+ * callable at any row count.  q must be 16-byte aligned. */
+int prana_qgemm(prana_ctx *ctx, const int8_t *q, const float *scales, const int32_t *sums, size_t n_tokens,
+                const prana_weight *w, float *out);
+/* Diagnostic: the per-block int32 dots the tensor cores produced, out
+ * [n_tokens][rows][blocks] (blocks = cols/32, or cols/16 for Q6_K) -- the
+ * quantities of dot_q8_q8_scalar / dot_q40_q8_scalar / dot_q4k_q8_scalar /
+ * dot_q6k_q8_scalar (matmul.rs:395-406, kquant.rs:240-318). */
+int prana_qgemm_block_dots(prana_ctx *ctx, const int8_t *q, const float *scales, const int32_t *sums,
+                           size_t n_tokens, const prana_weight *w, int32_t *out);
 /* matmul_f32 (matmul.rs:150-156) for F32 weights */
 int prana_matmul_f32(prana_ctx *ctx, const float *a, const prana_weight *w, size_t n_tokens, float *out);
 /* Per-block int32 dots of weight row `row` against one quantized activation row:

@@ -62,6 +62,8 @@ SIGNATURES = {
     "prana_matmul_q8_prefill": [P, P, P, P, SZ, P, P],
     "prana_matmul_kquant_prefill": [P, P, P, P, SZ, P, P],
     "prana_matmul_f32": [P, P, P, SZ, P],
+    "prana_qgemm": [P, P, P, P, SZ, P, P],
+    "prana_qgemm_block_dots": [P, P, P, P, SZ, P, P],
     "prana_block_dots": [P, P, SZ, P, P, P],
     "prana_rmsnorm": [P, P, P, SZ, SZ, C.c_float, P],
     "prana_silu": [P, P, SZ],

@@ -178,6 +178,23 @@ cudaError_t launch_wait_never(unsigned polls, unsigned* err, cudaStream_t st);
 // first maximum over ranks: all = [world][16] (8 best values, then 8 index bit patterns)
 cudaError_t launch_tp_argmax(const float* all, int world, int m, uint32_t* tok_out, int* tok_next, cudaStream_t st);
 
+// ---------------------------------------------------------------- tensor-core GEMM (qgemm.cu)
+struct QgemmArgs {
+  DevWeight w;
+  int N, K, M;          // weight rows, columns; activation rows
+  int m_pad;            // set by the launcher
+  float* out;           // [M][N] (null with dots)
+  const float* bias;    // [N] added to every row (nullable)
+  int resid;            // 1: out += result
+  int32_t* dots;        // diagnostic: per-block int32 [M][N][K/32 (x2 for Q6_K)] instead of out
+  unsigned* err;        // device error flag
+};
+// out = W . rows (q [M][K] int8, s / sums [M][K/32]); scratch >= qgemm_scratch_bytes
+cudaError_t launch_qgemm(QgemmArgs g, const int8_t* q, const float* s, const int32_t* sums, void* scratch,
+                         cudaStream_t st);
+size_t qgemm_scratch_bytes(int m, int k);
+int qgemm_tokens_per_tile(int m);
+
 // attention.cu
 int attn_max_rows_per_cta(int hd);
 // attention splits for a cache of `positions` rows (scratch is sized by it)

@@ -38,6 +38,7 @@
 // (bounded) for its own copies and MMAs, frees its TMEM and raises the error
 // flag.
 #include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <map>
 #include <mutex>
@@ -61,12 +62,12 @@ constexpr int QG_SMEM_MAX = 224 * 1024;
 template <int T> struct QgFmt;
 // BK: K values per stage; RAW: packed bytes per weight row per stage, staged
 // by TMA (0: TMA writes the int8 tile itself); A_TILES: int8 tiles per stage
-// (2 for Q6_K: lower and upper sub-block halves); WSC: weight-scale bytes per
-// row per stage staged by TMA (f16 d of every block).
-template <> struct QgFmt<T_Q8_0> { static constexpr int BK = 256, RAW = 0, A_TILES = 1, WSC = 16; };
-template <> struct QgFmt<T_Q4_0> { static constexpr int BK = 256, RAW = 128, A_TILES = 1, WSC = 16; };
-template <> struct QgFmt<T_Q4_K> { static constexpr int BK = 256, RAW = 144, A_TILES = 1, WSC = 0; };
-template <> struct QgFmt<T_Q6_K> { static constexpr int BK = 256, RAW = 192, A_TILES = 2, WSC = 16; };
+// (2 for Q6_K: lower and upper sub-block halves).  Q6_K's raw row is its ql
+// bytes (128) then its qh bytes (64), staged as two regions.
+template <> struct QgFmt<T_Q8_0> { static constexpr int BK = 256, RAW = 0, A_TILES = 1; };
+template <> struct QgFmt<T_Q4_0> { static constexpr int BK = 256, RAW = 128, A_TILES = 1; };
+template <> struct QgFmt<T_Q4_K> { static constexpr int BK = 256, RAW = 144, A_TILES = 1; };
+template <> struct QgFmt<T_Q6_K> { static constexpr int BK = 256, RAW = 192, A_TILES = 2; };
 
 template <int T, int NT>
 struct QgLayout {
@@ -78,13 +79,11 @@ struct QgLayout {
   static constexpr int A_BYTES = A_ATOM * KATOMS * F::A_TILES;
   static constexpr int B_BYTES = NT * BK;
   static constexpr int RAW_BYTES = QG_BM * F::RAW;
-  static constexpr int WSC_BYTES = QG_BM * F::WSC;
   static constexpr int SA_BYTES = BLK * NT * 4;             // activation scales [BLK][NT]
   static constexpr int SUM_BYTES = T == T_Q4_K ? BLK * NT * 4 : 0;  // activation group sums
   static constexpr int OFF_B = A_BYTES;
   static constexpr int OFF_RAW = OFF_B + B_BYTES;
-  static constexpr int OFF_WSC = OFF_RAW + RAW_BYTES;
-  static constexpr int OFF_SA = OFF_WSC + WSC_BYTES;
+  static constexpr int OFF_SA = OFF_RAW + RAW_BYTES;
   static constexpr int OFF_SUM = OFF_SA + SA_BYTES;
   static constexpr int STAGE = (OFF_SUM + SUM_BYTES + 1023) / 1024 * 1024;
   static constexpr int NS_FIT = (QG_SMEM_MAX - 2048) / STAGE;
@@ -95,7 +94,7 @@ struct QgLayout {
   static constexpr int SLOTS = SLOTS_MAX > 16 ? 16 : SLOTS_MAX;  // TMEM accumulator slots
   static constexpr int TMEM_COLS = SLOTS * NT < 32 ? 32 : SLOTS * NT;
   static constexpr size_t SMEM = (size_t)NS * STAGE + 1024 /* alignment */ + 1024 /* barriers */;
-  static constexpr uint32_t TX = (uint32_t)(B_BYTES + (F::RAW ? RAW_BYTES : A_BYTES) + WSC_BYTES + SA_BYTES + SUM_BYTES);
+  static constexpr uint32_t TX = (uint32_t)(B_BYTES + (F::RAW ? RAW_BYTES : A_BYTES) + SA_BYTES + SUM_BYTES);
 };
 
 // ---- tcgen05 / TMA primitives (inline PTX, sm_100a) ----
@@ -178,7 +177,7 @@ __device__ __forceinline__ bool qwait(uint64_t* bar, uint32_t phase, volatile in
 // TMA; the values they become are never scaled into a result (their blocks
 // lie past K, their rows past N).
 template <int T>
-__device__ __forceinline__ void unpack_row(const uint8_t* raw, uint8_t* a, int r) {
+__device__ __forceinline__ void unpack_row(const uint8_t* raw, const uint8_t* raw2, uint8_t* a, int r) {
   constexpr int ATOM = QG_BM * 128;
   if constexpr (T == T_Q4_0) {
     // 8 blocks of 16 bytes: byte j holds value j (low nibble) and j + 16 (high), q - 8
@@ -205,7 +204,7 @@ __device__ __forceinline__ void unpack_row(const uint8_t* raw, uint8_t* a, int r
       *reinterpret_cast<uint4*>(a + (c >> 3) * ATOM + sw_off(r, c & 7)) = v;
     }
   } else if constexpr (T == T_Q6_K) {
-    // one super-block: ql 128 bytes, then qh 64 bytes.  Half h, value e = 32 g + l
+    // one super-block: ql 128 bytes (raw), qh 64 bytes (raw2).  Half h, value e = 32 g + l
     // (g = 0..3): low 4 bits from ql[64 h + l + 32 (g & 1)] (high nibble when
     // g >= 2), high 2 bits from qh[32 h + l] >> 2g; minus 32.  16-value chunk c
     // (one sub-block) goes to the lower tile when c is even, to the upper when
@@ -216,7 +215,7 @@ __device__ __forceinline__ void unpack_row(const uint8_t* raw, uint8_t* a, int r
     for (int c = 0; c < 16; c++) {
       const int h = c >> 3, g = (c >> 1) & 3, l0 = (c & 1) * 16;
       const uint4 x = *reinterpret_cast<const uint4*>(raw + h * 64 + (g & 1) * 32 + l0);
-      const uint4 q = *reinterpret_cast<const uint4*>(raw + 128 + h * 32 + l0);
+      const uint4 q = *reinterpret_cast<const uint4*>(raw2 + h * 32 + l0);
       const int sh = (g >> 1) * 4, hs = 2 * g;
       const unsigned m4 = 0x0F0F0F0Fu, m2 = 0x03030303u, k = 0x20202020u;
       const uint4 v = make_uint4(__vsub4(((x.x >> sh) & m4) | (((q.x >> hs) & m2) << 4), k),
@@ -233,7 +232,7 @@ __device__ __forceinline__ void unpack_row(const uint8_t* raw, uint8_t* a, int r
 
 template <int T, int NT>
 __global__ void __launch_bounds__(QG_THREADS, 1)
-    qgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wsc,
+    qgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
                  const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_sa,
                  const __grid_constant__ CUtensorMap tm_sum, const QgemmArgs g) {
   using L = QgLayout<T, NT>;
@@ -247,7 +246,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   uint64_t* freed = bars + 2 * NS;         // [NS] MMAs completed and epilogue done with the stage
   uint64_t* acc_full = bars + 3 * NS;      // [SLOTS] one MMA landed in the slot
   uint64_t* acc_empty = acc_full + SLOTS;  // [SLOTS] epilogue warps read the slot
-  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(acc_empty + SLOTS);
+  uint64_t* mma_done = acc_empty + SLOTS;  // every MMA issued has completed (before TMEM is freed)
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mma_done + 1);
   __shared__ int s_abort;
   volatile int* abort = &s_abort;
 
@@ -270,6 +270,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], QG_EPI_WARPS);
     }
+    mbar_init(mma_done, 1);
     fence_barrier_init();
   }
   if (wi == 12) {
@@ -297,10 +298,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         if constexpr (F::RAW == 0) {
 #pragma unroll
           for (int a = 0; a < L::KATOMS; a++) tma_load_2d(sm + a * L::A_ATOM, &tm_w, k0 + a * 128, row0, &full[st]);
+        } else if constexpr (T == T_Q6_K) {
+          tma_load_2d(sm + L::OFF_RAW, &tm_w, s * 128, row0, &full[st]);                 // ql
+          tma_load_2d(sm + L::OFF_RAW + QG_BM * 128, &tm_w2, s * 64, row0, &full[st]);  // qh
         } else {
           tma_load_2d(sm + L::OFF_RAW, &tm_w, s * F::RAW, row0, &full[st]);
         }
-        if constexpr (F::WSC > 0) tma_load_2d(sm + L::OFF_WSC, &tm_wsc, s * F::WSC, row0, &full[st]);
         tma_load_2d(sm + L::OFF_SA, &tm_sa, tok0, s * BLK, &full[st]);
         if constexpr (L::SUM_BYTES > 0) tma_load_2d(sm + L::OFF_SUM, &tm_sum, tok0, s * BLK, &full[st]);
         issued = s + 1;
@@ -348,8 +351,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       }
       if (!ok) *abort = 1;
       // wind down: every MMA issued has completed before TMEM is freed
-      if (last_stage >= 0)
-        mbar_wait(&freed[last_stage % NS], (last_stage / NS) & 1, ok ? kMbarPolls : (1u << 16));
+      (void)last_stage;
+      tc_commit(mma_done);
+      mbar_wait(mma_done, 0);
     }
     __syncwarp();
   } else if (wi < 4) {
@@ -363,7 +367,10 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
           break;
         }
         uint8_t* sm = stage(st);
-        unpack_row<T>(sm + L::OFF_RAW + r * F::RAW, sm, r);
+        if constexpr (T == T_Q6_K)
+          unpack_row<T>(sm + L::OFF_RAW + r * 128, sm + L::OFF_RAW + QG_BM * 128 + r * 64, sm, r);
+        else
+          unpack_row<T>(sm + L::OFF_RAW + r * F::RAW, nullptr, sm, r);
         fence_async_smem();
         mbar_arrive(&conv[st]);
       }
@@ -373,27 +380,52 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     const int q4 = wi & 3, half = (wi - 4) >> 2;  // lane quarter, token half
     const int rl = q4 * 32 + lane;                 // row within the tile
     const int r = row0 + rl;
+    const int rr = min(r, N - 1);                  // rows past N read row N-1's scales (never stored)
     constexpr int NC = NT / 2;                     // tokens per thread
     const int c0 = half * NC;
     float acc[NC];
 #pragma unroll
     for (int c = 0; c < NC; c++) acc[c] = 0.0f;
+    // weight scales of a stage, loaded one stage ahead: Q8_0 / Q4_0 the f16 d
+    // of each block; Q6_K the super-block's d and its 16 int8 sub-block scales
+    // (Q4_K's live in the staged super-block header)
+    unsigned short dn[BLK], dc[BLK];
+    uint4 scn = make_uint4(0u, 0u, 0u, 0u), scc = scn;
+    auto load_scales = [&](int s) {
+      if (s >= n_stage) return;
+      if constexpr (T == T_Q8_0 || T == T_Q4_0) {
+        const unsigned short* d = reinterpret_cast<const unsigned short*>(g.w.d) + (size_t)rr * n_blk + s * BLK;
+        const int nb = min(BLK, n_blk - s * BLK);
+#pragma unroll
+        for (int j = 0; j < BLK; j++)
+          if (j < nb) dn[j] = __ldg(d + j);
+      } else if constexpr (T == T_Q6_K) {
+        dn[0] = __ldg(reinterpret_cast<const unsigned short*>(g.w.d) + (size_t)rr * (K / 256) + s);
+        scn = __ldg(reinterpret_cast<const uint4*>(g.w.sc + (size_t)rr * (K / 16)) + s);
+      }
+    };
+    load_scales(0);
     int mma = 0;
     bool ok = true;
     for (int s = 0; s < n_stage && ok; s++) {
       const int st = s % NS;
       const uint8_t* sm = stage(st);
+#pragma unroll
+      for (int j = 0; j < BLK; j++) dc[j] = dn[j];
+      scc = scn;
+      load_scales(s + 1);
       if (!qwait(&full[st], (s / NS) & 1, abort)) {
         ok = false;
         break;
       }
       const float* sa_s = reinterpret_cast<const float*>(sm + L::OFF_SA);
       const int nb = min(BLK, n_blk - s * BLK);
+#pragma unroll 1
       for (int j = 0; j < nb && ok; j++) {
         // weight scales of block j of this stage for row rl
         float ws0 = 0.0f, ws1 = 0.0f, wmin = 0.0f;
         if constexpr (T == T_Q8_0 || T == T_Q4_0) {
-          ws0 = h2f(reinterpret_cast<const unsigned short*>(sm + L::OFF_WSC + rl * 16)[j]);
+          ws0 = h2f(dc[j]);
         } else if constexpr (T == T_Q4_K) {
           const uint8_t* hdr = sm + L::OFF_RAW + rl * F::RAW;
           int sc, mn;
@@ -402,9 +434,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
           const float dmin = h2f((unsigned short)(hdr[2] | (hdr[3] << 8)));
           ws0 = __fmul_rn(d, (float)sc);
           wmin = __fmul_rn(dmin, (float)mn);
-        } else {  // Q6_K: d of the super-block (a row of g.w.d), sub-block scales staged
-          ws0 = h2f(__half_as_ushort(g.w.d[(size_t)min(r, N - 1) * (K / 256) + s]));
-          const int8_t* sc = reinterpret_cast<const int8_t*>(sm + L::OFF_WSC + rl * 16);
+        } else {
+          ws0 = h2f(dc[0]);
+          const int8_t* sc = reinterpret_cast<const int8_t*>(&scc);
           wmin = (float)sc[2 * j];
           ws1 = (float)sc[2 * j + 1];
         }
@@ -528,33 +560,125 @@ bool map2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, 
 }
 
 template <int T, int NT>
-cudaError_t qgemm_go(const QgemmArgs& g, cudaStream_t st) {
+cudaError_t qgemm_go(const QgemmArgs& g, const int8_t* q, const float* sa_t, const int32_t* sum_t, cudaStream_t st) {
   using L = QgLayout<T, NT>;
-  using F = QgFmt<T>;
   const DevWeight& w = g.w;
-  CUtensorMap tm_w{}, tm_wsc{}, tm_x{}, tm_sa{}, tm_sum{};
-  const uint64_t K = (uint64_t)g.K, N = (uint64_t)g.N;
-  bool ok = true;
+  CUtensorMap tm_w{}, tm_w2{}, tm_x{}, tm_sa{}, tm_sum{};
+  const uint64_t K = (uint64_t)g.K, N = (uint64_t)g.N, G = K / 32;
+  bool ok = map2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q, K, (uint64_t)g.M, K, 128, NT, CU_TENSOR_MAP_SWIZZLE_128B) &&
+            map2d(&tm_sa, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, sa_t, (uint64_t)g.m_pad, G, (uint64_t)g.m_pad * 4, NT,
+                  L::BLK, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (T == T_Q4_K)
+    ok = ok && map2d(&tm_sum, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, sum_t, (uint64_t)g.m_pad, G, (uint64_t)g.m_pad * 4, NT,
+                     L::BLK, CU_TENSOR_MAP_SWIZZLE_NONE);
   if constexpr (T == T_Q8_0) {
-    ok = map2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, K, N, K, 128, QG_BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    ok = ok && map2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, K, N, K, 128, QG_BM, CU_TENSOR_MAP_SWIZZLE_128B);
   } else if constexpr (T == T_Q4_0) {
-    ok = map2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, K / 2, N, K / 2, 128, QG_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    ok = ok && map2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, K / 2, N, K / 2, 128, QG_BM,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
   } else if constexpr (T == T_Q4_K) {
-    ok = map2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, K / 256 * 144, N, K / 256 * 144, 144, QG_BM,
-               CU_TENSOR_MAP_SWIZZLE_NONE);
+    ok = ok && map2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, K / 256 * 144, N, K / 256 * 144, 144, QG_BM,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
   } else {
-    // Q6_K: ql and qh of a super-block are staged side by side (128 + 64 bytes per row);
-    // the stage's raw area holds [128 rows][192 bytes]: ql then qh of each row.  The
-    // planes are separate in HBM, so the raw map covers ql only and qh travels in the
-    // weight-scale slot?  No: qh is copied by a second map below into the same rows.
+    ok = ok && map2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, K / 2, N, K / 2, 128, QG_BM,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) &&
+         map2d(&tm_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qh, K / 4, N, K / 4, 64, QG_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
   }
-  (void)tm_wsc;
-  (void)F::WSC;
-  (void)L::SMEM;
   if (!ok) return cudaErrorNotSupported;
-  return cudaErrorNotSupported;
+  auto kern = qgemm_kernel<T, NT>;
+  static bool attr_set[64] = {};  // per device and instantiation
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)L::SMEM);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const dim3 grid((unsigned)((N + QG_BM - 1) / QG_BM), (unsigned)(g.m_pad / NT));
+  kern<<<grid, QG_THREADS, L::SMEM, st>>>(tm_w, tm_w2, tm_x, tm_sa, tm_sum, g);
+  return cudaGetLastError();
+}
+
+template <int T>
+cudaError_t qgemm_t(const QgemmArgs& g, const int8_t* q, const float* sa_t, const int32_t* sum_t, cudaStream_t st) {
+  switch (qgemm_tokens_per_tile(g.M)) {
+    case 16: return qgemm_go<T, 16>(g, q, sa_t, sum_t, st);
+    case 32: return qgemm_go<T, 32>(g, q, sa_t, sum_t, st);
+    default: return qgemm_go<T, 64>(g, q, sa_t, sum_t, st);
+  }
 }
 
 }  // namespace
 
+int qgemm_tokens_per_tile(int m) { return m <= 16 ? 16 : m <= 32 ? 32 : 64; }
+
+size_t qgemm_scratch_bytes(int m, int k) {
+  const int nt = qgemm_tokens_per_tile(m);
+  const size_t m_pad = (size_t)(m + nt - 1) / nt * nt;
+  return 2 * m_pad * (size_t)(k / 32) * 4 + 256;
+}
+
+cudaError_t launch_qgemm(QgemmArgs g, const int8_t* q, const float* s, const int32_t* sums, void* scratch,
+                         cudaStream_t st) {
+  if (g.M < 1 || g.K % 32 || g.K != g.w.cols || g.N != g.w.rows || g.N < 1) return cudaErrorInvalidValue;
+  if ((g.w.type == T_Q4_K || g.w.type == T_Q6_K) && g.K % 256) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(q) & 15) return cudaErrorInvalidValue;
+  const int nt = qgemm_tokens_per_tile(g.M);
+  g.m_pad = (g.M + nt - 1) / nt * nt;
+  const int G = g.K / 32;
+  float* sa_t = static_cast<float*>(scratch);
+  int32_t* sum_t = reinterpret_cast<int32_t*>(sa_t + (size_t)g.m_pad * G);
+  const int n = G * g.m_pad;
+  qgemm_prep_kernel<<<(n + 255) / 256, 256, 0, st>>>(s, g.w.type == T_Q4_K ? sums : nullptr, g.M, G, g.m_pad, sa_t,
+                                                      g.w.type == T_Q4_K ? sum_t : nullptr);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  switch (g.w.type) {
+    case T_Q8_0: return qgemm_t<T_Q8_0>(g, q, sa_t, sum_t, st);
+    case T_Q4_0: return qgemm_t<T_Q4_0>(g, q, sa_t, sum_t, st);
+    case T_Q4_K: return qgemm_t<T_Q4_K>(g, q, sa_t, sum_t, st);
+    case T_Q6_K: return qgemm_t<T_Q6_K>(g, q, sa_t, sum_t, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
 }  // namespace prana
+
+// ---------------------------------------------------------------- C ABI
+
+using namespace prana;
+
+static int qgemm_entry(prana_ctx* c, const int8_t* q, const float* s, const int32_t* sums, size_t n_tokens,
+                       const prana_weight* w, float* out, int32_t* dots) {
+  if (!(c && q && s && sums && w && (out || dots))) return fail(PRANA_E_INVALID, "null argument");
+  if (w->dw.type == T_F32) return fail(PRANA_E_INVALID, "the tensor-core GEMM takes a quantized weight");
+  if (!n_tokens) return PRANA_OK;
+  if (n_tokens > (1u << 20)) return fail(PRANA_E_INVALID, "too many rows");
+  if (reinterpret_cast<uintptr_t>(q) & 15) return fail(PRANA_E_INVALID, "activation rows must be 16-byte aligned");
+  DevScope ds(c->device);
+  void* sp = nullptr;
+  if (int rc = ctx_scratch(c, qgemm_scratch_bytes((int)n_tokens, w->dw.cols), &sp)) return rc;
+  QgemmArgs g{};
+  g.w = w->dw;
+  g.N = w->dw.rows;
+  g.K = w->dw.cols;
+  g.M = (int)n_tokens;
+  g.out = out;
+  g.dots = dots;
+  g.err = c->err;
+  const cudaError_t e = launch_qgemm(g, q, s, sums, sp, c->stream);
+  if (e == cudaErrorNotSupported) return fail(PRANA_E_UNSUPPORTED, "tensor map for this shape could not be made");
+  PRANA_CK(e);
+  return PRANA_OK;
+}
+
+extern "C" int prana_qgemm(prana_ctx* c, const int8_t* q, const float* s, const int32_t* sums, size_t n_tokens,
+                           const prana_weight* w, float* out) {
+  return qgemm_entry(c, q, s, sums, n_tokens, w, out, nullptr);
+}
+
+extern "C" int prana_qgemm_block_dots(prana_ctx* c, const int8_t* q, const float* s, const int32_t* sums,
+                                      size_t n_tokens, const prana_weight* w, int32_t* dots) {
+  return qgemm_entry(c, q, s, sums, n_tokens, w, nullptr, dots);
+}

@@ -167,6 +167,27 @@ def matmul_kquant_prefill(acts: QuantActs, m: QuantMatrix) -> torch.Tensor:
     return out
 
 
+def qgemm(acts: QuantActs, w: QuantMatrix) -> torch.Tensor:
+    """The quantized rows times `w` on the tensor cores (tcgen05, one MMA per
+    block): the products of matmul_q8_prefill / matmul_kquant_prefill."""
+    n = acts.q.shape[0]
+    out = _out(n, w.rows, acts.q.device)
+    call("prana_qgemm", context(acts.q.device.index), _ptr(acts.q), _ptr(acts.scales), _ptr(acts.sums), n, w.handle,
+         _ptr(out))
+    return out
+
+
+def qgemm_block_dots(acts: QuantActs, w: QuantMatrix) -> torch.Tensor:
+    """Per-block int32 dots the tensor cores produce: [n_tokens, rows, blocks]
+    (blocks = cols / 32, or cols / 16 for Q6_K)."""
+    n = acts.q.shape[0]
+    nb = w.cols // 16 if w.ggml_type == TYPE_Q6_K else w.cols // 32
+    out = torch.zeros((n, w.rows, nb), dtype=torch.int32, device=acts.q.device)
+    call("prana_qgemm_block_dots", context(acts.q.device.index), _ptr(acts.q), _ptr(acts.scales), _ptr(acts.sums), n,
+         w.handle, _ptr(out))
+    return out
+
+
 def matmul_f32(a: torch.Tensor, w: QuantMatrix, n_tokens: int) -> torch.Tensor:
     """matmul_f32 (matmul.rs:150-156) over an F32 weight."""
     out = _out(n_tokens, w.rows, a.device)
