@@ -177,6 +177,57 @@ def margin(lg) -> float:
     return float((srt[-1] - srt[-2]) / max(float(np.max(np.abs(lg))), 1e-30))
 
 
+def forced_parity(path, model, ctx, rows_fn, n_layers, start_tok, gpu_toks, n_steps):
+    """The benchmarked token stream, step by step, against the CPU oracle in
+    forced mode (oracle/parity.py): the GPU's traced pass replays each step from
+    the same seeded cache (it must reproduce the benchmarked token), the oracle
+    takes the same step proving every int8 / f16 difference a rounding tie and
+    following the GPU's rows; logits must agree within 1e-3 and the token must
+    be the oracle's argmax wherever its top-2 margin exceeds 1e-3."""
+    from oracle import oracle as orc
+    from oracle.parity import Flips, forced_decode, rel
+    from prana_b200 import model as pm
+
+    orc.lib().or_pool_set_threads(os.cpu_count() or 1)
+    om = orc.OModel(str(path), orc.TIER_AUTO)
+    n_steps = min(n_steps, len(gpu_toks))
+    okv, gkv = om.kv(ctx + n_steps + 4), pm.KvCache(model, ctx + n_steps + 4)
+    try:
+        for layer in range(n_layers):
+            for is_v in (False, True):
+                rows = rows_fn(layer, is_v)
+                okv.set_layer(layer, is_v, rows)
+                gkv.write(layer, is_v, rows)
+        flips = Flips()
+        gated = same = replay = 0
+        worst = 0.0
+        tok = start_tok
+        err = None
+        for i in range(n_steps):
+            try:
+                lg_g, lg_o = forced_decode(om, okv, model, gkv, tok, ctx + i, flips, f"step {i}")
+            except AssertionError as e:
+                err = str(e)
+                break
+            g = int(np.argmax(lg_g))
+            replay += int(g == int(gpu_toks[i]))
+            worst = max(worst, rel(lg_g, lg_o))
+            if margin(lg_o) > 1e-3:
+                gated += 1
+                same += int(g == int(np.argmax(lg_o)))
+            tok = int(gpu_toks[i])
+        out = {"steps": n_steps, "replay_equals_benchmarked": replay, "margin_gated": gated, "identical": same,
+               "max_logit_rel_err": float(f"{worst:.3g}"), "int8_tie_flips": flips.flips,
+               "int8_compared": flips.total, "f16_kv_tie_flips": flips.kv_flips,
+               "rule": "oracle forced with the GPU's int8 rows and f16 K/V rows after each difference is proven "
+                       "a rounding tie; logits within 1e-3; identical where the oracle's top-2 margin > 1e-3"}
+        if err:
+            out["failed"] = err
+        return out
+    finally:
+        gkv.close()
+
+
 PARITY_RULE = ("CPU oracle fed the GPU's tokens (same seeded KV, same start); a token counts as gated when the "
                "oracle's top-2 margin exceeds 1e-3 of the largest logit, and identical when the GPU chose the "
                "oracle's argmax")
@@ -404,17 +455,35 @@ def suite_c1(torch, args, peak):
         t0 = time.perf_counter()
         ref = om.generate(prompt, steps)
         el = time.perf_counter() - t0
-        # greedy parity: the oracle fed the GPU's tokens, margin-gated
-        okv = om.kv(spec.ctx)
-        om.prefill(okv, prompt[:-1])
-        tok, gated, same = int(prompt[-1]), 0, 0
-        for i in range(len(got)):
-            lg = om.forward(okv, tok, len(prompt) - 1 + i)
-            if margin(lg) > 1e-3:
-                gated += 1
-                same += int(int(np.argmax(lg)) == int(got[i]))
-            tok = int(got[i])
+        # greedy parity, forced (oracle/parity.py): the prompt's prefill and each of the
+        # 248 steps of the GPU's stream, the traced replay reproducing the generated ids
+        from oracle.parity import Flips, forced_batch, forced_decode, rel
+
+        okv, gkv = om.kv(spec.ctx), pm.KvCache(model, spec.ctx)
+        flips = Flips()
+        gated = same = replay = 0
+        worst, err = 0.0, None
+        try:
+            forced_batch(om, okv, model, gkv, prompt[:-1], 0, True, flips, "prompt")
+            tok = int(prompt[-1])
+            for i in range(len(got)):
+                lg_g, lg_o = forced_decode(om, okv, model, gkv, tok, len(prompt) - 1 + i, flips, f"step {i}")
+                g = int(np.argmax(lg_g))
+                replay += int(g == int(got[i]))
+                worst = max(worst, rel(lg_g, lg_o))
+                if margin(lg_o) > 1e-3:
+                    gated += 1
+                    same += int(g == int(np.argmax(lg_o)))
+                tok = int(got[i])
+        except AssertionError as e:
+            err = str(e)
+        gkv.close()
         agree = int(np.argmax(np.concatenate([got != ref, [True]])))
+        forced = {"steps": len(got), "replay_equals_benchmarked": replay, "margin_gated": gated, "identical": same,
+                  "max_logit_rel_err": float(f"{worst:.3g}"), "int8_tie_flips": flips.flips,
+                  "f16_kv_tie_flips": flips.kv_flips}
+        if err:
+            forced["failed"] = err
         wb = spec.weight_bytes_per_token()
         return {
             "metric": "decode tok/s at batch 1 (greedy 248 tokens after an 8-id prompt)", "unit": UNIT,
@@ -426,8 +495,7 @@ def suite_c1(torch, args, peak):
                               "note": "16 MB per token fits in L2; the step is launch/latency-bound"},
             "cpu_baseline": {"value": round(steps / el, 1), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                              "sample": f"oracle generate, {steps} tokens, {el:.2f} s"},
-            "parity": {"tokens_compared": len(got), "margin_gated": gated, "identical": same,
-                       "free_running_identical_prefix": agree, "rule": PARITY_RULE},
+            "parity": {"forced": forced, "free_running_identical_prefix": agree},
             "config": {"workload": "stories15m_q8_0", "prompt": len(prompt), "steps": steps, "batch": 1},
         }
     finally:
@@ -577,6 +645,8 @@ def suite_c3(torch, args, peak):
         kv3.close()
         tps, n_cpu, threads, tier, el, parity = cpu_decode(path, ctx, rows_fn, c.n_layers, kv_dim, 10.0,
                                                            follow=follow)
+        parity = {"forced": forced_parity(path, model, ctx, rows_fn, c.n_layers, 17, follow, 16),
+                  "free_running": parity}
         kv_bytes = 2 * c.n_layers * (len(prompt) + steps // 2) * kv_dim * 2
         bt = spec.weight_bytes_per_token() + kv_bytes
         return {
@@ -639,6 +709,8 @@ def suite_c4q8(torch, args, peak):
         kv.close()
         tps, n_cpu, threads, tier, el, parity = cpu_decode(path, args.ctx, rows_fn, c.n_layers, kv_dim, 12.0,
                                                            follow=toks)
+        parity = {"forced": forced_parity(path, model, args.ctx, rows_fn, c.n_layers, 17, toks, 4),
+                  "free_running": parity}
         bt = spec.weight_bytes_per_token() + 2 * c.n_layers * (args.ctx + warm + steps // 2) * kv_dim * 2
         return {
             "metric": METRIC, "unit": UNIT, "value": round(1000.0 / ms, 2), "ms_per_step": round(ms, 4),
@@ -760,6 +832,8 @@ def prana_arm(args):
                                                     args.cpu_seconds / 2, threads=t8)
         cpu8 = {"value": round(tps8, 4), "unit": UNIT, "cores": t8, "kind": "port",
                 "sample": f"{steps8} greedy tokens at ctx {args.ctx + 1}.., {tier8} tier, {el8:.1f} s"}
+        parity = {"forced": forced_parity(path, model, args.ctx, rows_fn, c.n_layers, 17, toks, 6),
+                  "free_running": parity}
     suite = {}
     if rank == 0 and world == 1:
         todo = args.configs.split(",") if args.configs is not None else ["c1", "c2", "c3", "c4q8"]

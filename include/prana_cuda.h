@@ -191,6 +191,8 @@ int prana_kv_create(prana_model *m, size_t positions, prana_kv **out);
 int prana_kv_free(prana_kv *kv); /* only while its model is alive */
 /* copy one layer's K or V cache rows [0, rows) to host (f16 bits) */
 int prana_kv_read(prana_kv *kv, size_t layer, int is_v, size_t rows, uint16_t *host_out);
+/* copy rows [first, first + rows) of one layer's K or V cache to host */
+int prana_kv_read_rows(prana_kv *kv, size_t layer, int is_v, size_t first, size_t rows, uint16_t *host_out);
 
 /* overwrite one layer's K or V cache rows [0, rows) from host f16 bits */
 int prana_kv_write(prana_kv *kv, size_t layer, int is_v, size_t rows, const uint16_t *host_in);

@@ -1,4 +1,6 @@
-"""Shared parity checks of the GPU model path against the CPU oracle.
+"""Parity checks of the GPU model path against the CPU oracle (TEST
+INFRASTRUCTURE, not product code: used by tests/ and by bench.py's CPU leg,
+outside every timed region).
 
 The GPU quantizes the same f32 activations as the CPU path, but its f32 sums
 run in another order (tree reductions, per-lane partial sums), so a value that
@@ -135,7 +137,7 @@ def gpu_kv_rows(gkv, n_layers: int, first: int, n: int) -> np.ndarray:
     out = []
     for layer in range(n_layers):
         for is_v in (False, True):
-            out.append(gkv.read(layer, is_v, first + n)[first:first + n].reshape(-1))
+            out.append(gkv.read(layer, is_v, n, first).reshape(-1))
     return np.concatenate(out)
 
 

@@ -86,6 +86,7 @@ SIGNATURES = {
     "prana_kv_create": [P, SZ, C.POINTER(P)],
     "prana_kv_free": [P],
     "prana_kv_read": [P, SZ, I, SZ, P],
+    "prana_kv_read_rows": [P, SZ, I, SZ, SZ, P],
     "prana_forward": [P, P, C.c_uint32, SZ, P, P],
     "prana_forward_trace": [P, P, C.c_uint32, SZ, P, P, P, SZ, C.POINTER(SZ)],
     "prana_kv_write": [P, SZ, I, SZ, P],

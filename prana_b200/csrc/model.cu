@@ -1123,16 +1123,21 @@ int prana_kv_free(prana_kv* kv) {
   return PRANA_OK;
 }
 
-int prana_kv_read(prana_kv* kv, size_t layer, int is_v, size_t rows, uint16_t* host) {
+int prana_kv_read_rows(prana_kv* kv, size_t layer, int is_v, size_t first, size_t rows, uint16_t* host) {
   NEED(kv && host, "null argument");
   const auto& c = kv->m->cfg;
-  NEED(layer < (size_t)c.n_layers && rows <= kv->positions, "layer/rows out of range");
+  NEED(layer < (size_t)c.n_layers && first <= kv->positions && rows <= kv->positions - first,
+       "layer/rows out of range");
   DevScope ds(kv->m->ctx->device);
   const size_t kv_dim = (size_t)(kv->m->kv_heads_l * c.head_dim);  // this rank's kv heads
-  const __half* base = (is_v ? kv->v : kv->k) + layer * kv->positions * kv_dim;
+  const __half* base = (is_v ? kv->v : kv->k) + layer * kv->positions * kv_dim + first * kv_dim;
   PRANA_CK(cudaStreamSynchronize(kv->m->ctx->own));
   PRANA_CK(cudaMemcpy(host, base, rows * kv_dim * 2, cudaMemcpyDeviceToHost));
   return PRANA_OK;
+}
+
+int prana_kv_read(prana_kv* kv, size_t layer, int is_v, size_t rows, uint16_t* host) {
+  return prana_kv_read_rows(kv, layer, is_v, 0, rows, host);
 }
 
 int prana_forward(prana_model* m, prana_kv* kv, uint32_t token, size_t pos, float* logits, uint32_t* next) {

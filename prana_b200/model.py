@@ -128,9 +128,10 @@ class KvCache:
     def handle(self) -> C.c_void_p:
         return self._h
 
-    def read(self, layer: int, is_v: bool, rows: int) -> np.ndarray:
+    def read(self, layer: int, is_v: bool, rows: int, first: int = 0) -> np.ndarray:
+        """f16 bits of rows [first, first + rows) of one layer's K or V cache."""
         out = np.empty((rows, self.model.local_kv_dim()), dtype=np.uint16)
-        call("prana_kv_read", self._h, layer, int(is_v), rows, out.ctypes.data_as(C.c_void_p))
+        call("prana_kv_read_rows", self._h, layer, int(is_v), first, rows, out.ctypes.data_as(C.c_void_p))
         return out
 
     def write(self, layer: int, is_v: bool, rows: np.ndarray) -> None:

@@ -13,7 +13,7 @@ KV rows are the benchmark's seeded N(0, 0.5) f16 rows.
 import numpy as np
 import pytest
 
-from parity import Flips, check_logits, forced_decode
+from oracle.parity import Flips, check_logits, forced_decode
 from prana_b200 import model as pm
 from prana_b200 import synth
 

@@ -11,7 +11,7 @@ margin exceeds 1e-3 -- for single-token decode, prefill, forward_batch
 import numpy as np
 import pytest
 
-from parity import Flips, check_logits, forced_batch, forced_decode
+from oracle.parity import Flips, check_logits, forced_batch, forced_decode
 from prana_b200 import model as pm
 from prana_b200 import synth
 from prana_b200._ffi import TYPE_Q4_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0

@@ -13,7 +13,7 @@ K/V rows the first one wrote are exercised by the second.
 import numpy as np
 import pytest
 
-from parity import Flips, check_logits, check_trace, gpu_kv_rows, row_trace
+from oracle.parity import Flips, check_logits, check_trace, gpu_kv_rows, row_trace
 from prana_b200 import model as pm
 from prana_b200 import synth
 from prana_b200._ffi import TYPE_Q4_0, TYPE_Q6_K, TYPE_Q8_0, PranaError

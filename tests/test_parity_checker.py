@@ -8,7 +8,7 @@ rows must be caught."""
 import numpy as np
 import pytest
 
-from parity import Flips, check_logits, check_trace
+from oracle.parity import Flips, check_logits, check_trace
 from prana_b200 import synth
 from prana_b200._ffi import TYPE_Q4_0, TYPE_Q6_K, TYPE_Q8_0
 
