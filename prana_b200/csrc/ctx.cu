@@ -409,11 +409,17 @@ static int matmul_common(prana_ctx* c, const prana_weight* w, const float* a, co
     }
     return PRANA_OK;
   }
-  if (a) {  // quantize_acts into scratch first (matmul.rs:169, kquant.rs:329)
-    void* sp;
-    const size_t qb = (n_tokens * K + 255) & ~(size_t)255;
-    int rc = ctx_scratch(c, qb + n_tokens * G * 8 + 256, &sp);
+  // scratch: the quantized rows when given f32 rows (quantize_acts first,
+  // matmul.rs:169, kquant.rs:329), then the tensor-core GEMM's scale tables
+  const size_t qb = (n_tokens * K + 255) & ~(size_t)255;
+  const size_t act = a ? qb + ((n_tokens * G * 8 + 255) & ~(size_t)255) : 0;
+  const size_t gemm = n_tokens > 8 ? qgemm_scratch_bytes((int)n_tokens, (int)K) : 0;
+  void* sp = nullptr;
+  if (act + gemm) {
+    int rc = ctx_scratch(c, act + gemm, &sp);
     if (rc) return rc;
+  }
+  if (a) {
     int8_t* qq = static_cast<int8_t*>(sp);
     float* ss = reinterpret_cast<float*>(qq + qb);
     int32_t* mm = reinterpret_cast<int32_t*>(ss + n_tokens * G);
@@ -421,6 +427,19 @@ static int matmul_common(prana_ctx* c, const prana_weight* w, const float* a, co
     q = qq;
     s = ss;
     sum = mm;
+  }
+  if (n_tokens > 8) {  // more than 8 rows: the tensor cores (qgemm.cu)
+    QgemmArgs g{};
+    g.w = w->dw;
+    g.N = w->dw.rows;
+    g.K = (int)K;
+    g.M = (int)n_tokens;
+    g.out = out;
+    g.err = c->err;
+    const cudaError_t e = launch_qgemm(g, q, s, sum, static_cast<uint8_t*>(sp) + act, c->stream);
+    if (e == cudaErrorNotSupported) return fail(PRANA_E_UNSUPPORTED, "tensor map for this weight could not be made");
+    PRANA_CK(e);
+    return PRANA_OK;
   }
   for (size_t t0 = 0; t0 < n_tokens; t0 += 8) {
     const int m = (int)(n_tokens - t0 < 8 ? n_tokens - t0 : 8);

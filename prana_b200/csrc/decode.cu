@@ -49,6 +49,120 @@ __host__ __device__ __forceinline__ size_t gemv_staging_offset(int M, int K) {
 
 // ---------------------------------------------------------------- epilogue of one finished row group
 
+// Stored rows `row` (gate j) and row + 1 (up j) of activation row m:
+// h[m][j] = silu(g) * u exactly as norms.rs:27-31 and infer.rs:197-199.
+__device__ __forceinline__ void swiglu_pair(float* h, int N, int m, int row, float gv, float uv) {
+  const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+  h[(size_t)m * (N / 2) + row / 2] = __fmul_rn(__fmul_rn(gv, sg), uv);
+}
+
+// Stored rows `row` and row + 1 (a RoPE pair of one projection; rows of a
+// NeoX pair were made adjacent at upload) of activation row m: bias, RoPE at
+// the row's position, then q out / f16 K and V cache rows / the f32 in-window
+// K and V (infer.rs:164-178).
+__device__ __forceinline__ void qkv_pair(const QkvMap& qm, int m, int row, float va, float vb) {
+  int s = 0;
+  while (s + 1 < qm.nseg && row >= qm.seg_start[s + 1]) s++;
+  const int kind = qm.kind[s];
+  const int p = (row - qm.seg_start[s]) / 2;  // pair index inside the projection
+  const int half = qm.hd / 2;
+  int ra, rb;
+  if (kind != 2 && qm.neox) {
+    ra = (p / half) * qm.hd + p % half;
+    rb = ra + half;
+  } else {
+    ra = 2 * p;
+    rb = ra + 1;
+  }
+  const int j = p % half;
+  if (qm.bias[s]) {
+    va = __fadd_rn(va, qm.bias[s][ra]);
+    vb = __fadd_rn(vb, qm.bias[s][rb]);
+  }
+  const SeqRow* sr = qm.rows ? qm.rows + m : nullptr;
+  const int pos = sr ? sr->pos : (qm.pos_dev ? *qm.pos_dev : qm.pos0) + m;
+  if (kind != 2) {
+    const float c = qm.cos_t[(size_t)pos * half + j], sn = qm.sin_t[(size_t)pos * half + j];
+    const float a0 = va, b0 = vb;
+    va = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(b0, sn));
+    vb = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(b0, c));
+  }
+  if (kind == 0) {
+    qm.q_out[(size_t)m * qm.q_dim + ra] = va;
+    qm.q_out[(size_t)m * qm.q_dim + rb] = vb;
+  } else {
+    __half* cache = sr ? (kind == 1 ? sr->k : sr->v) + (size_t)qm.layer * sr->lstride : (kind == 1 ? qm.kc : qm.vc);
+    if (pos < (sr ? sr->cap : qm.cap)) {
+      cache[(size_t)pos * qm.kv_dim + ra] = __float2half_rn(va);
+      cache[(size_t)pos * qm.kv_dim + rb] = __float2half_rn(vb);
+    }
+    float* win = kind == 1 ? qm.k_f32 : qm.v_f32;
+    if (win) {
+      win[(size_t)m * qm.kv_dim + ra] = va;
+      win[(size_t)m * qm.kv_dim + rb] = vb;
+    }
+  }
+}
+
+// The batch path's epilogues over rows the tensor-core GEMM stored ([n][N]
+// f32): the same per-pair arithmetic as the streaming GEMV's.
+__global__ void qkv_finish_kernel(const float* y, int n, int N, const QkvMap qm) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;  // pair index over [n][N/2]
+  if (i >= (size_t)n * (N / 2)) return;
+  const int m = (int)(i / (N / 2)), row = 2 * (int)(i % (N / 2));
+  qkv_pair(qm, m, row, y[(size_t)m * N + row], y[(size_t)m * N + row + 1]);
+}
+
+__global__ void swiglu_finish_kernel(const float* y, int n, int N, float* h) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)n * (N / 2)) return;
+  const int m = (int)(i / (N / 2)), row = 2 * (int)(i % (N / 2));
+  swiglu_pair(h, N, m, row, y[(size_t)m * N + row], y[(size_t)m * N + row + 1]);
+}
+
+cudaError_t launch_qkv_finish(const float* y, int n, int N, const QkvMap& qm, cudaStream_t st) {
+  const size_t pairs = (size_t)n * (N / 2);
+  qkv_finish_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(y, n, N, qm);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_finish(const float* y, int n, int N, float* h, cudaStream_t st) {
+  const size_t pairs = (size_t)n * (N / 2);
+  swiglu_finish_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(y, n, N, h);
+  return cudaGetLastError();
+}
+
+// One CTA per row: (rmsnorm, then) per-32 quantization of an f32 row, with
+// the streaming GEMV prologue's own routine (same int8 rows either path).
+__global__ void __launch_bounds__(256) norm_quant_kernel(const float* x, const float* w, float eps, int K, int8_t* q,
+                                                          float* s, int32_t* sum) {
+  extern __shared__ __align__(16) float nq_smem[];
+  __shared__ float red[8];
+  __shared__ float inv_s[8];
+  float* xs = nq_smem;
+  float* ws = nq_smem + K;
+  const size_t r = blockIdx.x;
+  for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+    reinterpret_cast<float4*>(xs)[i] = __ldcg(reinterpret_cast<const float4*>(x + r * K) + i);
+    if (w) reinterpret_cast<float4*>(ws)[i] = __ldg(reinterpret_cast<const float4*>(w) + i);
+  }
+  __syncthreads();
+  block_quantize_smem(xs, w ? ws : nullptr, eps, K, q + r * K, s + r * (K / 32), sum + r * (K / 32), red, inv_s);
+}
+
+cudaError_t launch_norm_quant(const float* x, const float* w, float eps, int rows, int K, int8_t* q, float* s,
+                              int32_t* sum, cudaStream_t st) {
+  if (K % 32 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)K * 4 * (w ? 2 : 1);
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute((const void*)norm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  norm_quant_kernel<<<rows, 256, smem, st>>>(x, w, eps, K, q, s, sum);
+  return cudaGetLastError();
+}
+
 // Lane m (< g.m) holds v[r] = row (r0 + r) . activation row m.
 template <int EPI>
 __device__ __forceinline__ void finish_rows(const StreamArgs& g, int r0, int m, const float (&v)[DG_RPW], float& run_v,
@@ -75,63 +189,18 @@ __device__ __forceinline__ void finish_rows(const StreamArgs& g, int r0, int m, 
       }
     }
   } else if constexpr (EPI == EPI_SWIGLU) {
-    // stored rows 2j (gate) and 2j+1 (up): silu(g)*u exactly as norms.rs:27-31, infer.rs:197-199
 #pragma unroll
     for (int r = 0; r < DG_RPW; r += 2) {
       const int row = r0 + r;
       if (row >= N) break;
-      const float gv = v[r];
-      const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
-      g.out[(size_t)m * (N / 2) + row / 2] = __fmul_rn(__fmul_rn(gv, sg), v[r + 1]);
+      swiglu_pair(g.out, N, m, row, v[r], v[r + 1]);
     }
   } else {  // EPI_QKV
-    const QkvMap& qm = g.qkv;
 #pragma unroll
     for (int r = 0; r < DG_RPW; r += 2) {
       const int row = r0 + r;
       if (row >= N) break;
-      int s = 0;
-      while (s + 1 < qm.nseg && row >= qm.seg_start[s + 1]) s++;
-      const int kind = qm.kind[s];
-      const int p = (row - qm.seg_start[s]) / 2;  // pair index inside the projection
-      const int half = qm.hd / 2;
-      int ra, rb;
-      if (kind != 2 && qm.neox) {
-        ra = (p / half) * qm.hd + p % half;
-        rb = ra + half;
-      } else {
-        ra = 2 * p;
-        rb = ra + 1;
-      }
-      const int j = p % half;
-      float va = v[r], vb = v[r + 1];
-      if (qm.bias[s]) {
-        va = __fadd_rn(va, qm.bias[s][ra]);
-        vb = __fadd_rn(vb, qm.bias[s][rb]);
-      }
-      const SeqRow* sr = qm.rows ? qm.rows + m : nullptr;
-      const int pos = sr ? sr->pos : (qm.pos_dev ? *qm.pos_dev : qm.pos0) + m;
-      if (kind != 2) {
-        const float c = qm.cos_t[(size_t)pos * half + j], sn = qm.sin_t[(size_t)pos * half + j];
-        const float a0 = va, b0 = vb;
-        va = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(b0, sn));
-        vb = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(b0, c));
-      }
-      if (kind == 0) {
-        qm.q_out[(size_t)m * qm.q_dim + ra] = va;
-        qm.q_out[(size_t)m * qm.q_dim + rb] = vb;
-      } else {
-        __half* cache = sr ? (kind == 1 ? sr->k : sr->v) + (size_t)qm.layer * sr->lstride : (kind == 1 ? qm.kc : qm.vc);
-        if (pos < (sr ? sr->cap : qm.cap)) {
-          cache[(size_t)pos * qm.kv_dim + ra] = __float2half_rn(va);
-          cache[(size_t)pos * qm.kv_dim + rb] = __float2half_rn(vb);
-        }
-        float* win = kind == 1 ? qm.k_f32 : qm.v_f32;
-        if (win) {
-          win[(size_t)m * qm.kv_dim + ra] = va;
-          win[(size_t)m * qm.kv_dim + rb] = vb;
-        }
-      }
+      qkv_pair(g.qkv, m, row, v[r], v[r + 1]);
     }
   }
 }

@@ -155,6 +155,13 @@ struct StreamArgs {
 };
 
 cudaError_t launch_stream(const StreamArgs& g, int epi, int pro, cudaStream_t st, bool pdl);
+// Batch path around the tensor-core GEMM: rows (rmsnorm'd when w is set, then)
+// quantized once per projection; the EPI_QKV / EPI_SWIGLU arithmetic over
+// rows the GEMM stored ([n][N] f32).
+cudaError_t launch_norm_quant(const float* x, const float* w, float eps, int rows, int K, int8_t* q, float* s,
+                              int32_t* sum, cudaStream_t st);
+cudaError_t launch_qkv_finish(const float* y, int n, int N, const QkvMap& qm, cudaStream_t st);
+cudaError_t launch_swiglu_finish(const float* y, int n, int N, float* h, cudaStream_t st);
 int gemv_split_k(int type, int K, int N, int sm_count);
 size_t gemv_smem_bytes(int M, int K, int pro);
 

@@ -207,6 +207,12 @@ struct Bufs {
   float* logits_l = nullptr;  // tensor parallel: this rank's vocabulary slice
   uint32_t* toks = nullptr;     // input ids [rows]
   uint32_t* tok_out = nullptr;  // argmax per row [rows]
+  // batch path (rows > 8): quantized rows, GEMM outputs, GEMM scratch
+  int8_t* bq = nullptr;
+  float* bs = nullptr;
+  int32_t* bsum = nullptr;
+  float* y = nullptr;
+  void* qg = nullptr;
   std::vector<void*> owned;
   ~Bufs() {
     for (void* p : owned) cudaFree(p);
@@ -373,6 +379,17 @@ int make_bufs(prana_model* m, size_t rows, bool window, Bufs& b) {
   rc |= b.alloc(b.u, rows * hid);
   rc |= b.alloc(b.toks, rows);
   rc |= b.alloc(b.tok_out, rows);
+  if (rows > 8 && m->tp_world == 1) {
+    const size_t max_k = std::max(std::max(dim, q_dim), hid);
+    const size_t max_n = std::max(q_dim + 2 * kv_dim, 2 * hid);
+    rc |= b.alloc(b.bq, rows * max_k);
+    rc |= b.alloc(b.bs, rows * max_k / 32);
+    rc |= b.alloc(b.bsum, rows * max_k / 32);
+    rc |= b.alloc(b.y, rows * max_n);
+    uint8_t* qg = nullptr;
+    rc |= b.alloc(qg, qgemm_scratch_bytes((int)rows, (int)max_k));
+    b.qg = qg;
+  }
   if (window) {
     rc |= b.alloc(b.kf, rows * kv_dim);
     rc |= b.alloc(b.vf, rows * kv_dim);
@@ -441,6 +458,34 @@ int run_stream(prana_model* m, StreamArgs& a, int epi, int pro, bool pdl) {
   return PRANA_OK;
 }
 
+// Batch path: the n quantized rows in b.bq times w on the tensor cores.
+int run_qgemm(prana_model* m, Bufs& b, const StreamW& w, int n, float* out, int resid) {
+  QgemmArgs g{};
+  g.w = w.w.dw;
+  g.N = w.w.dw.rows;
+  g.K = w.w.dw.cols;
+  g.M = n;
+  g.out = out;
+  g.resid = resid;
+  g.err = m->err;
+  const cudaError_t e = launch_qgemm(g, b.bq, b.bs, b.bsum, b.qg, m->ctx->own);
+  if (e == cudaErrorNotSupported) return fail(PRANA_E_UNSUPPORTED, "tensor map for a [%d x %d] weight could not be made", g.N, g.K);
+  PRANA_CK(e);
+  return PRANA_OK;
+}
+
+// Batch path: rows x [n][k] (rmsnorm'd by w when set) quantized into b.bq / b.bs / b.bsum.
+int quantize_rows(prana_model* m, Bufs& b, const float* x, const float* w, int n, int k, Trace* tr) {
+  PRANA_CK(launch_norm_quant(x, w, m->cfg.norm_eps, n, k, b.bq, b.bs, b.bsum, m->ctx->own));
+  if (tr) {  // the site's rows, as the streaming kernels' CTA 0 copies them
+    PRANA_CK(cudaMemcpyAsync(tr->q + tr->nq, b.bq, (size_t)n * k, cudaMemcpyDeviceToDevice, m->ctx->own));
+    PRANA_CK(cudaMemcpyAsync(tr->s + tr->ns, b.bs, (size_t)n * k / 32 * 4, cudaMemcpyDeviceToDevice, m->ctx->own));
+    tr->nq += (size_t)n * k;
+    tr->ns += (size_t)n * k / 32;
+  }
+  return PRANA_OK;
+}
+
 // One pass of n rows through the model (infer.rs:142-211 for n = 1 and
 // :296-374 / :220-286 for the batched forms).  Rows sit at positions pos0..
 // (or *pos_dev.. when pos_dev is set, n == 1).  MODE_WINDOW attends over the
@@ -501,6 +546,9 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
   const int q_dim = (int)(m->heads_l * c.head_dim), kv_dim = (int)(m->kv_heads_l * c.head_dim);
   const size_t lstride = kv->positions * (size_t)kv_dim;
   int rc;
+  // more than 8 rows on one GPU: every projection's rows are quantized once and
+  // multiplied on the tensor cores (qgemm.cu); up to 8, the streaming GEMV
+  const bool batch = n > 8 && b.bq != nullptr;
   PRANA_CK(launch_embed(m->emb.dw, toks_dev, tok_dev, n, b.x, st, pdl));
   for (size_t l = 0; l < m->layers.size(); l++) {
     LayerW& L = m->layers[l];
@@ -508,11 +556,12 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
     __half* vc = kv->v + l * lstride;
     // --- rmsnorm -> Q|K|V -> bias -> RoPE -> KV-cache write
     bool first_part = true;
+    if (batch && (rc = quantize_rows(m, b, b.x, L.rms_att, n, dim, tr))) return rc;
     for (auto& part : L.qkv) {
-      for (int c0 = 0; c0 < n; c0 += 8) {
-        const int mc = std::min(8, n - c0);
+      for (int c0 = 0; c0 < n; c0 += batch ? n : 8) {
+        const int mc = batch ? n : std::min(8, n - c0);
         StreamArgs a = stream_args(m, part.sw, mc, b.x + (size_t)c0 * dim, L.rms_att);
-        if (tr && first_part) tr->site(a, dim);
+        if (tr && first_part && !batch) tr->site(a, dim);
         QkvMap& q = a.qkv;
         q.nseg = part.nseg;
         for (int s = 0; s <= part.nseg; s++) q.seg_start[s] = part.seg_start[s];
@@ -541,7 +590,12 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
           q.rows = mu->rows_dev + c0;
           q.layer = (int)l;
         }
-        if ((rc = run_stream(m, a, EPI_QKV, PRO_NORM, pdl))) return rc;
+        if (batch) {
+          if ((rc = run_qgemm(m, b, part.sw, n, b.y, 0))) return rc;
+          PRANA_CK(launch_qkv_finish(b.y, n, part.sw.w.dw.rows, q, st));
+        } else if ((rc = run_stream(m, a, EPI_QKV, PRO_NORM, pdl))) {
+          return rc;
+        }
       }
       first_part = false;
     }
@@ -595,7 +649,11 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       }
     }
     // --- quantize(attn) -> wo -> residual
-    for (int c0 = 0; c0 < n; c0 += 8) {
+    if (batch) {
+      if ((rc = quantize_rows(m, b, b.att, nullptr, n, q_dim, tr)) || (rc = run_qgemm(m, b, L.wo, n, b.x, 1)))
+        return rc;
+    }
+    for (int c0 = 0; c0 < n && !batch; c0 += 8) {
       const int mc = std::min(8, n - c0);
       StreamArgs a = stream_args(m, L.wo, mc, b.att + (size_t)c0 * q_dim, nullptr);
       if (tr) tr->site(a, q_dim);
@@ -605,7 +663,17 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
     }
     if (tp && (rc = tp_sum_rows(m, b.x, (size_t)n * dim, st, pdl))) return rc;
     // --- rmsnorm -> gate|up -> silu(gate) * up
-    for (int c0 = 0; c0 < n; c0 += 8) {
+    if (batch) {
+      if ((rc = quantize_rows(m, b, b.x, L.rms_ffn, n, dim, tr))) return rc;
+      if (L.fused_gu) {
+        if ((rc = run_qgemm(m, b, L.gu, n, b.y, 0))) return rc;
+        PRANA_CK(launch_swiglu_finish(b.y, n, L.gu.w.dw.rows, b.h, st));
+      } else {
+        if ((rc = run_qgemm(m, b, L.w1, n, b.h, 0)) || (rc = run_qgemm(m, b, L.w3, n, b.u, 0))) return rc;
+        PRANA_CK(launch_silu_mul(b.h, b.u, (size_t)n * hid, st));
+      }
+    }
+    for (int c0 = 0; c0 < n && !batch; c0 += 8) {
       const int mc = std::min(8, n - c0);
       if (L.fused_gu) {
         StreamArgs a = stream_args(m, L.gu, mc, b.x + (size_t)c0 * dim, L.rms_ffn);
@@ -625,7 +693,10 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
       }
     }
     // --- quantize(h) -> w2 -> residual
-    for (int c0 = 0; c0 < n; c0 += 8) {
+    if (batch) {
+      if ((rc = quantize_rows(m, b, b.h, nullptr, n, hid, tr)) || (rc = run_qgemm(m, b, L.w2, n, b.x, 1))) return rc;
+    }
+    for (int c0 = 0; c0 < n && !batch; c0 += 8) {
       const int mc = std::min(8, n - c0);
       StreamArgs a = stream_args(m, L.w2, mc, b.h + (size_t)c0 * hid, nullptr);
       if (tr) tr->site(a, hid);
@@ -642,6 +713,13 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
   }
   if (!head) return PRANA_OK;
   // --- final rmsnorm -> LM head -> argmax (Model::logits, checkpoint.rs:239-248; infer.rs:560-568)
+  if (batch) {  // logits_batch (checkpoint.rs:256-265): the head streams once for all rows
+    if ((rc = quantize_rows(m, b, b.x, m->rms_final, n, dim, tr)) ||
+        (rc = run_qgemm(m, b, m->head, n, b.logits, 0)))
+      return rc;
+    PRANA_CK(launch_argmax(b.logits, n, (int)c.vocab_size, b.tok_out, st));
+    return PRANA_OK;
+  }
   for (int c0 = 0; c0 < n; c0 += 8) {
     const int mc = std::min(8, n - c0);
     StreamArgs a = stream_args(m, m->head, mc, b.x + (size_t)c0 * dim, m->rms_final);
