@@ -195,6 +195,8 @@ struct QgemmArgs {
   int resid;            // 1: out += result
   int32_t* dots;        // diagnostic: per-block int32 [M][N][K/32 (x2 for Q6_K)] instead of out
   unsigned* err;        // device error flag
+  int splits;           // set by the launcher: K splits (partials in `part`, summed in split order)
+  float* part;
 };
 // out = W . rows (q [M][K] int8, s / sums [M][K/32]); scratch >= qgemm_scratch_bytes
 cudaError_t launch_qgemm(QgemmArgs g, const int8_t* q, const float* s, const int32_t* sums, void* scratch,

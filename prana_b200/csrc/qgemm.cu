@@ -257,7 +257,10 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   const int row0 = blockIdx.x * QG_BM, tok0 = blockIdx.y * NT;
   const int K = g.K, N = g.N;
   const int n_blk = K / 32;
-  const int n_stage = (K + BK - 1) / BK;
+  // split-K: this CTA takes stages [s_lo, s_lo + n_stage) of the row
+  const int all_stages = (K + BK - 1) / BK;
+  const int s_lo = (int)(((long long)all_stages * blockIdx.z) / gridDim.z);
+  const int n_stage = (int)(((long long)all_stages * (blockIdx.z + 1)) / gridDim.z) - s_lo;
 
   if (tid == 0) {
     s_abort = 0;
@@ -292,20 +295,20 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         if (*abort) break;
         uint8_t* sm = stage(st);
         mbar_arrive_expect_tx(&full[st], L::TX);
-        const int k0 = s * BK;
+        const int sg = s_lo + s, k0 = sg * BK;
 #pragma unroll
         for (int a = 0; a < L::KATOMS; a++) tma_load_2d(sm + L::OFF_B + a * NT * 128, &tm_x, k0 + a * 128, tok0, &full[st]);
         if constexpr (F::RAW == 0) {
 #pragma unroll
           for (int a = 0; a < L::KATOMS; a++) tma_load_2d(sm + a * L::A_ATOM, &tm_w, k0 + a * 128, row0, &full[st]);
         } else if constexpr (T == T_Q6_K) {
-          tma_load_2d(sm + L::OFF_RAW, &tm_w, s * 128, row0, &full[st]);                 // ql
-          tma_load_2d(sm + L::OFF_RAW + QG_BM * 128, &tm_w2, s * 64, row0, &full[st]);  // qh
+          tma_load_2d(sm + L::OFF_RAW, &tm_w, sg * 128, row0, &full[st]);                 // ql
+          tma_load_2d(sm + L::OFF_RAW + QG_BM * 128, &tm_w2, sg * 64, row0, &full[st]);  // qh
         } else {
-          tma_load_2d(sm + L::OFF_RAW, &tm_w, s * F::RAW, row0, &full[st]);
+          tma_load_2d(sm + L::OFF_RAW, &tm_w, sg * F::RAW, row0, &full[st]);
         }
-        tma_load_2d(sm + L::OFF_SA, &tm_sa, tok0, s * BLK, &full[st]);
-        if constexpr (L::SUM_BYTES > 0) tma_load_2d(sm + L::OFF_SUM, &tm_sum, tok0, s * BLK, &full[st]);
+        tma_load_2d(sm + L::OFF_SA, &tm_sa, tok0, sg * BLK, &full[st]);
+        if constexpr (L::SUM_BYTES > 0) tma_load_2d(sm + L::OFF_SUM, &tm_sum, tok0, sg * BLK, &full[st]);
         issued = s + 1;
       }
       // wind down: the copies still possibly in flight are those of the last NS stages issued
@@ -327,7 +330,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         if (!ok) break;
         tc_fence_after();
         const uint32_t a_base = smem_u32(stage(st)), b_base = a_base + L::OFF_B;
-        const int nb = min(BLK, n_blk - s * BLK);
+        const int nb = min(BLK, n_blk - (s_lo + s) * BLK);
         for (int j = 0; j < nb && ok; j++) {
           const uint32_t koff = (uint32_t)((j & 3) * 32);
           const uint32_t a_at = a_base + (uint32_t)((j >> 2) * L::A_ATOM) + koff;
@@ -391,8 +394,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     // (Q4_K's live in the staged super-block header)
     unsigned short dn[BLK], dc[BLK];
     uint4 scn = make_uint4(0u, 0u, 0u, 0u), scc = scn;
-    auto load_scales = [&](int s) {
-      if (s >= n_stage) return;
+    auto load_scales = [&](int s) {  // s: global stage
+      if (s >= s_lo + n_stage) return;
       if constexpr (T == T_Q8_0 || T == T_Q4_0) {
         const unsigned short* d = reinterpret_cast<const unsigned short*>(g.w.d) + (size_t)rr * n_blk + s * BLK;
         const int nb = min(BLK, n_blk - s * BLK);
@@ -404,22 +407,22 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         scn = __ldg(reinterpret_cast<const uint4*>(g.w.sc + (size_t)rr * (K / 16)) + s);
       }
     };
-    load_scales(0);
+    load_scales(s_lo);
     int mma = 0;
     bool ok = true;
     for (int s = 0; s < n_stage && ok; s++) {
-      const int st = s % NS;
+      const int st = s % NS, sg = s_lo + s;
       const uint8_t* sm = stage(st);
 #pragma unroll
       for (int j = 0; j < BLK; j++) dc[j] = dn[j];
       scc = scn;
-      load_scales(s + 1);
+      load_scales(sg + 1);
       if (!qwait(&full[st], (s / NS) & 1, abort)) {
         ok = false;
         break;
       }
       const float* sa_s = reinterpret_cast<const float*>(sm + L::OFF_SA);
-      const int nb = min(BLK, n_blk - s * BLK);
+      const int nb = min(BLK, n_blk - sg * BLK);
 #pragma unroll 1
       for (int j = 0; j < nb && ok; j++) {
         // weight scales of block j of this stage for row rl
@@ -457,7 +460,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[slot]);
           mma++;
-          const int b = s * BLK + j;  // global block
+          const int b = sg * BLK + j;  // global block
           if (g.dots) {
             if (r < N)
 #pragma unroll
@@ -495,14 +498,23 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     }
     if (!ok) *abort = 1;
     if (ok && r < N && !g.dots) {
+      if (gridDim.z > 1) {  // split-K: this split's partial, summed in split order by qgemm_reduce_kernel
+        float* pz = g.part + (size_t)blockIdx.z * g.M * N;
 #pragma unroll
-      for (int c = 0; c < NC; c++) {
-        const int t = tok0 + c0 + c;
-        if (t < g.M) {
-          float* o = g.out + (size_t)t * N + r;
-          float v = acc[c];
-          if (g.bias) v = __fadd_rn(v, g.bias[r]);
-          *o = g.resid ? __fadd_rn(*o, v) : v;
+        for (int c = 0; c < NC; c++) {
+          const int t = tok0 + c0 + c;
+          if (t < g.M) pz[(size_t)t * N + r] = acc[c];
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+          const int t = tok0 + c0 + c;
+          if (t < g.M) {
+            float* o = g.out + (size_t)t * N + r;
+            float v = acc[c];
+            if (g.bias) v = __fadd_rn(v, g.bias[r]);
+            *o = g.resid ? __fadd_rn(*o, v) : v;
+          }
         }
       }
     }
@@ -525,6 +537,19 @@ __global__ void qgemm_prep_kernel(const float* s, const int32_t* sum, int m, int
   const int b = i / m_pad, t = i - b * m_pad;
   s_t[i] = t < m ? s[(size_t)t * G + b] : 0.0f;
   if (sum_t) sum_t[i] = t < m ? sum[(size_t)t * G + b] : 0;
+}
+
+// Split-K partials [splits][M][N] summed in split order (the same bits every
+// run), then the epilogue: + bias, stored or added to out.
+__global__ void qgemm_reduce_kernel(const float* part, int splits, int M, int N, const float* bias, int resid,
+                                    float* out) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t mn = (size_t)M * N;
+  if (i >= mn) return;
+  float v = part[i];
+  for (int z = 1; z < splits; z++) v = __fadd_rn(v, part[(size_t)z * mn + i]);
+  if (bias) v = __fadd_rn(v, bias[i % N]);
+  out[i] = resid ? __fadd_rn(out[i], v) : v;
 }
 
 // ---- host: tensor maps, launch
@@ -595,8 +620,12 @@ cudaError_t qgemm_go(const QgemmArgs& g, const int8_t* q, const float* sa_t, con
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  const dim3 grid((unsigned)((N + QG_BM - 1) / QG_BM), (unsigned)(g.m_pad / NT));
+  const dim3 grid((unsigned)((N + QG_BM - 1) / QG_BM), (unsigned)(g.m_pad / NT), (unsigned)g.splits);
   kern<<<grid, QG_THREADS, L::SMEM, st>>>(tm_w, tm_w2, tm_x, tm_sa, tm_sum, g);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || g.splits == 1 || g.dots) return e;
+  const size_t mn = (size_t)g.M * g.N;
+  qgemm_reduce_kernel<<<(unsigned)((mn + 255) / 256), 256, 0, st>>>(g.part, g.splits, g.M, g.N, g.bias, g.resid, g.out);
   return cudaGetLastError();
 }
 
@@ -613,10 +642,28 @@ cudaError_t qgemm_t(const QgemmArgs& g, const int8_t* q, const float* sa_t, cons
 
 int qgemm_tokens_per_tile(int m) { return m <= 16 ? 16 : m <= 32 ? 32 : 64; }
 
+namespace {
+constexpr int QG_SPLIT_CTAS = 148;  // split K until the grid covers about one CTA per SM
+constexpr int QG_MAX_SPLITS = 16;
+// K splits for an [n x k] weight times m rows: enough CTAs to cover the SMs,
+// each split keeping at least 2 stages
+int qgemm_splits(int m, int n, int k) {
+  const int nt = qgemm_tokens_per_tile(m);
+  const int tiles = ((n + QG_BM - 1) / QG_BM) * ((m + nt - 1) / nt);
+  const int stages = (k + 255) / 256;
+  int sp = (QG_SPLIT_CTAS + tiles - 1) / tiles;
+  sp = min(sp, max(1, stages / 2));
+  return max(1, min(sp, QG_MAX_SPLITS));
+}
+}  // namespace
+
 size_t qgemm_scratch_bytes(int m, int k) {
   const int nt = qgemm_tokens_per_tile(m);
   const size_t m_pad = (size_t)(m + nt - 1) / nt * nt;
-  return 2 * m_pad * (size_t)(k / 32) * 4 + 256;
+  // scale tables, then split partials: splits x m x n <= (SM count + tiles) x 128 x nt floats,
+  // since splits only multiply grids smaller than the SM count
+  const size_t tables = (2 * m_pad * (size_t)(k / 32) * 4 + 255) & ~(size_t)255;
+  return tables + (size_t)(2 * QG_SPLIT_CTAS) * QG_BM * nt * 4 + 256;
 }
 
 cudaError_t launch_qgemm(QgemmArgs g, const int8_t* q, const float* s, const int32_t* sums, void* scratch,
@@ -629,6 +676,9 @@ cudaError_t launch_qgemm(QgemmArgs g, const int8_t* q, const float* s, const int
   const int G = g.K / 32;
   float* sa_t = static_cast<float*>(scratch);
   int32_t* sum_t = reinterpret_cast<int32_t*>(sa_t + (size_t)g.m_pad * G);
+  g.splits = g.dots ? 1 : qgemm_splits(g.M, g.N, g.K);
+  g.part = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) +
+                                    ((2 * (size_t)g.m_pad * G * 4 + 255) & ~(size_t)255));
   const int n = G * g.m_pad;
   qgemm_prep_kernel<<<(n + 255) / 256, 256, 0, st>>>(s, g.w.type == T_Q4_K ? sums : nullptr, g.M, G, g.m_pad, sa_t,
                                                       g.w.type == T_Q4_K ? sum_t : nullptr);
