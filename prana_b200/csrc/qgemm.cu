@@ -91,7 +91,12 @@ struct QgLayout {
   static_assert(NS >= 2, "stage too large");
   static constexpr int MPB = F::A_TILES;                    // MMAs per 32-value block
   static constexpr int SLOTS_MAX = 512 / NT;
-  static constexpr int SLOTS = SLOTS_MAX > 16 ? 16 : SLOTS_MAX;  // TMEM accumulator slots
+  static constexpr int SLOTS = SLOTS_MAX > 16 ? 16 : SLOTS_MAX;  // TMEM accumulator slots (one MMA each)
+  // MMAs are committed, waited on and released in groups of GS slots (a
+  // group never spans two stages); NG groups in flight
+  static constexpr int GS = SLOTS / 2 < 8 ? SLOTS / 2 : 8;
+  static constexpr int NG = SLOTS / GS;
+  static_assert((BLK * F::A_TILES) % GS == 0, "groups tile a stage");
   static constexpr int TMEM_COLS = SLOTS * NT < 32 ? 32 : SLOTS * NT;
   static constexpr size_t SMEM = (size_t)NS * STAGE + 1024 /* alignment */ + 1024 /* barriers */;
   static constexpr uint32_t TX = (uint32_t)(B_BYTES + (F::RAW ? RAW_BYTES : A_BYTES) + SA_BYTES + SUM_BYTES);
@@ -237,16 +242,16 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
                  const __grid_constant__ CUtensorMap tm_sum, const QgemmArgs g) {
   using L = QgLayout<T, NT>;
   using F = QgFmt<T>;
-  constexpr int NS = L::NS, BK = L::BK, SLOTS = L::SLOTS, MPB = L::MPB, BLK = L::BLK;
+  constexpr int NS = L::NS, BK = L::BK, SLOTS = L::SLOTS, MPB = L::MPB, BLK = L::BLK, GS = L::GS, NG = L::NG;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + NS * L::STAGE);
   uint64_t* full = bars;                   // [NS] every TMA byte of the stage landed
   uint64_t* conv = bars + NS;              // [NS] producers wrote the int8 tile
   uint64_t* freed = bars + 2 * NS;         // [NS] MMAs completed and epilogue done with the stage
-  uint64_t* acc_full = bars + 3 * NS;      // [SLOTS] one MMA landed in the slot
-  uint64_t* acc_empty = acc_full + SLOTS;  // [SLOTS] epilogue warps read the slot
-  uint64_t* mma_done = acc_empty + SLOTS;  // every MMA issued has completed (before TMEM is freed)
+  uint64_t* acc_full = bars + 3 * NS;      // [NG] a group's MMAs landed in its slots
+  uint64_t* acc_empty = acc_full + NG;     // [NG] every epilogue warp read the group's slots
+  uint64_t* mma_done = acc_empty + NG;     // every MMA issued has completed (before TMEM is freed)
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mma_done + 1);
   __shared__ int s_abort;
   volatile int* abort = &s_abort;
@@ -269,7 +274,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       mbar_init(&conv[i], QG_PRODUCERS);
       mbar_init(&freed[i], 1 + QG_EPI_WARPS);
     }
-    for (int i = 0; i < SLOTS; i++) {
+    for (int i = 0; i < NG; i++) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], QG_EPI_WARPS);
     }
@@ -321,7 +326,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     // ------------------------------------------------ MMA issue
     if (lane == 0) {
       constexpr uint32_t idesc = i8_idesc(NT);
-      int mma = 0, last_stage = -1;
+      int grp = 0, last_stage = -1;
       bool ok = true;
       for (int s = 0; s < n_stage && ok; s++) {
         const int st = s % NS, ph = (s / NS) & 1;
@@ -331,23 +336,24 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         tc_fence_after();
         const uint32_t a_base = smem_u32(stage(st)), b_base = a_base + L::OFF_B;
         const int nb = min(BLK, n_blk - (s_lo + s) * BLK);
-        for (int j = 0; j < nb && ok; j++) {
-          const uint32_t koff = (uint32_t)((j & 3) * 32);
-          const uint32_t a_at = a_base + (uint32_t)((j >> 2) * L::A_ATOM) + koff;
-          const uint32_t b_at = b_base + (uint32_t)((j >> 2) * NT * 128) + koff;
-#pragma unroll
-          for (int h = 0; h < MPB; h++) {
-            const int slot = mma % SLOTS, use = mma / SLOTS;
-            if (use > 0 && !qwait(&acc_empty[slot], (use - 1) & 1, abort)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            tc_mma_i8(tmem + (uint32_t)(slot * NT), sw128_desc(a_at + (uint32_t)(h * L::KATOMS * L::A_ATOM)),
-                      sw128_desc(b_at), idesc);
-            tc_commit(&acc_full[slot]);
-            mma++;
+        const int total = nb * MPB;  // MMAs of this stage: (block j, half h) in order
+        for (int i0 = 0; i0 < total && ok; i0 += GS, grp++) {
+          const int gslot = grp % NG;
+          if (grp >= NG && !qwait(&acc_empty[gslot], ((grp / NG) - 1) & 1, abort)) {
+            ok = false;
+            break;
           }
+          tc_fence_after();
+          const int cnt = min(GS, total - i0);
+          for (int i = 0; i < cnt; i++) {
+            const int j = (i0 + i) / MPB, h = (i0 + i) % MPB;
+            const uint32_t koff = (uint32_t)((j & 3) * 32);
+            const uint32_t a_at = a_base + (uint32_t)((j >> 2) * L::A_ATOM) + koff +
+                                  (uint32_t)(h * L::KATOMS * L::A_ATOM);
+            const uint32_t b_at = b_base + (uint32_t)((j >> 2) * NT * 128) + koff;
+            tc_mma_i8(tmem + (uint32_t)((gslot * GS + i) * NT), sw128_desc(a_at), sw128_desc(b_at), idesc);
+          }
+          tc_commit(&acc_full[gslot]);
         }
         tc_commit(&freed[st]);
         last_stage = s;
@@ -408,8 +414,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       }
     };
     load_scales(s_lo);
-    int mma = 0;
+    int grp = 0;
     bool ok = true;
+    constexpr int NB = (32 / NC) < 1 ? 1 : ((32 / NC) < GS ? (32 / NC) : GS);  // slots per load batch (<= 32 registers)
     for (int s = 0; s < n_stage && ok; s++) {
       const int st = s % NS, sg = s_lo + s;
       const uint8_t* sm = stage(st);
@@ -423,74 +430,79 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       }
       const float* sa_s = reinterpret_cast<const float*>(sm + L::OFF_SA);
       const int nb = min(BLK, n_blk - sg * BLK);
-#pragma unroll 1
-      for (int j = 0; j < nb && ok; j++) {
-        // weight scales of block j of this stage for row rl
-        float ws0 = 0.0f, ws1 = 0.0f, wmin = 0.0f;
-        if constexpr (T == T_Q8_0 || T == T_Q4_0) {
-          ws0 = h2f(dc[j]);
-        } else if constexpr (T == T_Q4_K) {
-          const uint8_t* hdr = sm + L::OFF_RAW + rl * F::RAW;
-          int sc, mn;
-          q4k_scale_min(j, hdr + 4, sc, mn);
-          const float d = h2f((unsigned short)(hdr[0] | (hdr[1] << 8)));
-          const float dmin = h2f((unsigned short)(hdr[2] | (hdr[3] << 8)));
-          ws0 = __fmul_rn(d, (float)sc);
-          wmin = __fmul_rn(dmin, (float)mn);
-        } else {
-          ws0 = h2f(dc[0]);
-          const int8_t* sc = reinterpret_cast<const int8_t*>(&scc);
-          wmin = (float)sc[2 * j];
-          ws1 = (float)sc[2 * j + 1];
+      const int total = nb * MPB;
+      for (int i0 = 0; i0 < total && ok; i0 += GS, grp++) {
+        const int gslot = grp % NG;
+        if (!qwait(&acc_full[gslot], (grp / NG) & 1, abort)) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        const int cnt = min(GS, total - i0);
+        for (int b0 = 0; b0 < cnt; b0 += NB) {
+          uint32_t v[NB][NC];
 #pragma unroll
-        for (int h = 0; h < MPB; h++) {
-          const int slot = mma % SLOTS, use = mma / SLOTS;
-          if (!qwait(&acc_full[slot], use & 1, abort)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          uint32_t v[NC];
+          for (int k = 0; k < NB; k++)
+            if (b0 + k < cnt) {
 #pragma unroll
-          for (int c = 0; c < NC; c += 8)
-            tc_ld8(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(slot * NT + c0 + c), v + c);
+              for (int c = 0; c < NC; c += 8)
+                tc_ld8(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)((gslot * GS + b0 + k) * NT + c0 + c), &v[k][c]);
+            }
           tc_wait_ld();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[slot]);
-          mma++;
-          const int b = sg * BLK + j;  // global block
-          if (g.dots) {
-            if (r < N)
+#pragma unroll
+          for (int k = 0; k < NB; k++) {
+            if (b0 + k >= cnt) break;
+            const int i = i0 + b0 + k, j = i / MPB, h = i % MPB;
+            const int b = sg * BLK + j;  // global block
+            if (g.dots) {
+              if (r < N)
+#pragma unroll
+                for (int c = 0; c < NC; c++) {
+                  const int t = tok0 + c0 + c;
+                  if (t < g.M)
+                    g.dots[((size_t)t * N + r) * (size_t)(n_blk * MPB) + (size_t)b * MPB + h] = (int32_t)v[k][c];
+                }
+              continue;
+            }
+            const float* sa = sa_s + j * NT + c0;
+            if constexpr (T == T_Q8_0 || T == T_Q4_0) {
+              // (d * sa) * dot (matmul.rs:395-406, kquant.rs:240-252)
+              unsigned short dj = dc[0];
+#pragma unroll
+              for (int q = 1; q < BLK; q++)
+                if (q == j) dj = dc[q];  // a register select, not an indexed local array
+              const float ws0 = h2f(dj);
+#pragma unroll
+              for (int c = 0; c < NC; c++) acc[c] = fmaf(__fmul_rn(ws0, sa[c]), (float)(int32_t)v[k][c], acc[c]);
+            } else if constexpr (T == T_Q4_K) {
+              // sa * (d sc * dot - dmin m * sum) (kquant.rs:257-282)
+              const uint8_t* hdr = sm + L::OFF_RAW + rl * F::RAW;
+              int sc, mn;
+              q4k_scale_min(j, hdr + 4, sc, mn);
+              const float d = h2f((unsigned short)(hdr[0] | (hdr[1] << 8)));
+              const float dmin = h2f((unsigned short)(hdr[2] | (hdr[3] << 8)));
+              const float dsc = __fmul_rn(d, (float)sc), dm = __fmul_rn(dmin, (float)mn);
+              const int32_t* sm_s = reinterpret_cast<const int32_t*>(sm + L::OFF_SUM) + j * NT + c0;
 #pragma unroll
               for (int c = 0; c < NC; c++) {
-                const int t = tok0 + c0 + c;
-                if (t < g.M) g.dots[((size_t)t * N + r) * (size_t)(n_blk * MPB) + (size_t)b * MPB + h] = (int32_t)v[c];
+                const float t = __fsub_rn(__fmul_rn(dsc, (float)(int32_t)v[k][c]), __fmul_rn(dm, (float)sm_s[c]));
+                acc[c] = fmaf(sa[c], t, acc[c]);
               }
-            continue;
-          }
-          const float* sa = sa_s + j * NT + c0;
-          if constexpr (T == T_Q8_0 || T == T_Q4_0) {
-            // (d * sa) * dot (matmul.rs:395-406, kquant.rs:240-252)
+            } else {
+              // (d * sa) * sc * dot per 16-value sub-block (kquant.rs:287-318)
+              const float d = h2f(dc[0]);
+              const int si = 2 * j + h;  // sub-block scale byte si of the 16
+              const unsigned word = si < 8 ? (si < 4 ? scc.x : scc.y) : (si < 12 ? scc.z : scc.w);
+              const float scf = (float)(int8_t)((word >> (8 * (si & 3))) & 0xffu);
 #pragma unroll
-            for (int c = 0; c < NC; c++) acc[c] = fmaf(__fmul_rn(ws0, sa[c]), (float)(int32_t)v[c], acc[c]);
-          } else if constexpr (T == T_Q4_K) {
-            // sa * (d sc * dot - dmin m * sum) (kquant.rs:257-282)
-            const int32_t* sm_s = reinterpret_cast<const int32_t*>(sm + L::OFF_SUM) + j * NT + c0;
-#pragma unroll
-            for (int c = 0; c < NC; c++) {
-              const float t = __fsub_rn(__fmul_rn(ws0, (float)(int32_t)v[c]), __fmul_rn(wmin, (float)sm_s[c]));
-              acc[c] = fmaf(sa[c], t, acc[c]);
+              for (int c = 0; c < NC; c++)
+                acc[c] = fmaf(__fmul_rn(__fmul_rn(d, sa[c]), scf), (float)(int32_t)v[k][c], acc[c]);
             }
-          } else {
-            // (d * sa) * sc * dot per 16-value sub-block (kquant.rs:287-318)
-            const float scf = h == 0 ? wmin : ws1;
-#pragma unroll
-            for (int c = 0; c < NC; c++)
-              acc[c] = fmaf(__fmul_rn(__fmul_rn(ws0, sa[c]), scf), (float)(int32_t)v[c], acc[c]);
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[gslot]);
       }
       // this warp is done with the stage's staged scales
       __syncwarp();
