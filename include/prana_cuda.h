@@ -76,6 +76,14 @@ int prana_debug_wait_timeout(prana_ctx *ctx, int which, unsigned polls);
  * (gguf.rs:208-267).  Q8_0/Q4_0 need cols % 32 == 0, Q4_K/Q6_K cols % 256 == 0. */
 int prana_weight_upload(prana_ctx *ctx, int ggml_type, size_t rows, size_t cols, const void *host_bytes,
                         prana_weight **out);
+/* quantize_q8 (matmul.rs:61-84), on the host: [rows, cols] f32 into int8 q
+ * [rows * cols] and one f32 scale per 32 values (amax / 127, round half away
+ * from zero, clamp to +-127).  No device is touched. */
+int prana_quantize_q8(size_t rows, size_t cols, const float *w, int8_t *q, float *scales);
+/* Linear::new(w, Precision::Q8) (checkpoint.rs): quantize_q8 of a host f32
+ * [rows, cols] matrix, resident in HBM (int8 plane and f32 scales); it takes
+ * prana_matmul_q8_f32 / prana_matmul_q8_prefill like a GGUF Q8_0 weight. */
+int prana_weight_upload_q8(prana_ctx *ctx, size_t rows, size_t cols, const float *w, prana_weight **out);
 int prana_weight_free(prana_weight *w);
 /* device bytes the packed matrix occupies */
 int prana_weight_bytes(const prana_weight *w, size_t *bytes);
@@ -167,8 +175,17 @@ typedef struct prana_model_config {
   int64_t weight_bytes; /* device bytes of all packed projection/embedding weights */
 } prana_model_config;
 
-/* gguf::load (gguf.rs:338-460) for llama / qwen2 into the device arena */
+/* gguf::load (gguf.rs:338-460) for llama / qwen2 into the device arena, at F32
+ * precision (the reference's default) */
 int prana_model_load_gguf(prana_ctx *ctx, const char *path, prana_model **out);
+/* gguf::load with an explicit Precision: PRANA_PRECISION_Q8 (`--q8`) turns
+ * every dense (F32 / F16) tensor the model multiplies -- projections and a tied
+ * classifier over an F32 / F16 / Q8_0 embedding table -- into quantize_q8 of it
+ * (gguf.rs:425-437, matmul.rs:61-84); PRANA_PRECISION_F32 keeps a tied dense
+ * table as the f32 classifier (matmul_f32) and rejects dense projections. */
+#define PRANA_PRECISION_F32 0
+#define PRANA_PRECISION_Q8 1
+int prana_model_load_gguf_ex(prana_ctx *ctx, const char *path, int precision, prana_model **out);
 /* Tensor parallelism over `world` GPUs, one process (or context) per rank
  * (the Megatron-style split of the survey: column-split Q/K/V by heads and
  * gate/up by FFN rows, row-split wo and ffn_down by input columns, vocabulary

@@ -333,7 +333,30 @@ static int load_linear(gguf *g, const char *name, or_matrix *m) {
   return or_matrix_from_gguf(m, (int)t->type, t->dims[1], t->dims[0], raw);
 }
 
+/* Linear::new(w, Precision::Q8) (checkpoint.rs): a dense matrix becomes
+ * quantize_q8 of it (matmul.rs:61-84), int8 plus f32 scales */
+static void requantize_q8(or_matrix *m) {
+  if (m->kind != OR_GGML_F32 || m->cols % 32) return;
+  size_t n = m->rows * m->cols;
+  int8_t *q = malloc(n);
+  float *sc = malloc(sizeof(float) * (n / 32));
+  or_quantize_q8(m->rows, m->cols, m->f32, q, sc);
+  free(m->f32);
+  m->f32 = NULL;
+  m->q = q;
+  m->scales = sc;
+  m->kind = OR_GGML_Q8_0;
+}
+
 or_model *or_model_load(const char *path, int tier, char *err, size_t errlen) {
+  return or_model_load_ex(path, tier, 0, err, errlen);
+}
+
+/* gguf::load(path, precision) (gguf.rs:338-460): precision 1 (Q8) turns every
+ * dense tensor the model multiplies -- projections, and a tied classifier over
+ * a densified (F32 / F16 / Q8_0) embedding table (gguf.rs:425-437) -- into
+ * quantize_q8 of it; precision 0 (F32) keeps them dense */
+or_model *or_model_load_ex(const char *path, int tier, int precision, char *err, size_t errlen) {
   FILE *f = fopen(path, "rb");
   if (!f) { snprintf(err, errlen, "cannot open %s", path); return NULL; }
   fseek(f, 0, SEEK_END);
@@ -422,7 +445,23 @@ or_model *or_model_load(const char *path, int tier, char *err, size_t errlen) {
     m->has_wcls = 1;
   } else {
     c->shared_classifier = 1;
+    if (precision == 1 && m->emb.kind == OR_GGML_F32 && c->dim % 32 == 0) {
+      m->wcls.kind = OR_GGML_F32;
+      m->wcls.rows = m->emb.rows;
+      m->wcls.cols = m->emb.cols;
+      m->wcls.f32 = malloc(sizeof(float) * m->emb.rows * m->emb.cols);
+      memcpy(m->wcls.f32, m->emb.f32, sizeof(float) * m->emb.rows * m->emb.cols);
+      requantize_q8(&m->wcls);
+      m->has_wcls = 1;
+    }
   }
+  if (precision == 1)
+    for (size_t i = 0; i < c->n_layers; i++) {
+      layer *L = &m->layers[i];
+      requantize_q8(&L->wq); requantize_q8(&L->wk); requantize_q8(&L->wv); requantize_q8(&L->wo);
+      requantize_q8(&L->w1); requantize_q8(&L->w2); requantize_q8(&L->w3);
+    }
+  if (precision == 1 && m->has_wcls) requantize_q8(&m->wcls);
   goto done;
 fail:
   or_model_free(m);

@@ -84,6 +84,7 @@ def lib() -> C.CDLL:
             "or_attention": ([P, P, P, SZ, SZ, SZ, SZ, P], None),
             "or_argmax": ([P, SZ], C.c_uint32),
             "or_model_load": ([C.c_char_p, C.c_int, C.c_char_p, SZ], P),
+            "or_model_load_ex": ([C.c_char_p, C.c_int, C.c_int, C.c_char_p, SZ], P),
             "or_model_free": ([P], None),
             "or_model_config": ([P, C.POINTER(Config)], None),
             "or_model_matrix": ([P, C.c_int, C.c_char_p], P),
@@ -171,6 +172,24 @@ class OMatrix:
             pass
 
 
+class OQ8Matrix(OMatrix):
+    """The reference's in-memory QuantMatrix built by quantize_q8 (int8 plus f32
+    scales, matmul.rs:21-30, 61-84), multiplied by the oracle's Q8 kernels."""
+
+    def __init__(self, rows: int, cols: int, w: np.ndarray):
+        w = np.ascontiguousarray(w, np.float32).reshape(-1)
+        self._q = np.empty(rows * cols, np.int8)
+        self._s = np.empty(rows * cols // 32, np.float32)
+        lib().or_quantize_q8(rows, cols, ptr(w), ptr(self._q), ptr(self._s))
+        self.m = Matrix()
+        self.m.kind, self.m.rows, self.m.cols = 8, rows, cols
+        self.m.q, self.m.scales = self._q.ctypes.data, self._s.ctypes.data
+        self.rows, self.cols = rows, cols
+
+    def __del__(self):  # the planes belong to numpy
+        pass
+
+
 def block_dots(ggml_type: int, aq: np.ndarray, row_bytes: np.ndarray, k: int) -> np.ndarray:
     n = k // 16 if ggml_type == 14 else k // 32
     out = np.zeros(n, np.int32)
@@ -179,9 +198,10 @@ def block_dots(ggml_type: int, aq: np.ndarray, row_bytes: np.ndarray, k: int) ->
 
 
 class OModel:
-    def __init__(self, path: str, tier: int = TIER_AUTO):
+    def __init__(self, path: str, tier: int = TIER_AUTO, precision: int = 0):
+        """gguf::load(path, precision): precision 0 = F32 (the default), 1 = Q8 (`--q8`)."""
         err = C.create_string_buffer(512)
-        self.h = lib().or_model_load(str(path).encode(), tier, err, 512)
+        self.h = lib().or_model_load_ex(str(path).encode(), tier, precision, err, 512)
         if not self.h:
             raise ValueError("oracle load failed: " + err.value.decode())
         self.c = Config()

@@ -148,6 +148,7 @@ typedef struct or_config {
 } or_config;
 
 or_model *or_model_load(const char *path, int tier, char *err, size_t errlen);
+or_model *or_model_load_ex(const char *path, int tier, int precision, char *err, size_t errlen);
 void or_model_free(or_model *m);
 void or_model_config(const or_model *m, or_config *c);
 const or_matrix *or_model_matrix(const or_model *m, int layer, const char *which);

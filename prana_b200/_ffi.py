@@ -55,6 +55,8 @@ SIGNATURES = {
     "prana_debug_wait_timeout": [P, I, C.c_uint],
     "prana_weight_upload": [P, I, SZ, SZ, P, C.POINTER(P)],
     "prana_weight_free": [P],
+    "prana_quantize_q8": [SZ, SZ, P, P, P],
+    "prana_weight_upload_q8": [P, SZ, SZ, P, C.POINTER(P)],
     "prana_weight_bytes": [P, C.POINTER(SZ)],
     "prana_quantize_acts": [P, P, SZ, SZ, P, P, P],
     "prana_matmul_q8_f32": [P, P, P, SZ, P],
@@ -78,6 +80,7 @@ SIGNATURES = {
     "prana_attention": [P, P, P, P, SZ, SZ, SZ, SZ, P],
     "prana_argmax": [P, P, SZ, SZ, P],
     "prana_model_load_gguf": [P, C.c_char_p, C.POINTER(P)],
+    "prana_model_load_gguf_ex": [P, C.c_char_p, I, C.POINTER(P)],
     "prana_model_load_gguf_tp": [P, C.c_char_p, I, I, P, C.POINTER(P)],
     "prana_tp_unique_id": [P],
     "prana_model_tp_get": [P, C.POINTER(I), C.POINTER(I), C.POINTER(I)],

@@ -9,8 +9,11 @@
 
 namespace prana {
 
-// ggml type ids (crates/prana-model/src/gguf.rs:33-38)
-enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
+// ggml type ids (crates/prana-model/src/gguf.rs:33-38), and one of this
+// library: T_Q8S, the reference's in-memory QuantMatrix (int8 plane and one f32
+// scale per 32 values, matmul.rs:21-30) that quantize_q8 (matmul.rs:61-84)
+// produces -- its scales are arbitrary f32, not f16 like GGUF Q8_0's
+enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14, T_Q8S = 108 };
 
 constexpr int WARP = 32;
 
@@ -20,6 +23,7 @@ constexpr int WARP = 32;
 //   Q4_K: qs = GGUF super-blocks verbatim    [rows][cols/256][144] (144 = 9 x 16 B, so every
 //         super-block is 16-byte aligned and needs no repacking)
 //   Q6_K: qs = ql plane [rows][cols/2], qh = [rows][cols/4], sc = int8 [rows][cols/16], d = f16 [rows][cols/256]
+//   Q8S : qs = int8 plane [rows][cols],      ds = f32 [rows][cols/32]
 //   F32 : f32 = [rows][cols]
 struct DevWeight {
   int type;
@@ -29,6 +33,7 @@ struct DevWeight {
   const int8_t* sc;
   const __half* d;
   const float* f32;
+  const float* ds;
 };
 
 // ---- loads ----

@@ -212,6 +212,56 @@ int upload_weight(prana_ctx* ctx, int type, size_t rows, size_t cols, const void
   return PRANA_OK;
 }
 
+// quantize_q8 (matmul.rs:61-84): per 32 values amax (f32::max fold from 0),
+// scale = amax / 127 (1 when amax is 0), q = round(x * (1 / scale)) clamped
+// to +-127, round half away from zero; NaN becomes 0 as Rust's `as i8` does.
+void quantize_q8_host(size_t rows, size_t cols, const float* w, int8_t* q, float* scales) {
+  const size_t groups = cols / 32;
+  for (size_t r = 0; r < rows; r++)
+    for (size_t g = 0; g < groups; g++) {
+      const float* blk = w + r * cols + g * 32;
+      float amax = 0.0f;
+      for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(blk[i]));
+      const float scale = amax > 0.0f ? amax / 127.0f : 1.0f;
+      const float inv = 1.0f / scale;
+      for (int i = 0; i < 32; i++) {
+        float v = roundf(blk[i] * inv);
+        v = fminf(fmaxf(v, -127.0f), 127.0f);
+        q[r * cols + g * 32 + i] = (v != v) ? 0 : (int8_t)v;
+      }
+      scales[r * groups + g] = scale;
+    }
+}
+
+int upload_q8s(prana_ctx* ctx, size_t rows, size_t cols, const float* host, prana_weight* w) {
+  if (!rows || !cols) return fail(PRANA_E_INVALID, "empty weight [%zu, %zu]", rows, cols);
+  if (cols % 32) return fail(PRANA_E_INVALID, "quantize_q8 needs cols %% 32 == 0 (cols=%zu)", cols);
+  if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX) return fail(PRANA_E_INVALID, "weight too large");
+  const size_t n = rows * cols, off = al256(n), total = off + al256(n / 32 * 4);
+  std::vector<uint8_t> buf(total);
+  quantize_q8_host(rows, cols, host, reinterpret_cast<int8_t*>(buf.data()), reinterpret_cast<float*>(buf.data() + off));
+  void* mem = nullptr;
+  if (cudaMalloc(&mem, total) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(PRANA_E_OOM, "device allocation of %zu bytes failed", total);
+  }
+  if (cudaMemcpy(mem, buf.data(), total, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(mem);
+    return fail(PRANA_E_CUDA, "weight upload failed");
+  }
+  DevWeight dw{};
+  dw.type = T_Q8S;
+  dw.rows = (int)rows;
+  dw.cols = (int)cols;
+  dw.qs = static_cast<uint8_t*>(mem);
+  dw.ds = reinterpret_cast<const float*>(static_cast<uint8_t*>(mem) + off);
+  w->ctx = ctx;
+  w->dw = dw;
+  w->mem = mem;
+  w->bytes = total;
+  return PRANA_OK;
+}
+
 void free_weight(prana_weight* w) {
   if (w && w->mem) {
     cudaFree(w->mem);
@@ -369,6 +419,31 @@ int prana_weight_upload(prana_ctx* c, int type, size_t rows, size_t cols, const 
   API_END
 }
 
+int prana_quantize_q8(size_t rows, size_t cols, const float* w, int8_t* q, float* scales) {
+  API_BEGIN
+  NEED(w && q && scales, "null argument");
+  NEED(cols % 32 == 0, "cols must be a multiple of 32 (cols=%zu)", cols);
+  quantize_q8_host(rows, cols, w, q, scales);
+  return PRANA_OK;
+  API_END
+}
+
+int prana_weight_upload_q8(prana_ctx* c, size_t rows, size_t cols, const float* host, prana_weight** out) {
+  API_BEGIN
+  NEED(c && host && out, "null argument");
+  *out = nullptr;
+  DevScope ds(c->device);
+  prana_weight* w = new prana_weight();
+  int rc = upload_q8s(c, rows, cols, host, w);
+  if (rc) {
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return PRANA_OK;
+  API_END
+}
+
 int prana_weight_free(prana_weight* w) {
   if (!w) return PRANA_OK;
   DevScope ds(w->ctx->device);
@@ -460,7 +535,7 @@ static int matmul_common(prana_ctx* c, const prana_weight* w, const float* a, co
 
 int prana_matmul_q8_f32(prana_ctx* c, const float* a, const prana_weight* w, size_t n_tokens, float* out) {
   NEED(c && a && w && out, "null argument");
-  NEED(w->dw.type == T_Q8_0, "matmul_q8_f32 needs a Q8_0 weight (type %d)", w->dw.type);
+  NEED(w->dw.type == T_Q8_0 || w->dw.type == T_Q8S, "matmul_q8_f32 needs a Q8 weight (type %d)", w->dw.type);
   return matmul_common(c, w, a, nullptr, nullptr, nullptr, n_tokens, out);
 }
 
@@ -474,7 +549,7 @@ int prana_matmul_kquant_f32(prana_ctx* c, const float* a, const prana_weight* w,
 int prana_matmul_q8_prefill(prana_ctx* c, const int8_t* q, const float* s, const int32_t* sum, size_t n_tokens,
                             const prana_weight* w, float* out) {
   NEED(c && q && s && sum && w && out, "null argument");
-  NEED(w->dw.type == T_Q8_0, "matmul_q8_prefill needs a Q8_0 weight");
+  NEED(w->dw.type == T_Q8_0 || w->dw.type == T_Q8S, "matmul_q8_prefill needs a Q8 weight");
   return matmul_common(c, w, nullptr, q, s, sum, n_tokens, out);
 }
 

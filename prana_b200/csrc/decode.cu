@@ -217,6 +217,9 @@ __device__ __forceinline__ void prefetch_group(const DevWeight& w, int r0, int u
   if constexpr (T == T_Q8_0) {
     if (p == 0) prefetch_span(w.qs, row * K + (size_t)u0 * 32, n * 32);
     if (p == 1) prefetch_span(w.d, row * (K / 16) + (size_t)u0 * 2, n * 2);
+  } else if constexpr (T == T_Q8S) {
+    if (p == 0) prefetch_span(w.qs, row * K + (size_t)u0 * 32, n * 32);
+    if (p == 1) prefetch_span(w.ds, row * (K / 8) + (size_t)u0 * 4, n * 4);
   } else if constexpr (T == T_Q4_0) {
     if (p == 0) prefetch_span(w.qs, row * (K / 2) + (size_t)u0 * 16, n * 16);
     if (p == 1) prefetch_span(w.d, row * (K / 16) + (size_t)u0 * 2, n * 2);
@@ -353,7 +356,7 @@ __global__ void __launch_bounds__(DG_THREADS, 2) stream_gemv(const StreamArgs g)
   bool first = true;
   // Batch 1 with whole rows per warp: a flat sequence of (row group, chunk)
   // items with the next item's weights in flight while the current one computes.
-  constexpr bool kPipe = M == 1 && (T == T_Q4_0 || T == T_Q8_0);
+  constexpr bool kPipe = M == 1 && (T == T_Q4_0 || T == T_Q8_0 || T == T_Q8S);
   if (kPipe && ks == 1) {
     Unit<T> nb[DG_RPW][CH];
     int c0 = u_lo, gcur = g_first;
@@ -645,6 +648,7 @@ template <int EPI, int PRO>
 static cudaError_t stream_t(const StreamArgs& g, cudaStream_t st, bool pdl) {
   switch (g.w.type) {
     case T_Q8_0: return stream_m<T_Q8_0, EPI, PRO>(g, st, pdl);
+    case T_Q8S: return stream_m<T_Q8S, EPI, PRO>(g, st, pdl);
     case T_Q4_0: return stream_m<T_Q4_0, EPI, PRO>(g, st, pdl);
     case T_Q4_K: return stream_m<T_Q4_K, EPI, PRO>(g, st, pdl);
     case T_Q6_K: return stream_m<T_Q6_K, EPI, PRO>(g, st, pdl);

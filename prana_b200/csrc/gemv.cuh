@@ -47,6 +47,10 @@ __device__ __forceinline__ void prefetch_rows(const DevWeight& w, int r0, int R)
       prefetch_span(w.qs, r0 * K, R * K);
       prefetch_span(w.d, r0 * K / 16, R * K / 16);
       break;
+    case T_Q8S:
+      prefetch_span(w.qs, r0 * K, R * K);
+      prefetch_span(w.ds, r0 * K / 8, R * K / 8);
+      break;
     case T_Q4_0:
       prefetch_span(w.qs, r0 * K / 2, R * K / 2);
       prefetch_span(w.d, r0 * K / 16, R * K / 16);
@@ -65,6 +69,7 @@ __device__ __forceinline__ void prefetch_rows(const DevWeight& w, int r0, int R)
 
 template <int T> struct Unit;
 template <> struct Unit<T_Q8_0> { uint4 a, b; unsigned short d; };
+template <> struct Unit<T_Q8S> { uint4 a, b; float d; };
 template <> struct Unit<T_Q4_0> { uint4 q; unsigned short d; };
 template <> struct Unit<T_Q4_K> { uint4 a, b, meta; };
 template <> struct Unit<T_Q6_K> { uint4 lo, hi, qh; uint2 sc; unsigned short d; };
@@ -77,6 +82,14 @@ template <> __device__ __forceinline__ Unit<T_Q8_0> load_unit<T_Q8_0>(const DevW
   x.a = ld_stream16(p);
   x.b = ld_stream16(p + 16);
   x.d = ld_stream_u16(w.d + (size_t)row * (w.cols / 32) + u);
+  return x;
+}
+template <> __device__ __forceinline__ Unit<T_Q8S> load_unit<T_Q8S>(const DevWeight& w, int row, int u) {
+  Unit<T_Q8S> x;
+  const uint8_t* p = w.qs + (size_t)row * w.cols + (size_t)u * 32;
+  x.a = ld_stream16(p);
+  x.b = ld_stream16(p + 16);
+  x.d = __ldg(w.ds + (size_t)row * (w.cols / 32) + u);
   return x;
 }
 template <> __device__ __forceinline__ Unit<T_Q4_0> load_unit<T_Q4_0>(const DevWeight& w, int row, int u) {
@@ -108,7 +121,8 @@ template <> __device__ __forceinline__ Unit<T_Q6_K> load_unit<T_Q6_K>(const DevW
 __device__ __forceinline__ int dp4(unsigned a, int b, int c) { return __dp4a((int)a, b, c); }
 
 // ---- per-unit integer dots (exact) ----
-__device__ __forceinline__ int idot_q8(const Unit<T_Q8_0>& x, const int8_t* a) {
+template <class U>
+__device__ __forceinline__ int idot_q8(const U& x, const int8_t* a) {
   const int4 a0 = *reinterpret_cast<const int4*>(a), a1 = *reinterpret_cast<const int4*>(a + 16);
   int s = dp4(x.a.x, a0.x, 0);
   s = dp4(x.a.y, a0.y, s); s = dp4(x.a.z, a0.z, s); s = dp4(x.a.w, a0.w, s);
@@ -193,6 +207,15 @@ __device__ __forceinline__ void accum_unit(const Unit<T_Q8_0>& x, int u, const A
     }
 }
 template <int M>
+__device__ __forceinline__ void accum_unit(const Unit<T_Q8S>& x, int u, const Acts& a, int m_rt, float (&acc)[M]) {
+#pragma unroll
+  for (int m = 0; m < M; m++)
+    if (m < m_rt) {
+      const int s = idot_q8(x, a.q + m * a.K + u * 32);
+      acc[m] = fmaf(__fmul_rn(x.d, a.s[m * a.G + u]), (float)s, acc[m]);
+    }
+}
+template <int M>
 __device__ __forceinline__ void accum_unit(const Unit<T_Q4_0>& x, int u, const Acts& a, int m_rt, float (&acc)[M]) {
   const float d = h2f(x.d);
 #pragma unroll
@@ -251,6 +274,7 @@ __device__ __forceinline__ void accum_unit(const Unit<T_Q6_K>& x, int u, const A
 // a single activation row, operation for operation.
 template <int T> struct ActU;
 template <> struct ActU<T_Q8_0> { int4 a0, a1; float s; };
+template <> struct ActU<T_Q8S> { int4 a0, a1; float s; };
 template <> struct ActU<T_Q4_0> { int4 a0, a1; float s; int sum8; };
 template <> struct ActU<T_Q4_K> { int4 l0, l1, h0, h1; float s1, s2; int sum1, sum2; };
 template <> struct ActU<T_Q6_K> { int4 a[4]; float s[4]; };
@@ -258,6 +282,13 @@ template <> struct ActU<T_Q6_K> { int4 a[4]; float s[4]; };
 template <int T> __device__ __forceinline__ ActU<T> load_act(const Acts& a, int u);
 template <> __device__ __forceinline__ ActU<T_Q8_0> load_act<T_Q8_0>(const Acts& a, int u) {
   ActU<T_Q8_0> r;
+  r.a0 = *reinterpret_cast<const int4*>(a.q + u * 32);
+  r.a1 = *reinterpret_cast<const int4*>(a.q + u * 32 + 16);
+  r.s = a.s[u];
+  return r;
+}
+template <> __device__ __forceinline__ ActU<T_Q8S> load_act<T_Q8S>(const Acts& a, int u) {
+  ActU<T_Q8S> r;
   r.a0 = *reinterpret_cast<const int4*>(a.q + u * 32);
   r.a1 = *reinterpret_cast<const int4*>(a.q + u * 32 + 16);
   r.s = a.s[u];
@@ -302,6 +333,12 @@ __device__ __forceinline__ void accum_r(const Unit<T_Q8_0>& x, const ActU<T_Q8_0
   s = dp4(x.a.y, a.a0.y, s); s = dp4(x.a.z, a.a0.z, s); s = dp4(x.a.w, a.a0.w, s);
   s = dp4(x.b.x, a.a1.x, s); s = dp4(x.b.y, a.a1.y, s); s = dp4(x.b.z, a.a1.z, s); s = dp4(x.b.w, a.a1.w, s);
   acc = fmaf(__fmul_rn(h2f(x.d), a.s), (float)s, acc);
+}
+__device__ __forceinline__ void accum_r(const Unit<T_Q8S>& x, const ActU<T_Q8S>& a, int, float& acc) {
+  int s = dp4(x.a.x, a.a0.x, 0);
+  s = dp4(x.a.y, a.a0.y, s); s = dp4(x.a.z, a.a0.z, s); s = dp4(x.a.w, a.a0.w, s);
+  s = dp4(x.b.x, a.a1.x, s); s = dp4(x.b.y, a.a1.y, s); s = dp4(x.b.z, a.a1.z, s); s = dp4(x.b.w, a.a1.w, s);
+  acc = fmaf(__fmul_rn(x.d, a.s), (float)s, acc);
 }
 __device__ __forceinline__ void accum_r(const Unit<T_Q4_0>& x, const ActU<T_Q4_0>& a, int, float& acc) {
   const unsigned m = 0x0F0F0F0Fu;
@@ -443,7 +480,7 @@ __device__ __forceinline__ float embed_value(const DevWeight& w, uint32_t tok, i
 template <int T>
 __device__ __forceinline__ void unit_block_dots(const DevWeight& w, int row, int u, const Acts& a, int32_t* out) {
   Unit<T> x = load_unit<T>(w, row, u);
-  if constexpr (T == T_Q8_0) {
+  if constexpr (T == T_Q8_0 || T == T_Q8S) {
     out[u] = idot_q8(x, a.q + u * 32);
   } else if constexpr (T == T_Q4_0) {
     out[u] = idot_q4_0(x, a.q + u * 32) - 8 * a.sum[u];

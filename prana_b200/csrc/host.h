@@ -64,6 +64,9 @@ int ctx_scratch(prana_ctx* ctx, size_t bytes, void** out);
 int ctx_rope(prana_ctx* ctx, int head_dim, float theta, int neox, int positions, const RopeTable** out);
 // Repack GGUF bytes of a [rows, cols] tensor into device layout.
 int upload_weight(prana_ctx* ctx, int type, size_t rows, size_t cols, const void* host, prana_weight* w);
+// quantize_q8 (matmul.rs:61-84) on the host, then upload as T_Q8S
+void quantize_q8_host(size_t rows, size_t cols, const float* w, int8_t* q, float* scales);
+int upload_q8s(prana_ctx* ctx, size_t rows, size_t cols, const float* host, prana_weight* w);
 void free_weight(prana_weight* w);
 // Read and clear the error word of prana_attention_decode_noalloc on `device`.
 int noalloc_take_error(int device, unsigned* out);

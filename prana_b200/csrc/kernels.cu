@@ -343,6 +343,7 @@ cudaError_t launch_block_dots(const DevWeight& w, int row, const int8_t* aq, con
   const int grid = ceil_div(nu, 128);
   switch (w.type) {
     case T_Q8_0: block_dots_kernel<T_Q8_0><<<grid, 128, 0, st>>>(w, row, aq, asum, out); break;
+    case T_Q8S: block_dots_kernel<T_Q8S><<<grid, 128, 0, st>>>(w, row, aq, asum, out); break;
     case T_Q4_0: block_dots_kernel<T_Q4_0><<<grid, 128, 0, st>>>(w, row, aq, asum, out); break;
     case T_Q4_K: block_dots_kernel<T_Q4_K><<<grid, 128, 0, st>>>(w, row, aq, asum, out); break;
     case T_Q6_K: block_dots_kernel<T_Q6_K><<<grid, 128, 0, st>>>(w, row, aq, asum, out); break;

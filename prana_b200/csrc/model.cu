@@ -207,6 +207,9 @@ struct Bufs {
   float* logits_l = nullptr;  // tensor parallel: this rank's vocabulary slice
   uint32_t* toks = nullptr;     // input ids [rows]
   uint32_t* tok_out = nullptr;  // argmax per row [rows]
+  // dense f32 classifier: the final-norm rows and (for a trace) their group sums
+  float* xn = nullptr;
+  int32_t* xsum = nullptr;
   // batch path (rows > 8): quantized rows, GEMM outputs, GEMM scratch
   int8_t* bq = nullptr;
   float* bs = nullptr;
@@ -251,6 +254,7 @@ struct prana_model {
   int* h_io = nullptr;        // pinned mirror
   uint32_t* h_tok = nullptr;
   bool pdl = true;
+  int precision = 0;  // PRANA_PRECISION_F32 / _Q8 (gguf::load's precision, gguf.rs:338-460)
   std::vector<prana_kv*> caches;  // live KV caches (freed with the model)
   // tensor parallelism: this rank's share of heads, FFN rows and vocabulary
   // (the whole model when tp_world == 1)
@@ -299,7 +303,8 @@ int dev_vec(prana_model* m, const std::vector<float>& h, float** out) {
 
 // The linear loading rule of gguf.rs:271-305: Q8_0 (cols%32), Q4_0 (cols%32),
 // Q4_K/Q6_K (cols%256) stay quantized.  Dense projections are not built.
-int linear_raw(const Gguf& g, const std::string& name, size_t rows, size_t cols, uint32_t* type, const uint8_t** raw) {
+int linear_raw(const Gguf& g, const std::string& name, size_t rows, size_t cols, uint32_t* type, const uint8_t** raw,
+               int precision) {
   const GgufTensor* t;
   int rc = tensor_raw(g, name, &t, raw);
   if (rc) return rc;
@@ -308,10 +313,15 @@ int linear_raw(const Gguf& g, const std::string& name, size_t rows, size_t cols,
     return fail(PRANA_E_FORMAT, "tensor '%s' is [%llu, %llu], expected [%zu, %zu]", name.c_str(),
                 (unsigned long long)t->dims[1], (unsigned long long)t->dims[0], rows, cols);
   const uint32_t ty = t->type;
-  const bool ok = (ty == T_Q8_0 && cols % 32 == 0) || (ty == T_Q4_0 && cols % 32 == 0) ||
-                  ((ty == T_Q4_K || ty == T_Q6_K) && cols % 256 == 0);
-  if (!ok)
-    return fail(PRANA_E_UNSUPPORTED, "tensor '%s': type %u with %zu cols would run the dense f32 matmul, not built",
+  const bool packed = (ty == T_Q8_0 && cols % 32 == 0) || (ty == T_Q4_0 && cols % 32 == 0) ||
+                      ((ty == T_Q4_K || ty == T_Q6_K) && cols % 256 == 0);
+  // dense tensors (F32, F16) become Linear::new(w, precision): quantize_q8 under
+  // Q8 precision (matmul.rs:61-84); the dense f32 matmul for projections is not built
+  const bool dense_q8 = (ty == T_F32 || ty == T_F16) && precision == PRANA_PRECISION_Q8 && cols % 32 == 0;
+  if (!packed && !dense_q8)
+    return fail(PRANA_E_UNSUPPORTED,
+                "tensor '%s': type %u with %zu cols would run the dense f32 matmul for a projection, not built "
+                "(load with Q8 precision to quantize it)",
                 name.c_str(), ty, cols);
   *type = ty;
   return PRANA_OK;
@@ -331,7 +341,35 @@ int slice_cols(uint32_t type, size_t rows, size_t cols, const uint8_t* raw, size
   return PRANA_OK;
 }
 
+// f32 values of `rows` rows of a dense (F32 / F16) or Q8_0 GGUF tensor, as the
+// reference's tensor_f32 densifies them (gguf.rs:208-267)
+std::vector<float> densify(uint32_t type, size_t rows, size_t cols, const uint8_t* raw) {
+  std::vector<float> out(rows * cols);
+  const size_t n = rows * cols;
+  if (type == T_F32) {
+    memcpy(out.data(), raw, n * 4);
+  } else if (type == T_F16) {
+    for (size_t i = 0; i < n; i++) {
+      uint16_t h;
+      memcpy(&h, raw + 2 * i, 2);
+      out[i] = f16_host(h);
+    }
+  } else {  // Q8_0: q * d in f32
+    for (size_t b = 0; b < n / 32; b++) {
+      uint16_t h;
+      memcpy(&h, raw + b * 34, 2);
+      const float d = f16_host(h);
+      for (int i = 0; i < 32; i++) out[b * 32 + i] = (float)(int8_t)raw[b * 34 + 2 + i] * d;
+    }
+  }
+  return out;
+}
+
 int upload_stream(prana_model* m, uint32_t type, size_t rows, size_t cols, const uint8_t* bytes, StreamW* sw) {
+  if (type == T_F32 || type == T_F16) {  // Q8 precision: quantize_q8 of the dense rows
+    const std::vector<float> f = densify(type, rows, cols, bytes);
+    return upload_q8s(m->ctx, rows, cols, f.data(), &sw->w);
+  }
   return upload_weight(m->ctx, (int)type, rows, cols, bytes, &sw->w);
 }
 
@@ -379,6 +417,10 @@ int make_bufs(prana_model* m, size_t rows, bool window, Bufs& b) {
   rc |= b.alloc(b.u, rows * hid);
   rc |= b.alloc(b.toks, rows);
   rc |= b.alloc(b.tok_out, rows);
+  if (m->head.w.dw.type == T_F32) {
+    rc |= b.alloc(b.xn, rows * dim);
+    rc |= b.alloc(b.xsum, rows * dim / 32);
+  }
   if (rows > 8 && m->tp_world == 1) {
     const size_t max_k = std::max(std::max(dim, q_dim), hid);
     const size_t max_n = std::max(q_dim + 2 * kv_dim, 2 * hid);
@@ -713,6 +755,26 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
   }
   if (!head) return PRANA_OK;
   // --- final rmsnorm -> LM head -> argmax (Model::logits, checkpoint.rs:239-248; infer.rs:560-568)
+  if (m->head.w.dw.type == T_F32) {  // dense f32 tied classifier: matmul_f32 over the table
+    PRANA_CK(launch_rmsnorm(b.x, m->rms_final, n, dim, c.norm_eps, b.xn, st));
+    if (tr) {  // the site's rows as the CPU path quantizes them for its own record
+      PRANA_CK(launch_quantize_acts(b.xn, n, dim, tr->q + tr->nq, tr->s + tr->ns, b.xsum, st));
+      tr->nq += (size_t)n * dim;
+      tr->ns += (size_t)n * dim / 32;
+    }
+    for (int c0 = 0; c0 < n; c0 += 8) {
+      GemvArgs gv{};
+      gv.w = m->head.w.dw;
+      gv.m = std::min(8, n - c0);
+      gv.x = b.xn + (size_t)c0 * dim;
+      gv.out = b.logits + (size_t)c0 * c.vocab_size;
+      PRANA_CK(launch_gemv(gv, PRO_F32, EPI_STORE, st, false));
+    }
+    PRANA_CK(launch_argmax(b.logits, n, (int)c.vocab_size, b.tok_out, st));
+    if (n == 1 && tok_dev)
+      PRANA_CK(cudaMemcpyAsync(const_cast<int*>(tok_dev), b.tok_out, 4, cudaMemcpyDeviceToDevice, st));
+    return PRANA_OK;
+  }
   if (batch) {  // logits_batch (checkpoint.rs:256-265): the head streams once for all rows
     if ((rc = quantize_rows(m, b, b.x, m->rms_final, n, dim, tr)) ||
         (rc = run_qgemm(m, b, m->head, n, b.logits, 0)))
@@ -848,9 +910,11 @@ extern "C" {
 // rank's query / kv heads, FFN rows and vocabulary rows; wo and ffn_down keep
 // this rank's input columns.  nccl_id (NCCL_UNIQUE_ID_BYTES) names the
 // communicator every rank joins.
-static int load_model(prana_ctx* ctx, const char* path, int world, int rank, const void* nccl_id, prana_model** out) {
+static int load_model(prana_ctx* ctx, const char* path, int world, int rank, const void* nccl_id, int precision,
+                      prana_model** out) {
   API_BEGIN
   NEED(ctx && path && out, "null argument");
+  NEED(precision == PRANA_PRECISION_F32 || precision == PRANA_PRECISION_Q8, "unknown precision %d", precision);
   NEED(world >= 1 && rank >= 0 && rank < world && (world == 1 || nccl_id), "bad tensor-parallel rank %d of %d", rank,
        world);
   *out = nullptr;
@@ -893,6 +957,7 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
   };
   std::unique_ptr<prana_model, void (*)(prana_model*)> m(new prana_model(), free_model);
   m->ctx = ctx;
+  m->precision = precision;
   auto& c = m->cfg;
   if (!meta_int("embedding_length", &c.dim)) return fail(PRANA_E_FORMAT, "missing metadata '%s.embedding_length'", arch.c_str());
   if (!meta_int("block_count", &c.n_layers)) return fail(PRANA_E_FORMAT, "missing metadata '%s.block_count'", arch.c_str());
@@ -953,7 +1018,7 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
     uint32_t types[3];
     const uint8_t* raws[3];
     for (int s = 0; s < 3; s++) {
-      if ((rc = linear_raw(g, p + names[s], full_rows[s], dim, &types[s], &raws[s]))) return rc;
+      if ((rc = linear_raw(g, p + names[s], full_rows[s], dim, &types[s], &raws[s], precision))) return rc;
       raws[s] += (size_t)rank * seg_rows[s] * gguf_row_bytes(types[s], dim);
     }
     for (int s0 = 0; s0 < 3;) {
@@ -988,15 +1053,15 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
     uint32_t ty;
     const uint8_t* raw;
     std::vector<uint8_t> cols;
-    if ((rc = linear_raw(g, p + "attn_output.weight", dim, q_dim, &ty, &raw)) ||
+    if ((rc = linear_raw(g, p + "attn_output.weight", dim, q_dim, &ty, &raw, precision)) ||
         (rc = slice_cols(ty, dim, q_dim, raw, rank * q_dim_l, (rank + 1) * q_dim_l, cols)) ||
         (rc = upload_stream(m.get(), ty, dim, q_dim_l, cols.data(), &L.wo)))
       return rc;
     // gate|up: interleave rows (gate j, up j) when both have one type
     uint32_t t1, t3;
     const uint8_t *r1, *r3;
-    if ((rc = linear_raw(g, p + "ffn_gate.weight", hid, dim, &t1, &r1)) ||
-        (rc = linear_raw(g, p + "ffn_up.weight", hid, dim, &t3, &r3)))
+    if ((rc = linear_raw(g, p + "ffn_gate.weight", hid, dim, &t1, &r1, precision)) ||
+        (rc = linear_raw(g, p + "ffn_up.weight", hid, dim, &t3, &r3, precision)))
       return rc;
     r1 += (size_t)rank * hid_l * gguf_row_bytes(t1, dim);  // this rank's FFN rows
     r3 += (size_t)rank * hid_l * gguf_row_bytes(t3, dim);
@@ -1014,7 +1079,7 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
           (rc = upload_stream(m.get(), t3, hid_l, dim, r3, &L.w3)))
         return rc;
     }
-    if ((rc = linear_raw(g, p + "ffn_down.weight", dim, hid, &ty, &raw)) ||
+    if ((rc = linear_raw(g, p + "ffn_down.weight", dim, hid, &ty, &raw, precision)) ||
         (rc = slice_cols(ty, dim, hid, raw, rank * hid_l, (rank + 1) * hid_l, cols)) ||
         (rc = upload_stream(m.get(), ty, dim, hid_l, cols.data(), &L.w2)))
       return rc;
@@ -1037,24 +1102,36 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
   if (g.tensors.count("output.weight")) {
     uint32_t ty;
     const uint8_t* raw;
-    if ((rc = linear_raw(g, "output.weight", (size_t)c.vocab_size, dim, &ty, &raw))) return rc;
+    if ((rc = linear_raw(g, "output.weight", (size_t)c.vocab_size, dim, &ty, &raw, precision))) return rc;
     raw += (size_t)m->vocab_off * gguf_row_bytes(ty, dim);  // this rank's vocabulary rows
     if ((rc = upload_stream(m.get(), ty, (size_t)m->vocab_l, dim, raw, &m->head))) return rc;
   } else {
-    // tied classifier over a packed table runs the quantized kernel (checkpoint.rs:246)
+    // tied classifier (gguf.rs:425-437, checkpoint.rs:239-248): a packed table
+    // (Q4_0 / Q4_K / Q6_K) runs the quantized kernel over the table itself; a
+    // table the reference densifies (F32, F16, Q8_0) becomes quantize_q8 of it
+    // under Q8 precision, else the dense f32 head (matmul_f32)
     c.shared_classifier = 1;
     const int et = m->emb.dw.type;
-    if (et != T_Q4_0 && et != T_Q4_K && et != T_Q6_K)
-      return fail(PRANA_E_UNSUPPORTED, "tied classifier over a dense table is not built");
-    if (world == 1) {
-      m->head.w = m->emb;
-      m->head.owns = false;
+    const GgufTensor* t;
+    const uint8_t* raw;
+    if ((rc = tensor_raw(g, "token_embd.weight", &t, &raw))) return rc;
+    raw += (size_t)m->vocab_off * gguf_row_bytes(t->type, dim);
+    if (et == T_Q4_0 || et == T_Q4_K || et == T_Q6_K) {
+      if (world == 1) {
+        m->head.w = m->emb;
+        m->head.owns = false;
+      } else if ((rc = upload_stream(m.get(), t->type, (size_t)m->vocab_l, dim, raw, &m->head))) {
+        return rc;
+      }
     } else {
-      const GgufTensor* t;
-      const uint8_t* raw;
-      if ((rc = tensor_raw(g, "token_embd.weight", &t, &raw))) return rc;
-      raw += (size_t)m->vocab_off * gguf_row_bytes(t->type, dim);
-      if ((rc = upload_stream(m.get(), t->type, (size_t)m->vocab_l, dim, raw, &m->head))) return rc;
+      const std::vector<float> f = densify(t->type, (size_t)m->vocab_l, dim, raw);
+      if (precision == PRANA_PRECISION_Q8 && dim % 32 == 0) {
+        if ((rc = upload_q8s(ctx, (size_t)m->vocab_l, dim, f.data(), &m->head.w))) return rc;
+      } else {
+        NEED(world == 1, "the dense f32 tied classifier runs on a single-GPU model");
+        NEED(dim * 8 * 4 <= 200 * 1024, "dense f32 classifier: dim %zu too wide for the f32 GEMV", dim);
+        if ((rc = upload_weight(ctx, T_F32, (size_t)m->vocab_l, dim, f.data(), &m->head.w))) return rc;
+      }
     }
   }
   // weight bytes on the device
@@ -1109,12 +1186,16 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
 }
 
 int prana_model_load_gguf(prana_ctx* ctx, const char* path, prana_model** out) {
-  return load_model(ctx, path, 1, 0, nullptr, out);
+  return load_model(ctx, path, 1, 0, nullptr, PRANA_PRECISION_F32, out);
+}
+
+int prana_model_load_gguf_ex(prana_ctx* ctx, const char* path, int precision, prana_model** out) {
+  return load_model(ctx, path, 1, 0, nullptr, precision, out);
 }
 
 int prana_model_load_gguf_tp(prana_ctx* ctx, const char* path, int world, int rank, const void* nccl_id,
                              prana_model** out) {
-  return load_model(ctx, path, world, rank, nccl_id, out);
+  return load_model(ctx, path, world, rank, nccl_id, PRANA_PRECISION_F32, out);
 }
 
 int prana_tp_unique_id(void* out) {

@@ -65,6 +65,7 @@ template <int T> struct QgFmt;
 // (2 for Q6_K: lower and upper sub-block halves).  Q6_K's raw row is its ql
 // bytes (128) then its qh bytes (64), staged as two regions.
 template <> struct QgFmt<T_Q8_0> { static constexpr int BK = 256, RAW = 0, A_TILES = 1; };
+template <> struct QgFmt<T_Q8S> { static constexpr int BK = 256, RAW = 0, A_TILES = 1; };
 template <> struct QgFmt<T_Q4_0> { static constexpr int BK = 256, RAW = 128, A_TILES = 1; };
 template <> struct QgFmt<T_Q4_K> { static constexpr int BK = 256, RAW = 144, A_TILES = 1; };
 template <> struct QgFmt<T_Q6_K> { static constexpr int BK = 256, RAW = 192, A_TILES = 2; };
@@ -399,6 +400,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     // of each block; Q6_K the super-block's d and its 16 int8 sub-block scales
     // (Q4_K's live in the staged super-block header)
     unsigned short dn[BLK], dc[BLK];
+    float dnf[BLK], dcf[BLK];  // Q8S: f32 scales
     uint4 scn = make_uint4(0u, 0u, 0u, 0u), scc = scn;
     auto load_scales = [&](int s) {  // s: global stage
       if (s >= s_lo + n_stage) return;
@@ -408,6 +410,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
 #pragma unroll
         for (int j = 0; j < BLK; j++)
           if (j < nb) dn[j] = __ldg(d + j);
+      } else if constexpr (T == T_Q8S) {
+        const float* d = g.w.ds + (size_t)rr * n_blk + s * BLK;
+        const int nb = min(BLK, n_blk - s * BLK);
+#pragma unroll
+        for (int j = 0; j < BLK; j++)
+          if (j < nb) dnf[j] = __ldg(d + j);
       } else if constexpr (T == T_Q6_K) {
         dn[0] = __ldg(reinterpret_cast<const unsigned short*>(g.w.d) + (size_t)rr * (K / 256) + s);
         scn = __ldg(reinterpret_cast<const uint4*>(g.w.sc + (size_t)rr * (K / 16)) + s);
@@ -421,7 +429,10 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       const int st = s % NS, sg = s_lo + s;
       const uint8_t* sm = stage(st);
 #pragma unroll
-      for (int j = 0; j < BLK; j++) dc[j] = dn[j];
+      for (int j = 0; j < BLK; j++) {
+        dc[j] = dn[j];
+        dcf[j] = dnf[j];
+      }
       scc = scn;
       load_scales(sg + 1);
       if (!qwait(&full[st], (s / NS) & 1, abort)) {
@@ -465,13 +476,21 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
               continue;
             }
             const float* sa = sa_s + j * NT + c0;
-            if constexpr (T == T_Q8_0 || T == T_Q4_0) {
+            if constexpr (T == T_Q8_0 || T == T_Q4_0 || T == T_Q8S) {
               // (d * sa) * dot (matmul.rs:395-406, kquant.rs:240-252)
-              unsigned short dj = dc[0];
+              float ws0;
+              if constexpr (T == T_Q8S) {
+                ws0 = dcf[0];
 #pragma unroll
-              for (int q = 1; q < BLK; q++)
-                if (q == j) dj = dc[q];  // a register select, not an indexed local array
-              const float ws0 = h2f(dj);
+                for (int q = 1; q < BLK; q++)
+                  if (q == j) ws0 = dcf[q];  // a register select, not an indexed local array
+              } else {
+                unsigned short dj = dc[0];
+#pragma unroll
+                for (int q = 1; q < BLK; q++)
+                  if (q == j) dj = dc[q];
+                ws0 = h2f(dj);
+              }
 #pragma unroll
               for (int c = 0; c < NC; c++) acc[c] = fmaf(__fmul_rn(ws0, sa[c]), (float)(int32_t)v[k][c], acc[c]);
             } else if constexpr (T == T_Q4_K) {
@@ -608,7 +627,7 @@ cudaError_t qgemm_go(const QgemmArgs& g, const int8_t* q, const float* sa_t, con
   if (T == T_Q4_K)
     ok = ok && map2d(&tm_sum, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, sum_t, (uint64_t)g.m_pad, G, (uint64_t)g.m_pad * 4, NT,
                      L::BLK, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if constexpr (T == T_Q8_0) {
+  if constexpr (T == T_Q8_0 || T == T_Q8S) {
     ok = ok && map2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, K, N, K, 128, QG_BM, CU_TENSOR_MAP_SWIZZLE_128B);
   } else if constexpr (T == T_Q4_0) {
     ok = ok && map2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, K / 2, N, K / 2, 128, QG_BM,
@@ -698,6 +717,7 @@ cudaError_t launch_qgemm(QgemmArgs g, const int8_t* q, const float* s, const int
   if (e != cudaSuccess) return e;
   switch (g.w.type) {
     case T_Q8_0: return qgemm_t<T_Q8_0>(g, q, sa_t, sum_t, st);
+    case T_Q8S: return qgemm_t<T_Q8S>(g, q, sa_t, sum_t, st);
     case T_Q4_0: return qgemm_t<T_Q4_0>(g, q, sa_t, sum_t, st);
     case T_Q4_K: return qgemm_t<T_Q4_K>(g, q, sa_t, sum_t, st);
     case T_Q6_K: return qgemm_t<T_Q6_K>(g, q, sa_t, sum_t, st);

@@ -40,6 +40,16 @@ def context(device: int | None = None) -> C.c_void_p:
     return ctx
 
 
+def quantize_q8(rows: int, cols: int, w) -> tuple[np.ndarray, np.ndarray]:
+    """quantize_q8 (matmul.rs:61-84) on the host: (int8 [rows, cols], f32 scales [rows, cols / 32])."""
+    w = np.ascontiguousarray(w, dtype=np.float32).reshape(rows, cols)
+    q = np.empty((rows, cols), np.int8)
+    s = np.empty((rows, cols // 32), np.float32)
+    call("prana_quantize_q8", rows, cols, w.ctypes.data_as(C.c_void_p), q.ctypes.data_as(C.c_void_p),
+         s.ctypes.data_as(C.c_void_p))
+    return q, s
+
+
 def synchronize(device: int | None = None) -> None:
     """Wait for this device's kernel-level calls; raises PranaError
     (PRANA_E_TIMEOUT) when a bounded device wait gave up in one of them."""
@@ -87,6 +97,19 @@ class QuantMatrix:
         self._h = C.c_void_p()
         call("prana_weight_upload", context(self.device), ggml_type, rows, cols, buf.ctypes.data_as(C.c_void_p), C.byref(self._h))
 
+    @classmethod
+    def quantize_q8(cls, rows: int, cols: int, w, device: int | None = None) -> "QuantMatrix":
+        """Linear::new(w, Precision::Q8): quantize_q8 (matmul.rs:61-84) of a dense
+        f32 [rows, cols] matrix, resident in HBM as int8 with f32 scales."""
+        self = cls.__new__(cls)
+        self.ggml_type, self.rows, self.cols = TYPE_Q8_0, rows, cols
+        self.device = torch.cuda.current_device() if device is None else device
+        self._h = C.c_void_p()
+        f = np.ascontiguousarray(w, dtype=np.float32).reshape(rows, cols)
+        call("prana_weight_upload_q8", context(self.device), rows, cols, f.ctypes.data_as(C.c_void_p),
+             C.byref(self._h))
+        return self
+
     @property
     def handle(self) -> C.c_void_p:
         return self._h
@@ -97,13 +120,13 @@ class QuantMatrix:
         return n.value
 
     def __del__(self):
-        h = getattr(self, "_h", None)
-        if h is not None and h.value:
-            try:
+        try:
+            h = getattr(self, "_h", None)
+            if h is not None and h.value:
                 _ffi.lib().prana_weight_free(h)
-            except Exception:
-                pass
-            self._h = C.c_void_p()
+                self._h = None
+        except Exception:  # interpreter shutdown: the library may already be gone
+            pass
 
 
 KQuantMatrix = QuantMatrix

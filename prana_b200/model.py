@@ -56,6 +56,9 @@ def tp_unique_id() -> bytes:
     return buf.raw
 
 
+PRECISION_F32, PRECISION_Q8 = 0, 1
+
+
 class Model:
     def __init__(self, handle: C.c_void_p, device: int):
         self._h = handle
@@ -72,12 +75,18 @@ class Model:
         self.peer_exchange = bool(peer.value)
 
     @classmethod
-    def load(cls, path: str, device: int = 0, tp: "tuple[int, int, bytes] | None" = None) -> "Model":
-        """Load a GGUF model; tp = (world, rank, unique_id) loads this rank's
-        tensor-parallel shard (every rank then calls the same model methods in
-        the same order)."""
+    def load(cls, path: str, device: int = 0, tp: "tuple[int, int, bytes] | None" = None,
+             precision: int = PRECISION_F32) -> "Model":
+        """Load a GGUF model (gguf::load, gguf.rs:338-460); tp = (world, rank,
+        unique_id) loads this rank's tensor-parallel shard (every rank then calls
+        the same model methods in the same order).  precision PRECISION_Q8 is
+        the reference's `--q8`: dense tensors become quantize_q8 of them."""
         h = C.c_void_p()
-        if tp is None or tp[0] == 1:
+        if precision != PRECISION_F32:
+            if tp is not None and tp[0] != 1:
+                raise ValueError("tensor parallelism loads at F32 precision")
+            call("prana_model_load_gguf_ex", context(device), str(path).encode(), precision, C.byref(h))
+        elif tp is None or tp[0] == 1:
             call("prana_model_load_gguf", context(device), str(path).encode(), C.byref(h))
         else:
             world, rank, uid = tp
