@@ -86,11 +86,12 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // ---- exact scalar semantics of the reference ----
-// Rust `(x * inv).round().clamp(-127.0, 127.0) as i32`: roundf is round-half-away.
+// Rust `(x * inv).round().clamp(-127.0, 127.0) as i32`: roundf is round-half-away;
+// clamp keeps a NaN (fminf/fmaxf would drop it) and `as` turns it into 0.
 __device__ __forceinline__ int round_clamp127(float v) {
-  float r = roundf(v);
-  r = fminf(fmaxf(r, -127.0f), 127.0f);
-  return (r != r) ? 0 : (int)r;
+  const float r = roundf(v);
+  if (r != r) return 0;
+  return (int)fminf(fmaxf(r, -127.0f), 127.0f);
 }
 
 // Quantize one 32-group held one value per lane (crates/prana-kernels/src/matmul.rs:109-126):

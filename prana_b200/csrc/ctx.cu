@@ -225,9 +225,8 @@ void quantize_q8_host(size_t rows, size_t cols, const float* w, int8_t* q, float
       const float scale = amax > 0.0f ? amax / 127.0f : 1.0f;
       const float inv = 1.0f / scale;
       for (int i = 0; i < 32; i++) {
-        float v = roundf(blk[i] * inv);
-        v = fminf(fmaxf(v, -127.0f), 127.0f);
-        q[r * cols + g * 32 + i] = (v != v) ? 0 : (int8_t)v;
+        const float v = roundf(blk[i] * inv);  // a NaN survives clamp and becomes 0
+        q[r * cols + g * 32 + i] = (v != v) ? 0 : (int8_t)fminf(fmaxf(v, -127.0f), 127.0f);
       }
       scales[r * groups + g] = scale;
     }

@@ -205,3 +205,18 @@ def test_attention_prefill(gpu, oracle, nh, nkv, hd, seq):
     oracle.lib().or_attention(oracle.ptr(q), oracle.ptr(k), oracle.ptr(v), seq, nh, nkv, hd, oracle.ptr(ref))
     got = K.attention(cuda(q), cuda(k), cuda(v), seq, nh, nkv, hd).cpu().numpy()
     assert rel(got, ref) < 2e-5
+
+
+def test_quantize_acts_nan_is_zero(gpu, oracle):
+    """A NaN activation quantizes to 0 (Rust's clamp keeps the NaN, `as` makes it
+    0) and leaves its group's scale to the other values (matmul.rs:109-126)."""
+    a = acts(3, 2, 256)
+    a[0, 40] = np.nan
+    a[1, 100] = np.nan
+    qa = K.quantize_acts(cuda(a))
+    torch.cuda.synchronize()
+    for r in range(2):
+        q, s, sm = oracle.quantize_acts(a[r])
+        assert np.array_equal(qa.q[r].cpu().numpy(), q)
+        assert np.array_equal(qa.scales[r].cpu().numpy().view(np.uint32), s.view(np.uint32))
+        assert np.array_equal(qa.sums[r].cpu().numpy(), sm)
