@@ -310,6 +310,14 @@ int synth_encode_row(int type, const float *x, size_t cols, uint8_t *out) {
 /* ---------------- parallel tensor generation ---------------- */
 
 typedef struct {
+  int code;          /* 0: plain; 1: embedding rows P c_t; 2: head rows P c_{s(j)} (synth_model.code_rank) */
+  int rank;
+  uint64_t code_seed;
+  float noise;
+  const float *proj; /* [cols][rank] */
+} code_spec;
+
+typedef struct {
   int type;
   size_t rows, cols;
   uint64_t seed, tid;
@@ -318,24 +326,71 @@ typedef struct {
   uint8_t *out;
   size_t r0, r1;
   int rc;
+  const code_spec *cs;
 } gen_job;
+
+#define CODE_TID 0xC0DEull
+#define PROJ_TID 0x9E07ull
+#define SUCC_A 48271u
+#define SUCC_B 12345u
+
+/* s(j): the token whose successor is j, succ(t) = (A t + B) mod V */
+static uint64_t succ_inverse(uint64_t j, uint64_t v) {
+  /* A^-1 mod V by the extended Euclid algorithm */
+  int64_t t0 = 0, t1 = 1, r0 = (int64_t)v, r1 = (int64_t)(SUCC_A % v);
+  while (r1) {
+    int64_t q = r0 / r1, tt = t0 - q * t1, rr = r0 - q * r1;
+    t0 = t1;
+    t1 = tt;
+    r0 = r1;
+    r1 = rr;
+  }
+  uint64_t inv = (uint64_t)((t0 % (int64_t)v + (int64_t)v) % (int64_t)v);
+  uint64_t d = (j + v - (SUCC_B % v)) % v;
+  return (uint64_t)(((unsigned __int128)inv * d) % v);
+}
+
+/* row r of a shared-code table: P c_t (+ noise) */
+static void code_row(const code_spec *cs, uint64_t seed, uint64_t tid, uint64_t r, size_t rows, size_t cols,
+                     float *row, float *code) {
+  const uint64_t t = cs->code == 1 ? r : succ_inverse(r, rows);
+  synth_normal_row(cs->code_seed, CODE_TID, t, (size_t)cs->rank, 1.0f, code);
+  synth_normal_row(seed, tid, r, cols, cs->noise, row);
+  for (size_t d = 0; d < cols; d++) {
+    double acc = 0.0;
+    for (int k = 0; k < cs->rank; k++) acc += (double)cs->proj[d * cs->rank + k] * code[k];
+    row[d] += (float)acc;
+  }
+}
 
 static void *gen_rows(void *arg) {
   gen_job *j = arg;
   float *row = malloc(sizeof(float) * j->cols);
+  float *code = j->cs ? malloc(sizeof(float) * (size_t)j->cs->rank) : NULL;
   size_t rb = synth_row_bytes(j->type, j->cols);
   for (size_t r = j->r0; r < j->r1; r++) {
-    if (j->std == 0.0f)
+    if (j->cs)
+      code_row(j->cs, j->seed, j->tid, r, j->rows, j->cols, row, code);
+    else if (j->std == 0.0f)
       for (size_t i = 0; i < j->cols; i++) row[i] = j->constant;
     else synth_normal_row(j->seed, j->tid, r, j->cols, j->std, row);
     if (synth_encode_row(j->type, row, j->cols, j->out + r * rb)) j->rc = -1;
   }
   free(row);
+  free(code);
   return NULL;
 }
 
+static int gen_tensor(int type, size_t rows, size_t cols, uint64_t seed, uint64_t tid, float std, float constant,
+                      int threads, uint8_t *out, const code_spec *cs);
+
 int synth_tensor(int type, size_t rows, size_t cols, uint64_t seed, uint64_t tid, float std,
                  float constant, int threads, uint8_t *out) {
+  return gen_tensor(type, rows, cols, seed, tid, std, constant, threads, out, NULL);
+}
+
+static int gen_tensor(int type, size_t rows, size_t cols, uint64_t seed, uint64_t tid, float std, float constant,
+                      int threads, uint8_t *out, const code_spec *cs) {
   if (!synth_row_bytes(type, cols)) return -1;
   if (threads < 1) threads = 1;
   if ((size_t)threads > rows) threads = (int)(rows ? rows : 1);
@@ -344,7 +399,7 @@ int synth_tensor(int type, size_t rows, size_t cols, uint64_t seed, uint64_t tid
   size_t per = (rows + threads - 1) / threads;
   int rc = 0;
   for (int t = 0; t < threads; t++) {
-    jobs[t] = (gen_job){type, rows, cols, seed, tid, std, constant, out, t * per, (t + 1) * per, 0};
+    jobs[t] = (gen_job){type, rows, cols, seed, tid, std, constant, out, t * per, (t + 1) * per, 0, cs};
     if (jobs[t].r1 > rows) jobs[t].r1 = rows;
     if (jobs[t].r0 > rows) jobs[t].r0 = rows;
     pthread_create(&th[t], NULL, gen_rows, &jobs[t]);
@@ -405,6 +460,7 @@ typedef struct {
   float std, constant;
   uint64_t tid;
   size_t bytes, offset;
+  int code; /* shared-code table: 1 embedding, 2 head */
 } tdesc;
 
 #define ALIGN 32
@@ -432,6 +488,7 @@ int synth_write_gguf(const synth_model *c, const char *path, int threads) {
   char nm[64];
   float s = c->std;
   ADD("token_embd.weight", c->type_embd, (size_t)c->vocab, (size_t)c->dim, 0, s * c->embd_std_mult, 0.0f);
+  if (c->code_rank > 0) T[n_t - 1].code = 1;
   for (int i = 0; i < c->n_layers; i++) {
     snprintf(nm, sizeof nm, "blk.%d.attn_norm.weight", i);
     ADD(nm, SYNTH_F32, 1, (size_t)c->dim, 1, 0.0f, 1.0f);
@@ -461,7 +518,10 @@ int synth_write_gguf(const synth_model *c, const char *path, int threads) {
     ADD(nm, c->type_up, (size_t)c->hidden, (size_t)c->dim, 0, s, 0.0f);
   }
   ADD("output_norm.weight", SYNTH_F32, 1, (size_t)c->dim, 1, 0.0f, 1.0f);
-  if (!c->tied) ADD("output.weight", c->type_output, (size_t)c->vocab, (size_t)c->dim, 0, s * c->head_std_mult, 0.0f);
+  if (!c->tied || c->code_rank > 0) {
+    ADD("output.weight", c->type_output, (size_t)c->vocab, (size_t)c->dim, 0, s * c->head_std_mult, 0.0f);
+    if (c->code_rank > 0) T[n_t - 1].code = 2;
+  }
 #undef ADD
   for (int i = 0; i < n_t; i++)
     if (!T[i].bytes) {
@@ -546,6 +606,16 @@ int synth_write_gguf(const synth_model *c, const char *path, int threads) {
     return -3;
   }
   int rc = fwrite(h.p, 1, h.len, f) == h.len ? 0 : -4;
+  /* the shared-code projection of this model: [dim][code_rank], N(0, 1/code_rank) */
+  float *proj = NULL;
+  code_spec cs = {0, c->code_rank, c->code_seed, c->code_noise, NULL};
+  if (c->code_rank > 0) {
+    proj = malloc(sizeof(float) * (size_t)c->dim * (size_t)c->code_rank);
+    for (int d = 0; d < c->dim; d++)
+      synth_normal_row(c->seed, PROJ_TID, (uint64_t)d, (size_t)c->code_rank, 1.0f / sqrtf((float)c->code_rank),
+                       proj + (size_t)d * c->code_rank);
+    cs.proj = proj;
+  }
   size_t written = 0;
   for (int i = 0; i < n_t && !rc; i++) {
     while (written < T[i].offset) {
@@ -554,13 +624,17 @@ int synth_write_gguf(const synth_model *c, const char *path, int threads) {
       written++;
     }
     uint8_t *data = malloc(T[i].bytes);
-    if (synth_tensor(T[i].type, T[i].rows, T[i].cols, c->seed, T[i].tid, T[i].std, T[i].constant, threads, data))
+    code_spec csi = cs;
+    csi.code = T[i].code;
+    if (gen_tensor(T[i].type, T[i].rows, T[i].cols, c->seed, T[i].tid, T[i].std, T[i].constant, threads, data,
+                   T[i].code ? &csi : NULL))
       rc = -5;
     if (!rc && fwrite(data, 1, T[i].bytes, f) != T[i].bytes) rc = -4;
     written += T[i].bytes;
     free(data);
   }
   fclose(f);
+  free(proj);
   free(h.p);
   free(T);
   return rc;

@@ -25,6 +25,18 @@ typedef struct synth_model {
   float out_proj_mult; /* std multiplier for attn_output / ffn_down (1.0) */
   float embd_std_mult; /* std multiplier for token_embd (1.0) */
   float head_std_mult; /* std multiplier for output.weight (1.0) */
+  /* Shared-code construction (code_rank > 0): every model built with the same
+   * code_seed and vocab shares a token code c_t ~ N(0, 1)^code_rank.  Row t of
+   * token_embd is P c_t and row j of output.weight is P c_{s(j)}, with P a
+   * [dim, code_rank] N(0, 1/code_rank) projection of this model's own seed and
+   * s the inverse of the successor map succ(t) = (48271 t + 12345) mod vocab:
+   * head . norm(emb(t)) then peaks at succ(t) in every such model.  On top,
+   * this model's own N(0, code_noise) noise on both tables decides how often
+   * two models pick different tokens.  The output table is written even when
+   * `tied` is set (the tables then stay separate). */
+  int code_rank;
+  uint64_t code_seed;
+  float code_noise;
 } synth_model;
 
 /* N(0, std) f32 values of row `row` of tensor `tensor` under `seed` */

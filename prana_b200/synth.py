@@ -31,6 +31,7 @@ class _SynthModel(C.Structure):
         ("type_output", C.c_int),
         ("seed", C.c_uint64),
         ("std", C.c_float), ("out_proj_mult", C.c_float), ("embd_std_mult", C.c_float), ("head_std_mult", C.c_float),
+        ("code_rank", C.c_int), ("code_seed", C.c_uint64), ("code_noise", C.c_float),
     ]
 
 
@@ -87,6 +88,12 @@ class ModelSpec:
     out_proj_mult: float = 1.0
     embd_std_mult: float = 1.0
     head_std_mult: float = 1.0
+    # shared-code construction (synth.h): embedding and head rows from a token code
+    # shared by every model with the same code_seed; code_noise sets how often two
+    # such models pick different greedy tokens
+    code_rank: int = 0
+    code_seed: int = 0
+    code_noise: float = 0.0
 
     def with_types(self, t: int) -> "ModelSpec":
         return replace(self, type_embd=t, type_q=t, type_k=t, type_v=t, type_o=t, type_gate=t, type_up=t,
@@ -133,6 +140,14 @@ LLAMA3_8B_Q8_0_L2 = replace(LLAMA3_8B_Q8_0, n_layers=2)
 QWEN2_0P5B_Q8 = replace(QWEN2_0P5B_MIX.with_types(TYPE_Q8_0), ctx=4096)
 QWEN2_1P5B_Q8 = ModelSpec("qwen2", 1536, 8960, 28, 12, 2, 128, 151936, 4096, 1e6, 1e-6, has_bias=True).with_types(TYPE_Q8_0)
 
+# C5 speculative pair at context 1024: both models near-bigram (block outputs
+# scaled by out_proj_mult) over a shared token code, per-model noise tuned so
+# the greedy draft's tokens are accepted about 60% of the time
+C5_CODE = dict(code_rank=64, code_seed=2024, out_proj_mult=0.05)
+C5_NOISE = 1.0
+QWEN2_0P5B_Q8_SPEC = replace(QWEN2_0P5B_Q8, ctx=1024, seed=1201, code_noise=C5_NOISE, **C5_CODE)
+QWEN2_1P5B_Q8_SPEC = replace(QWEN2_1P5B_Q8, ctx=1024, seed=1501, code_noise=C5_NOISE, **C5_CODE)
+
 PRESETS = {
     "stories15m_q8_0": STORIES15M_Q8,
     "qwen2_0p5b_mix": QWEN2_0P5B_MIX,
@@ -143,6 +158,8 @@ PRESETS = {
     "llama3_8b_q8_0_l2": LLAMA3_8B_Q8_0_L2,
     "qwen2_0p5b_q8_0": QWEN2_0P5B_Q8,
     "qwen2_1p5b_q8_0": QWEN2_1P5B_Q8,
+    "qwen2_0p5b_q8_0_spec": QWEN2_0P5B_Q8_SPEC,
+    "qwen2_1p5b_q8_0_spec": QWEN2_1P5B_Q8_SPEC,
 }
 
 
