@@ -65,7 +65,7 @@ def parse():
                    help="also time this many independent sequences per step (0: skip; single GPU only)")
     p.add_argument("--configs", default=None,
                    help="comma list of the other BASELINE configs to measure in the same line "
-                        "(c1,c2,c3,c4q8; default: all on one GPU, none under tensor parallelism)")
+                        "(c1,c2,c3,c4q8,c5; default: all on one GPU, none under tensor parallelism)")
     return p.parse_args()
 
 
@@ -728,7 +728,74 @@ def suite_c4q8(torch, args, peak):
         model.close()
 
 
-SUITE = {"c1": suite_c1, "c2": suite_c2, "c3": suite_c3, "c4q8": suite_c4q8}
+def suite_c5(torch, args, peak):
+    """C5: greedy speculative decode, Qwen2-0.5B-shape Q8_0 draft and 1.5B-shape
+    Q8_0 target over a shared vocabulary (151936), k = 4, context 1024; the
+    pair's shared-code construction (synth.py C5_*) makes ~60 % of the drafted
+    tokens acceptable.  Plain greedy decode of the target is timed beside it."""
+    from oracle import oracle as orc
+    from prana_b200 import model as pm
+
+    _, dpath = _preset_path(args, "qwen2_0p5b_q8_0_spec")
+    tspec, tpath = _preset_path(args, "qwen2_1p5b_q8_0_spec")
+    dm, tm = pm.Model.load(str(dpath), 0), pm.Model.load(str(tpath), 0)
+    try:
+        rng = np.random.default_rng(16)
+        prompt = rng.integers(tspec.vocab, size=16).astype(np.uint32)
+        steps, k = 256, 4
+        stream = torch.cuda.ExternalStream(tm.stream())
+        pm.generate(tm, prompt, 8)
+        pm.generate_speculative(tm, dm, prompt, 8, k)
+        torch.cuda.synchronize()
+        e0, e1 = _events(torch)
+        e0.record(stream)
+        plain = pm.generate(tm, prompt, steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_plain = e0.elapsed_time(e1)
+        e0, e1 = _events(torch)
+        e0.record(stream)
+        spec, (proposed, accepted) = pm.generate_speculative(tm, dm, prompt, steps, k)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_spec = e0.elapsed_time(e1)
+        # CPU oracle: the reference's own loops over the same pair, bounded samples
+        orc.lib().or_pool_set_threads(os.cpu_count() or 1)
+        od, ot = orc.OModel(str(dpath), orc.TIER_AUTO), orc.OModel(str(tpath), orc.TIER_AUTO)
+        n_cpu = 12
+        t0 = time.perf_counter()
+        cpu_plain = ot.generate(prompt, n_cpu)
+        el_plain = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        cpu_spec, (cp, ca) = ot.generate_speculative(od, prompt, n_cpu, k)
+        el_spec = time.perf_counter() - t0
+        return {
+            "metric": "speculative decode tok/s at batch 1 (greedy, k = 4)", "unit": UNIT,
+            "value": round(len(spec) * 1000.0 / ms_spec, 1),
+            "plain_greedy": {"value": round(len(plain) * 1000.0 / ms_plain, 1), "unit": UNIT,
+                             "path": "prana_generate: prefill, then the device decode loop"},
+            "e2e": {"value": round(len(spec) * 1000.0 / ms_spec, 1), "unit": UNIT,
+                    "path": "prana_generate_speculative per call (draft steps and the (k+1)-row verify host-driven)",
+                    "h2d_bytes_per_step": None, "d2h_bytes_per_step": None},
+            "acceptance": round(accepted / max(proposed, 1), 3), "proposed": proposed, "accepted": accepted,
+            "speedup_vs_plain": round(ms_plain / ms_spec * len(spec) / max(len(plain), 1), 3),
+            "cpu_baseline": {"value": round(n_cpu / el_spec, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                             "plain_value": round(n_cpu / el_plain, 3), "acceptance": round(ca / max(cp, 1), 3),
+                             "sample": f"oracle generate_speculative and generate, {n_cpu} tokens each, "
+                                       f"{el_spec:.1f} s and {el_plain:.1f} s"},
+            "parity": {"spec_equals_greedy": bool(np.array_equal(spec, plain)),
+                       "cpu_spec_equals_cpu_greedy": bool(np.array_equal(cpu_spec, cpu_plain)),
+                       "gpu_greedy_prefix_equals_cpu": int(np.argmax(np.concatenate([plain[:n_cpu] != cpu_plain,
+                                                                                     [True]])))},
+            "config": {"workload": "qwen2_0p5b_q8_0 draft -> qwen2_1p5b_q8_0 target", "k": k, "prompt": len(prompt),
+                       "steps": steps, "ctx": tspec.ctx, "batch": 1},
+        }
+    finally:
+        dm.close()
+        tm.close()
+
+
+SUITE = {"c1": suite_c1, "c2": suite_c2, "c3": suite_c3, "c4q8": suite_c4q8, "c5": suite_c5}
 
 
 def prana_arm(args):
@@ -836,7 +903,7 @@ def prana_arm(args):
                   "free_running": parity}
     suite = {}
     if rank == 0 and world == 1:
-        todo = args.configs.split(",") if args.configs is not None else ["c1", "c2", "c3", "c4q8"]
+        todo = args.configs.split(",") if args.configs is not None else ["c1", "c2", "c3", "c4q8", "c5"]
         for name in [x.strip() for x in todo if x.strip()]:
             fn = SUITE.get(name)
             if fn is None:

@@ -144,7 +144,7 @@ QWEN2_1P5B_Q8 = ModelSpec("qwen2", 1536, 8960, 28, 12, 2, 128, 151936, 4096, 1e6
 # scaled by out_proj_mult) over a shared token code, per-model noise tuned so
 # the greedy draft's tokens are accepted about 60% of the time
 C5_CODE = dict(code_rank=64, code_seed=2024, out_proj_mult=0.05)
-C5_NOISE = 1.0
+C5_NOISE = 1.75  # measured on B200: 1.7 -> 67 %, 1.8 -> 54 % of drafted tokens accepted
 QWEN2_0P5B_Q8_SPEC = replace(QWEN2_0P5B_Q8, ctx=1024, seed=1201, code_noise=C5_NOISE, **C5_CODE)
 QWEN2_1P5B_Q8_SPEC = replace(QWEN2_1P5B_Q8, ctx=1024, seed=1501, code_noise=C5_NOISE, **C5_CODE)
 
