@@ -69,6 +69,33 @@ int prana_ctx_stream(prana_ctx *ctx, void **cuda_stream);
  * raised and the context stays usable. */
 int prana_debug_wait_timeout(prana_ctx *ctx, int which, unsigned polls);
 
+/* ---------------------------------------------------------------- device arena / buffer pool
+ * BufferPool (crates/prana-tensor/src/pool.rs:13-103) with its storage in one
+ * reservation: prana_pool_create makes the only allocator call (cudaMalloc of
+ * `capacity` bytes on the context's device; ctx NULL: host memory, for
+ * bookkeeping tests).  acquire rounds a request up to the reference's bucket
+ * (a power of two, at least 1 KiB; requests above 64 MiB are carved at their
+ * own 256-byte-aligned size), reuses a released buffer of that bucket or carves
+ * a new one, and returns it zeroed (a device pool clears it on the context's
+ * stream).  release returns a buffer to its bucket's list; clear hands every
+ * listed buffer back to the arena (coalesced).  active / pooled / peak are the
+ * reference's counters; carved is the arena space in use (checked out or
+ * listed).  A full arena returns PRANA_E_OOM. */
+typedef struct prana_pool prana_pool;
+int prana_pool_create(prana_ctx *ctx, size_t capacity, prana_pool **out);
+int prana_pool_destroy(prana_pool *pool); /* idempotent on NULL; the arena's buffers die with it */
+int prana_pool_acquire(prana_pool *pool, size_t bytes, void **ptr, size_t *bucket_bytes);
+int prana_pool_release(prana_pool *pool, void *ptr);
+int prana_pool_clear(prana_pool *pool);
+int prana_pool_stats(prana_pool *pool, size_t *active, size_t *pooled, size_t *peak, size_t *carved);
+/* Every later device allocation of the context -- weights, models, KV caches,
+ * activation buffers, kernel scratch -- comes from the pool (NULL: back to
+ * cudaMalloc).  Switching first waits for the context's streams and returns
+ * its kernel scratch and RoPE tables to where they came from.  Weights,
+ * models and caches made while a pool was attached must be freed before it is
+ * detached or destroyed. */
+int prana_ctx_use_pool(prana_ctx *ctx, prana_pool *pool);
+
 /* ---------------------------------------------------------------- weights
  * Upload one [rows, cols] tensor given in its GGUF byte layout and repack it
  * for 128-bit loads (replaces QuantMatrix::from_parts, matmul.rs:34-39, and

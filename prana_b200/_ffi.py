@@ -53,6 +53,13 @@ SIGNATURES = {
     "prana_ctx_synchronize": [P],
     "prana_ctx_stream": [P, C.POINTER(P)],
     "prana_debug_wait_timeout": [P, I, C.c_uint],
+    "prana_pool_create": [P, SZ, C.POINTER(P)],
+    "prana_pool_destroy": [P],
+    "prana_pool_acquire": [P, SZ, C.POINTER(P), C.POINTER(SZ)],
+    "prana_pool_release": [P, P],
+    "prana_pool_clear": [P],
+    "prana_pool_stats": [P, C.POINTER(SZ), C.POINTER(SZ), C.POINTER(SZ), C.POINTER(SZ)],
+    "prana_ctx_use_pool": [P, P],
     "prana_weight_upload": [P, I, SZ, SZ, P, C.POINTER(P)],
     "prana_weight_free": [P],
     "prana_quantize_q8": [SZ, SZ, P, P, P],

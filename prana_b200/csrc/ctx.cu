@@ -27,15 +27,12 @@ int ctx_scratch(prana_ctx* ctx, size_t bytes, void** out) {
   if (ctx->scratch.bytes < bytes) {
     if (ctx->scratch.base) {
       PRANA_CK(cudaStreamSynchronize(ctx->stream));
-      cudaFree(ctx->scratch.base);
+      dev_free(ctx, ctx->scratch.base);
       ctx->scratch.base = nullptr;
       ctx->scratch.bytes = 0;
     }
     size_t want = bytes < ((size_t)16 << 20) ? ((size_t)16 << 20) : bytes;
-    if (cudaMalloc(&ctx->scratch.base, want) != cudaSuccess) {
-      cudaGetLastError();
-      return fail(PRANA_E_OOM, "scratch allocation of %zu bytes failed", want);
-    }
+    if (int rc = dev_alloc(ctx, want, &ctx->scratch.base)) return rc;
     ctx->scratch.bytes = want;
   }
   *out = ctx->scratch.base;
@@ -71,8 +68,14 @@ int ctx_rope(prana_ctx* ctx, int hd, float theta, int neox, int positions, const
       t.cos = t.sin = nullptr;
       t.positions = 0;
     }
-    PRANA_CK(cudaMalloc(&t.cos, c.size() * 4));
-    PRANA_CK(cudaMalloc(&t.sin, s.size() * 4));
+    void *pc = nullptr, *ps = nullptr;
+    if (int rc = dev_alloc(ctx, c.size() * 4, &pc)) return rc;
+    if (int rc = dev_alloc(ctx, s.size() * 4, &ps)) {
+      dev_free(ctx, pc);
+      return rc;
+    }
+    t.cos = static_cast<float*>(pc);
+    t.sin = static_cast<float*>(ps);
     PRANA_CK(cudaMemcpy(t.cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
     PRANA_CK(cudaMemcpy(t.sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
     t.positions = n;
@@ -174,12 +177,9 @@ int upload_weight(prana_ctx* ctx, int type, size_t rows, size_t cols, const void
       return fail(PRANA_E_UNSUPPORTED, "ggml type %d is not supported", type);
   }
   void* mem = nullptr;
-  if (cudaMalloc(&mem, total) != cudaSuccess) {
-    cudaGetLastError();
-    return fail(PRANA_E_OOM, "device allocation of %zu bytes failed", total);
-  }
+  if (int rc = dev_alloc(ctx, total, &mem)) return rc;
   if (cudaMemcpy(mem, buf.data(), total, cudaMemcpyHostToDevice) != cudaSuccess) {
-    cudaFree(mem);
+    dev_free(ctx, mem);
     return fail(PRANA_E_CUDA, "weight upload failed");
   }
   uint8_t* base = static_cast<uint8_t*>(mem);
@@ -240,12 +240,9 @@ int upload_q8s(prana_ctx* ctx, size_t rows, size_t cols, const float* host, pran
   std::vector<uint8_t> buf(total);
   quantize_q8_host(rows, cols, host, reinterpret_cast<int8_t*>(buf.data()), reinterpret_cast<float*>(buf.data() + off));
   void* mem = nullptr;
-  if (cudaMalloc(&mem, total) != cudaSuccess) {
-    cudaGetLastError();
-    return fail(PRANA_E_OOM, "device allocation of %zu bytes failed", total);
-  }
+  if (int rc = dev_alloc(ctx, total, &mem)) return rc;
   if (cudaMemcpy(mem, buf.data(), total, cudaMemcpyHostToDevice) != cudaSuccess) {
-    cudaFree(mem);
+    dev_free(ctx, mem);
     return fail(PRANA_E_CUDA, "weight upload failed");
   }
   DevWeight dw{};
@@ -263,7 +260,7 @@ int upload_q8s(prana_ctx* ctx, size_t rows, size_t cols, const float* host, pran
 
 void free_weight(prana_weight* w) {
   if (w && w->mem) {
-    cudaFree(w->mem);
+    dev_free(w->ctx, w->mem);
     w->mem = nullptr;
   }
 }
@@ -327,11 +324,11 @@ int prana_ctx_destroy(prana_ctx* c) {
   DevScope ds(c->device);
   cudaStreamSynchronize(c->stream);
   for (auto& kv : c->rope) {
-    cudaFree(kv.second.cos);
-    cudaFree(kv.second.sin);
+    dev_free(c, kv.second.cos);
+    dev_free(c, kv.second.sin);
   }
-  for (void* p : c->retired) cudaFree(p);
-  cudaFree(c->scratch.base);
+  for (void* p : c->retired) dev_free(c, p);
+  dev_free(c, c->scratch.base);
   cudaFree(c->counters);
   cudaStreamDestroy(c->own);
   delete c;

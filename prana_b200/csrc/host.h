@@ -40,6 +40,7 @@ struct Scratch {
 
 struct prana_ctx {
   int device = 0;
+  prana_pool* pool = nullptr;  // when set, the context's device memory comes from it
   int sm_count = 148;
   cudaStream_t own = nullptr;
   cudaStream_t stream = nullptr;
@@ -68,6 +69,9 @@ int upload_weight(prana_ctx* ctx, int type, size_t rows, size_t cols, const void
 void quantize_q8_host(size_t rows, size_t cols, const float* w, int8_t* q, float* scales);
 int upload_q8s(prana_ctx* ctx, size_t rows, size_t cols, const float* host, prana_weight* w);
 void free_weight(prana_weight* w);
+// Device memory of a context: its pool's when attached, else cudaMalloc.
+int dev_alloc(prana_ctx* ctx, size_t bytes, void** out);
+void dev_free(prana_ctx* ctx, void* p);
 // Read and clear the error word of prana_attention_decode_noalloc on `device`.
 int noalloc_take_error(int device, unsigned* out);
 struct DevScope {

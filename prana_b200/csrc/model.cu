@@ -217,16 +217,15 @@ struct Bufs {
   float* y = nullptr;
   void* qg = nullptr;
   std::vector<void*> owned;
+  prana_ctx* ctx = nullptr;  // device memory from its pool when one is attached
+  explicit Bufs(prana_ctx* c) : ctx(c) {}
   ~Bufs() {
-    for (void* p : owned) cudaFree(p);
+    for (void* p : owned) dev_free(ctx, p);
   }
   template <typename T>
   int alloc(T*& p, size_t n) {
     void* v = nullptr;
-    if (cudaMalloc(&v, std::max<size_t>(n, 1) * sizeof(T)) != cudaSuccess) {
-      cudaGetLastError();
-      return fail(PRANA_E_OOM, "activation buffer allocation failed");
-    }
+    if (int rc = dev_alloc(ctx, std::max<size_t>(n, 1) * sizeof(T), &v)) return rc;
     owned.push_back(v);
     p = static_cast<T*>(v);
     return PRANA_OK;
@@ -290,10 +289,7 @@ namespace {
 
 int dev_vec(prana_model* m, const std::vector<float>& h, float** out) {
   void* p = nullptr;
-  if (cudaMalloc(&p, h.size() * 4) != cudaSuccess) {
-    cudaGetLastError();
-    return fail(PRANA_E_OOM, "allocation failed");
-  }
+  if (int rc = dev_alloc(m->ctx, h.size() * 4, &p)) return rc;
   m->owned.push_back(p);
   if (cudaMemcpy(p, h.data(), h.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
     return fail(PRANA_E_CUDA, "upload failed");
@@ -394,7 +390,7 @@ void free_model(prana_model* m) {
     free_stream(L.w3);
     free_stream(L.w2);
   }
-  for (void* p : m->owned) cudaFree(p);
+  for (void* p : m->owned) dev_free(m->ctx, p);
   m->dec.reset();
   if (m->peers_ok) tp_peers_release(&m->peers, m->peers_mem);
   if (m->comm) {
@@ -876,11 +872,12 @@ void destroy_kv(prana_kv* kv) {
   cs.erase(std::remove(cs.begin(), cs.end(), kv), cs.end());
   if (kv->g_step) cudaGraphExecDestroy(kv->g_step);
   if (kv->g_loop) cudaGraphExecDestroy(kv->g_loop);
-  cudaFree(kv->k);
-  cudaFree(kv->v);
-  cudaFree(kv->part_ml);
-  cudaFree(kv->counters);
-  cudaFree(kv->ring);
+  prana_ctx* c = kv->m->ctx;
+  dev_free(c, kv->k);
+  dev_free(c, kv->v);
+  dev_free(c, kv->part_ml);
+  dev_free(c, kv->counters);
+  dev_free(c, kv->ring);
   delete kv;
 }
 
@@ -1145,15 +1142,15 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
   rc = ctx_rope(ctx, (int)c.head_dim, c.rope_theta, c.rope_neox, (int)c.seq_len + 8, &m->rope);
   if (rc) return rc;
   // decode buffers, argmax partials, counters, error flag
-  m->dec.reset(new Bufs());
+  m->dec.reset(new Bufs(ctx));
   if ((rc = make_bufs(m.get(), 8, false, *m->dec))) return rc;
   m->n_parts = 1024;
   void* p = nullptr;
-  PRANA_CK(cudaMalloc(&p, (size_t)8 * m->n_parts * 8));
+  if ((rc = dev_alloc(ctx, (size_t)8 * m->n_parts * 8, &p))) return rc;
   m->owned.push_back(p);
   m->part_val = static_cast<float*>(p);
   m->part_idx = reinterpret_cast<int*>(static_cast<float*>(p) + (size_t)8 * m->n_parts);
-  PRANA_CK(cudaMalloc(&p, 256));
+  if ((rc = dev_alloc(ctx, 256, &p))) return rc;
   m->owned.push_back(p);
   PRANA_CK(cudaMemset(p, 0, 256));
   m->ctr = static_cast<unsigned*>(p);
@@ -1162,7 +1159,7 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
   PRANA_CK(cudaHostAlloc((void**)&m->h_io, 64, cudaHostAllocDefault));
   m->h_tok = reinterpret_cast<uint32_t*>(m->h_io + 4);
   if (world > 1) {
-    PRANA_CK(cudaMalloc(&p, (size_t)(world + 1) * 16 * 4));
+    if ((rc = dev_alloc(ctx, (size_t)(world + 1) * 16 * 4, &p))) return rc;
     m->owned.push_back(p);
     m->tp_local = static_cast<float*>(p);
     m->tp_all = m->tp_local + 16;
@@ -1242,9 +1239,13 @@ int prana_kv_create(prana_model* m, size_t positions, prana_kv** out) {
   kv->positions = positions;
   const size_t kv_dim = (size_t)(m->kv_heads_l * c.head_dim);
   const size_t per = (size_t)c.n_layers * positions * kv_dim;
-  if (cudaMalloc(&kv->k, per * 2) != cudaSuccess || cudaMalloc(&kv->v, per * 2) != cudaSuccess) {
-    cudaGetLastError();
-    return fail(PRANA_E_OOM, "kv cache allocation (%zu bytes) failed", per * 4);
+  {
+    void *pk = nullptr, *pv = nullptr;
+    int rc = dev_alloc(m->ctx, per * 2, &pk);
+    kv->k = static_cast<__half*>(pk);
+    if (!rc) rc = dev_alloc(m->ctx, per * 2, &pv);
+    kv->v = static_cast<__half*>(pv);
+    if (rc) return fail(PRANA_E_OOM, "kv cache allocation (%zu bytes) failed", per * 4);
   }
   PRANA_CK(cudaMemset(kv->k, 0, per * 2));
   PRANA_CK(cudaMemset(kv->v, 0, per * 2));
@@ -1265,11 +1266,18 @@ int prana_kv_create(prana_model* m, size_t positions, prana_kv** out) {
   const size_t vh = (size_t)rows_cta * group;  // largest row chunk one attention CTA takes
   const size_t ml = ((size_t)m->kv_heads_l * kv->n_splits * vh * 2 + 3) / 4 * 4;  // part_o 16-byte aligned
   const size_t po = (size_t)m->kv_heads_l * kv->n_splits * vh * c.head_dim;
-  PRANA_CK(cudaMalloc(&kv->part_ml, (ml + po) * 4));
+  {
+    void *pm = nullptr, *pc = nullptr, *pr = nullptr;
+    int rc = dev_alloc(m->ctx, (ml + po) * 4, &pm);
+    kv->part_ml = static_cast<float*>(pm);
+    if (!rc) rc = dev_alloc(m->ctx, 1024 * sizeof(unsigned), &pc);
+    kv->counters = static_cast<unsigned*>(pc);
+    if (!rc) rc = dev_alloc(m->ctx, (positions + 64) * sizeof(uint32_t), &pr);
+    kv->ring = static_cast<uint32_t*>(pr);
+    if (rc) return rc;
+  }
   kv->part_o = kv->part_ml + ml;
-  PRANA_CK(cudaMalloc(&kv->counters, 1024 * sizeof(unsigned)));
   PRANA_CK(cudaMemset(kv->counters, 0, 1024 * sizeof(unsigned)));
-  PRANA_CK(cudaMalloc(&kv->ring, (positions + 64) * sizeof(uint32_t)));
   kv->ring_n = reinterpret_cast<int*>(kv->ring + positions + 32);
   m->caches.push_back(kv.get());
   *out = kv.release();
@@ -1372,7 +1380,7 @@ int prana_forward_batch_trace(prana_model* m, prana_kv* kv, const uint32_t* toke
   NEED(cap >= need, "trace buffer holds %zu values, %zu needed", cap, need);
   DevScope ds(m->ctx->device);
   cudaStream_t st = m->ctx->own;
-  Bufs b;
+  Bufs b(m->ctx);
   int rc = make_bufs(m, n, prefill != 0, b);
   if (rc) return rc;
   Trace tr;
@@ -1420,7 +1428,7 @@ int prana_prefill(prana_model* m, prana_kv* kv, const uint32_t* tokens, size_t n
   NEED(n <= kv->positions, "prefill of %zu tokens beyond kv capacity %zu", n, kv->positions);
   for (size_t i = 0; i < n; i++) NEED(tokens[i] < (uint64_t)m->cfg.vocab_size, "token out of vocabulary");
   DevScope ds(m->ctx->device);
-  Bufs b;
+  Bufs b(m->ctx);
   int rc = make_bufs(m, n, true, b);
   if (rc) return rc;
   cudaStream_t st = m->ctx->own;
@@ -1445,7 +1453,7 @@ int prana_forward_batch(prana_model* m, prana_kv* kv, const uint32_t* tokens, si
   std::unique_ptr<Bufs> tmp;
   Bufs* b = m->dec.get();
   if (n > b->rows) {
-    tmp.reset(new Bufs());
+    tmp.reset(new Bufs(m->ctx));
     int rc = make_bufs(m, n, false, *tmp);
     if (rc) return rc;
     b = tmp.get();
@@ -1483,7 +1491,7 @@ static int forward_multi_impl(prana_model* m, prana_kv* const* kvs, size_t n, co
   std::unique_ptr<Bufs> tmp;
   Bufs* b = m->dec.get();
   if (n > b->rows) {
-    tmp.reset(new Bufs());
+    tmp.reset(new Bufs(m->ctx));
     int rc = make_bufs(m, n, false, *tmp);
     if (rc) return rc;
     b = tmp.get();
@@ -1516,7 +1524,7 @@ static int forward_multi_impl(prana_model* m, prana_kv* const* kvs, size_t n, co
   }
   SeqRow* rows_dev = nullptr;
   AttnSeq* att_dev = nullptr;
-  Bufs scratch;
+  Bufs scratch(m->ctx);
   if (int rc = scratch.alloc(rows_dev, n)) return rc;
   if (int rc = scratch.alloc(att_dev, att.size())) return rc;
   PRANA_CK(cudaMemcpyAsync(b->toks, tokens, n * 4, cudaMemcpyHostToDevice, st));
