@@ -19,7 +19,7 @@ CSRC = PKG / "csrc"
 LIB = PKG / "_lib"
 ROOT = PKG.parent
 
-CUDA_SOURCES = ["kernels.cu", "attention.cu", "decode.cu", "ctx.cu", "model.cu", "noalloc.cu", "comm.cu", "qgemm.cu", "tokenizer.cpp", "sampler.cpp", "pool.cu"]
+CUDA_SOURCES = ["kernels.cu", "attention.cu", "decode.cu", "ctx.cu", "model.cu", "noalloc.cu", "comm.cu", "qgemm.cu", "tokenizer.cpp", "sampler.cpp", "pool.cu", "loader.cu"]
 CUDA_HEADERS = ["common.cuh", "gemv.cuh", "finish.cuh", "mbar.cuh", "comm.h", "internal.h", "host.h", "unicode_alpha.h"]
 NVCC_FLAGS = [
     "-O3",

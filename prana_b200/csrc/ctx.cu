@@ -1,5 +1,6 @@
 // ctx.cu -- context, error reporting, weight upload/repack and the
 // kernel-level C-ABI entry points (the prana-kernels function surface).
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -84,132 +85,17 @@ int ctx_rope(prana_ctx* ctx, int hd, float theta, int neox, int positions, const
   return PRANA_OK;
 }
 
-static float h2f_host(uint16_t h) {
-  const uint32_t sign = (h >> 15) & 1u, exp = (h >> 10) & 0x1fu, frac = h & 0x3ffu;
-  uint32_t bits;
-  if (exp == 0 && frac == 0) bits = sign << 31;
-  else if (exp == 0) {
-    const float v = (float)frac * 5.9604644775390625e-08f;
-    return sign ? -v : v;
-  } else if (exp == 0x1f) bits = (sign << 31) | 0x7f800000u | (frac << 13);
-  else bits = (sign << 31) | ((exp + 112u) << 23) | (frac << 13);
-  float f;
-  memcpy(&f, &bits, 4);
-  return f;
-}
-
 static size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// Split GGUF blocks into the planes the GEMV streams (see common.cuh DevWeight).
+// One tensor through a streamer whose chunk holds it whole (at most 64 MiB).
 int upload_weight(prana_ctx* ctx, int type, size_t rows, size_t cols, const void* host, prana_weight* w) {
-  if (!rows || !cols) return fail(PRANA_E_INVALID, "empty weight [%zu, %zu]", rows, cols);
-  if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX) return fail(PRANA_E_INVALID, "weight too large");
   const uint8_t* src = static_cast<const uint8_t*>(host);
-  const size_t n = rows * cols;
-  size_t off[4] = {0, 0, 0, 0}, total = 0;
-  std::vector<uint8_t> buf;
-  switch (type) {
-    case T_Q8_0: {
-      if (cols % 32) return fail(PRANA_E_INVALID, "Q8_0 needs cols %% 32 == 0 (cols=%zu)", cols);
-      off[1] = al256(n);
-      total = off[1] + al256(n / 32 * 2);
-      buf.resize(total);
-      int8_t* q = reinterpret_cast<int8_t*>(buf.data());
-      uint16_t* d = reinterpret_cast<uint16_t*>(buf.data() + off[1]);
-      for (size_t b = 0; b < n / 32; b++) {
-        memcpy(&d[b], src + b * 34, 2);
-        memcpy(q + b * 32, src + b * 34 + 2, 32);
-      }
-      break;
-    }
-    case T_Q4_0: {
-      if (cols % 32) return fail(PRANA_E_INVALID, "Q4_0 needs cols %% 32 == 0 (cols=%zu)", cols);
-      off[1] = al256(n / 2);
-      total = off[1] + al256(n / 32 * 2);
-      buf.resize(total);
-      uint16_t* d = reinterpret_cast<uint16_t*>(buf.data() + off[1]);
-      for (size_t b = 0; b < n / 32; b++) {
-        memcpy(&d[b], src + b * 18, 2);
-        memcpy(buf.data() + b * 16, src + b * 18 + 2, 16);
-      }
-      break;
-    }
-    case T_Q4_K: {
-      if (cols % 256) return fail(PRANA_E_INVALID, "Q4_K needs cols %% 256 == 0 (cols=%zu)", cols);
-      total = al256(n / 256 * 144);
-      buf.assign(src, src + n / 256 * 144);
-      buf.resize(total);
-      break;
-    }
-    case T_Q6_K: {
-      if (cols % 256) return fail(PRANA_E_INVALID, "Q6_K needs cols %% 256 == 0 (cols=%zu)", cols);
-      const size_t nb = n / 256;
-      off[1] = al256(n / 2);
-      off[2] = off[1] + al256(n / 4);
-      off[3] = off[2] + al256(n / 16);
-      total = off[3] + al256(nb * 2);
-      buf.resize(total);
-      for (size_t b = 0; b < nb; b++) {
-        const uint8_t* blk = src + b * 210;
-        memcpy(buf.data() + b * 128, blk, 128);
-        memcpy(buf.data() + off[1] + b * 64, blk + 128, 64);
-        memcpy(buf.data() + off[2] + b * 16, blk + 192, 16);
-        memcpy(buf.data() + off[3] + b * 2, blk + 208, 2);
-      }
-      break;
-    }
-    case T_F32:
-    case T_F16: {
-      total = al256(n * 4);
-      buf.resize(total);
-      float* f = reinterpret_cast<float*>(buf.data());
-      if (type == T_F32) memcpy(f, src, n * 4);
-      else
-        for (size_t i = 0; i < n; i++) {
-          uint16_t h;
-          memcpy(&h, src + 2 * i, 2);
-          f[i] = h2f_host(h);
-        }
-      type = T_F32;
-      break;
-    }
-    default:
-      return fail(PRANA_E_UNSUPPORTED, "ggml type %d is not supported", type);
-  }
-  void* mem = nullptr;
-  if (int rc = dev_alloc(ctx, total, &mem)) return rc;
-  if (cudaMemcpy(mem, buf.data(), total, cudaMemcpyHostToDevice) != cudaSuccess) {
-    dev_free(ctx, mem);
-    return fail(PRANA_E_CUDA, "weight upload failed");
-  }
-  uint8_t* base = static_cast<uint8_t*>(mem);
-  DevWeight dw{};
-  dw.type = type;
-  dw.rows = (int)rows;
-  dw.cols = (int)cols;
-  switch (type) {
-    case T_Q8_0:
-    case T_Q4_0:
-      dw.qs = base;
-      dw.d = reinterpret_cast<const __half*>(base + off[1]);
-      break;
-    case T_Q4_K:
-      dw.qs = base;
-      break;
-    case T_Q6_K:
-      dw.qs = base;
-      dw.qh = base + off[1];
-      dw.sc = reinterpret_cast<const int8_t*>(base + off[2]);
-      dw.d = reinterpret_cast<const __half*>(base + off[3]);
-      break;
-    default:
-      dw.f32 = reinterpret_cast<const float*>(base);
-  }
-  w->ctx = ctx;
-  w->dw = dw;
-  w->mem = mem;
-  w->bytes = total;
-  return PRANA_OK;
+  const size_t rb = gguf_bytes_per_row(type, cols);
+  WeightStreamer ws(ctx, std::max<size_t>(std::min(rows * rb, size_t(64) << 20), std::max<size_t>(rb, 1)));
+  int rc = ws.upload(type, rows, cols, [src, rb](size_t r) { return src + r * rb; }, w);
+  if (!rc) rc = ws.finish();
+  if (rc && w->mem) free_weight(w);
+  return rc;
 }
 
 // quantize_q8 (matmul.rs:61-84): per 32 values amax (f32::max fold from 0),

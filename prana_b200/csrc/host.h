@@ -3,7 +3,9 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstdint>
 #include <cstdio>
+#include <functional>
 #include <map>
 #include <string>
 #include <tuple>
@@ -63,6 +65,34 @@ namespace prana {
 int ctx_scratch(prana_ctx* ctx, size_t bytes, void** out);
 // Table for (head_dim, theta, neox) covering at least `positions` rows.
 int ctx_rope(prana_ctx* ctx, int head_dim, float theta, int neox, int positions, const RopeTable** out);
+// Address of row r's GGUF bytes (a [rows, cols] matrix taken from a file in any row order).
+using RowSrc = std::function<const uint8_t*(size_t)>;
+
+// Streams GGUF tensors to the device: rows are gathered into one of two pinned
+// chunks, copied asynchronously on the context's own stream, and split into
+// planes there by a repack kernel while the next chunk is gathered.  The
+// destination is ready once finish() returns.
+class WeightStreamer {
+ public:
+  WeightStreamer(prana_ctx* ctx, size_t chunk_bytes);
+  ~WeightStreamer();
+  WeightStreamer(const WeightStreamer&) = delete;
+  WeightStreamer& operator=(const WeightStreamer&) = delete;
+  int upload(int type, size_t rows, size_t cols, const RowSrc& row_src, prana_weight* w);
+  int finish();
+  size_t bytes_streamed = 0;
+
+ private:
+  int ready();
+  prana_ctx* ctx;
+  size_t chunk;
+  uint8_t* pinned[2] = {nullptr, nullptr};
+  uint8_t* stage[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  int cur = 0;
+};
+// Bytes of one GGUF row of `type` holding `cols` values (0 for other types).
+size_t gguf_bytes_per_row(int type, size_t cols);
 // Repack GGUF bytes of a [rows, cols] tensor into device layout.
 int upload_weight(prana_ctx* ctx, int type, size_t rows, size_t cols, const void* host, prana_weight* w);
 // quantize_q8 (matmul.rs:61-84) on the host, then upload as T_Q8S

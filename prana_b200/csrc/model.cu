@@ -325,15 +325,19 @@ int linear_raw(const Gguf& g, const std::string& name, size_t rows, size_t cols,
 
 size_t gguf_row_bytes(uint32_t type, size_t cols) { return type_size(type, cols); }
 
-// Columns [c0, c1) of every row of a [rows, cols] GGUF tensor (whole blocks).
-int slice_cols(uint32_t type, size_t rows, size_t cols, const uint8_t* raw, size_t c0, size_t c1,
-               std::vector<uint8_t>& out) {
+// Rows of a GGUF tensor stored one after another from `raw`.
+RowSrc linear_rows(const uint8_t* raw, size_t rb) {
+  return [raw, rb](size_t r) { return raw + r * rb; };
+}
+
+// Columns [c0, c1) of every row of a [rows, cols] GGUF tensor (whole blocks),
+// as rows of a [rows, c1 - c0] tensor.
+int col_rows(uint32_t type, size_t cols, const uint8_t* raw, size_t c0, size_t c1, RowSrc* out) {
   const size_t blk = (type == T_Q4_K || type == T_Q6_K) ? 256 : (type == T_Q8_0 || type == T_Q4_0) ? 32 : 1;
   if (c0 % blk || c1 % blk || c1 > cols || c0 >= c1)
     return fail(PRANA_E_UNSUPPORTED, "column shard [%zu, %zu) does not fall on %zu-value blocks", c0, c1, blk);
-  const size_t rb = gguf_row_bytes(type, cols), sb = gguf_row_bytes(type, c1 - c0), off = gguf_row_bytes(type, c0);
-  out.resize(rows * sb);
-  for (size_t r = 0; r < rows; r++) memcpy(out.data() + r * sb, raw + r * rb + off, sb);
+  const size_t rb = gguf_row_bytes(type, cols), off = gguf_row_bytes(type, c0);
+  *out = [raw, rb, off](size_t r) { return raw + r * rb + off; };
   return PRANA_OK;
 }
 
@@ -361,12 +365,16 @@ std::vector<float> densify(uint32_t type, size_t rows, size_t cols, const uint8_
   return out;
 }
 
-int upload_stream(prana_model* m, uint32_t type, size_t rows, size_t cols, const uint8_t* bytes, StreamW* sw) {
+int upload_stream(prana_model* m, WeightStreamer& ws, uint32_t type, size_t rows, size_t cols, const RowSrc& src,
+                  StreamW* sw) {
   if (type == T_F32 || type == T_F16) {  // Q8 precision: quantize_q8 of the dense rows
-    const std::vector<float> f = densify(type, rows, cols, bytes);
+    const size_t rb = gguf_row_bytes(type, cols);
+    std::vector<uint8_t> raw(rows * rb);
+    for (size_t r = 0; r < rows; r++) memcpy(&raw[r * rb], src(r), rb);
+    const std::vector<float> f = densify(type, rows, cols, raw.data());
     return upload_q8s(m->ctx, rows, cols, f.data(), &sw->w);
   }
-  return upload_weight(m->ctx, (int)type, rows, cols, bytes, &sw->w);
+  return ws.upload((int)type, rows, cols, src, &sw->w);
 }
 
 void free_stream(StreamW& s) {
@@ -881,12 +889,6 @@ void destroy_kv(prana_kv* kv) {
   delete kv;
 }
 
-// Rows of a GGUF tensor reordered / interleaved into one stored matrix.
-struct RowSrc {
-  const uint8_t* raw;
-  size_t row_bytes;
-};
-
 }  // namespace
 
 #define API_BEGIN try {
@@ -955,6 +957,7 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
   std::unique_ptr<prana_model, void (*)(prana_model*)> m(new prana_model(), free_model);
   m->ctx = ctx;
   m->precision = precision;
+  WeightStreamer ws(ctx, size_t(64) << 20);  // destroyed before m: its copies end first
   auto& c = m->cfg;
   if (!meta_int("embedding_length", &c.dim)) return fail(PRANA_E_FORMAT, "missing metadata '%s.embedding_length'", arch.c_str());
   if (!meta_int("block_count", &c.n_layers)) return fail(PRANA_E_FORMAT, "missing metadata '%s.block_count'", arch.c_str());
@@ -997,7 +1000,7 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
     uint64_t nv = 1;
     for (auto d : t->dims) nv *= d;
     if (nv != (uint64_t)c.vocab_size * dim) return fail(PRANA_E_FORMAT, "token_embd.weight size mismatch with vocab");
-    rc = upload_weight(ctx, (int)t->type, (size_t)c.vocab_size, dim, raw, &m->emb);
+    rc = ws.upload((int)t->type, (size_t)c.vocab_size, dim, linear_rows(raw, gguf_row_bytes(t->type, dim)), &m->emb);
     if (rc) return rc;
   }
   m->layers.resize((size_t)c.n_layers);
@@ -1022,14 +1025,11 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
       int s1 = s0 + 1;
       while (s1 < 3 && types[s1] == types[s0]) s1++;
       const size_t rb = gguf_row_bytes(types[s0], dim);
-      size_t total_rows = 0;
-      for (int s = s0; s < s1; s++) total_rows += seg_rows[s];
-      std::vector<uint8_t> buf(total_rows * rb);
+      std::vector<const uint8_t*> rows;  // stored row -> GGUF row
       QkvPart part;
       part.nseg = s1 - s0;
-      size_t at = 0;
       for (int s = s0; s < s1; s++) {
-        part.seg_start[s - s0] = (int)at;
+        part.seg_start[s - s0] = (int)rows.size();
         part.kind[s - s0] = s;
         for (size_t pp = 0; pp < seg_rows[s] / 2; pp++) {
           size_t ra = 2 * pp, rbw = 2 * pp + 1;
@@ -1037,22 +1037,23 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
             ra = (pp / half) * (size_t)c.head_dim + pp % half;
             rbw = ra + half;
           }
-          memcpy(&buf[(at + 2 * pp) * rb], raws[s] + ra * rb, rb);
-          memcpy(&buf[(at + 2 * pp + 1) * rb], raws[s] + rbw * rb, rb);
+          rows.push_back(raws[s] + ra * rb);
+          rows.push_back(raws[s] + rbw * rb);
         }
-        at += seg_rows[s];
       }
-      part.seg_start[part.nseg] = (int)at;
+      part.seg_start[part.nseg] = (int)rows.size();
       L.qkv.push_back(part);
-      if ((rc = upload_stream(m.get(), types[s0], total_rows, dim, buf.data(), &L.qkv.back().sw))) return rc;
+      if ((rc = upload_stream(m.get(), ws, types[s0], rows.size(), dim, [&rows](size_t r) { return rows[r]; },
+                              &L.qkv.back().sw)))
+        return rc;
       s0 = s1;
     }
     uint32_t ty;
     const uint8_t* raw;
-    std::vector<uint8_t> cols;
+    RowSrc cols;
     if ((rc = linear_raw(g, p + "attn_output.weight", dim, q_dim, &ty, &raw, precision)) ||
-        (rc = slice_cols(ty, dim, q_dim, raw, rank * q_dim_l, (rank + 1) * q_dim_l, cols)) ||
-        (rc = upload_stream(m.get(), ty, dim, q_dim_l, cols.data(), &L.wo)))
+        (rc = col_rows(ty, q_dim, raw, rank * q_dim_l, (rank + 1) * q_dim_l, &cols)) ||
+        (rc = upload_stream(m.get(), ws, ty, dim, q_dim_l, cols, &L.wo)))
       return rc;
     // gate|up: interleave rows (gate j, up j) when both have one type
     uint32_t t1, t3;
@@ -1064,21 +1065,17 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
     r3 += (size_t)rank * hid_l * gguf_row_bytes(t3, dim);
     if (t1 == t3) {
       const size_t rb = gguf_row_bytes(t1, dim);
-      std::vector<uint8_t> buf(2 * hid_l * rb);
-      for (size_t j = 0; j < hid_l; j++) {
-        memcpy(&buf[(2 * j) * rb], r1 + j * rb, rb);
-        memcpy(&buf[(2 * j + 1) * rb], r3 + j * rb, rb);
-      }
       L.fused_gu = true;
-      if ((rc = upload_stream(m.get(), t1, 2 * hid_l, dim, buf.data(), &L.gu))) return rc;
+      const RowSrc gu = [r1, r3, rb](size_t r) { return (r & 1 ? r3 : r1) + (r >> 1) * rb; };
+      if ((rc = upload_stream(m.get(), ws, t1, 2 * hid_l, dim, gu, &L.gu))) return rc;
     } else {
-      if ((rc = upload_stream(m.get(), t1, hid_l, dim, r1, &L.w1)) ||
-          (rc = upload_stream(m.get(), t3, hid_l, dim, r3, &L.w3)))
+      if ((rc = upload_stream(m.get(), ws, t1, hid_l, dim, linear_rows(r1, gguf_row_bytes(t1, dim)), &L.w1)) ||
+          (rc = upload_stream(m.get(), ws, t3, hid_l, dim, linear_rows(r3, gguf_row_bytes(t3, dim)), &L.w3)))
         return rc;
     }
     if ((rc = linear_raw(g, p + "ffn_down.weight", dim, hid, &ty, &raw, precision)) ||
-        (rc = slice_cols(ty, dim, hid, raw, rank * hid_l, (rank + 1) * hid_l, cols)) ||
-        (rc = upload_stream(m.get(), ty, dim, hid_l, cols.data(), &L.w2)))
+        (rc = col_rows(ty, hid, raw, rank * hid_l, (rank + 1) * hid_l, &cols)) ||
+        (rc = upload_stream(m.get(), ws, ty, dim, hid_l, cols, &L.w2)))
       return rc;
     // gguf.rs:388-394: each bias optional
     const char* bn[3] = {"attn_q.bias", "attn_k.bias", "attn_v.bias"};
@@ -1101,7 +1098,9 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
     const uint8_t* raw;
     if ((rc = linear_raw(g, "output.weight", (size_t)c.vocab_size, dim, &ty, &raw, precision))) return rc;
     raw += (size_t)m->vocab_off * gguf_row_bytes(ty, dim);  // this rank's vocabulary rows
-    if ((rc = upload_stream(m.get(), ty, (size_t)m->vocab_l, dim, raw, &m->head))) return rc;
+    if ((rc = upload_stream(m.get(), ws, ty, (size_t)m->vocab_l, dim, linear_rows(raw, gguf_row_bytes(ty, dim)),
+                            &m->head)))
+      return rc;
   } else {
     // tied classifier (gguf.rs:425-437, checkpoint.rs:239-248): a packed table
     // (Q4_0 / Q4_K / Q6_K) runs the quantized kernel over the table itself; a
@@ -1117,7 +1116,8 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
       if (world == 1) {
         m->head.w = m->emb;
         m->head.owns = false;
-      } else if ((rc = upload_stream(m.get(), t->type, (size_t)m->vocab_l, dim, raw, &m->head))) {
+      } else if ((rc = upload_stream(m.get(), ws, t->type, (size_t)m->vocab_l, dim,
+                                     linear_rows(raw, gguf_row_bytes(t->type, dim)), &m->head))) {
         return rc;
       }
     } else {
@@ -1127,10 +1127,13 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
       } else {
         NEED(world == 1, "the dense f32 tied classifier runs on a single-GPU model");
         NEED(dim * 8 * 4 <= 200 * 1024, "dense f32 classifier: dim %zu too wide for the f32 GEMV", dim);
-        if ((rc = upload_weight(ctx, T_F32, (size_t)m->vocab_l, dim, f.data(), &m->head.w))) return rc;
+        if ((rc = ws.upload(T_F32, (size_t)m->vocab_l, dim, linear_rows(reinterpret_cast<const uint8_t*>(f.data()), dim * 4),
+                            &m->head.w)))
+          return rc;
       }
     }
   }
+  if ((rc = ws.finish())) return rc;
   // weight bytes on the device
   size_t wb = m->emb.bytes + (m->head.owns ? m->head.w.bytes : 0);
   for (auto& L : m->layers) {
