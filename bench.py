@@ -48,6 +48,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "decode tok/s at batch 1"
 UNIT = "tok/s"
+SAMPLE_TEMP, SAMPLE_SEED = 0.8, 2024  # the sampled-loop line: Sampler::new(0.8, 2024)
 
 
 def parse():
@@ -829,7 +830,7 @@ def prana_arm(args):
     c = model.config
     kv_dim = c.kv_dim()
     kv_l = model.local_kv_dim()  # this rank's kv heads
-    cap = args.ctx + 2 * (args.warmup + args.steps) + 16
+    cap = args.ctx + 3 * (args.warmup + args.steps) + 16
     kv = pm.KvCache(model, cap)
     for layer in range(c.n_layers):
         for is_v in (False, True):
@@ -883,6 +884,24 @@ def prana_arm(args):
         t = torch.tensor([ms, ms_e2e], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, ms_e2e = float(t[0]), float(t[1])
+    # ---- the device loop with temperature sampling (Sampler::sample on the device)
+    sampled = None
+    if world == 1:
+        from prana_b200.sampler import Sampler
+
+        loop.begin(int(tok), pos, sampler=Sampler(SAMPLE_TEMP, SAMPLE_SEED))
+        loop.run(args.warmup)
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        loop.run(args.steps)
+        g1.record(stream)
+        barrier()
+        ms_s = g0.elapsed_time(g1) / args.steps
+        pos += args.warmup + args.steps
+        sampled = {"value": round(1000.0 / ms_s, 3), "unit": UNIT, "ms_per_step": round(ms_s, 4),
+                   "temperature": SAMPLE_TEMP, "seed": SAMPLE_SEED,
+                   "path": "device decode loop, Sampler::sample on the device (logits stay in HBM)"}
     batch = batch_decode(torch, model, args, stream) if world == 1 and args.batch_seqs > 0 else None
     roof = gemv_roofline(torch, peak) if rank == 0 else None
     cpu = cpu8 = parity = None
@@ -931,7 +950,7 @@ def prana_arm(args):
             "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": round(step_gbs, 1),
                               "frac": round(step_gbs / peak, 4)},
             "cpu_baseline": cpu, "cpu_baseline_default_threads": cpu8, "parity": parity,
-            "batch_decode": batch, "clocks": clk,
+            "sampled_decode": sampled, "batch_decode": batch, "clocks": clk,
             "gpu_launches": launches_per_step(spec, world, model.peer_exchange) * args.steps,
             "load_s": round(t_load, 1),
             "configs": suite or None,

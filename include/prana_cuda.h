@@ -331,7 +331,7 @@ int prana_detokenize(const prana_tokenizer *t, uint32_t prev, uint32_t token, ch
 /* Tokenize::is_stop: the EOS or BOS id */
 int prana_tokenizer_is_stop(const prana_tokenizer *t, uint32_t token, int *out);
 
-/* ---- sampling (host only) ----
+/* ---- sampling ----
  * Sampler::new (sampler.rs:13-20): greedy when temperature <= 0, else temperature
  * sampling driven by xorshift64* from seed (0 reads as 1) */
 typedef struct prana_sampler prana_sampler;
@@ -342,6 +342,22 @@ int prana_sampler_free(prana_sampler *s);
 int prana_sample(prana_sampler *s, const float *logits, size_t n, uint32_t *token);
 /* XorShift::next_f32 (sampler.rs:67-70): the stream's next uniform draw in [0, 1) */
 int prana_sampler_next_f32(prana_sampler *s, float *out);
+/* Sampler::sample on the device over n device logits (n <= 393216), writing the
+ * token to device memory on the context stream: a greedy sampler takes the first
+ * maximum; otherwise the kernel takes the sampler's next draw, which the host
+ * stream skips over.  The cumulative probabilities are summed in f64, so the id
+ * is prana_sample's except where the draw lies within the reference's
+ * sequential f32 rounding of a bucket boundary. */
+int prana_sample_logits(prana_ctx *ctx, const float *logits, size_t n, prana_sampler *s, uint32_t *token);
+/* prana_decode_begin whose loop samples each next token on the device with the
+ * sampler's temperature and stream (the sampler itself is not advanced; greedy
+ * or NULL: prana_decode_begin) */
+int prana_decode_begin_sampled(prana_model *m, prana_kv *kv, uint32_t token, size_t pos, const prana_sampler *s);
+/* generate (infer.rs:696-771) with a Sampler: every sampled position draws on the
+ * device, and s is left advanced by the draws the reference's loop makes (one
+ * per sampled position, up to and including a stop token) */
+int prana_generate_sampled(prana_model *m, const uint32_t *prompt, size_t p, size_t steps, int64_t stop_id,
+                           prana_sampler *s, uint32_t *out, size_t *n_out);
 
 #ifdef __cplusplus
 }

@@ -345,6 +345,45 @@ void or_softmax(const float *x, size_t n, float *out) {
   for (size_t i = 0; i < n; i++) out[i] *= inv;
 }
 
+/* ---- sampler (sampler.rs) ---- */
+
+/* XorShift::next_u64 (sampler.rs:59-66): xorshift64* */
+uint64_t or_xorshift_next(uint64_t *state) {
+  uint64_t x = *state;
+  x ^= x >> 12;
+  x ^= x << 25;
+  x ^= x >> 27;
+  *state = x;
+  return x * 0x2545F4914F6CDD1DULL;
+}
+
+/* XorShift::next_f32 (sampler.rs:67-70): the top 24 bits over 2^24 */
+float or_xorshift_f32(uint64_t *state) { return (float)(or_xorshift_next(state) >> 40) / (float)(1ULL << 24); }
+
+/* Sampler::sample (sampler.rs:22-37): greedy (argmax) when temp <= 0, else
+ * softmax(logits / temp), one draw r, and the first i whose running
+ * r -= p[i] reaches <= 0 (the last index when round-off never gets there).
+ * probs (may be NULL) receives the softmax; *r_out (may be NULL) the draw. */
+uint32_t or_sample(const float *logits, size_t n, float temp, uint64_t *state, float *probs, float *r_out) {
+  if (temp <= 0.0f) return or_argmax(logits, n); /* a NaN temperature samples */
+  float *p = malloc(sizeof(float) * n);
+  for (size_t i = 0; i < n; i++) p[i] = logits[i] / temp;
+  or_softmax(p, n, p);
+  float r = or_xorshift_f32(state);
+  if (r_out) *r_out = r;
+  if (probs) memcpy(probs, p, sizeof(float) * n);
+  uint32_t tok = (uint32_t)(n - 1);
+  for (size_t i = 0; i < n; i++) {
+    r -= p[i];
+    if (r <= 0.0f) {
+      tok = (uint32_t)i;
+      break;
+    }
+  }
+  free(p);
+  return tok;
+}
+
 /* ---- RoPE (attention.rs:59-121) ---- */
 
 void or_rope_interleaved(float *x, size_t n, size_t pos, size_t hd, float theta) {

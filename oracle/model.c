@@ -834,9 +834,10 @@ size_t or_batch_trace(const or_model *m, or_kv *kv, const uint32_t *tokens, size
 }
 
 /* infer.rs:696-771 generate, greedy, over ids */
-size_t or_generate(const or_model *m, const uint32_t *prompt, size_t p, size_t steps, int64_t stop_id,
-                   uint32_t *out) {
+size_t or_generate_sampled(const or_model *m, const uint32_t *prompt, size_t p, size_t steps, int64_t stop_id,
+                           float temp, uint64_t *state, uint32_t *out) {
   if (p == 0) return 0;
+  if (*state == 0) *state = 1; /* XorShift::new: seed.max(1) */
   size_t max_pos = m->c.seq_len < p + steps ? m->c.seq_len : p + steps;
   or_kv *kv = or_kv_create(m, max_pos);
   float *lg = malloc(sizeof(float) * m->c.vocab_size);
@@ -851,7 +852,7 @@ size_t or_generate(const or_model *m, const uint32_t *prompt, size_t p, size_t s
     int need = pos + 1 >= p && pos + 1 < max_pos;
     or_forward(m, kv, token, pos, need ? lg : NULL);
     if (pos + 1 >= max_pos) break;
-    uint32_t next = pos + 1 < p ? prompt[pos + 1] : or_argmax(lg, m->c.vocab_size);
+    uint32_t next = pos + 1 < p ? prompt[pos + 1] : or_sample(lg, m->c.vocab_size, temp, state, NULL, NULL);
     if (pos + 1 >= p) {
       if (stop_id >= 0 && next == (uint32_t)stop_id) break;
       out[generated++] = next;
@@ -861,6 +862,12 @@ size_t or_generate(const or_model *m, const uint32_t *prompt, size_t p, size_t s
   free(lg);
   or_kv_free(kv);
   return generated;
+}
+
+size_t or_generate(const or_model *m, const uint32_t *prompt, size_t p, size_t steps, int64_t stop_id,
+                   uint32_t *out) {
+  uint64_t state = 1;
+  return or_generate_sampled(m, prompt, p, steps, stop_id, 0.0f, &state, out);
 }
 
 /* infer.rs:581-690 generate_speculative */

@@ -83,6 +83,10 @@ def lib() -> C.CDLL:
             "or_attention_verify": ([P, P, P, SZ, SZ, SZ, SZ, SZ, P], None),
             "or_attention": ([P, P, P, SZ, SZ, SZ, SZ, P], None),
             "or_argmax": ([P, SZ], C.c_uint32),
+            "or_xorshift_next": ([P], C.c_uint64),
+            "or_xorshift_f32": ([P], C.c_float),
+            "or_sample": ([P, SZ, C.c_float, P, P, P], C.c_uint32),
+            "or_generate_sampled": ([P, P, SZ, SZ, C.c_int64, C.c_float, P, P], SZ),
             "or_model_load": ([C.c_char_p, C.c_int, C.c_char_p, SZ], P),
             "or_model_load_ex": ([C.c_char_p, C.c_int, C.c_int, C.c_char_p, SZ], P),
             "or_model_free": ([P], None),
@@ -134,6 +138,28 @@ def quantize_acts(a: np.ndarray):
 def quantize_acts_rows(a: np.ndarray):
     rows = [quantize_acts(r) for r in np.asarray(a, np.float32).reshape(-1, a.shape[-1])]
     return (np.stack([r[0] for r in rows]), np.stack([r[1] for r in rows]), np.stack([r[2] for r in rows]))
+
+
+class OSampler:
+    """Sampler (sampler.rs:6-37): greedy when temperature <= 0, else temperature
+    sampling over the xorshift64* stream seeded with seed (0 reads as 1)."""
+
+    def __init__(self, temperature: float, seed: int):
+        self.temperature = float(temperature)
+        self.state = np.array([max(int(seed), 1)], np.uint64)
+
+    def next_f32(self) -> float:
+        return float(lib().or_xorshift_f32(ptr(self.state)))
+
+    def sample(self, logits: np.ndarray):
+        """(token, softmax probabilities or None, draw r or None)"""
+        lg = np.ascontiguousarray(logits, np.float32)
+        greedy = self.temperature <= 0.0
+        probs = None if greedy else np.empty(lg.size, np.float32)
+        r = np.zeros(1, np.float32)
+        tok = lib().or_sample(ptr(lg), lg.size, self.temperature, ptr(self.state),
+                              None if greedy else ptr(probs), ptr(r))
+        return int(tok), probs, (None if greedy else float(r[0]))
 
 
 class OMatrix:
@@ -316,6 +342,14 @@ class OModel:
         out = np.empty(max(steps, 1), np.uint32)
         n = lib().or_generate(self.h, ptr(p), p.size, steps, stop_id, ptr(out))
         return out[:n].copy()
+
+    def generate_sampled(self, prompt, steps: int, temperature: float, seed: int, stop_id: int = -1):
+        """generate with Sampler::new(temperature, seed); returns (tokens, xorshift state after the last draw)."""
+        p = np.ascontiguousarray(prompt, np.uint32)
+        out = np.empty(max(steps, 1), np.uint32)
+        st = np.array([seed], np.uint64)
+        n = lib().or_generate_sampled(self.h, ptr(p), p.size, steps, stop_id, temperature, ptr(st), ptr(out))
+        return out[:n].copy(), int(st[0])
 
     def generate_speculative(self, draft: "OModel", prompt, steps: int, k: int, stop_id: int = -1):
         p = np.ascontiguousarray(prompt, np.uint32)

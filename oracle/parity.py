@@ -194,3 +194,29 @@ def forced_batch(om, okv, gm, gkv, tokens, pos0: int, prefill: bool, flips: Flip
     flips.check_kv(kv_g, kv_o, kv_v, where, c.n_kv_heads * c.head_dim)
     check_trace(c, q_g, s_g, q_o, s_o, v_o, flips, where, rows=n, final=not prefill)
     return lg_g, lg_o
+
+
+# ---- temperature sampling (sampler.rs:22-37) ----
+# The reference subtracts the f32 probabilities from the draw r one at a time;
+# the device sums them in f64.  Where the two pick different ids, r must lie at
+# every bucket boundary between them within the reference's own rounding of its
+# running value there (measured) plus SAMPLE_TOL, which covers the device's
+# softmax (CUDA expf, an f64 sum before the f32 1 / sum) on identical logits.
+SAMPLE_TOL = 1e-5
+
+
+def sample_boundary_gap(probs, r: float, a: int, b: int) -> float:
+    """Largest excess over the allowed tolerance of |r - C(k)| for k in [a, b),
+    where C is the exact cumulative of the oracle's f32 probabilities; <= 0
+    means every boundary between ids a and b is within tolerance of r."""
+    p = np.asarray(probs, np.float32)
+    run = np.float32(r)
+    worst = -np.inf
+    exact = 0.0
+    for k in range(b):
+        run = np.float32(run - p[k])  # the reference's running value, f32
+        exact += float(p[k])
+        if k >= a:
+            seq_err = abs((float(r) - exact) - float(run))
+            worst = max(worst, abs(float(r) - exact) - seq_err - SAMPLE_TOL)
+    return worst

@@ -139,6 +139,13 @@ void or_attention(const float *q, const float *k, const float *v, size_t seq, si
                   size_t n_kv_heads, size_t head_dim, float *out);
 uint32_t or_argmax(const float *x, size_t n);
 
+/* ---- sampler (sampler.rs) ---- */
+uint64_t or_xorshift_next(uint64_t *state);
+float or_xorshift_f32(uint64_t *state);
+/* Sampler::sample: argmax when temp <= 0; probs / r_out (may be NULL) receive
+ * the softmax and the draw */
+uint32_t or_sample(const float *logits, size_t n, float temp, uint64_t *state, float *probs, float *r_out);
+
 /* ---- model (checkpoint.rs, gguf.rs:338-460, infer.rs) ---- */
 typedef struct or_model or_model;
 typedef struct or_config {
@@ -184,6 +191,11 @@ void or_forward_batch(const or_model *m, or_kv *kv, const uint32_t *tokens, size
  * stop_id < 0 disables the stop check. */
 size_t or_generate(const or_model *m, const uint32_t *prompt, size_t p, size_t steps,
                    int64_t stop_id, uint32_t *out_tokens);
+/* generate with Sampler::new(temp, seed) (infer.rs:696-771, sampler.rs:13-37):
+ * *state is the xorshift state (a zero seed reads as 1) and is left where the
+ * last draw put it */
+size_t or_generate_sampled(const or_model *m, const uint32_t *prompt, size_t p, size_t steps,
+                           int64_t stop_id, float temp, uint64_t *state, uint32_t *out_tokens);
 /* greedy speculative decode (infer.rs:581-690); stats[0]=proposed, stats[1]=accepted */
 size_t or_generate_speculative(const or_model *target, const or_model *draft,
                                const uint32_t *prompt, size_t p, size_t steps, size_t k,

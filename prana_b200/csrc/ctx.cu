@@ -8,6 +8,7 @@
 
 #include "comm.h"
 #include "host.h"
+#include "sampler.h"
 
 namespace prana {
 
@@ -592,6 +593,24 @@ int prana_argmax(prana_ctx* c, const float* x, size_t rows, size_t n, uint32_t* 
   if (!rows) return PRANA_OK;
   DevScope ds(c->device);
   PRANA_CK(launch_argmax(x, (int)rows, (int)n, out, c->stream));
+  return PRANA_OK;
+}
+
+int prana_sample_logits(prana_ctx* c, const float* logits, size_t n, prana_sampler* s, uint32_t* token) {
+  NEED(c && logits && s && token, "null argument");
+  NEED(n > 0, "sampling from empty logits");
+  NEED(n <= (size_t)sample_max_vocab(), "%zu logits exceed the device sampler's %d", n, sample_max_vocab());
+  DevScope ds(c->device);
+  if (s->greedy) {
+    PRANA_CK(launch_argmax(logits, 1, (int)n, token, c->stream));
+    return PRANA_OK;
+  }
+  void* p = nullptr;
+  if (int rc = ctx_scratch(c, sizeof(SampleState), &p)) return rc;
+  const SampleState h{s->state, s->temp, 0};
+  PRANA_CK(cudaMemcpyAsync(p, &h, sizeof h, cudaMemcpyHostToDevice, c->stream));
+  PRANA_CK(launch_sample(logits, (int)n, static_cast<SampleState*>(p), token, nullptr, c->stream));
+  s->next_u64();  // the kernel took one draw of the stream
   return PRANA_OK;
 }
 

@@ -177,6 +177,17 @@ cudaError_t launch_kv_write(__half* cache, size_t start, const float* src, size_
 cudaError_t launch_embed(const DevWeight& w, const uint32_t* toks, const int* tok_single, int m, float* x,
                          cudaStream_t st, bool pdl);
 cudaError_t launch_argmax(const float* x, int rows, int n, uint32_t* out, cudaStream_t st);
+// Sampler state the device advances: the xorshift64* word and the temperature
+struct SampleState {
+  unsigned long long rng;
+  float temp;
+  int pad;
+};
+// Sampler::sample over one row of n logits (temperature > 0 or NaN): one draw
+// from *state (advanced), the token to tok_out[0] and, when set, *tok_next
+cudaError_t launch_sample(const float* logits, int n, SampleState* state, uint32_t* tok_out, int* tok_next,
+                          cudaStream_t st);
+int sample_max_vocab();
 cudaError_t launch_block_dots(const DevWeight& w, int row, const int8_t* aq, const int32_t* asum, int32_t* out,
                               cudaStream_t st);
 cudaError_t launch_advance(int* tok, int* pos, uint32_t* ring, int ring_cap, int* ring_n, cudaStream_t st, bool pdl);

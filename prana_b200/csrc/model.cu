@@ -17,6 +17,7 @@
 
 #include "comm.h"
 #include "host.h"
+#include "sampler.h"
 
 namespace prana {
 
@@ -250,6 +251,7 @@ struct prana_model {
   unsigned* ctr = nullptr;    // ticket counter of the streaming kernels
   unsigned* err = nullptr;    // device error flag
   int* d_tokpos = nullptr;    // [token, pos] of the graph-driven step
+  SampleState* d_sample = nullptr;  // sampler state of the sampled decode loop
   int* h_io = nullptr;        // pinned mirror
   uint32_t* h_tok = nullptr;
   bool pdl = true;
@@ -281,8 +283,10 @@ struct prana_kv {
   int* ring_n = nullptr;
   cudaGraphExec_t g_step = nullptr;
   cudaGraphExec_t g_loop = nullptr;
+  cudaGraphExec_t g_loop_s = nullptr;  // the loop with Sampler::sample on the device
   size_t loop_pos = 0;  // host mirror of the device-loop position
   bool loop_active = false;
+  bool loop_sampled = false;
 };
 
 namespace {
@@ -829,14 +833,18 @@ int check_err(prana_model* m) {
   return PRANA_OK;
 }
 
-int capture(prana_model* m, prana_kv* kv, bool loop, cudaGraphExec_t* out) {
+int capture(prana_model* m, prana_kv* kv, bool loop, bool sampled, cudaGraphExec_t* out) {
   cudaStream_t st = m->ctx->own;
   for (int attempt = 0; attempt < 2; attempt++) {
     const bool pdl = m->pdl && attempt == 0;
     cudaGraph_t graph = nullptr;
     PRANA_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
     int rc = enqueue_rows(m, kv, *m->dec, 1, nullptr, m->d_tokpos, 0, m->d_tokpos + 1, MODE_CACHE, true, pdl, nullptr,
-                          !loop);
+                          !loop || sampled);
+    if (!rc && sampled) {  // the draw replaces the argmax as the next token
+      cudaError_t e = launch_sample(m->dec->logits, (int)m->cfg.vocab_size, m->d_sample, m->dec->tok_out, m->d_tokpos, st);
+      if (e != cudaSuccess) rc = fail(PRANA_E_CUDA, "sample launch: %s", cudaGetErrorString(e));
+    }
     if (!rc && loop) {
       cudaError_t e = launch_advance(m->d_tokpos, m->d_tokpos + 1, kv->ring, (int)kv->positions, kv->ring_n, st, pdl);
       if (e != cudaSuccess) rc = fail(PRANA_E_CUDA, "advance launch: %s", cudaGetErrorString(e));
@@ -860,13 +868,17 @@ int capture(prana_model* m, prana_kv* kv, bool loop, cudaGraphExec_t* out) {
   return fail(PRANA_E_CUDA, "decode graph capture failed");
 }
 
-int ensure_graphs(prana_model* m, prana_kv* kv, bool loop) {
+int ensure_graphs(prana_model* m, prana_kv* kv, bool loop, bool sampled = false) {
   if (!kv->g_step) {
-    int rc = capture(m, kv, false, &kv->g_step);
+    int rc = capture(m, kv, false, false, &kv->g_step);
     if (rc) return rc;
   }
-  if (loop && !kv->g_loop) {
-    int rc = capture(m, kv, true, &kv->g_loop);
+  if (loop && !sampled && !kv->g_loop) {
+    int rc = capture(m, kv, true, false, &kv->g_loop);
+    if (rc) return rc;
+  }
+  if (loop && sampled && !kv->g_loop_s) {
+    int rc = capture(m, kv, true, true, &kv->g_loop_s);
     if (rc) return rc;
   }
   return PRANA_OK;
@@ -880,6 +892,7 @@ void destroy_kv(prana_kv* kv) {
   cs.erase(std::remove(cs.begin(), cs.end(), kv), cs.end());
   if (kv->g_step) cudaGraphExecDestroy(kv->g_step);
   if (kv->g_loop) cudaGraphExecDestroy(kv->g_loop);
+  if (kv->g_loop_s) cudaGraphExecDestroy(kv->g_loop_s);
   prana_ctx* c = kv->m->ctx;
   dev_free(c, kv->k);
   dev_free(c, kv->v);
@@ -1159,6 +1172,7 @@ static int load_model(prana_ctx* ctx, const char* path, int world, int rank, con
   m->ctr = static_cast<unsigned*>(p);
   m->err = m->ctr + 4;
   m->d_tokpos = reinterpret_cast<int*>(static_cast<uint8_t*>(p) + 64);
+  m->d_sample = reinterpret_cast<SampleState*>(static_cast<uint8_t*>(p) + 128);
   PRANA_CK(cudaHostAlloc((void**)&m->h_io, 64, cudaHostAllocDefault));
   m->h_tok = reinterpret_cast<uint32_t*>(m->h_io + 4);
   if (world > 1) {
@@ -1580,31 +1594,49 @@ int prana_forward_multi_trace(prana_model* m, prana_kv* const* kvs, size_t n, co
   API_END
 }
 
-int prana_decode_begin(prana_model* m, prana_kv* kv, uint32_t token, size_t pos) {
+static int decode_begin(prana_model* m, prana_kv* kv, uint32_t token, size_t pos, const prana_sampler* smp) {
   API_BEGIN
   NEED(m && kv && kv->m == m, "null or mismatched argument");
   NEED(pos < kv->positions, "position beyond kv capacity");
   NEED(token < (uint64_t)m->cfg.vocab_size, "token out of vocabulary");
+  const bool sampled = smp && !smp->greedy;
+  NEED(!sampled || m->cfg.vocab_size <= sample_max_vocab(), "vocabulary of %lld exceeds the device sampler's %d",
+       (long long)m->cfg.vocab_size, sample_max_vocab());
   DevScope ds(m->ctx->device);
-  int rc = ensure_graphs(m, kv, true);
+  int rc = ensure_graphs(m, kv, true, sampled);
   if (rc) return rc;
   cudaStream_t st = m->ctx->own;
   m->h_io[0] = (int)token;
   m->h_io[1] = (int)pos;
   PRANA_CK(cudaMemcpyAsync(m->d_tokpos, m->h_io, 8, cudaMemcpyHostToDevice, st));
+  if (sampled) {
+    SampleState* h = reinterpret_cast<SampleState*>(m->h_io + 8);
+    *h = SampleState{smp->state, smp->temp, 0};
+    PRANA_CK(cudaMemcpyAsync(m->d_sample, h, sizeof(SampleState), cudaMemcpyHostToDevice, st));
+  }
   PRANA_CK(cudaMemsetAsync(kv->ring_n, 0, sizeof(int), st));
   PRANA_CK(cudaStreamSynchronize(st));
   kv->loop_pos = pos;
   kv->loop_active = true;
+  kv->loop_sampled = sampled;
   return PRANA_OK;
   API_END
+}
+
+int prana_decode_begin(prana_model* m, prana_kv* kv, uint32_t token, size_t pos) {
+  return decode_begin(m, kv, token, pos, nullptr);
+}
+
+int prana_decode_begin_sampled(prana_model* m, prana_kv* kv, uint32_t token, size_t pos, const prana_sampler* s) {
+  return decode_begin(m, kv, token, pos, s);
 }
 
 int prana_decode_run(prana_model* m, prana_kv* kv, size_t n_steps) {
   NEED(m && kv && kv->m == m && kv->loop_active, "decode loop not started");
   NEED(kv->loop_pos + n_steps <= kv->positions, "decode loop would pass kv capacity %zu", kv->positions);
   DevScope ds(m->ctx->device);
-  for (size_t i = 0; i < n_steps; i++) PRANA_CK(cudaGraphLaunch(kv->g_loop, m->ctx->own));
+  cudaGraphExec_t g = kv->loop_sampled ? kv->g_loop_s : kv->g_loop;
+  for (size_t i = 0; i < n_steps; i++) PRANA_CK(cudaGraphLaunch(g, m->ctx->own));
   kv->loop_pos += n_steps;
   return PRANA_OK;
 }
@@ -1621,8 +1653,8 @@ int prana_decode_tokens(prana_model* m, prana_kv* kv, uint32_t* out, size_t max,
   return check_err(m);
 }
 
-int prana_generate(prana_model* m, const uint32_t* prompt, size_t p, size_t steps, int64_t stop_id, uint32_t* out,
-                   size_t* n_out) {
+static int generate(prana_model* m, const uint32_t* prompt, size_t p, size_t steps, int64_t stop_id, prana_sampler* smp,
+                    uint32_t* out, size_t* n_out) {
   API_BEGIN
   NEED(m && prompt && n_out && (out || !steps), "null argument");
   NEED(p > 0, "prompt encoded to zero tokens");
@@ -1649,19 +1681,38 @@ int prana_generate(prana_model* m, const uint32_t* prompt, size_t p, size_t step
   if (pos + 1 < max_pos) {
     // every remaining position samples: run them on the device back to back
     const size_t n = max_pos - 1 - pos;
-    if ((rc = prana_decode_begin(m, kv, token, pos))) return rc;
+    if ((rc = decode_begin(m, kv, token, pos, smp))) return rc;
     if ((rc = prana_decode_run(m, kv, n))) return rc;
     std::vector<uint32_t> ids(n);
     size_t got = 0;
     if ((rc = prana_decode_tokens(m, kv, ids.data(), n, &got))) return rc;
+    size_t draws = got;  // Sampler::sample calls the reference's loop makes
     for (size_t i = 0; i < got && produced < steps; i++) {
-      if (stop_id >= 0 && ids[i] == (uint64_t)stop_id) break;
+      if (stop_id >= 0 && ids[i] == (uint64_t)stop_id) {
+        draws = i + 1;
+        break;
+      }
       out[produced++] = ids[i];
     }
+    // the caller's sampler continues where the reference's would: one draw per
+    // sampled position up to and including a stop token
+    if (smp && !smp->greedy)
+      for (size_t i = 0; i < draws; i++) smp->next_u64();
   }
   *n_out = produced;
   return PRANA_OK;
   API_END
+}
+
+int prana_generate(prana_model* m, const uint32_t* prompt, size_t p, size_t steps, int64_t stop_id, uint32_t* out,
+                   size_t* n_out) {
+  return generate(m, prompt, p, steps, stop_id, nullptr, out, n_out);
+}
+
+int prana_generate_sampled(prana_model* m, const uint32_t* prompt, size_t p, size_t steps, int64_t stop_id,
+                           prana_sampler* s, uint32_t* out, size_t* n_out) {
+  NEED(s, "null sampler");
+  return generate(m, prompt, p, steps, stop_id, s, out, n_out);
 }
 
 int prana_generate_speculative(prana_model* target, prana_model* draft, const uint32_t* prompt, size_t p,

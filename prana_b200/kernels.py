@@ -324,3 +324,15 @@ def argmax(logits: torch.Tensor) -> torch.Tensor:
     out = torch.empty(x2.shape[0], dtype=torch.int32, device=logits.device)
     call("prana_argmax", context(logits.device.index), _ptr(x2), x2.shape[0], x2.shape[1], _ptr(out))
     return out
+
+
+def sample(sampler, logits: torch.Tensor) -> torch.Tensor:
+    """Sampler::sample (sampler.rs:22-37) on the device over one row of f32
+    logits; returns the token as a one-element int32 device tensor and moves
+    the sampler's stream past the draw the kernel took."""
+    x = logits.contiguous().reshape(-1)
+    if x.dtype != torch.float32:
+        raise TypeError("logits must be float32")
+    out = torch.empty(1, dtype=torch.int32, device=logits.device)
+    call("prana_sample_logits", context(logits.device.index), _ptr(x), x.numel(), sampler.handle, _ptr(out))
+    return out

@@ -266,6 +266,18 @@ def generate(model: Model, prompt, steps: int, stop_id: int = -1) -> np.ndarray:
     return out[: n.value].copy()
 
 
+def generate_sampled(model: Model, prompt, steps: int, sampler, stop_id: int = -1) -> np.ndarray:
+    """generate (infer.rs:696-771) with a Sampler (prana_b200.sampler.Sampler):
+    each sampled position draws on the device; the sampler is left where the
+    reference's loop leaves it."""
+    p = _u32(prompt)
+    out = np.empty(max(steps, 1), dtype=np.uint32)
+    n = C.c_size_t()
+    call("prana_generate_sampled", model.handle, p.ctypes.data_as(C.c_void_p), p.size, steps, stop_id,
+         sampler.handle, out.ctypes.data_as(C.c_void_p), C.byref(n))
+    return out[: n.value].copy()
+
+
 def generate_speculative(target: Model, draft: Model, prompt, steps: int, k: int, stop_id: int = -1):
     """generate_speculative (infer.rs:581-690): returns (ids, (proposed, accepted))."""
     p = _u32(prompt)
@@ -278,14 +290,18 @@ def generate_speculative(target: Model, draft: Model, prompt, steps: int, k: int
 
 
 class DecodeLoop:
-    """Device-resident greedy decode: the per-token graph replays back to back
-    with the sampled id fed back on the device."""
+    """Device-resident decode: the per-token graph replays back to back with
+    the next id (greedy, or drawn by a sampler on the device) fed back on the
+    device."""
 
     def __init__(self, model: Model, cache: KvCache):
         self.model, self.cache = model, cache
 
-    def begin(self, token: int, pos: int) -> None:
-        call("prana_decode_begin", self.model.handle, self.cache.handle, token, pos)
+    def begin(self, token: int, pos: int, sampler=None) -> None:
+        if sampler is None:
+            call("prana_decode_begin", self.model.handle, self.cache.handle, token, pos)
+        else:
+            call("prana_decode_begin_sampled", self.model.handle, self.cache.handle, token, pos, sampler.handle)
 
     def run(self, n_steps: int) -> None:
         call("prana_decode_run", self.model.handle, self.cache.handle, n_steps)

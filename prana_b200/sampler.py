@@ -1,6 +1,7 @@
-"""Token sampling on the host (sampler.rs): greedy argmax, or temperature
-sampling with the reference's seeded xorshift64* stream.  Nothing here
-touches a GPU; the logits come from prana_b200.model.forward."""
+"""Token sampling (sampler.rs): greedy argmax, or temperature sampling with
+the reference's seeded xorshift64* stream.  Sampler.sample runs on host
+logits; the same sampler drives the device forms (prana_b200.kernels.sample,
+prana_b200.model.generate_sampled and DecodeLoop.begin(..., sampler=))."""
 from __future__ import annotations
 
 import ctypes as C
@@ -23,6 +24,10 @@ class Sampler:
         t = C.c_uint32()
         call("prana_sample", self._h, x.ctypes.data_as(C.c_void_p), x.size, C.byref(t))
         return t.value
+
+    @property
+    def handle(self):
+        return self._h
 
     def next_f32(self) -> float:
         """XorShift::next_f32: the stream's next uniform draw in [0, 1)."""

@@ -71,3 +71,21 @@ def test_nan_temperature_samples_like_the_reference():
     ref = XorShift(5)
     ref.next_f32()
     assert np.float32(s.next_f32()) == ref.next_f32()
+
+
+def test_oracle_sampler_matches_host_sampler():
+    """The oracle's or_sample (the checker of the device sampler) against the
+    host sampler, draw for draw, including non-finite rows."""
+    rng = np.random.default_rng(8)
+    rows = [(rng.standard_normal(5000) * 2).astype(np.float32),
+            np.where(np.arange(700) % 4 == 0, -np.inf, rng.standard_normal(700)).astype(np.float32)]
+    bad = rows[0].copy()
+    bad[17] = np.nan
+    rows.append(bad)
+    for logits in rows:
+        for temp, seed in [(0.8, 7), (1.2, 0)]:
+            s, o = Sampler(temp, seed), orc.OSampler(temp, seed)
+            for _ in range(50):
+                assert s.sample(logits) == o.sample(logits)[0]
+            assert s.next_f32() == o.next_f32()
+    assert orc.OSampler(0.0, 3).sample(np.array([1, 5, 5, 2], np.float32))[0] == 1
