@@ -197,19 +197,24 @@ def forced_batch(om, okv, gm, gkv, tokens, pos0: int, prefill: bool, flips: Flip
 
 
 # ---- temperature sampling (sampler.rs:22-37) ----
-# The reference subtracts the f32 probabilities from the draw r one at a time;
-# the device sums them in f64.  Where the two pick different ids, r must lie at
-# every bucket boundary between them within the reference's own rounding of its
-# running value there (measured) plus SAMPLE_TOL, which covers the device's
-# softmax (CUDA expf, an f64 sum before the f32 1 / sum) on identical logits.
-SAMPLE_TOL = 1e-5
+# The reference subtracts the f32 probabilities from the draw r one at a time
+# after summing the exps sequentially in f32; the device sums in f64.  Where
+# the two pick different ids, r must lie at every bucket boundary k between
+# them within what the reference's own arithmetic moves that boundary:
+#   - its running value r_k versus r - C(k) exactly (measured here), and
+#   - its sequential f32 sum of the exps, which scales every probability by
+#     sum(p) - 1 (measured here), plus 1e-6 relative for CUDA's expf (2 ulp)
+#     and the device's f64 sum rounded once to f32.
+SAMPLE_REL_TOL = 1e-6
 
 
-def sample_boundary_gap(probs, r: float, a: int, b: int) -> float:
-    """Largest excess over the allowed tolerance of |r - C(k)| for k in [a, b),
+def sample_boundary_gap(probs, r: float, a: int, b: int, tol: float | None = None) -> float:
+    """Largest excess over the allowed distance of |r - C(k)| for k in [a, b),
     where C is the exact cumulative of the oracle's f32 probabilities; <= 0
-    means every boundary between ids a and b is within tolerance of r."""
+    means every boundary between ids a and b is within tolerance of r.  tol
+    (absolute) replaces the softmax terms when the logits themselves differ."""
     p = np.asarray(probs, np.float32)
+    scale_err = abs(float(np.sum(p, dtype=np.float64)) - 1.0) + SAMPLE_REL_TOL
     run = np.float32(r)
     worst = -np.inf
     exact = 0.0
@@ -218,5 +223,6 @@ def sample_boundary_gap(probs, r: float, a: int, b: int) -> float:
         exact += float(p[k])
         if k >= a:
             seq_err = abs((float(r) - exact) - float(run))
-            worst = max(worst, abs(float(r) - exact) - seq_err - SAMPLE_TOL)
+            allowed = seq_err + (tol if tol is not None else scale_err * exact + 1e-9)
+            worst = max(worst, abs(float(r) - exact) - allowed)
     return worst

@@ -20,7 +20,7 @@ LIB = PKG / "_lib"
 ROOT = PKG.parent
 
 CUDA_SOURCES = ["kernels.cu", "attention.cu", "decode.cu", "ctx.cu", "model.cu", "noalloc.cu", "comm.cu", "qgemm.cu", "tokenizer.cpp", "sampler.cpp", "pool.cu", "loader.cu", "sample.cu"]
-CUDA_HEADERS = ["common.cuh", "gemv.cuh", "finish.cuh", "mbar.cuh", "comm.h", "internal.h", "host.h", "unicode_alpha.h", "sampler.h"]
+CUDA_HEADERS = ["common.cuh", "gemv.cuh", "finish.cuh", "mbar.cuh", "comm.h", "internal.h", "host.h", "unicode_alpha.h", "sampler.h", "tc.cuh"]
 NVCC_FLAGS = [
     "-O3",
     "-std=c++17",

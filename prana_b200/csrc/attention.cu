@@ -23,6 +23,7 @@
 
 #include "internal.h"
 #include "mbar.cuh"
+#include "tc.cuh"
 
 namespace prana {
 
@@ -251,14 +252,14 @@ __device__ __forceinline__ unsigned ticket_acq_rel(unsigned* counter) {
 // otherwise they are published as a partial and the last CTA of the kv head
 // to finish merges every split.  `smem_raw` is shared memory the caller no
 // longer needs (>= 3 x VH x n_splits floats), `red` >= 4 KB.
-template <int HD>
+template <int HD, int NTH = AD_THREADS>
 __device__ __forceinline__ void attn_finish(const AttnArgs& a, int kvh, int split, int row0, int VH, int group,
                                             const float* o_s, const float* m_run, float* l_run, uint8_t* smem_raw,
                                             float* red) {
   const int tid = threadIdx.x, lane = tid & 31, wi = tid >> 5;
   const int q_stride = a.n_heads * HD;
   if (a.n_splits == 1) {
-    for (int e = tid; e < VH * HD; e += AD_THREADS) {
+    for (int e = tid; e < VH * HD; e += NTH) {
       const int vh = e / HD, d = e - vh * HD;
       const int row = vh / group, head = kvh * group + vh % group;
       a.out[(size_t)(row0 + row) * q_stride + head * HD + d] = o_s[e] / l_run[vh];
@@ -267,9 +268,9 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int kvh, int spli
   }
   // ---- publish this split's (max, sum, o); the last split CTA of the kv head merges
   const size_t base = ((size_t)kvh * a.n_splits + split) * VH;
-  for (int vh = tid; vh < VH; vh += AD_THREADS)
+  for (int vh = tid; vh < VH; vh += NTH)
     reinterpret_cast<float2*>(a.part_ml)[base + vh] = make_float2(m_run[vh], l_run[vh]);
-  for (int e = tid; e < VH * HD / 4; e += AD_THREADS)
+  for (int e = tid; e < VH * HD / 4; e += NTH)
     reinterpret_cast<float4*>(a.part_o + base * HD)[e] = reinterpret_cast<const float4*>(o_s)[e];
   __shared__ unsigned ticket;
   __syncthreads();
@@ -281,13 +282,13 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int kvh, int spli
   const int NS = a.n_splits;
   float2* ml_s = reinterpret_cast<float2*>(smem_raw);  // [VH][NS]
   const size_t hb = (size_t)kvh * NS * VH;  // this kv head's first partial
-  for (int i = tid; i < VH * NS; i += AD_THREADS) {
+  for (int i = tid; i < VH * NS; i += NTH) {
     const int vh = i / NS, s = i - vh * NS;
     ml_s[i] = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + hb + (size_t)s * VH + vh);
   }
   __syncthreads();
   float* w_s = reinterpret_cast<float*>(ml_s + VH * NS);  // [VH][NS]
-  for (int vh = wi; vh < VH; vh += AD_THREADS / 32) {
+  for (int vh = wi; vh < VH; vh += NTH / 32) {
     float mx = -INFINITY;
     for (int s = lane; s < NS; s += 32) mx = fmaxf(mx, ml_s[vh * NS + s].x);
     mx = warp_max(mx);
@@ -305,10 +306,10 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int kvh, int spli
   // weighted sum of the partial outputs: item = 4 dims of one head; the
   // splits of an item are shared by `nsub` threads so all loads go out at once
   const int items = VH * HD / 4;
-  const int nsub = items >= AD_THREADS ? 1 : AD_THREADS / items;
+  const int nsub = items >= NTH ? 1 : NTH / items;
   const int sub = tid / items < nsub ? tid / items : nsub;  // == nsub: idle
   float4* red4 = reinterpret_cast<float4*>(red);  // [nsub][items] when nsub > 1
-  for (int it = tid % items; sub < nsub && it < items; it += (nsub > 1 ? items : AD_THREADS)) {
+  for (int it = tid % items; sub < nsub && it < items; it += (nsub > 1 ? items : NTH)) {
     const int vh = (it * 4) / HD;
     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll 8
@@ -331,7 +332,7 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int kvh, int spli
   }
   if (nsub > 1) {
     __syncthreads();
-    for (int it = tid; it < items; it += AD_THREADS) {
+    for (int it = tid; it < items; it += NTH) {
       const int vh = (it * 4) / HD, d = it * 4 - vh * HD, row = vh / group, head = kvh * group + vh % group;
       float4 acc = red4[it];
       for (int s = 1; s < nsub; s++) {
@@ -1146,6 +1147,455 @@ __global__ void __launch_bounds__(256, 2) attn_decode_cluster(const __grid_const
   if (tid == 0) counters[kvh] = 0u;
 }
 
+// ---------------------------------------------------------------- tcgen05 decode / verify
+// The same attention on the 5th-generation tensor cores, one tile of 128
+// positions at a time, warp-specialized:
+//   warp 4 (one lane)   TMA: K and V boxes of each tile into a 3-stage ring,
+//                       the tiles before pos0 ahead of the programmatic wait
+//   warp 5 (one lane)   MMAs: S = K . [q_hi | q_lo]^T (M = 128 positions,
+//                       N = 32: the hi and lo halves side by side) into one of
+//                       two TMEM buffers as soon as a tile lands, and
+//                       O^T = V^T . [P_hi | P_lo] (M = 128 dims, V read
+//                       MN-major straight from its TMA box) once P is written
+//   warps 0-3           one thread per position: scores = hi + lo columns,
+//                       masked and scaled, exp against a running reference
+//                       max that moves only when a score passes it by more
+//                       than 8 (then the tile's exact max, and a rescale);
+//                       P to shared memory as f16 hi / lo; then one thread per
+//                       dim folds O_hi + O_lo of the previous tile into its
+//                       registers.  Per-thread sums of P meet once at the end.
+// q and P enter as f16 hi + lo pairs (each product carries ~22 bits of the
+// f32 operand; K and V are f16 already); accumulation is f32.  The n_splits
+// position ranges of a kv head meet as in attn_finish.
+constexpr int TC_C = 128;
+constexpr int TC_THREADS = 192;   // warps 0-3 softmax, 4 TMA, 5 MMA
+constexpr int TC_COLS = 128;      // TMEM: S buffers [0, 64), O buffers [64, 128)
+constexpr float TC_TAU = 8.0f;    // largest exponent before the reference max moves
+
+template <int HD, int NS>
+struct TcSmem {
+  static constexpr int NB = HD / AC_BOX;                   // 64-dim boxes per K (or V) row
+  static constexpr size_t BOX = (size_t)TC_C * AC_BOX * 2;  // 16 KB
+  static constexpr size_t STAGE = 2 * NB * BOX;             // K boxes, then V boxes
+  static constexpr size_t OP = 32 * 128 * 2;                // a 32-row x 128-value f16 operand tile
+  static constexpr size_t OFF_Q = NS * STAGE;
+  static constexpr size_t OFF_P = OFF_Q + OP;               // two P tiles
+  static constexpr size_t OFF_RED = OFF_P + 2 * OP;         // [4 warps][16] floats
+  static constexpr size_t bytes = 1024 + OFF_RED + 4 * 16 * sizeof(float) + 64;
+  static_assert(sizeof(float) * 16 * HD <= STAGE, "o staging");
+};
+
+// byte offset of element (row r < 32, column k < 128) of a K-major f16
+// operand tile: 128-byte swizzle atoms of 64 columns x 32 rows, 4 KB apart
+__device__ __forceinline__ int op_off(int r, int k) {
+  return (k >> 6) * 4096 + (r >> 3) * 1024 + (r & 7) * 128 + ((((k & 63) >> 3) ^ (r & 7)) << 4) + (k & 7) * 2;
+}
+// f16 instruction descriptor: f32 accumulate, M = 128, N = n; A MN-major when `a_mn`
+constexpr uint32_t f16_idesc(bool a_mn, int n) {
+  return (1u << 4) | ((a_mn ? 1u : 0u) << 15) | ((uint32_t)(n >> 3) << 17) | ((128u >> 4) << 24);
+}
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t* r) {
+  tc_ld16(taddr, r);
+  tc_ld16(taddr + 16, r + 16);
+}
+// Bounded wait that also gives up once another role of the CTA has.
+__device__ __forceinline__ bool twait(uint64_t* bar, uint32_t phase, volatile int* abort) {
+  for (uint32_t i = 0; i < kMbarPolls; i++) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if ((i & 255) == 255 && *abort) return false;
+  }
+  *abort = 1;
+  return false;
+}
+// named barrier of the four softmax warps; the OR of `pred` over them
+__device__ __forceinline__ void sm_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ bool sm_any(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)pred)
+      : "memory");
+  return r != 0;
+}
+
+// The n_splits partials of one kv head (and sequence) of attn_decode_tc meet
+// here, in the kernel launched right behind it: the (max, sum) pairs by plain
+// loads while one bulk copy brings the o rows (contiguous per kv head) into
+// shared memory when they fit, then attn_finish's arithmetic.  One thread
+// per dim.
+constexpr size_t TC_MERGE_SMEM = 160 * 1024;
+template <int HD>
+__global__ void __launch_bounds__(HD) attn_merge_tc(const __grid_constant__ AttnArgs a, int row0, int n_rows) {
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float l_s[16];
+  const int kvh = blockIdx.x, z = blockIdx.y, tid = threadIdx.x, lane = tid & 31, wi = tid >> 5;
+  const int group = a.n_heads / a.n_kv, VH = n_rows * group, NS = a.n_splits;
+  const int q_stride = a.n_heads * HD;
+  const AttnSeq* sq = a.seqs ? a.seqs + z : nullptr;
+  const float* part_ml = sq ? sq->part_ml : a.part_ml;
+  const float* part_o = sq ? sq->part_o : a.part_o;
+  float* out = a.out + (sq ? (size_t)z * q_stride : 0);
+  const size_t hb = (size_t)kvh * NS * VH;  // this kv head's first partial
+  const size_t o_bytes = (size_t)NS * VH * HD * 4;
+  float* w_s = reinterpret_cast<float*>(smem_dyn);  // [VH][NS]
+  float* po = w_s + ((VH * NS + 3) & ~3);           // [NS][VH][HD] when it fits
+  const bool bulk = (size_t)((VH * NS + 3) & ~3) * 4 + o_bytes <= TC_MERGE_SMEM;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_wait();  // the attention grid has finished and its partials are visible
+  pdl_trigger();
+  if (bulk && tid == 0) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    mbar_arrive_expect_tx(&bar, (uint32_t)o_bytes);
+    bulk_g2s(po, part_o + hb * HD, (uint32_t)o_bytes, &bar);
+  }
+  // (max, sum) of every split -> weights exp(m_s - max) and the total
+  for (int vh = wi; vh < VH; vh += HD / 32) {
+    float mx = -INFINITY;
+    for (int s = lane; s < NS; s += 32) mx = fmaxf(mx, __ldcg(reinterpret_cast<const float2*>(part_ml) + hb + (size_t)s * VH + vh).x);
+    mx = warp_max(mx);
+    float lsum = 0.0f;
+    for (int s = lane; s < NS; s += 32) {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(part_ml) + hb + (size_t)s * VH + vh);
+      const float w = v.x == -INFINITY ? 0.0f : expf(v.x - mx);
+      w_s[vh * NS + s] = w;
+      lsum = fmaf(v.y, w, lsum);
+    }
+    lsum = warp_sum(lsum);
+    if (lane == 0) l_s[vh] = lsum;
+  }
+  if (bulk && !mbar_wait(&bar, 0) && a.err) atomicExch(a.err, ERR_TIMEOUT);
+  __syncthreads();
+  for (int vh = 0; vh < VH; vh++) {
+    float acc = 0.0f;
+    if (bulk) {
+      for (int s = 0; s < NS; s++) acc = fmaf(po[((size_t)s * VH + vh) * HD + tid], w_s[vh * NS + s], acc);
+    } else {
+#pragma unroll 8
+      for (int s = 0; s < NS; s++) acc = fmaf(__ldcg(part_o + (hb + (size_t)s * VH + vh) * HD + tid), w_s[vh * NS + s], acc);
+    }
+    const int row = vh / group, head = kvh * group + vh % group;
+    out[(size_t)(row0 + row) * q_stride + head * HD + tid] = acc / l_s[vh];
+  }
+}
+
+// NQ: virtual-head columns of each half (8 when VH <= 8, else 16); NS: K/V stages
+template <int HD, int NQ, int NS>
+__global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_constant__ AttnArgs a, int row0, int n_rows) {
+  using S = TcSmem<HD, NS>;
+  constexpr int TC_NS = NS;
+  constexpr int NB = S::NB, KSTEPS = HD / 16, PSTEPS = TC_C / 16;
+  constexpr uint32_t IDESC_S = f16_idesc(false, 2 * NQ), IDESC_O = f16_idesc(true, 2 * NQ);
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~(uintptr_t)1023);
+  uint8_t* q_t = base + S::OFF_Q;
+  uint8_t* p_t = base + S::OFF_P;
+  float* red = reinterpret_cast<float*>(base + S::OFF_RED);  // [4][16]
+  // full[3] stage_free[3] s_full[2] s_free[2] p_full[2] o_full[2] o_free[2] q_ready mma_done
+  __shared__ __align__(8) uint64_t bars[18];
+  uint64_t* full = bars;
+  uint64_t* stage_free = bars + 3;
+  uint64_t* s_full = bars + 6;
+  uint64_t* s_free = bars + 8;
+  uint64_t* p_full = bars + 10;
+  uint64_t* o_full = bars + 12;
+  uint64_t* o_free = bars + 14;
+  uint64_t* q_ready = bars + 16;
+  uint64_t* mma_done = bars + 17;
+  __shared__ uint32_t tmem_s;
+  __shared__ int s_abort;
+  volatile int* abort = &s_abort;
+
+  const int group = a.n_heads / a.n_kv, VH = n_rows * group;  // VH <= NQ
+  const int split = blockIdx.x, kvh = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, wi = tid >> 5;
+  const int q_stride = a.n_heads * HD;
+  const float scale = 1.0f / sqrtf((float)HD);
+  const AttnSeq* sq = a.seqs ? a.seqs + blockIdx.z : nullptr;
+  const CUtensorMap* tm_k = sq ? &sq->tm_k : &a.tm_k;
+  const CUtensorMap* tm_v = sq ? &sq->tm_v : &a.tm_v;
+  const float* qz = a.q + (sq ? (size_t)blockIdx.z * q_stride : 0);
+
+  // the position counter of a graph-driven step was advanced before the
+  // previous step's kernels finished, so it is safe to read before the wait
+  const int pos0 = sq ? sq->pos0 : (a.pos_dev ? *a.pos_dev : a.pos0);
+  const int L = pos0 + row0 + n_rows;
+  int per = (L + a.n_splits - 1) / a.n_splits;
+  per = (per + 15) / 16 * 16;
+  const int t_begin = min(L, split * per), t_end = min(L, t_begin + per);
+  const int n_tiles = (t_end - t_begin + TC_C - 1) / TC_C;
+
+  auto kbox = [&](int st, int b) { return base + st * S::STAGE + b * S::BOX; };
+  auto vbox = [&](int st, int b) { return base + st * S::STAGE + (NB + b) * S::BOX; };
+
+  if (tid == 0) {
+    s_abort = 0;
+    for (int i = 0; i < 3; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&stage_free[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 128);
+    }
+    mbar_init(q_ready, 128);
+    mbar_init(mma_done, 1);
+    fence_barrier_init();
+  }
+  if (wi == 5) {
+    tc_alloc(&tmem_s, TC_COLS);
+    tc_relinquish();
+  }
+  // P rows >= VH (and their lo rows) stay zero; the others are rewritten every tile
+  for (int i = tid; i < (int)(2 * S::OP / 16); i += TC_THREADS)
+    reinterpret_cast<uint4*>(p_t)[i] = make_uint4(0u, 0u, 0u, 0u);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_s;
+  pdl_trigger();
+  bool ok = true;
+
+  if (wi == 4) {
+    // ------------------------------------------------ TMA
+    if (lane == 0) {
+      auto issue = [&](int i) {
+        const int st = i % TC_NS, t0 = t_begin + i * TC_C;
+        mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * NB * S::BOX));
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+          tma_load_3d(kbox(st, b), tm_k, b * AC_BOX, kvh, t0, &full[st]);
+          tma_load_3d(vbox(st, b), tm_v, b * AC_BOX, kvh, t0, &full[st]);
+        }
+      };
+      int i = 0;
+      // tiles holding only rows written by earlier steps load before the wait
+      for (; i < TC_NS && i < n_tiles && t_begin + (i + 1) * TC_C <= pos0; i++) issue(i);
+      pdl_wait();
+      int issued = i;
+      for (; i < n_tiles; i++) {
+        const int st = i % TC_NS;
+        if (i >= TC_NS && !twait(&stage_free[st], ((i / TC_NS) - 1) & 1, abort)) break;
+        issue(i);
+        issued = i + 1;
+      }
+      // wind down: every copy issued has landed before the CTA may exit
+      for (int j = issued > TC_NS ? issued - TC_NS : 0; j < issued; j++)
+        ok = mbar_wait(&full[j % TC_NS], (j / TC_NS) & 1, *abort ? (1u << 16) : kMbarPolls) && ok;
+    }
+    __syncwarp();
+  } else if (wi == 5) {
+    // ------------------------------------------------ MMA: S of the next tile goes ahead of P.V of this one
+    if (lane == 0) {
+      const uint64_t qd = sw128_desc(smem_u32(q_t));
+      auto issue_s = [&](int j) {
+        const int st = j % TC_NS, sb = j & 1;
+        if (!twait(&full[st], (j / TC_NS) & 1, abort)) return false;
+        if (j >= 2 && !twait(&s_free[sb], ((j - 2) >> 1) & 1, abort)) return false;
+        tc_fence_after();
+        const uint64_t k0 = sw128_desc(smem_u32(kbox(st, 0)));
+#pragma unroll
+        for (int ks = 0; ks < KSTEPS; ks++)
+          tc_mma_f16(tmem + (uint32_t)(sb * 32), k0 + (uint64_t)((ks >> 2) * (S::BOX >> 4) + (ks & 3) * 2),
+                     qd + (uint64_t)((ks >> 2) * 256 + (ks & 3) * 2), IDESC_S, ks > 0);
+        tc_commit(&s_full[sb]);
+        return true;
+      };
+      bool go = twait(q_ready, 0, abort) && (n_tiles == 0 || issue_s(0));
+      for (int i = 0; go && i < n_tiles; i++) {
+        if (i + 1 < n_tiles && !issue_s(i + 1)) break;
+        const int st = i % TC_NS, pb = i & 1;
+        if (!twait(&p_full[pb], (i >> 1) & 1, abort)) break;
+        if (i >= 2 && !twait(&o_free[pb], ((i - 2) >> 1) & 1, abort)) break;
+        tc_fence_after();
+        const uint64_t v0 = sw128_desc_mn(smem_u32(vbox(st, 0)), (uint32_t)S::BOX, 1024u);
+        const uint64_t p0 = sw128_desc(smem_u32(p_t + pb * S::OP));
+#pragma unroll
+        for (int ks = 0; ks < PSTEPS; ks++)
+          tc_mma_f16(tmem + 64u + (uint32_t)(pb * 32), v0 + (uint64_t)(ks * 128),
+                     p0 + (uint64_t)((ks >> 2) * 256 + (ks & 3) * 2), IDESC_O, ks > 0);
+        tc_commit(&o_full[pb]);
+        tc_commit(&stage_free[st]);
+      }
+      // wind down: every MMA issued has completed before TMEM is freed
+      tc_commit(mma_done);
+      ok = mbar_wait(mma_done, 0, *abort ? (1u << 16) : kMbarPolls) && ok;
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ softmax / output (warps 0-3)
+    pdl_wait();
+    // q rows of the virtual heads as f16 hi (rows 0..NQ) and lo (NQ..2 NQ); rows >= VH zero
+    for (int c = tid; c < NQ * (HD / 4); c += 128) {
+      const int vh = c / (HD / 4), d = (c - vh * (HD / 4)) * 4;
+      float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (vh < VH)
+        x = *reinterpret_cast<const float4*>(qz + (size_t)(row0 + vh / group) * q_stride +
+                                             (size_t)(kvh * group + vh % group) * HD + d);
+      const float xs[4] = {x.x, x.y, x.z, x.w};
+      __half hh[4], hl[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        hh[e] = __float2half_rn(xs[e]);
+        hl[e] = __float2half_rn(xs[e] - __half2float(hh[e]));
+      }
+      *reinterpret_cast<uint2*>(q_t + op_off(vh, d)) = *reinterpret_cast<const uint2*>(hh);
+      *reinterpret_cast<uint2*>(q_t + op_off(NQ + vh, d)) = *reinterpret_cast<const uint2*>(hl);
+    }
+    fence_async_smem();
+    mbar_arrive(q_ready);
+
+    float m_run[NQ], l_thr[NQ], o_acc[NQ], alpha_prev[NQ];
+#pragma unroll
+    for (int h = 0; h < NQ; h++) {
+      m_run[h] = -INFINITY;
+      l_thr[h] = 0.0f;
+      o_acc[h] = 0.0f;
+      alpha_prev[h] = 1.0f;
+    }
+    const int r = tid;  // TMEM lane: tile position r for S, dim r for O
+    const uint32_t lane_base = (uint32_t)(wi * 32) << 16;
+    auto ld_cols = [&](uint32_t taddr, uint32_t* v) {  // 2 NQ columns of this lane
+      if constexpr (NQ == 8)
+        tc_ld16(taddr, v);
+      else
+        tc_ld32(taddr, v);
+      tc_wait_ld();
+    };
+    // O of tile i into the registers, rescaled by that tile's alpha
+    auto fold = [&](int i, const float* al) {
+      const int pb = i & 1;
+      ok = twait(&o_full[pb], (i >> 1) & 1, abort) && ok;
+      tc_fence_after();
+      uint32_t ov[2 * NQ];
+      ld_cols(tmem + lane_base + 64u + (uint32_t)(pb * 32), ov);
+      tc_fence_before();
+      mbar_arrive(&o_free[pb]);
+#pragma unroll
+      for (int h = 0; h < NQ; h++)
+        o_acc[h] = fmaf(o_acc[h], al[h], __uint_as_float(ov[h]) + __uint_as_float(ov[NQ + h]));
+    };
+    for (int i = 0; i < n_tiles; i++) {
+      const int sb = i & 1, st = i % TC_NS, t = t_begin + i * TC_C + r;
+      ok = twait(&s_full[sb], (i >> 1) & 1, abort) && ok;
+      tc_fence_after();
+      uint32_t sv[2 * NQ];
+      ld_cols(tmem + lane_base + (uint32_t)(sb * 32), sv);
+      tc_fence_before();
+      mbar_arrive(&s_free[sb]);
+      float sc[NQ], alpha[NQ];
+      bool over = false;
+#pragma unroll
+      for (int h = 0; h < NQ; h++) {
+        const bool vis = h < VH && t < t_end && t <= pos0 + row0 + h / group;
+        sc[h] = vis ? __fmul_rn(__uint_as_float(sv[h]) + __uint_as_float(sv[NQ + h]), scale) : -INFINITY;
+        over |= sc[h] > m_run[h] + TC_TAU;
+        alpha[h] = 1.0f;
+      }
+      if (sm_any(over || *abort != 0)) {
+        if (sm_any(*abort != 0)) break;  // a uniform decision: the named barriers stay matched
+        // the tile's exact max becomes the reference
+#pragma unroll
+        for (int h = 0; h < NQ; h++)
+          if (h < VH) {
+            const float mw = warp_max(sc[h]);
+            if (lane == 0) red[wi * 16 + h] = mw;
+          }
+        sm_sync();
+#pragma unroll
+        for (int h = 0; h < NQ; h++)
+          if (h < VH) {
+            const float mt = fmaxf(fmaxf(red[h], red[16 + h]), fmaxf(red[32 + h], red[48 + h]));
+            const float m_new = fmaxf(m_run[h], mt);
+            alpha[h] = m_run[h] == -INFINITY ? 0.0f : expf(m_run[h] - m_new);
+            m_run[h] = m_new;
+            l_thr[h] *= alpha[h];
+          }
+      }
+      uint8_t* pt = p_t + sb * S::OP;
+#pragma unroll
+      for (int h = 0; h < NQ; h++)
+        if (h < VH) {
+          const float pv = sc[h] == -INFINITY ? 0.0f : expf(sc[h] - m_run[h]);
+          l_thr[h] += pv;
+          const __half ph = __float2half_rn(pv);
+          *reinterpret_cast<__half*>(pt + op_off(h, r)) = ph;
+          *reinterpret_cast<__half*>(pt + op_off(NQ + h, r)) = __float2half_rn(pv - __half2float(ph));
+        }
+      // V rows at positions not yet written may hold anything: zero them (P is 0 there)
+      if (t >= L) {
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+#pragma unroll
+          for (int c = 0; c < 8; c++)
+            *reinterpret_cast<uint4*>(vbox(st, b) + r * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      fence_async_smem();
+      mbar_arrive(&p_full[sb]);
+      if (i >= 1) fold(i - 1, alpha_prev);
+#pragma unroll
+      for (int h = 0; h < NQ; h++) alpha_prev[h] = alpha[h];
+    }
+    if (n_tiles >= 1 && !*abort) fold(n_tiles - 1, alpha_prev);
+    // the sums over the positions, once
+#pragma unroll
+    for (int h = 0; h < NQ; h++)
+      if (h < VH) {
+        const float sw = warp_sum(l_thr[h]);
+        if (lane == 0) red[wi * 16 + h] = sw;
+      }
+    sm_sync();
+    float* o_s = reinterpret_cast<float*>(base);  // stage 0, idle now
+    float* ml = reinterpret_cast<float*>(base + S::STAGE);
+#pragma unroll
+    for (int h = 0; h < NQ; h++)
+      if (h < VH) o_s[h * HD + r] = o_acc[h];
+    if (tid < VH) {
+      float mv = m_run[0];
+#pragma unroll
+      for (int h = 1; h < NQ; h++)
+        if (h == tid) mv = m_run[h];
+      ml[tid] = mv;
+      ml[16 + tid] = (red[tid] + red[16 + tid]) + (red[32 + tid] + red[48 + tid]);
+    }
+  }
+  if (!ok) *abort = 1;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (*abort && tid == 0 && a.err) atomicExch(a.err, ERR_TIMEOUT);
+  if (wi == 5) tc_dealloc(tmem, TC_COLS);
+
+  // ---- this split's (max, sum, o): the final rows with one split, else a
+  // partial for attn_merge_tc (stage 0 holds o, stage 1 m / l)
+  const float* o_s = reinterpret_cast<const float*>(base);
+  const float* ml = reinterpret_cast<const float*>(base + S::STAGE);
+  float* out = a.out + (sq ? (size_t)blockIdx.z * q_stride : 0);
+  if (a.n_splits == 1) {
+    for (int e = tid; e < VH * HD; e += TC_THREADS) {
+      const int vh = e / HD, d = e - vh * HD;
+      const int row = vh / group, head = kvh * group + vh % group;
+      out[(size_t)(row0 + row) * q_stride + head * HD + d] = o_s[e] / ml[16 + vh];
+    }
+    return;
+  }
+  float* part_ml = sq ? sq->part_ml : a.part_ml;
+  float* part_o = sq ? sq->part_o : a.part_o;
+  const size_t pbase = ((size_t)kvh * a.n_splits + split) * VH;
+  for (int vh = tid; vh < VH; vh += TC_THREADS)
+    reinterpret_cast<float2*>(part_ml)[pbase + vh] = make_float2(ml[vh], ml[16 + vh]);
+  for (int e = tid; e < VH * HD / 4; e += TC_THREADS)
+    reinterpret_cast<float4*>(part_o + pbase * HD)[e] = reinterpret_cast<const float4*>(o_s)[e];
+}
+
 template <int HD, bool MMA>
 static cudaError_t decode_go(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const int group = a.n_heads / a.n_kv;
@@ -1307,6 +1757,83 @@ static cudaError_t cluster_go(const AttnArgs& a, ClusterPlan pl, cudaStream_t st
   return cudaSuccess;
 }
 
+// SMs of the current device (asked once per device)
+static int device_sms() {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) n = 148;
+  cudaGetLastError();
+  cache[dev] = n;
+  return n;
+}
+
+// tcgen05 attention: one CTA per SM across (splits, kv heads, sequences);
+// the split count is capped by the partial scratch the caller sized
+template <int HD>
+static cudaError_t tc_go(const AttnArgs& a, cudaStream_t st, bool pdl, int n_seq) {
+  const int group = a.n_heads / a.n_kv;
+  // up to 8 virtual heads per launch run the narrow form (N = 16), else N = 32
+  const bool narrow = a.m * group <= 8;
+  const int max_rows = (narrow ? 8 : 16) / group;
+  if (max_rows < 1) return cudaErrorInvalidValue;
+  AttnArgs aa = a;
+  aa.n_splits = std::max(1, std::min(a.n_splits, device_sms() / (a.n_kv * n_seq)));
+  // at most two tiles per CTA at full capacity: two stages, which leaves room
+  // for the previous kernel's CTAs, else three
+  const int cap = a.cap > 0 ? a.cap : a.pos0 + a.m;
+  const bool two = (cap + aa.n_splits - 1) / aa.n_splits <= 2 * TC_C;
+  const void* kern = narrow ? (two ? (const void*)attn_decode_tc<HD, 8, 2> : (const void*)attn_decode_tc<HD, 8, 3>)
+                            : (two ? (const void*)attn_decode_tc<HD, 16, 2> : (const void*)attn_decode_tc<HD, 16, 3>);
+  const size_t smem = two ? TcSmem<HD, 2>::bytes : TcSmem<HD, 3>::bytes;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  if (aa.n_splits > 1) {
+    e = cudaFuncSetAttribute((const void*)attn_merge_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)TC_MERGE_SMEM);
+    if (e != cudaSuccess) return e;
+  }
+  for (int row0 = 0; row0 < a.m; row0 += max_rows) {
+    int n_rows = min(max_rows, a.m - row0);
+    void* args[] = {&aa, (void*)&row0, (void*)&n_rows};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(aa.n_splits, a.n_kv, n_seq);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    if (pdl && row0 == 0) {
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+    }
+    e = cudaLaunchKernelExC(&cfg, kern, args);
+    if (e != cudaSuccess) return e;
+    if (aa.n_splits > 1) {  // the merge, right behind (programmatic: it waits for the whole grid)
+      const size_t vhn = (size_t)n_rows * group * aa.n_splits, w_bytes = ((vhn + 3) & ~(size_t)3) * 4;
+      const size_t need = w_bytes + vhn * HD * 4;
+      cudaLaunchConfig_t mc = {};
+      mc.gridDim = dim3(a.n_kv, n_seq);
+      mc.blockDim = dim3(HD);
+      mc.dynamicSmemBytes = need <= TC_MERGE_SMEM ? need : w_bytes;
+      mc.stream = st;
+      if (pdl) {
+        mc.attrs = attr;
+        mc.numAttrs = 1;
+      }
+      e = cudaLaunchKernelExC(&mc, (const void*)attn_merge_tc<HD>, args);
+      if (e != cudaSuccess) return e;
+    }
+  }
+  return cudaSuccess;
+}
+
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   if (a.n_kv <= 0 || a.n_heads % a.n_kv || a.m < 1 || a.n_splits < 1) return cudaErrorInvalidValue;
   // tensor cores for the common head sizes while a kv head's query heads fit one MMA tile;
@@ -1323,8 +1850,8 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
     case 96: return decode_go<96, false>(a, st, pdl);
     case 128: {
       if (!mma) return decode_go<128, false>(a, st, pdl);
-      const ClusterPlan pl = a.has_tm ? cluster_plan<128>(a.n_kv, a.n_splits) : ClusterPlan{};
-      return pl.c ? cluster_go<128>(a, pl, st, pdl) : decode_go<128, true>(a, st, pdl);
+      if (a.has_tm) return tc_go<128>(a, st, pdl, 1);
+      return decode_go<128, true>(a, st, pdl);
     }
     case 256: return decode_go<256, false>(a, st, pdl);
   }
@@ -1336,9 +1863,10 @@ cudaError_t launch_attn_decode_seqs(const AttnArgs& a, int n_seq, cudaStream_t s
     return cudaErrorInvalidValue;
   if (a.n_heads / a.n_kv > AM_ROWS || !a.has_tm || !(a.hd == 64 || a.hd == 128) || n_seq > 65535)
     return cudaErrorNotSupported;
-  const ClusterPlan pl = a.hd == 64 ? cluster_plan<64>(a.n_kv, a.n_splits) : cluster_plan<128>(a.n_kv, a.n_splits);
+  if (a.hd == 128) return tc_go<128>(a, st, pdl, n_seq);
+  const ClusterPlan pl = cluster_plan<64>(a.n_kv, a.n_splits);
   if (!pl.c) return cudaErrorNotSupported;
-  return a.hd == 64 ? cluster_go<64>(a, pl, st, pdl, n_seq) : cluster_go<128>(a, pl, st, pdl, n_seq);
+  return cluster_go<64>(a, pl, st, pdl, n_seq);
 }
 
 template <int HD>

@@ -233,6 +233,31 @@ struct Bufs {
   }
 };
 
+// A captured multi-sequence step for one ordered set of caches: its own row
+// buffers and per-sequence device views; a call copies the tokens and the
+// positions in, replays the graph (whose first kernel writes the positions
+// into the views) and reads the ids back.
+struct MultiPlan {
+  std::vector<prana_kv*> kvs;
+  std::unique_ptr<Bufs> bufs;
+  SeqRow* rows_dev = nullptr;
+  AttnSeq* att_dev = nullptr;
+  int* pos_dev = nullptr;
+  uint32_t* h_stage = nullptr;  // pinned: tokens [n], then positions [n]
+  cudaGraphExec_t graph = nullptr;
+  explicit MultiPlan(prana_ctx* c) : bufs(new Bufs(c)) {}
+  ~MultiPlan() {
+    if (graph) cudaGraphExecDestroy(graph);
+    if (h_stage) cudaFreeHost(h_stage);
+  }
+};
+
+__global__ void multi_positions_kernel(const int* pos, int n, int n_att, SeqRow* rows, AttnSeq* att) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) rows[i].pos = pos[i];
+  for (int j = i; j < n_att; j += gridDim.x * blockDim.x) att[j].pos0 = pos[j % n];
+}
+
 }  // namespace
 
 struct prana_model {
@@ -267,6 +292,7 @@ struct prana_model {
   prana::TpPeers peers;       // one-shot all-reduce over peer memory (world == 1: unused)
   void* peers_mem = nullptr;
   bool peers_ok = false;
+  std::unique_ptr<MultiPlan> multi;  // the last captured multi-sequence step
 };
 
 struct prana_kv {
@@ -391,6 +417,7 @@ void free_model(prana_model* m) {
   if (!m) return;
   DevScope ds(m->ctx->device);
   cudaStreamSynchronize(m->ctx->own);
+  m->multi.reset();
   while (!m->caches.empty()) destroy_kv(m->caches.back());
   free_weight(&m->emb);
   free_stream(m->head);
@@ -668,6 +695,7 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
         a.has_tm = mu->all_tm ? 1 : 0;
         a.err = m->err;
         a.seqs = mu->attn_dev + l * (size_t)n;
+        for (int s0 = 0; s0 < n; s0++) a.cap = std::max(a.cap, (int)mu->kvs[s0]->positions);
         es = launch_attn_decode_seqs(a, n, st, pdl);
         if (es != cudaErrorNotSupported) PRANA_CK(es);
       }
@@ -680,11 +708,13 @@ int enqueue_rows(prana_model* m, prana_kv* kv, Bufs& b, int n, const uint32_t* t
         a.vc = mu ? kq->v + l * ls : vc;
         a.m = mu ? 1 : n;
         a.pos0 = mu ? (int)mu->pos[s0] : pos0;
-        a.pos_dev = mu ? nullptr : pos_dev;
+        // a captured multi-sequence step reads each position from its row view
+        a.pos_dev = mu ? &(mu->rows_dev + s0)->pos : pos_dev;
         a.n_heads = (int)m->heads_l;
         a.n_kv = (int)m->kv_heads_l;
         a.hd = hd;
         a.n_splits = kq->n_splits;
+        a.cap = (int)kq->positions;
         a.part_ml = kq->part_ml;
         a.part_o = kq->part_o;
         a.counters = kq->counters;
@@ -888,6 +918,10 @@ void destroy_kv(prana_kv* kv) {
   if (!kv) return;
   DevScope ds(kv->m->ctx->device);
   cudaStreamSynchronize(kv->m->ctx->own);
+  if (kv->m->multi) {
+    const auto& ks = kv->m->multi->kvs;
+    if (std::find(ks.begin(), ks.end(), kv) != ks.end()) kv->m->multi.reset();
+  }
   auto& cs = kv->m->caches;
   cs.erase(std::remove(cs.begin(), cs.end(), kv), cs.end());
   if (kv->g_step) cudaGraphExecDestroy(kv->g_step);
@@ -1505,14 +1539,6 @@ static int forward_multi_impl(prana_model* m, prana_kv* const* kvs, size_t n, co
   }
   DevScope ds(m->ctx->device);
   cudaStream_t st = m->ctx->own;
-  std::unique_ptr<Bufs> tmp;
-  Bufs* b = m->dec.get();
-  if (n > b->rows) {
-    tmp.reset(new Bufs(m->ctx));
-    int rc = make_bufs(m, n, false, *tmp);
-    if (rc) return rc;
-    b = tmp.get();
-  }
   // per layer and sequence: the cache's tensor maps, scratch and position
   const size_t nl = m->layers.size();
   std::vector<AttnSeq> att(nl * n);
@@ -1539,6 +1565,71 @@ static int forward_multi_impl(prana_model* m, prana_kv* const* kvs, size_t n, co
       }
     }
   }
+  if (!tr) {
+    // ---- the captured step: build it once for this ordered set of caches
+    MultiPlan* pl = m->multi.get();
+    if (!pl || pl->kvs.size() != n || !std::equal(pl->kvs.begin(), pl->kvs.end(), kvs)) {
+      m->multi.reset();
+      std::unique_ptr<MultiPlan> np(new MultiPlan(m->ctx));
+      np->kvs.assign(kvs, kvs + n);
+      Bufs& nb = *np->bufs;
+      int rc = make_bufs(m, std::max<size_t>(n, 8), false, nb);
+      if (!rc) rc = nb.alloc(np->rows_dev, n);
+      if (!rc) rc = nb.alloc(np->att_dev, att.size());
+      if (!rc) rc = nb.alloc(np->pos_dev, n);
+      if (rc) return rc;
+      PRANA_CK(cudaHostAlloc((void**)&np->h_stage, 2 * n * sizeof(uint32_t), cudaHostAllocDefault));
+      PRANA_CK(cudaMemcpyAsync(np->rows_dev, rows.data(), n * sizeof(SeqRow), cudaMemcpyHostToDevice, st));
+      PRANA_CK(cudaMemcpyAsync(np->att_dev, att.data(), att.size() * sizeof(AttnSeq), cudaMemcpyHostToDevice, st));
+      PRANA_CK(cudaStreamSynchronize(st));
+      const Multi mu{np->rows_dev, np->kvs.data(), positions, np->att_dev, min_splits, all_tm};
+      for (int attempt = 0; attempt < 2 && !np->graph; attempt++) {
+        const bool pdl = m->pdl && attempt == 0;
+        cudaGraph_t graph = nullptr;
+        PRANA_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
+        multi_positions_kernel<<<1, 256, 0, st>>>(np->pos_dev, (int)n, (int)att.size(), np->rows_dev, np->att_dev);
+        cudaError_t el = cudaGetLastError();
+        rc = el == cudaSuccess ? enqueue_rows(m, kvs[0], nb, (int)n, nb.toks, nullptr, 0, nullptr, MODE_CACHE, true,
+                                              pdl, nullptr, true, &mu)
+                               : fail(PRANA_E_CUDA, "positions launch: %s", cudaGetErrorString(el));
+        const cudaError_t ec = cudaStreamEndCapture(st, &graph);
+        if (rc) {
+          if (graph) cudaGraphDestroy(graph);
+          cudaGetLastError();
+          return rc;
+        }
+        if (ec == cudaSuccess) {
+          const cudaError_t ei = cudaGraphInstantiate(&np->graph, graph, 0);
+          if (ei != cudaSuccess) np->graph = nullptr;
+        }
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+      }
+      if (!np->graph) return fail(PRANA_E_CUDA, "multi-sequence graph capture failed");
+      m->multi = std::move(np);
+      pl = m->multi.get();
+    }
+    Bufs& b = *pl->bufs;
+    memcpy(pl->h_stage, tokens, n * 4);
+    for (size_t i = 0; i < n; i++) pl->h_stage[n + i] = (uint32_t)positions[i];
+    PRANA_CK(cudaMemcpyAsync(b.toks, pl->h_stage, n * 4, cudaMemcpyHostToDevice, st));
+    PRANA_CK(cudaMemcpyAsync(pl->pos_dev, pl->h_stage + n, n * 4, cudaMemcpyHostToDevice, st));
+    PRANA_CK(cudaGraphLaunch(pl->graph, st));
+    if (logits) PRANA_CK(cudaMemcpyAsync(logits, b.logits, n * (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, st));
+    if (argmax) PRANA_CK(cudaMemcpyAsync(argmax, b.tok_out, n * 4, cudaMemcpyDeviceToHost, st));
+    PRANA_CK(cudaStreamSynchronize(st));
+    for (size_t i = 0; i < n; i++) kvs[i]->loop_active = false;
+    return check_err(m);
+  }
+  // ---- the diagnostic trace: eager
+  std::unique_ptr<Bufs> tmp;
+  Bufs* b = m->dec.get();
+  if (n > b->rows) {
+    tmp.reset(new Bufs(m->ctx));
+    int rc = make_bufs(m, n, false, *tmp);
+    if (rc) return rc;
+    b = tmp.get();
+  }
   SeqRow* rows_dev = nullptr;
   AttnSeq* att_dev = nullptr;
   Bufs scratch(m->ctx);
@@ -1548,11 +1639,10 @@ static int forward_multi_impl(prana_model* m, prana_kv* const* kvs, size_t n, co
   PRANA_CK(cudaMemcpyAsync(rows_dev, rows.data(), n * sizeof(SeqRow), cudaMemcpyHostToDevice, st));
   PRANA_CK(cudaMemcpyAsync(att_dev, att.data(), att.size() * sizeof(AttnSeq), cudaMemcpyHostToDevice, st));
   const Multi mu{rows_dev, kvs, positions, att_dev, min_splits, all_tm};
-  int rc = enqueue_rows(m, kvs[0], *b, (int)n, b->toks, nullptr, 0, nullptr, MODE_CACHE, true, tr == nullptr, tr,
+  int rc = enqueue_rows(m, kvs[0], *b, (int)n, b->toks, nullptr, 0, nullptr, MODE_CACHE, true, false, tr,
                         logits != nullptr, &mu);
   if (rc) return rc;
   if (logits) PRANA_CK(cudaMemcpyAsync(logits, b->logits, n * (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, st));
-  if (argmax) PRANA_CK(cudaMemcpyAsync(argmax, b->tok_out, n * 4, cudaMemcpyDeviceToHost, st));
   PRANA_CK(cudaStreamSynchronize(st));
   for (size_t i = 0; i < n; i++) kvs[i]->loop_active = false;
   return check_err(m);
