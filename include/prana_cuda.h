@@ -349,6 +349,11 @@ int prana_sampler_next_f32(prana_sampler *s, float *out);
  * is prana_sample's except where the draw lies within the reference's
  * sequential f32 rounding of a bucket boundary. */
 int prana_sample_logits(prana_ctx *ctx, const float *logits, size_t n, prana_sampler *s, uint32_t *token);
+/* prana_forward whose next token is Sampler::sample on the device over the
+ * step's logits (which stay in HBM); a greedy sampler is prana_forward's argmax.
+ * s moves past the draw taken. */
+int prana_forward_sampled(prana_model *m, prana_kv *kv, uint32_t token, size_t pos, prana_sampler *s,
+                          uint32_t *next);
 /* prana_decode_begin whose loop samples each next token on the device with the
  * sampler's temperature and stream (the sampler itself is not advanced; greedy
  * or NULL: prana_decode_begin) */

@@ -120,6 +120,7 @@ SIGNATURES = {
     "prana_sample_logits": [P, P, SZ, P, P],
     "prana_generate_sampled": [P, P, SZ, SZ, C.c_int64, P, P, C.POINTER(SZ)],
     "prana_decode_begin_sampled": [P, P, C.c_uint32, SZ, P],
+    "prana_forward_sampled": [P, P, C.c_uint32, SZ, P, C.POINTER(C.c_uint32)],
     "prana_generate": [P, P, SZ, SZ, C.c_int64, P, C.POINTER(SZ)],
     "prana_generate_speculative": [P, P, P, SZ, SZ, SZ, C.c_int64, P, C.POINTER(SZ), P],
     "prana_decode_begin": [P, P, C.c_uint32, SZ],

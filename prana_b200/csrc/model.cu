@@ -1380,6 +1380,36 @@ int prana_forward(prana_model* m, prana_kv* kv, uint32_t token, size_t pos, floa
   API_END
 }
 
+int prana_forward_sampled(prana_model* m, prana_kv* kv, uint32_t token, size_t pos, prana_sampler* s,
+                          uint32_t* next) {
+  API_BEGIN
+  NEED(m && kv && kv->m == m && s && next, "null or mismatched argument");
+  if (s->greedy) return prana_forward(m, kv, token, pos, nullptr, next);
+  NEED(pos < kv->positions, "position %zu beyond kv capacity %zu", pos, kv->positions);
+  NEED(token < (uint64_t)m->cfg.vocab_size, "token %u out of vocabulary", token);
+  NEED(m->cfg.vocab_size <= sample_max_vocab(), "vocabulary of %lld exceeds the device sampler's %d",
+       (long long)m->cfg.vocab_size, sample_max_vocab());
+  DevScope ds(m->ctx->device);
+  int rc = ensure_graphs(m, kv, false);
+  if (rc) return rc;
+  cudaStream_t st = m->ctx->own;
+  m->h_io[0] = (int)token;
+  m->h_io[1] = (int)pos;
+  SampleState* h = reinterpret_cast<SampleState*>(m->h_io + 8);
+  *h = SampleState{s->state, s->temp, 0};
+  PRANA_CK(cudaMemcpyAsync(m->d_tokpos, m->h_io, 8, cudaMemcpyHostToDevice, st));
+  PRANA_CK(cudaMemcpyAsync(m->d_sample, h, sizeof(SampleState), cudaMemcpyHostToDevice, st));
+  PRANA_CK(cudaGraphLaunch(kv->g_step, st));  // the step leaves the whole logits row in HBM
+  PRANA_CK(launch_sample(m->dec->logits, (int)m->cfg.vocab_size, m->d_sample, m->dec->tok_out, nullptr, st));
+  PRANA_CK(cudaMemcpyAsync(m->h_tok, m->dec->tok_out, 4, cudaMemcpyDeviceToHost, st));
+  PRANA_CK(cudaStreamSynchronize(st));
+  *next = m->h_tok[0];
+  s->next_u64();  // the draw the kernel took
+  kv->loop_active = false;
+  return check_err(m);
+  API_END
+}
+
 int prana_forward_trace(prana_model* m, prana_kv* kv, uint32_t token, size_t pos, float* logits, int8_t* q_host,
                         float* s_host, size_t cap, size_t* n_out) {
   API_BEGIN

@@ -266,6 +266,14 @@ def generate(model: Model, prompt, steps: int, stop_id: int = -1) -> np.ndarray:
     return out[: n.value].copy()
 
 
+def forward_sampled(model: Model, cache: KvCache, token: int, pos: int, sampler) -> int:
+    """forward_impl (infer.rs:142-211) followed by Sampler::sample on the device
+    over the step's logits; returns the next id (the sampler moves past its draw)."""
+    out = C.c_uint32()
+    call("prana_forward_sampled", model.handle, cache.handle, token, pos, sampler.handle, C.byref(out))
+    return out.value
+
+
 def generate_sampled(model: Model, prompt, steps: int, sampler, stop_id: int = -1) -> np.ndarray:
     """generate (infer.rs:696-771) with a Sampler (prana_b200.sampler.Sampler):
     each sampled position draws on the device; the sampler is left where the

@@ -64,7 +64,16 @@ def fake(monkeypatch):
         logits[nxt] = 50.0
         return (logits if want_logits else None), nxt
 
+    def forward_sampled(model, cache, token, pos, sampler):
+        # the device sampler over the step's logits, stood in by the host sampler
+        assert pos < cache.n
+        model.calls.append((token, pos, "sampled"))
+        logits = np.zeros(model.config.vocab_size, np.float32)
+        logits[successor(token)] = 50.0
+        return sampler.sample(logits)
+
     prefilled = []
+    monkeypatch.setattr(pm, "forward_sampled", forward_sampled)
     monkeypatch.setattr(pm, "KvCache", Cache)
     monkeypatch.setattr(pm, "prefill", lambda model, cache, toks: prefilled.append(list(toks)))
     monkeypatch.setattr(pm, "forward", forward)
@@ -89,12 +98,13 @@ def test_context_limit_stops_before_the_next_position(fake):
     assert [c[1] for c in m.calls] == [1, 2]
 
 
-def test_sampled_positions_read_logits(fake):
+def test_sampled_positions_sample_on_the_device(fake):
     m = FakeModel(64)
     out, _ = gen.generate_text(m, tokenizer(), "abc", 10, sampler=Sampler(0.5, 9))
     assert out == b"d"  # the logits put (almost) all mass on the successor
-    # positions whose successor is sampled read their logits; the last position does not exist
-    assert [(c[1], c[2]) for c in m.calls] == [(2, True), (3, True)]
+    # positions whose successor is sampled draw it beside their logits (no logits
+    # copied back); the last position does not exist
+    assert [(c[1], c[2]) for c in m.calls] == [(2, "sampled"), (3, "sampled")]
 
 
 def test_empty_prompt_is_rejected(fake):

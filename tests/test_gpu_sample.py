@@ -179,3 +179,22 @@ def test_decode_loop_sampled(small_model):
         loop.run(steps)
         assert np.array_equal(loop.tokens(steps), want)
         kv.close()
+
+
+def test_forward_sampled_matches_loop(small_model):
+    """Token by token (prana_forward_sampled) the draws are the sampled loop's,
+    and the sampler ends where generate_sampled leaves it."""
+    _, _, gm = small_model
+    prompt = np.array([1, 17, 250, 3, 999], np.uint32)
+    s_loop = Sampler(0.7, 31)
+    want = pm.generate_sampled(gm, prompt, 20, s_loop)
+    kv = pm.KvCache(gm, len(prompt) + 20)
+    pm.prefill(gm, kv, prompt[:-1])
+    s = Sampler(0.7, 31)
+    tok, got = int(prompt[-1]), []
+    for pos in range(len(prompt) - 1, len(prompt) - 1 + 20):
+        tok = pm.forward_sampled(gm, kv, tok, pos, s)
+        got.append(tok)
+    kv.close()
+    assert np.array_equal(np.array(got, np.uint32), want)
+    assert s.next_f32() == s_loop.next_f32()
