@@ -40,6 +40,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <climits>
 #include <map>
 #include <mutex>
 
@@ -47,6 +49,7 @@
 #include "host.h"
 #include "internal.h"
 #include "mbar.cuh"
+#include "tc.cuh"
 
 namespace prana {
 
@@ -54,9 +57,6 @@ namespace {
 
 constexpr int QG_BM = 128;         // weight rows per CTA (MMA M)
 constexpr int QG_PRODUCERS = 128;  // warps 0-3
-constexpr int QG_EPI_WARPS = 8;    // warps 4-11
-constexpr int QG_WARPS = 14;
-constexpr int QG_THREADS = QG_WARPS * 32;
 constexpr int QG_SMEM_MAX = 224 * 1024;
 
 template <int T> struct QgFmt;
@@ -101,66 +101,14 @@ struct QgLayout {
   static constexpr int TMEM_COLS = SLOTS * NT < 32 ? 32 : SLOTS * NT;
   static constexpr size_t SMEM = (size_t)NS * STAGE + 1024 /* alignment */ + 1024 /* barriers */;
   static constexpr uint32_t TX = (uint32_t)(B_BYTES + (F::RAW ? RAW_BYTES : A_BYTES) + SA_BYTES + SUM_BYTES);
+  // warps: 0-3 producers, then the epilogue (four per TMEM lane quarter at 16
+  // tokens, where a thread's share is small; two otherwise), MMA, TMA
+  static constexpr int EPI = NT == 16 ? 16 : 8;
+  static constexpr int MMA_WARP = 4 + EPI;
+  static constexpr int TMA_WARP = MMA_WARP + 1;
+  static constexpr int THREADS = (TMA_WARP + 1) * 32;
 };
 
-// ---- tcgen05 / TMA primitives (inline PTX, sm_100a) ----
-__device__ __forceinline__ void tc_alloc(uint32_t* dst, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tc_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tc_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-// D[tmem] = A[smem] . B[smem]^T (s8 x s8 -> s32) into a fresh accumulator
-__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-      : "memory");
-}
-// arrive on `bar` once every tcgen05 operation this thread issued so far has completed
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t* r) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// generic-proxy shared-memory writes become visible to the tensor core (async proxy)
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Shared-memory matrix descriptor of a K-major operand in 128-byte swizzled
-// atoms (8 rows x 128 bytes, 8-row groups 1024 bytes apart); version 1
-// (tcgen05), layout type 2 (SWIZZLE_128B).  Within an atom, the K offset of
-// the j-th 32-byte step is added to the start address.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: 8-row groups
-  d |= (uint64_t)1 << 46;            // descriptor version
-  d |= (uint64_t)2 << 61;            // SWIZZLE_128B
-  return d;
-}
 // Instruction descriptor: s8 x s8 -> s32, K-major A and B, M = 128, N = nt.
 constexpr uint32_t i8_idesc(int nt) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(QG_BM >> 4) << 24);
@@ -186,9 +134,12 @@ template <int T>
 __device__ __forceinline__ void unpack_row(const uint8_t* raw, const uint8_t* raw2, uint8_t* a, int r) {
   constexpr int ATOM = QG_BM * 128;
   if constexpr (T == T_Q4_0) {
-    // 8 blocks of 16 bytes: byte j holds value j (low nibble) and j + 16 (high), q - 8
+    // 8 blocks of 16 bytes: byte j holds value j (low nibble) and j + 16 (high), q - 8.
+    // Rows are 128 bytes apart: each row starts at another block (bank) so a
+    // warp's reads spread over the banks.
 #pragma unroll
-    for (int b = 0; b < 8; b++) {
+    for (int b_ = 0; b_ < 8; b_++) {
+      const int b = (b_ + r) & 7;
       const uint4 x = *reinterpret_cast<const uint4*>(raw + b * 16);
       const unsigned m = 0x0F0F0F0Fu, e = 0x08080808u;
       const uint4 lo = make_uint4(__vsub4(x.x & m, e), __vsub4(x.y & m, e), __vsub4(x.z & m, e), __vsub4(x.w & m, e));
@@ -218,7 +169,8 @@ __device__ __forceinline__ void unpack_row(const uint8_t* raw, const uint8_t* ra
     uint8_t* lo_t = a;
     uint8_t* hi_t = a + 2 * ATOM;
 #pragma unroll
-    for (int c = 0; c < 16; c++) {
+    for (int c_ = 0; c_ < 16; c_++) {
+      const int c = (c_ + r) & 15;  // rows start at different chunks: spread banks
       const int h = c >> 3, g = (c >> 1) & 3, l0 = (c & 1) * 16;
       const uint4 x = *reinterpret_cast<const uint4*>(raw + h * 64 + (g & 1) * 32 + l0);
       const uint4 q = *reinterpret_cast<const uint4*>(raw2 + h * 32 + l0);
@@ -237,7 +189,7 @@ __device__ __forceinline__ void unpack_row(const uint8_t* raw, const uint8_t* ra
 }
 
 template <int T, int NT>
-__global__ void __launch_bounds__(QG_THREADS, 1)
+__global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
                  const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_sa,
                  const __grid_constant__ CUtensorMap tm_sum, const QgemmArgs g) {
@@ -273,16 +225,16 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     for (int i = 0; i < NS; i++) {
       mbar_init(&full[i], 1);
       mbar_init(&conv[i], QG_PRODUCERS);
-      mbar_init(&freed[i], 1 + QG_EPI_WARPS);
+      mbar_init(&freed[i], 1 + L::EPI);
     }
     for (int i = 0; i < NG; i++) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], QG_EPI_WARPS);
+      mbar_init(&acc_empty[i], L::EPI);
     }
     mbar_init(mma_done, 1);
     fence_barrier_init();
   }
-  if (wi == 12) {
+  if (wi == L::MMA_WARP) {
     tc_alloc(tmem_base_s, L::TMEM_COLS);
     tc_relinquish();
   }
@@ -291,7 +243,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_base_s;
 
-  if (wi == 13) {
+  if (wi == L::TMA_WARP) {
     // ------------------------------------------------ TMA issue
     if (lane == 0) {
       int issued = 0;
@@ -323,7 +275,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         mbar_wait(&full[s % NS], (s / NS) & 1, ab ? (1u << 16) : kMbarPolls);
     }
     __syncwarp();
-  } else if (wi == 12) {
+  } else if (wi == L::MMA_WARP) {
     // ------------------------------------------------ MMA issue
     if (lane == 0) {
       constexpr uint32_t idesc = i8_idesc(NT);
@@ -387,12 +339,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     }
   } else {
     // ------------------------------------------------ epilogue
-    const int q4 = wi & 3, half = (wi - 4) >> 2;  // lane quarter, token half
+    const int q4 = wi & 3, part = (wi - 4) >> 2;  // lane quarter, token slice
     const int rl = q4 * 32 + lane;                 // row within the tile
     const int r = row0 + rl;
     const int rr = min(r, N - 1);                  // rows past N read row N-1's scales (never stored)
-    constexpr int NC = NT / 2;                     // tokens per thread
-    const int c0 = half * NC;
+    constexpr int NC = NT / (L::EPI / 4);    // tokens per thread
+    const int c0 = part * NC;
     float acc[NC];
 #pragma unroll
     for (int c = 0; c < NC; c++) acc[c] = 0.0f;
@@ -455,9 +407,13 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < NB; k++)
             if (b0 + k < cnt) {
+              if constexpr (NC == 4) {
+                tc_ld4(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)((gslot * GS + b0 + k) * NT + c0), &v[k][0]);
+              } else {
 #pragma unroll
-              for (int c = 0; c < NC; c += 8)
-                tc_ld8(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)((gslot * GS + b0 + k) * NT + c0 + c), &v[k][c]);
+                for (int c = 0; c < NC; c += 8)
+                  tc_ld8(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)((gslot * GS + b0 + k) * NT + c0 + c), &v[k][c]);
+              }
             }
           tc_wait_ld();
 #pragma unroll
@@ -553,7 +509,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   if (tid == 0 && s_abort && g.err) atomicExch(g.err, ERR_TIMEOUT);
-  if (wi == 12) {
+  if (wi == L::MMA_WARP) {
     tc_fence_after();
     tc_dealloc(tmem, L::TMEM_COLS);
   }
@@ -652,7 +608,7 @@ cudaError_t qgemm_go(const QgemmArgs& g, const int8_t* q, const float* sa_t, con
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const dim3 grid((unsigned)((N + QG_BM - 1) / QG_BM), (unsigned)(g.m_pad / NT), (unsigned)g.splits);
-  kern<<<grid, QG_THREADS, L::SMEM, st>>>(tm_w, tm_w2, tm_x, tm_sa, tm_sum, g);
+  kern<<<grid, L::THREADS, L::SMEM, st>>>(tm_w, tm_w2, tm_x, tm_sa, tm_sum, g);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || g.splits == 1 || g.dots) return e;
   const size_t mn = (size_t)g.M * g.N;
@@ -674,27 +630,36 @@ cudaError_t qgemm_t(const QgemmArgs& g, const int8_t* q, const float* sa_t, cons
 int qgemm_tokens_per_tile(int m) { return m <= 16 ? 16 : m <= 32 ? 32 : 64; }
 
 namespace {
-constexpr int QG_SPLIT_CTAS = 148;  // split K until the grid covers about one CTA per SM
+constexpr int QG_SMS = 148;
 constexpr int QG_MAX_SPLITS = 16;
-// K splits for an [n x k] weight times m rows: enough CTAs to cover the SMs,
-// each split keeping at least 2 stages
+constexpr int QG_MAX_CTAS = 4 * QG_SMS;  // split grids stay within this (partial scratch)
+// K splits for an [n x k] weight times m rows: the count whose waves of one
+// CTA per SM, each CTA paying about three stages of pipeline fill, finish
+// first; each split keeps at least 2 stages
 int qgemm_splits(int m, int n, int k) {
   const int nt = qgemm_tokens_per_tile(m);
   const int tiles = ((n + QG_BM - 1) / QG_BM) * ((m + nt - 1) / nt);
   const int stages = (k + 255) / 256;
-  int sp = (QG_SPLIT_CTAS + tiles - 1) / tiles;
-  sp = min(sp, max(1, stages / 2));
-  return max(1, min(sp, QG_MAX_SPLITS));
+  int best = 1;
+  long long best_cost = LLONG_MAX;
+  for (int sp = 1; sp <= QG_MAX_SPLITS && sp <= std::max(1, stages / 2) && (sp == 1 || tiles * sp <= QG_MAX_CTAS); sp++) {
+    const long long waves = (tiles * (long long)sp + QG_SMS - 1) / QG_SMS;
+    const long long cost = waves * ((stages + sp - 1) / sp + 3);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  return best;
 }
 }  // namespace
 
 size_t qgemm_scratch_bytes(int m, int k) {
   const int nt = qgemm_tokens_per_tile(m);
   const size_t m_pad = (size_t)(m + nt - 1) / nt * nt;
-  // scale tables, then split partials: splits x m x n <= (SM count + tiles) x 128 x nt floats,
-  // since splits only multiply grids smaller than the SM count
+  // scale tables, then split partials: splits x m x n <= QG_MAX_CTAS x 128 x nt floats
   const size_t tables = (2 * m_pad * (size_t)(k / 32) * 4 + 255) & ~(size_t)255;
-  return tables + (size_t)(2 * QG_SPLIT_CTAS) * QG_BM * nt * 4 + 256;
+  return tables + (size_t)QG_MAX_CTAS * QG_BM * nt * 4 + 256;
 }
 
 cudaError_t launch_qgemm(QgemmArgs g, const int8_t* q, const float* s, const int32_t* sums, void* scratch,
