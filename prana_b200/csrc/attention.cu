@@ -1587,13 +1587,93 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_con
     }
     return;
   }
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = (int)cluster.num_blocks();
+  if (C == a.n_splits) {
+    // the splits of this kv head form one cluster: they meet through
+    // distributed shared memory, CTA r finishing its share of the outputs
+    __shared__ float w_c[16 * 16];  // [vh][split] weights exp(m_j - max)
+    __shared__ float l_c[16];
+    cluster.sync();
+    for (int vh = wi; vh < VH; vh += TC_THREADS / 32) {
+      float mj = -INFINITY, lj = 0.0f;
+      if (lane < C) {
+        mj = *cluster.map_shared_rank(ml + vh, lane);
+        lj = *cluster.map_shared_rank(ml + 16 + vh, lane);
+      }
+      const float mx = warp_max(mj);
+      const float w = mj == -INFINITY ? 0.0f : expf(mj - mx);
+      const float lt = warp_sum(w * lj);
+      if (lane < C) w_c[vh * 16 + lane] = w;
+      if (lane == 0) l_c[vh] = lt;
+    }
+    __syncthreads();
+    const int E = VH * HD, chunk = (E + C - 1) / C;
+    const int e_end = min(E, ((int)cluster.block_rank() + 1) * chunk);
+    for (int e = (int)cluster.block_rank() * chunk + tid; e < e_end; e += TC_THREADS) {
+      const int vh = e / HD, d = e - vh * HD;
+      float acc = 0.0f;
+      for (int j = 0; j < C; j++) acc = fmaf(*cluster.map_shared_rank(o_s + e, j), w_c[vh * 16 + j], acc);
+      const int row = vh / group, head = kvh * group + vh % group;
+      out[(size_t)(row0 + row) * q_stride + head * HD + d] = acc / l_c[vh];
+    }
+    cluster.sync();  // every CTA's shared memory stays alive until the others have read it
+    return;
+  }
   float* part_ml = sq ? sq->part_ml : a.part_ml;
   float* part_o = sq ? sq->part_o : a.part_o;
-  const size_t pbase = ((size_t)kvh * a.n_splits + split) * VH;
+  const int NSP = a.n_splits;
+  const size_t pbase = ((size_t)kvh * NSP + split) * VH;
   for (int vh = tid; vh < VH; vh += TC_THREADS)
     reinterpret_cast<float2*>(part_ml)[pbase + vh] = make_float2(ml[vh], ml[16 + vh]);
   for (int e = tid; e < VH * HD / 4; e += TC_THREADS)
     reinterpret_cast<float4*>(part_o + pbase * HD)[e] = reinterpret_cast<const float4*>(o_s)[e];
+  if (!a.tail_merge) return;  // attn_merge_tc follows
+  // ---- the last split CTA of the kv head merges: every split's o rows by one
+  // bulk copy into the idle stages, the (max, sum) pairs by plain loads
+  unsigned* counters = sq ? sq->counters : a.counters;
+  __shared__ unsigned ticket;
+  __syncthreads();
+  if (tid == 0) ticket = ticket_acq_rel(counters + kvh);
+  __syncthreads();
+  if (ticket != (unsigned)NSP - 1) return;
+  const size_t hb = (size_t)kvh * NSP * VH;
+  const uint32_t o_bytes = (uint32_t)((size_t)NSP * VH * HD * 4);
+  float* po = reinterpret_cast<float*>(base + S::STAGE);  // [NSP][VH][HD] (the host checked it fits)
+  __shared__ float w_m[16 * 64];                           // [vh][split] weights (splits <= 64)
+  __shared__ float l_m[16];
+  if (tid == 0) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // the acquired partials, to the bulk copy
+    mbar_arrive_expect_tx(&bars[0], o_bytes);
+    bulk_g2s(po, part_o + hb * HD, o_bytes, &bars[0]);
+  }
+  for (int vh = wi; vh < VH; vh += TC_THREADS / 32) {
+    float mx = -INFINITY;
+    for (int j = lane; j < NSP; j += 32) mx = fmaxf(mx, __ldcg(reinterpret_cast<const float2*>(part_ml) + hb + (size_t)j * VH + vh).x);
+    mx = warp_max(mx);
+    float lsum = 0.0f;
+    for (int j = lane; j < NSP; j += 32) {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(part_ml) + hb + (size_t)j * VH + vh);
+      const float w = v.x == -INFINITY ? 0.0f : expf(v.x - mx);
+      w_m[vh * 64 + j] = w;
+      lsum = fmaf(v.y, w, lsum);
+    }
+    lsum = warp_sum(lsum);
+    if (lane == 0) l_m[vh] = lsum;
+  }
+  // full[0] completed every use the tile loop made of it; this is its next phase
+  const int uses0 = (n_tiles + NS - 1) / NS;
+  if (!mbar_wait(&bars[0], uses0 & 1) && a.err) atomicExch(a.err, ERR_TIMEOUT);
+  __syncthreads();
+  for (int e = tid; e < VH * HD; e += TC_THREADS) {
+    const int vh = e / HD, d = e - vh * HD;
+    float acc = 0.0f;
+    for (int j = 0; j < NSP; j++) acc = fmaf(po[((size_t)j * VH + vh) * HD + d], w_m[vh * 64 + j], acc);
+    const int row = vh / group, head = kvh * group + vh % group;
+    out[(size_t)(row0 + row) * q_stride + head * HD + d] = acc / l_m[vh];
+  }
+  if (tid == 0) counters[kvh] = 0u;
 }
 
 template <int HD, bool MMA>
@@ -1775,6 +1855,46 @@ static int device_sms() {
 
 // tcgen05 attention: one CTA per SM across (splits, kv heads, sequences);
 // the split count is capped by the partial scratch the caller sized
+// Cluster size for one decode sequence over n_kv kv heads: the largest C <= 16
+// for which all n_kv clusters of `kern` are resident at once (0: none).
+// Asked once per device, kernel and n_kv.
+static int tc_cluster_size(const void* kern, size_t smem, int n_kv) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({dev, kern, n_kv});
+  if (it != cache.end()) return it->second;
+  int best = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+    for (int c = 16; c >= 2 && !best; c--) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(c, n_kv);
+      cfg.blockDim = dim3(TC_THREADS);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = c;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n >= n_kv) best = c;
+    }
+  }
+  cudaGetLastError();
+  cache[{dev, kern, n_kv}] = best;
+  return best;
+}
+
+template <int HD, int NQ>
+static const void* tc_kernel(bool two) {
+  return two ? (const void*)attn_decode_tc<HD, NQ, 2> : (const void*)attn_decode_tc<HD, NQ, 3>;
+}
+
 template <int HD>
 static cudaError_t tc_go(const AttnArgs& a, cudaStream_t st, bool pdl, int n_seq) {
   const int group = a.n_heads / a.n_kv;
@@ -1782,18 +1902,47 @@ static cudaError_t tc_go(const AttnArgs& a, cudaStream_t st, bool pdl, int n_seq
   const bool narrow = a.m * group <= 8;
   const int max_rows = (narrow ? 8 : 16) / group;
   if (max_rows < 1) return cudaErrorInvalidValue;
-  AttnArgs aa = a;
-  aa.n_splits = std::max(1, std::min(a.n_splits, device_sms() / (a.n_kv * n_seq)));
-  // at most two tiles per CTA at full capacity: two stages, which leaves room
-  // for the previous kernel's CTAs, else three
   const int cap = a.cap > 0 ? a.cap : a.pos0 + a.m;
-  const bool two = (cap + aa.n_splits - 1) / aa.n_splits <= 2 * TC_C;
-  const void* kern = narrow ? (two ? (const void*)attn_decode_tc<HD, 8, 2> : (const void*)attn_decode_tc<HD, 8, 3>)
-                            : (two ? (const void*)attn_decode_tc<HD, 16, 2> : (const void*)attn_decode_tc<HD, 16, 3>);
+  auto pick = [&](int splits) {  // at most two tiles per CTA: two stages, else three
+    return (cap + splits - 1) / splits <= 2 * TC_C;
+  };
+  AttnArgs aa = a;
+  // one sequence: the splits of a kv head as one cluster (merged in distributed
+  // shared memory) when the clusters fit; otherwise one CTA per SM over
+  // (splits, kv heads, sequences) and a merge kernel behind
+  int cluster = 0;
+  bool two = false;
+  if (n_seq == 1) {
+    for (int c = 16; c >= 2 && !cluster; c--) {
+      const bool t = pick(c);
+      const int cs = tc_cluster_size(narrow ? tc_kernel<HD, 8>(t) : tc_kernel<HD, 16>(t),
+                                     t ? TcSmem<HD, 2>::bytes : TcSmem<HD, 3>::bytes, a.n_kv);
+      if (cs == c) {
+        cluster = c;
+        two = t;
+      } else if (cs > 0 && cs < c) {
+        c = cs + 1;  // retry at the size that fits
+      }
+    }
+  }
+  if (cluster) {
+    aa.n_splits = cluster;
+  } else {
+    aa.n_splits = std::max(1, std::min(a.n_splits, device_sms() / (a.n_kv * n_seq)));
+    two = pick(aa.n_splits);
+  }
+  const void* kern = narrow ? tc_kernel<HD, 8>(two) : tc_kernel<HD, 16>(two);
   const size_t smem = two ? TcSmem<HD, 2>::bytes : TcSmem<HD, 3>::bytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  if (aa.n_splits > 1) {
+  // split partials: merged by the kernel's last CTA when every split's o rows
+  // fit its idle stages, else by attn_merge_tc behind it
+  const size_t stage_bytes = TcSmem<HD, 2>::STAGE;
+  const int max_vh = std::min(a.m, max_rows) * group;
+  aa.tail_merge = !cluster && aa.n_splits > 1 && aa.n_splits <= 64 &&
+                  (size_t)aa.n_splits * max_vh * HD * 4 <= (two ? 1 : 2) * stage_bytes;
+  const bool merge = aa.n_splits > 1 && !cluster && !aa.tail_merge;
+  if (merge) {
     e = cudaFuncSetAttribute((const void*)attn_merge_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)TC_MERGE_SMEM);
     if (e != cudaSuccess) return e;
@@ -1801,30 +1950,42 @@ static cudaError_t tc_go(const AttnArgs& a, cudaStream_t st, bool pdl, int n_seq
   for (int row0 = 0; row0 < a.m; row0 += max_rows) {
     int n_rows = min(max_rows, a.m - row0);
     void* args[] = {&aa, (void*)&row0, (void*)&n_rows};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (cluster) {
+      attr[na].id = cudaLaunchAttributeClusterDimension;
+      attr[na].val.clusterDim.x = cluster;
+      attr[na].val.clusterDim.y = 1;
+      attr[na].val.clusterDim.z = 1;
+      na++;
+    }
+    if (pdl && row0 == 0) {
+      attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[na].val.programmaticStreamSerializationAllowed = 1;
+      na++;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(aa.n_splits, a.n_kv, n_seq);
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    if (pdl && row0 == 0) {
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-    }
+    cfg.attrs = na ? attr : nullptr;
+    cfg.numAttrs = na;
     e = cudaLaunchKernelExC(&cfg, kern, args);
     if (e != cudaSuccess) return e;
-    if (aa.n_splits > 1) {  // the merge, right behind (programmatic: it waits for the whole grid)
+    if (merge) {  // the merge, right behind (programmatic: it waits for the whole grid)
       const size_t vhn = (size_t)n_rows * group * aa.n_splits, w_bytes = ((vhn + 3) & ~(size_t)3) * 4;
       const size_t need = w_bytes + vhn * HD * 4;
+      cudaLaunchAttribute pa[1];
+      pa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      pa[0].val.programmaticStreamSerializationAllowed = 1;
       cudaLaunchConfig_t mc = {};
       mc.gridDim = dim3(a.n_kv, n_seq);
       mc.blockDim = dim3(HD);
       mc.dynamicSmemBytes = need <= TC_MERGE_SMEM ? need : w_bytes;
       mc.stream = st;
       if (pdl) {
-        mc.attrs = attr;
+        mc.attrs = pa;
         mc.numAttrs = 1;
       }
       e = cudaLaunchKernelExC(&mc, (const void*)attn_merge_tc<HD>, args);

@@ -75,6 +75,7 @@ struct AttnArgs {
   float* out;            // [m][n_heads*hd]
   unsigned* err;         // device error flag for bounded waits (nullable)
   int cap;               // positions the cache holds (0: pos0 + m); sizes the launch, not the work
+  int tail_merge;        // tcgen05 attention: the last split CTA merges (else a merge kernel follows)
   // non-null: gridDim.z sequences, sequence z = seqs[z] (one query row each,
   // at q / out row z); seqs replaces tm_*, kc, vc, pos0, part_*, counters
   const AttnSeq* seqs;

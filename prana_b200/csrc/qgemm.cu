@@ -219,6 +219,12 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
   const int all_stages = (K + BK - 1) / BK;
   const int s_lo = (int)(((long long)all_stages * blockIdx.z) / gridDim.z);
   const int n_stage = (int)(((long long)all_stages * (blockIdx.z + 1)) / gridDim.z) - s_lo;
+  // CTAs walk their stages from different starting points, so that at any
+  // moment the grid's copies read different offsets of the weight rows rather
+  // than one column band of every row (which concentrates on few DRAM
+  // channels); each CTA's order is fixed, so results are reproducible
+  const int rot = n_stage > 0 ? (int)(blockIdx.x % (unsigned)n_stage) : 0;
+  auto gstage = [&](int s) { return s_lo + (s + rot) % n_stage; };
 
   if (tid == 0) {
     s_abort = 0;
@@ -253,7 +259,7 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
         if (*abort) break;
         uint8_t* sm = stage(st);
         mbar_arrive_expect_tx(&full[st], L::TX);
-        const int sg = s_lo + s, k0 = sg * BK;
+        const int sg = gstage(s), k0 = sg * BK;
 #pragma unroll
         for (int a = 0; a < L::KATOMS; a++) tma_load_2d(sm + L::OFF_B + a * NT * 128, &tm_x, k0 + a * 128, tok0, &full[st]);
         if constexpr (F::RAW == 0) {
@@ -288,7 +294,7 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
         if (!ok) break;
         tc_fence_after();
         const uint32_t a_base = smem_u32(stage(st)), b_base = a_base + L::OFF_B;
-        const int nb = min(BLK, n_blk - (s_lo + s) * BLK);
+        const int nb = min(BLK, n_blk - gstage(s) * BLK);
         const int total = nb * MPB;  // MMAs of this stage: (block j, half h) in order
         for (int i0 = 0; i0 < total && ok; i0 += GS, grp++) {
           const int gslot = grp % NG;
@@ -354,8 +360,8 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
     unsigned short dn[BLK], dc[BLK];
     float dnf[BLK], dcf[BLK];  // Q8S: f32 scales
     uint4 scn = make_uint4(0u, 0u, 0u, 0u), scc = scn;
-    auto load_scales = [&](int s) {  // s: global stage
-      if (s >= s_lo + n_stage) return;
+    auto load_scales = [&](int s) {  // s: global stage (< 0: none)
+      if (s < 0) return;
       if constexpr (T == T_Q8_0 || T == T_Q4_0) {
         const unsigned short* d = reinterpret_cast<const unsigned short*>(g.w.d) + (size_t)rr * n_blk + s * BLK;
         const int nb = min(BLK, n_blk - s * BLK);
@@ -373,12 +379,12 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
         scn = __ldg(reinterpret_cast<const uint4*>(g.w.sc + (size_t)rr * (K / 16)) + s);
       }
     };
-    load_scales(s_lo);
+    load_scales(n_stage > 0 ? gstage(0) : -1);
     int grp = 0;
     bool ok = true;
     constexpr int NB = (32 / NC) < 1 ? 1 : ((32 / NC) < GS ? (32 / NC) : GS);  // slots per load batch (<= 32 registers)
     for (int s = 0; s < n_stage && ok; s++) {
-      const int st = s % NS, sg = s_lo + s;
+      const int st = s % NS, sg = gstage(s);
       const uint8_t* sm = stage(st);
 #pragma unroll
       for (int j = 0; j < BLK; j++) {
@@ -386,7 +392,7 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
         dcf[j] = dnf[j];
       }
       scc = scn;
-      load_scales(sg + 1);
+      load_scales(s + 1 < n_stage ? gstage(s + 1) : -1);
       if (!qwait(&full[st], (s / NS) & 1, abort)) {
         ok = false;
         break;
