@@ -357,7 +357,10 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
     // weight scales of a stage, loaded one stage ahead: Q8_0 / Q4_0 the f16 d
     // of each block; Q6_K the super-block's d and its 16 int8 sub-block scales
     // (Q4_K's live in the staged super-block header)
-    unsigned short dn[BLK], dc[BLK];
+    // f16 scales: two per word at up to 32 tokens, one per register at 64
+    // (where the epilogue's accumulators leave fewer registers)
+    uint32_t dn[BLK / 2], dc[BLK / 2];
+    unsigned short dn1[BLK], dc1[BLK];
     float dnf[BLK], dcf[BLK];  // Q8S: f32 scales
     uint4 scn = make_uint4(0u, 0u, 0u, 0u), scc = scn;
     auto load_scales = [&](int s) {  // s: global stage (< 0: none)
@@ -365,15 +368,37 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
       if constexpr (T == T_Q8_0 || T == T_Q4_0) {
         const unsigned short* d = reinterpret_cast<const unsigned short*>(g.w.d) + (size_t)rr * n_blk + s * BLK;
         const int nb = min(BLK, n_blk - s * BLK);
+        // the stage's 8 scales: one 16-byte load (16-token tiles, whose
+        // epilogue has the registers to spare)
+        if (NT <= 32 && nb == BLK && (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(d));
+          dn[0] = v.x;
+          dn[1] = v.y;
+          dn[2] = v.z;
+          dn[3] = v.w;
+        } else if constexpr (NT <= 32) {
 #pragma unroll
-        for (int j = 0; j < BLK; j++)
-          if (j < nb) dn[j] = __ldg(d + j);
+          for (int j = 0; j < BLK / 2; j++) dn[j] = 0u;
+#pragma unroll
+          for (int j = 0; j < BLK; j++)
+            if (j < nb) dn[j >> 1] |= (uint32_t)__ldg(d + j) << (16 * (j & 1));
+        } else {
+#pragma unroll
+          for (int j = 0; j < BLK; j++)
+            if (j < nb) dn1[j] = __ldg(d + j);
+        }
       } else if constexpr (T == T_Q8S) {
         const float* d = g.w.ds + (size_t)rr * n_blk + s * BLK;
         const int nb = min(BLK, n_blk - s * BLK);
+        if (NT <= 32 && nb == BLK && (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
+          const float4 v0 = __ldg(reinterpret_cast<const float4*>(d)), v1 = __ldg(reinterpret_cast<const float4*>(d) + 1);
+          dnf[0] = v0.x; dnf[1] = v0.y; dnf[2] = v0.z; dnf[3] = v0.w;
+          dnf[4] = v1.x; dnf[5] = v1.y; dnf[6] = v1.z; dnf[7] = v1.w;
+        } else {
 #pragma unroll
-        for (int j = 0; j < BLK; j++)
-          if (j < nb) dnf[j] = __ldg(d + j);
+          for (int j = 0; j < BLK; j++)
+            if (j < nb) dnf[j] = __ldg(d + j);
+        }
       } else if constexpr (T == T_Q6_K) {
         dn[0] = __ldg(reinterpret_cast<const unsigned short*>(g.w.d) + (size_t)rr * (K / 256) + s);
         scn = __ldg(reinterpret_cast<const uint4*>(g.w.sc + (size_t)rr * (K / 16)) + s);
@@ -387,10 +412,11 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
       const int st = s % NS, sg = gstage(s);
       const uint8_t* sm = stage(st);
 #pragma unroll
-      for (int j = 0; j < BLK; j++) {
-        dc[j] = dn[j];
-        dcf[j] = dnf[j];
-      }
+      for (int j = 0; j < BLK / 2; j++) dc[j] = dn[j];
+#pragma unroll
+      for (int j = 0; j < BLK; j++) dc1[j] = dn1[j];
+#pragma unroll
+      for (int j = 0; j < BLK; j++) dcf[j] = dnf[j];
       scc = scn;
       load_scales(s + 1 < n_stage ? gstage(s + 1) : -1);
       if (!qwait(&full[st], (s / NS) & 1, abort)) {
@@ -447,11 +473,19 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
                 for (int q = 1; q < BLK; q++)
                   if (q == j) ws0 = dcf[q];  // a register select, not an indexed local array
               } else {
-                unsigned short dj = dc[0];
+                if constexpr (NT <= 32) {
+                  uint32_t wsel = dc[0];
 #pragma unroll
-                for (int q = 1; q < BLK; q++)
-                  if (q == j) dj = dc[q];
-                ws0 = h2f(dj);
+                  for (int q = 1; q < BLK / 2; q++)
+                    if (q == (j >> 1)) wsel = dc[q];  // register selects, not an indexed local array
+                  ws0 = h2f((unsigned short)(wsel >> (16 * (j & 1))));
+                } else {
+                  unsigned short dj = dc1[0];
+#pragma unroll
+                  for (int q = 1; q < BLK; q++)
+                    if (q == j) dj = dc1[q];
+                  ws0 = h2f(dj);
+                }
               }
 #pragma unroll
               for (int c = 0; c < NC; c++) acc[c] = fmaf(__fmul_rn(ws0, sa[c]), (float)(int32_t)v[k][c], acc[c]);
@@ -471,7 +505,7 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
               }
             } else {
               // (d * sa) * sc * dot per 16-value sub-block (kquant.rs:287-318)
-              const float d = h2f(dc[0]);
+              const float d = h2f((unsigned short)dc[0]);
               const int si = 2 * j + h;  // sub-block scale byte si of the 16
               const unsigned word = si < 8 ? (si < 4 ? scc.x : scc.y) : (si < 12 ? scc.z : scc.w);
               const float scf = (float)(int8_t)((word >> (8 * (si & 3))) & 0xffu);
