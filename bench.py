@@ -379,7 +379,7 @@ def batch_decode(torch, model, args, stream, steps=24, warmup=3):
         ms = e0.elapsed_time(e1) / steps
         return {"value": round(n * 1000.0 / ms, 2), "unit": "tok/s", "sequences": n, "ms_per_step": round(ms, 3),
                 "steps": steps, "ctx": args.ctx, "h2d_bytes_per_step": 4 * n + 8 * n, "d2h_bytes_per_step": 4 * n,
-                "path": "prana_forward_multi: GEMV rows in chunks of 8, attention per sequence"}
+                "path": "prana_forward_multi, one CUDA graph per cache set: tensor-core GEMMs over the 16 rows, one attention launch over all sequences"}
     finally:
         for kv in caches:
             kv.close()
@@ -657,7 +657,7 @@ def suite_c3(torch, args, peak):
                     "d2h_bytes_per_step": 4},
             "prefill": {"tokens": len(prompt) - 1, "ms": round(ms_prefill, 2),
                         "tok_s": round((len(prompt) - 1) * 1000.0 / ms_prefill, 1),
-                        "path": "streaming GEMV, 8 rows per launch; f32 in-window attention"},
+                        "path": "tensor-core GEMMs over the prompt rows; f32 in-window attention"},
             "step_roofline": {"bytes_per_token": bt, "achieved_gbs": round(bt / ms / 1e6, 1),
                               "frac": round(bt / ms / 1e6 / peak, 4)},
             "cpu_baseline": {"value": round(tps, 3), "unit": UNIT, "cores": threads, "kind": "port",
