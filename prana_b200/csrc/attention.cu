@@ -1150,25 +1150,33 @@ __global__ void __launch_bounds__(256, 2) attn_decode_cluster(const __grid_const
 // ---------------------------------------------------------------- tcgen05 decode / verify
 // The same attention on the 5th-generation tensor cores, one tile of 128
 // positions at a time, warp-specialized:
-//   warp 4 (one lane)   TMA: K and V boxes of each tile into a 3-stage ring,
-//                       the tiles before pos0 ahead of the programmatic wait
-//   warp 5 (one lane)   MMAs: S = K . [q_hi | q_lo]^T (M = 128 positions,
-//                       N = 32: the hi and lo halves side by side) into one of
-//                       two TMEM buffers as soon as a tile lands, and
+//   warp 8 (one lane)   TMA: K and V boxes of each tile into a 2- or 3-stage
+//                       ring, the tiles before pos0 ahead of the programmatic
+//                       wait
+//   warp 9 (one lane)   MMAs: S = K . [q_hi | q_lo]^T (M = 128 positions,
+//                       N = 2 NQ: the hi and lo halves side by side) into one
+//                       of two TMEM buffers as soon as a tile lands, and
 //                       O^T = V^T . [P_hi | P_lo] (M = 128 dims, V read
-//                       MN-major straight from its TMA box) once P is written
-//   warps 0-3           one thread per position: scores = hi + lo columns,
-//                       masked and scaled, exp against a running reference
-//                       max that moves only when a score passes it by more
-//                       than 8 (then the tile's exact max, and a rescale);
-//                       P to shared memory as f16 hi / lo; then one thread per
-//                       dim folds O_hi + O_lo of the previous tile into its
-//                       registers.  Per-thread sums of P meet once at the end.
+//                       MN-major straight from its TMA box) once P is
+//                       written; whichever of the two is ready goes first, so
+//                       a late tile never holds back the P.V of an earlier one
+//   warps 0-3, 4-7      two softmax groups on alternate tiles (group g takes
+//                       tiles g, g + 2, ...: its own S, P and O buffers), one
+//                       thread per position: scores = hi + lo columns,
+//                       masked and scaled, exp against the group's running
+//                       reference max that moves only when a score passes it
+//                       by more than 8 (then the tile's exact max, and a
+//                       rescale); P to shared memory as f16 hi / lo; one
+//                       thread per dim folds O_hi + O_lo of the group's
+//                       previous tile into its registers.  Per-thread sums of
+//                       P meet once at the end, then the two groups' (max,
+//                       sum, o) as two partials.
 // q and P enter as f16 hi + lo pairs (each product carries ~22 bits of the
 // f32 operand; K and V are f16 already); accumulation is f32.  The n_splits
 // position ranges of a kv head meet as in attn_finish.
 constexpr int TC_C = 128;
-constexpr int TC_THREADS = 192;   // warps 0-3 softmax, 4 TMA, 5 MMA
+constexpr int TC_THREADS = 320;   // warps 0-7 softmax (two groups), 8 TMA, 9 MMA
+constexpr int TC_TMA_WARP = 8, TC_MMA_WARP = 9;
 constexpr int TC_COLS = 128;      // TMEM: S buffers [0, 64), O buffers [64, 128)
 constexpr float TC_TAU = 8.0f;    // largest exponent before the reference max moves
 
@@ -1180,8 +1188,8 @@ struct TcSmem {
   static constexpr size_t OP = 32 * 128 * 2;                // a 32-row x 128-value f16 operand tile
   static constexpr size_t OFF_Q = NS * STAGE;
   static constexpr size_t OFF_P = OFF_Q + OP;               // two P tiles
-  static constexpr size_t OFF_RED = OFF_P + 2 * OP;         // [4 warps][16] floats
-  static constexpr size_t bytes = 1024 + OFF_RED + 4 * 16 * sizeof(float) + 64;
+  static constexpr size_t OFF_RED = OFF_P + 2 * OP;         // [2 groups][4 warps][16] floats
+  static constexpr size_t bytes = 1024 + OFF_RED + 8 * 16 * sizeof(float) + 64;
   static_assert(sizeof(float) * 16 * HD <= STAGE, "o staging");
 };
 
@@ -1207,14 +1215,16 @@ __device__ __forceinline__ bool twait(uint64_t* bar, uint32_t phase, volatile in
   *abort = 1;
   return false;
 }
-// named barrier of the four softmax warps; the OR of `pred` over them
-__device__ __forceinline__ void sm_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-__device__ __forceinline__ bool sm_any(bool pred) {
+// named barriers of softmax group g (1 + g: its four warps) and of both
+// groups (3); the OR of `pred` over a group
+__device__ __forceinline__ void grp_sync(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
+__device__ __forceinline__ void both_sync() { asm volatile("bar.sync 3, 256;" ::: "memory"); }
+__device__ __forceinline__ bool grp_any(int g, bool pred) {
   uint32_t r;
   asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}"
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, 128, p;\n selp.u32 %0, 1, 0, q;\n}"
       : "=r"(r)
-      : "r"((uint32_t)pred)
+      : "r"((uint32_t)pred), "r"(1 + g)
       : "memory");
   return r != 0;
 }
@@ -1284,9 +1294,11 @@ __global__ void __launch_bounds__(HD) attn_merge_tc(const __grid_constant__ Attn
   }
 }
 
-// NQ: virtual-head columns of each half (8 when VH <= 8, else 16); NS: K/V stages
-template <int HD, int NQ, int NS>
+// NQ: virtual-head columns of each half (8 when VH <= 8, else 16); NS: K/V
+// stages; VHC: a compile-time bound on VH, the heads the per-position loops run
+template <int HD, int NQ, int NS, int VHC>
 __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_constant__ AttnArgs a, int row0, int n_rows) {
+  static_assert(VHC <= NQ, "virtual heads");
   using S = TcSmem<HD, NS>;
   constexpr int TC_NS = NS;
   constexpr int NB = S::NB, KSTEPS = HD / 16, PSTEPS = TC_C / 16;
@@ -1295,7 +1307,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_con
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~(uintptr_t)1023);
   uint8_t* q_t = base + S::OFF_Q;
   uint8_t* p_t = base + S::OFF_P;
-  float* red = reinterpret_cast<float*>(base + S::OFF_RED);  // [4][16]
+  float* red = reinterpret_cast<float*>(base + S::OFF_RED);  // [2][4][16]
   // full[3] stage_free[3] s_full[2] s_free[2] p_full[2] o_full[2] o_free[2] q_ready mma_done
   __shared__ __align__(8) uint64_t bars[18];
   uint64_t* full = bars;
@@ -1311,7 +1323,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_con
   __shared__ int s_abort;
   volatile int* abort = &s_abort;
 
-  const int group = a.n_heads / a.n_kv, VH = n_rows * group;  // VH <= NQ
+  const int group = a.n_heads / a.n_kv, VH = n_rows * group;  // VH <= VHC
   const int split = blockIdx.x, kvh = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, wi = tid >> 5;
   const int q_stride = a.n_heads * HD;
@@ -1333,13 +1345,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_con
   auto kbox = [&](int st, int b) { return base + st * S::STAGE + b * S::BOX; };
   auto vbox = [&](int st, int b) { return base + st * S::STAGE + (NB + b) * S::BOX; };
 
-  if (tid == 0) {
+  auto issue = [&](int i) {  // the K and V boxes of tile i
+    const int st = i % TC_NS, t0 = t_begin + i * TC_C;
+    mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * NB * S::BOX));
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+      tma_load_3d(kbox(st, b), tm_k, b * AC_BOX, kvh, t0, &full[st]);
+      tma_load_3d(vbox(st, b), tm_v, b * AC_BOX, kvh, t0, &full[st]);
+    }
+  };
+  int pre = 0;  // tiles issued ahead of the setup barrier
+  if (wi == TC_TMA_WARP && lane == 0) {
     s_abort = 0;
     for (int i = 0; i < 3; i++) {
       mbar_init(&full[i], 1);
       mbar_init(&stage_free[i], 1);
     }
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < 2; i++) {  // buffer i belongs to softmax group i
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
@@ -1349,12 +1371,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_con
     mbar_init(q_ready, 128);
     mbar_init(mma_done, 1);
     fence_barrier_init();
+    // tiles holding only rows written by earlier steps go first, before the
+    // programmatic wait and the rest of the setup
+    for (; pre < TC_NS && pre < n_tiles && t_begin + (pre + 1) * TC_C <= pos0; pre++) issue(pre);
   }
-  if (wi == 5) {
+  if (wi == TC_MMA_WARP) {
     tc_alloc(&tmem_s, TC_COLS);
     tc_relinquish();
   }
-  // P rows >= VH (and their lo rows) stay zero; the others are rewritten every tile
+  // P rows >= VHC (and their lo rows) stay zero; the others are rewritten every tile
   for (int i = tid; i < (int)(2 * S::OP / 16); i += TC_THREADS)
     reinterpret_cast<uint4*>(p_t)[i] = make_uint4(0u, 0u, 0u, 0u);
   tc_fence_before();
@@ -1364,21 +1389,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_con
   pdl_trigger();
   bool ok = true;
 
-  if (wi == 4) {
+  if (wi == TC_TMA_WARP) {
     // ------------------------------------------------ TMA
     if (lane == 0) {
-      auto issue = [&](int i) {
-        const int st = i % TC_NS, t0 = t_begin + i * TC_C;
-        mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * NB * S::BOX));
-#pragma unroll
-        for (int b = 0; b < NB; b++) {
-          tma_load_3d(kbox(st, b), tm_k, b * AC_BOX, kvh, t0, &full[st]);
-          tma_load_3d(vbox(st, b), tm_v, b * AC_BOX, kvh, t0, &full[st]);
-        }
-      };
-      int i = 0;
-      // tiles holding only rows written by earlier steps load before the wait
-      for (; i < TC_NS && i < n_tiles && t_begin + (i + 1) * TC_C <= pos0; i++) issue(i);
+      int i = pre;
       pdl_wait();
       int issued = i;
       for (; i < n_tiles; i++) {
@@ -1392,38 +1406,53 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_con
         ok = mbar_wait(&full[j % TC_NS], (j / TC_NS) & 1, *abort ? (1u << 16) : kMbarPolls) && ok;
     }
     __syncwarp();
-  } else if (wi == 5) {
-    // ------------------------------------------------ MMA: S of the next tile goes ahead of P.V of this one
+  } else if (wi == TC_MMA_WARP) {
+    // ------------------------------------------------ MMA
+    // S(j) goes once its tile has landed and group j & 1 has read S(j - 2);
+    // P.V(j) once P(j) is written and the group has folded O(j - 2) (the
+    // group folds O(j - 2) before it writes P(j), so that P tile is free).
+    // Non-blocking tests: neither stream waits behind the other.
     if (lane == 0) {
       const uint64_t qd = sw128_desc(smem_u32(q_t));
-      auto issue_s = [&](int j) {
-        const int st = j % TC_NS, sb = j & 1;
-        if (!twait(&full[st], (j / TC_NS) & 1, abort)) return false;
-        if (j >= 2 && !twait(&s_free[sb], ((j - 2) >> 1) & 1, abort)) return false;
-        tc_fence_after();
-        const uint64_t k0 = sw128_desc(smem_u32(kbox(st, 0)));
+      bool go = twait(q_ready, 0, abort);
+      int ns = 0, np = 0;
+      uint32_t idle = 0;
+      while (go && np < n_tiles) {
+        bool moved = false;
+        if (ns < n_tiles && mbar_test_wait(&full[ns % TC_NS], (ns / TC_NS) & 1) &&
+            (ns < 2 || mbar_test_wait(&s_free[ns & 1], ((ns - 2) >> 1) & 1))) {
+          const int st = ns % TC_NS, sb = ns & 1;
+          tc_fence_after();
+          const uint64_t k0 = sw128_desc(smem_u32(kbox(st, 0)));
 #pragma unroll
-        for (int ks = 0; ks < KSTEPS; ks++)
-          tc_mma_f16(tmem + (uint32_t)(sb * 32), k0 + (uint64_t)((ks >> 2) * (S::BOX >> 4) + (ks & 3) * 2),
-                     qd + (uint64_t)((ks >> 2) * 256 + (ks & 3) * 2), IDESC_S, ks > 0);
-        tc_commit(&s_full[sb]);
-        return true;
-      };
-      bool go = twait(q_ready, 0, abort) && (n_tiles == 0 || issue_s(0));
-      for (int i = 0; go && i < n_tiles; i++) {
-        if (i + 1 < n_tiles && !issue_s(i + 1)) break;
-        const int st = i % TC_NS, pb = i & 1;
-        if (!twait(&p_full[pb], (i >> 1) & 1, abort)) break;
-        if (i >= 2 && !twait(&o_free[pb], ((i - 2) >> 1) & 1, abort)) break;
-        tc_fence_after();
-        const uint64_t v0 = sw128_desc_mn(smem_u32(vbox(st, 0)), (uint32_t)S::BOX, 1024u);
-        const uint64_t p0 = sw128_desc(smem_u32(p_t + pb * S::OP));
+          for (int ks = 0; ks < KSTEPS; ks++)
+            tc_mma_f16(tmem + (uint32_t)(sb * 32), k0 + (uint64_t)((ks >> 2) * (S::BOX >> 4) + (ks & 3) * 2),
+                       qd + (uint64_t)((ks >> 2) * 256 + (ks & 3) * 2), IDESC_S, ks > 0);
+          tc_commit(&s_full[sb]);
+          ns++;
+          moved = true;
+        }
+        if (np < ns && mbar_test_wait(&p_full[np & 1], (np >> 1) & 1) &&
+            (np < 2 || mbar_test_wait(&o_free[np & 1], ((np - 2) >> 1) & 1))) {
+          const int st = np % TC_NS, pb = np & 1;
+          tc_fence_after();
+          const uint64_t v0 = sw128_desc_mn(smem_u32(vbox(st, 0)), (uint32_t)S::BOX, 1024u);
+          const uint64_t p0 = sw128_desc(smem_u32(p_t + pb * S::OP));
 #pragma unroll
-        for (int ks = 0; ks < PSTEPS; ks++)
-          tc_mma_f16(tmem + 64u + (uint32_t)(pb * 32), v0 + (uint64_t)(ks * 128),
-                     p0 + (uint64_t)((ks >> 2) * 256 + (ks & 3) * 2), IDESC_O, ks > 0);
-        tc_commit(&o_full[pb]);
-        tc_commit(&stage_free[st]);
+          for (int ks = 0; ks < PSTEPS; ks++)
+            tc_mma_f16(tmem + 64u + (uint32_t)(pb * 32), v0 + (uint64_t)(ks * 128),
+                       p0 + (uint64_t)((ks >> 2) * 256 + (ks & 3) * 2), IDESC_O, ks > 0);
+          tc_commit(&o_full[pb]);
+          tc_commit(&stage_free[st]);
+          np++;
+          moved = true;
+        }
+        if (moved) {
+          idle = 0;
+        } else if (++idle >= kMbarPolls || ((idle & 255) == 255 && *abort)) {
+          *abort = 1;
+          break;
+        }
       }
       // wind down: every MMA issued has completed before TMEM is freed
       tc_commit(mma_done);
@@ -1431,105 +1460,117 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_con
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------ softmax / output (warps 0-3)
+    // ------------------------------------------------ softmax groups (warps 0-3, 4-7)
+    const int g = wi >> 2, wq = wi & 3;  // group; warp in the group = its TMEM lane quarter
+    const int r = tid & 127;              // TMEM lane: tile position r for S, dim r for O
     pdl_wait();
-    // q rows of the virtual heads as f16 hi (rows 0..NQ) and lo (NQ..2 NQ); rows >= VH zero
-    for (int c = tid; c < NQ * (HD / 4); c += 128) {
-      const int vh = c / (HD / 4), d = (c - vh * (HD / 4)) * 4;
-      float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (vh < VH)
-        x = *reinterpret_cast<const float4*>(qz + (size_t)(row0 + vh / group) * q_stride +
-                                             (size_t)(kvh * group + vh % group) * HD + d);
-      const float xs[4] = {x.x, x.y, x.z, x.w};
-      __half hh[4], hl[4];
+    if (g == 0) {
+      // q rows of the virtual heads as f16 hi (rows 0..NQ) and lo (NQ..2 NQ); rows >= VH zero
+      for (int c = r; c < NQ * (HD / 4); c += 128) {
+        const int vh = c / (HD / 4), d = (c - vh * (HD / 4)) * 4;
+        float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (vh < VH)
+          x = *reinterpret_cast<const float4*>(qz + (size_t)(row0 + vh / group) * q_stride +
+                                               (size_t)(kvh * group + vh % group) * HD + d);
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+        __half hh[4], hl[4];
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        hh[e] = __float2half_rn(xs[e]);
-        hl[e] = __float2half_rn(xs[e] - __half2float(hh[e]));
+        for (int e = 0; e < 4; e++) {
+          hh[e] = __float2half_rn(xs[e]);
+          hl[e] = __float2half_rn(xs[e] - __half2float(hh[e]));
+        }
+        *reinterpret_cast<uint2*>(q_t + op_off(vh, d)) = *reinterpret_cast<const uint2*>(hh);
+        *reinterpret_cast<uint2*>(q_t + op_off(NQ + vh, d)) = *reinterpret_cast<const uint2*>(hl);
       }
-      *reinterpret_cast<uint2*>(q_t + op_off(vh, d)) = *reinterpret_cast<const uint2*>(hh);
-      *reinterpret_cast<uint2*>(q_t + op_off(NQ + vh, d)) = *reinterpret_cast<const uint2*>(hl);
+      fence_async_smem();
+      mbar_arrive(q_ready);
     }
-    fence_async_smem();
-    mbar_arrive(q_ready);
 
-    float m_run[NQ], l_thr[NQ], o_acc[NQ], alpha_prev[NQ];
+    float m_run[VHC], l_thr[VHC], o_acc[VHC], alpha_prev[VHC];
 #pragma unroll
-    for (int h = 0; h < NQ; h++) {
+    for (int h = 0; h < VHC; h++) {
       m_run[h] = -INFINITY;
       l_thr[h] = 0.0f;
       o_acc[h] = 0.0f;
       alpha_prev[h] = 1.0f;
     }
-    const int r = tid;  // TMEM lane: tile position r for S, dim r for O
-    const uint32_t lane_base = (uint32_t)(wi * 32) << 16;
-    auto ld_cols = [&](uint32_t taddr, uint32_t* v) {  // 2 NQ columns of this lane
-      if constexpr (NQ == 8)
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const uint32_t s_col = (uint32_t)(g * 32), o_col = 64u + (uint32_t)(g * 32);
+    // hi columns [0, VHC) and lo columns [NQ, NQ + VHC) of this lane
+    auto ld_cols = [&](uint32_t taddr, uint32_t* v) {
+      if constexpr (VHC <= 4) {
+        tc_ld4(taddr, v);
+        tc_ld4(taddr + NQ, v + NQ);
+      } else if constexpr (NQ == 8) {
         tc_ld16(taddr, v);
-      else
+      } else {
         tc_ld32(taddr, v);
+      }
       tc_wait_ld();
     };
-    // O of tile i into the registers, rescaled by that tile's alpha
+    // O of the group's tile i into the registers, rescaled by that tile's alpha
     auto fold = [&](int i, const float* al) {
-      const int pb = i & 1;
-      ok = twait(&o_full[pb], (i >> 1) & 1, abort) && ok;
+      ok = twait(&o_full[g], (i >> 1) & 1, abort) && ok;
       tc_fence_after();
       uint32_t ov[2 * NQ];
-      ld_cols(tmem + lane_base + 64u + (uint32_t)(pb * 32), ov);
+      ld_cols(tmem + lane_base + o_col, ov);
       tc_fence_before();
-      mbar_arrive(&o_free[pb]);
+      mbar_arrive(&o_free[g]);
 #pragma unroll
-      for (int h = 0; h < NQ; h++)
+      for (int h = 0; h < VHC; h++)
         o_acc[h] = fmaf(o_acc[h], al[h], __uint_as_float(ov[h]) + __uint_as_float(ov[NQ + h]));
     };
-    for (int i = 0; i < n_tiles; i++) {
-      const int sb = i & 1, st = i % TC_NS, t = t_begin + i * TC_C + r;
-      ok = twait(&s_full[sb], (i >> 1) & 1, abort) && ok;
+    int last = -1;  // the group's last tile
+    for (int i = g; i < n_tiles; i += 2) {
+      const int st = i % TC_NS, t = t_begin + i * TC_C + r;
+      // O of the group's previous tile while S(i) is on its way; once it is
+      // in, P.V(i - 2) has completed and its P tile may be rewritten
+      if (i >= 2) fold(i - 2, alpha_prev);
+      ok = twait(&s_full[g], (i >> 1) & 1, abort) && ok;
       tc_fence_after();
       uint32_t sv[2 * NQ];
-      ld_cols(tmem + lane_base + (uint32_t)(sb * 32), sv);
+      ld_cols(tmem + lane_base + s_col, sv);
       tc_fence_before();
-      mbar_arrive(&s_free[sb]);
-      float sc[NQ], alpha[NQ];
+      mbar_arrive(&s_free[g]);
+      float sc[VHC], alpha[VHC];
       bool over = false;
 #pragma unroll
-      for (int h = 0; h < NQ; h++) {
+      for (int h = 0; h < VHC; h++) {
         const bool vis = h < VH && t < t_end && t <= pos0 + row0 + h / group;
         sc[h] = vis ? __fmul_rn(__uint_as_float(sv[h]) + __uint_as_float(sv[NQ + h]), scale) : -INFINITY;
         over |= sc[h] > m_run[h] + TC_TAU;
         alpha[h] = 1.0f;
       }
-      if (sm_any(over || *abort != 0)) {
-        if (sm_any(*abort != 0)) break;  // a uniform decision: the named barriers stay matched
+      if (grp_any(g, over || *abort != 0)) {
+        if (grp_any(g, *abort != 0)) break;  // a uniform decision: the named barriers stay matched
         // the tile's exact max becomes the reference
+        float* rg = red + g * 64;
 #pragma unroll
-        for (int h = 0; h < NQ; h++)
+        for (int h = 0; h < VHC; h++)
           if (h < VH) {
             const float mw = warp_max(sc[h]);
-            if (lane == 0) red[wi * 16 + h] = mw;
+            if (lane == 0) rg[wq * 16 + h] = mw;
           }
-        sm_sync();
+        grp_sync(g);
 #pragma unroll
-        for (int h = 0; h < NQ; h++)
+        for (int h = 0; h < VHC; h++)
           if (h < VH) {
-            const float mt = fmaxf(fmaxf(red[h], red[16 + h]), fmaxf(red[32 + h], red[48 + h]));
+            const float mt = fmaxf(fmaxf(rg[h], rg[16 + h]), fmaxf(rg[32 + h], rg[48 + h]));
             const float m_new = fmaxf(m_run[h], mt);
             alpha[h] = m_run[h] == -INFINITY ? 0.0f : expf(m_run[h] - m_new);
             m_run[h] = m_new;
             l_thr[h] *= alpha[h];
           }
       }
-      uint8_t* pt = p_t + sb * S::OP;
+      uint8_t* pt = p_t + g * S::OP;
 #pragma unroll
-      for (int h = 0; h < NQ; h++)
-        if (h < VH) {
-          const float pv = sc[h] == -INFINITY ? 0.0f : expf(sc[h] - m_run[h]);
-          l_thr[h] += pv;
-          const __half ph = __float2half_rn(pv);
-          *reinterpret_cast<__half*>(pt + op_off(h, r)) = ph;
-          *reinterpret_cast<__half*>(pt + op_off(NQ + h, r)) = __float2half_rn(pv - __half2float(ph));
-        }
+      for (int h = 0; h < VHC; h++) {
+        const float pv = sc[h] == -INFINITY ? 0.0f : expf(sc[h] - m_run[h]);
+        l_thr[h] += pv;
+        const __half ph = __float2half_rn(pv);
+        *reinterpret_cast<__half*>(pt + op_off(h, r)) = ph;
+        *reinterpret_cast<__half*>(pt + op_off(NQ + h, r)) = __float2half_rn(pv - __half2float(ph));
+      }
       // V rows at positions not yet written may hold anything: zero them (P is 0 there)
       if (t >= L) {
 #pragma unroll
@@ -1539,32 +1580,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_con
             *reinterpret_cast<uint4*>(vbox(st, b) + r * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
       }
       fence_async_smem();
-      mbar_arrive(&p_full[sb]);
-      if (i >= 1) fold(i - 1, alpha_prev);
+      mbar_arrive(&p_full[g]);
 #pragma unroll
-      for (int h = 0; h < NQ; h++) alpha_prev[h] = alpha[h];
+      for (int h = 0; h < VHC; h++) alpha_prev[h] = alpha[h];
+      last = i;
     }
-    if (n_tiles >= 1 && !*abort) fold(n_tiles - 1, alpha_prev);
-    // the sums over the positions, once
+    if (last >= 0 && !*abort) fold(last, alpha_prev);
+    // the sums over the group's positions, once
 #pragma unroll
-    for (int h = 0; h < NQ; h++)
+    for (int h = 0; h < VHC; h++)
       if (h < VH) {
         const float sw = warp_sum(l_thr[h]);
-        if (lane == 0) red[wi * 16 + h] = sw;
+        if (lane == 0) red[g * 64 + wq * 16 + h] = sw;
       }
-    sm_sync();
-    float* o_s = reinterpret_cast<float*>(base);  // stage 0, idle now
-    float* ml = reinterpret_cast<float*>(base + S::STAGE);
+    // both groups' last folds are done, so every MMA has completed: the
+    // stages are idle.  Group g's o goes to stage 0 at g * NQ * HD, its
+    // (max, sum) to stage 1 at 32 g.
+    both_sync();
+    float* o_g = reinterpret_cast<float*>(base) + g * NQ * HD;
+    float* ml = reinterpret_cast<float*>(base + S::STAGE) + 32 * g;
 #pragma unroll
-    for (int h = 0; h < NQ; h++)
-      if (h < VH) o_s[h * HD + r] = o_acc[h];
-    if (tid < VH) {
+    for (int h = 0; h < VHC; h++)
+      if (h < VH) o_g[h * HD + r] = o_acc[h];
+    if (r < VH) {
       float mv = m_run[0];
 #pragma unroll
-      for (int h = 1; h < NQ; h++)
-        if (h == tid) mv = m_run[h];
-      ml[tid] = mv;
-      ml[16 + tid] = (red[tid] + red[16 + tid]) + (red[32 + tid] + red[48 + tid]);
+      for (int h = 1; h < VHC; h++)
+        if (h == r) mv = m_run[h];
+      const float* rg = red + g * 64;
+      ml[r] = mv;
+      ml[16 + r] = (rg[r] + rg[16 + r]) + (rg[32 + r] + rg[48 + r]);
     }
   }
   if (!ok) *abort = 1;
@@ -1572,7 +1617,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_con
   __syncthreads();
   tc_fence_after();
   if (*abort && tid == 0 && a.err) atomicExch(a.err, ERR_TIMEOUT);
-  if (wi == 5) tc_dealloc(tmem, TC_COLS);
+  if (wi == TC_MMA_WARP) tc_dealloc(tmem, TC_COLS);
+  {
+    // the two groups' partials -> this split's (max, sum) in stage 1 [0, 32)
+    // and o in stage 0 [0, VH * HD)
+    float* o_s = reinterpret_cast<float*>(base);
+    float* ml = reinterpret_cast<float*>(base + S::STAGE);
+    __shared__ float wg[2][16];
+    if (tid < VH) {
+      const float m0 = ml[tid], m1 = ml[32 + tid], mx = fmaxf(m0, m1);
+      const float w0 = m0 == -INFINITY ? 0.0f : expf(m0 - mx), w1 = m1 == -INFINITY ? 0.0f : expf(m1 - mx);
+      wg[0][tid] = w0;
+      wg[1][tid] = w1;
+      ml[tid] = mx;
+      ml[16 + tid] = fmaf(ml[16 + tid], w0, ml[48 + tid] * w1);
+    }
+    __syncthreads();
+    for (int e = tid; e < VH * HD; e += TC_THREADS) {
+      const int vh = e / HD;
+      o_s[e] = fmaf(o_s[e], wg[0][vh], o_s[NQ * HD + e] * wg[1][vh]);
+    }
+    __syncthreads();
+  }
 
   // ---- this split's (max, sum, o): the final rows with one split, else a
   // partial for attn_merge_tc (stage 0 holds o, stage 1 m / l)
@@ -1585,40 +1651,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_decode_tc(const __grid_con
       const int row = vh / group, head = kvh * group + vh % group;
       out[(size_t)(row0 + row) * q_stride + head * HD + d] = o_s[e] / ml[16 + vh];
     }
-    return;
-  }
-  namespace cg = cooperative_groups;
-  cg::cluster_group cluster = cg::this_cluster();
-  const int C = (int)cluster.num_blocks();
-  if (C == a.n_splits) {
-    // the splits of this kv head form one cluster: they meet through
-    // distributed shared memory, CTA r finishing its share of the outputs
-    __shared__ float w_c[16 * 16];  // [vh][split] weights exp(m_j - max)
-    __shared__ float l_c[16];
-    cluster.sync();
-    for (int vh = wi; vh < VH; vh += TC_THREADS / 32) {
-      float mj = -INFINITY, lj = 0.0f;
-      if (lane < C) {
-        mj = *cluster.map_shared_rank(ml + vh, lane);
-        lj = *cluster.map_shared_rank(ml + 16 + vh, lane);
-      }
-      const float mx = warp_max(mj);
-      const float w = mj == -INFINITY ? 0.0f : expf(mj - mx);
-      const float lt = warp_sum(w * lj);
-      if (lane < C) w_c[vh * 16 + lane] = w;
-      if (lane == 0) l_c[vh] = lt;
-    }
-    __syncthreads();
-    const int E = VH * HD, chunk = (E + C - 1) / C;
-    const int e_end = min(E, ((int)cluster.block_rank() + 1) * chunk);
-    for (int e = (int)cluster.block_rank() * chunk + tid; e < e_end; e += TC_THREADS) {
-      const int vh = e / HD, d = e - vh * HD;
-      float acc = 0.0f;
-      for (int j = 0; j < C; j++) acc = fmaf(*cluster.map_shared_rank(o_s + e, j), w_c[vh * 16 + j], acc);
-      const int row = vh / group, head = kvh * group + vh % group;
-      out[(size_t)(row0 + row) * q_stride + head * HD + d] = acc / l_c[vh];
-    }
-    cluster.sync();  // every CTA's shared memory stays alive until the others have read it
     return;
   }
   float* part_ml = sq ? sq->part_ml : a.part_ml;
@@ -1855,93 +1887,65 @@ static int device_sms() {
 
 // tcgen05 attention: one CTA per SM across (splits, kv heads, sequences);
 // the split count is capped by the partial scratch the caller sized
-// Cluster size for one decode sequence over n_kv kv heads: the largest C <= 16
-// for which all n_kv clusters of `kern` are resident at once (0: none).
-// Asked once per device, kernel and n_kv.
-static int tc_cluster_size(const void* kern, size_t smem, int n_kv) {
-  static std::mutex mu;
-  static std::map<std::tuple<int, const void*, int>, int> cache;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  std::lock_guard<std::mutex> lock(mu);
-  auto it = cache.find({dev, kern, n_kv});
-  if (it != cache.end()) return it->second;
-  int best = 0;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
-    for (int c = 16; c >= 2 && !best; c--) {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(c, n_kv);
-      cfg.blockDim = dim3(TC_THREADS);
-      cfg.dynamicSmemBytes = smem;
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = c;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n >= n_kv) best = c;
-    }
-  }
-  cudaGetLastError();
-  cache[{dev, kern, n_kv}] = best;
-  return best;
+template <int HD, int NQ, int VHC>
+static const void* tc_kernel_v(bool two) {
+  return two ? (const void*)attn_decode_tc<HD, NQ, 2, VHC> : (const void*)attn_decode_tc<HD, NQ, 3, VHC>;
+}
+// the kernel for launches of at most `vh` virtual heads
+template <int HD>
+static const void* tc_kernel(int vh, bool two) {
+  if (vh <= 2) return tc_kernel_v<HD, 8, 2>(two);
+  if (vh <= 4) return tc_kernel_v<HD, 8, 4>(two);
+  if (vh <= 8) return tc_kernel_v<HD, 8, 8>(two);
+  return tc_kernel_v<HD, 16, 16>(two);
 }
 
-template <int HD, int NQ>
-static const void* tc_kernel(bool two) {
-  return two ? (const void*)attn_decode_tc<HD, NQ, 2> : (const void*)attn_decode_tc<HD, NQ, 3>;
+// Launch shape of the tcgen05 decode kernel for `n_seq` sequences.
+struct TcPlan {
+  int splits = 1;
+  bool two = false;  // two K/V stages (at most two tiles per CTA), else three
+  int max_rows = 0, max_vh = 0;
+};
+template <int HD>
+static bool tc_plan(const AttnArgs& a, int n_seq, TcPlan& p) {
+  const int group = a.n_heads / a.n_kv;
+  // up to 8 virtual heads per launch run the narrow form (N = 16), else N = 32
+  const bool narrow = a.m * group <= 8;
+  p.max_rows = (narrow ? 8 : 16) / group;
+  if (p.max_rows < 1) return false;
+  p.max_vh = std::min(a.m, p.max_rows) * group;
+  const int cap = a.cap > 0 ? a.cap : a.pos0 + a.m;
+  auto pick = [&](int splits) {  // at most two tiles per CTA: two stages, else three
+    return (cap + splits - 1) / splits <= 2 * TC_C;
+  };
+  // one CTA per SM over (splits, kv heads, sequences); the splits of a kv
+  // head meet in its last CTA or in a merge kernel behind.  (Clusters of a kv
+  // head's splits merging through distributed shared memory measured slower:
+  // fewer SMs, and the cluster waits for its slowest CTA at two barriers.)
+  p.splits = std::max(1, std::min(a.n_splits, device_sms() / (a.n_kv * n_seq)));
+  p.two = pick(p.splits);
+  return true;
 }
 
 template <int HD>
 static cudaError_t tc_go(const AttnArgs& a, cudaStream_t st, bool pdl, int n_seq) {
   const int group = a.n_heads / a.n_kv;
-  // up to 8 virtual heads per launch run the narrow form (N = 16), else N = 32
-  const bool narrow = a.m * group <= 8;
-  const int max_rows = (narrow ? 8 : 16) / group;
-  if (max_rows < 1) return cudaErrorInvalidValue;
-  const int cap = a.cap > 0 ? a.cap : a.pos0 + a.m;
-  auto pick = [&](int splits) {  // at most two tiles per CTA: two stages, else three
-    return (cap + splits - 1) / splits <= 2 * TC_C;
-  };
+  TcPlan pl;
+  if (!tc_plan<HD>(a, n_seq, pl)) return cudaErrorInvalidValue;
+  const int max_rows = pl.max_rows, max_vh = pl.max_vh;
+  const bool two = pl.two;
   AttnArgs aa = a;
-  // one sequence: the splits of a kv head as one cluster (merged in distributed
-  // shared memory) when the clusters fit; otherwise one CTA per SM over
-  // (splits, kv heads, sequences) and a merge kernel behind
-  int cluster = 0;
-  bool two = false;
-  if (n_seq == 1) {
-    for (int c = 16; c >= 2 && !cluster; c--) {
-      const bool t = pick(c);
-      const int cs = tc_cluster_size(narrow ? tc_kernel<HD, 8>(t) : tc_kernel<HD, 16>(t),
-                                     t ? TcSmem<HD, 2>::bytes : TcSmem<HD, 3>::bytes, a.n_kv);
-      if (cs == c) {
-        cluster = c;
-        two = t;
-      } else if (cs > 0 && cs < c) {
-        c = cs + 1;  // retry at the size that fits
-      }
-    }
-  }
-  if (cluster) {
-    aa.n_splits = cluster;
-  } else {
-    aa.n_splits = std::max(1, std::min(a.n_splits, device_sms() / (a.n_kv * n_seq)));
-    two = pick(aa.n_splits);
-  }
-  const void* kern = narrow ? tc_kernel<HD, 8>(two) : tc_kernel<HD, 16>(two);
+  aa.n_splits = pl.splits;
+  const void* kern = tc_kernel<HD>(max_vh, two);
   const size_t smem = two ? TcSmem<HD, 2>::bytes : TcSmem<HD, 3>::bytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   // split partials: merged by the kernel's last CTA when every split's o rows
   // fit its idle stages, else by attn_merge_tc behind it
   const size_t stage_bytes = TcSmem<HD, 2>::STAGE;
-  const int max_vh = std::min(a.m, max_rows) * group;
-  aa.tail_merge = !cluster && aa.n_splits > 1 && aa.n_splits <= 64 &&
+  aa.tail_merge = aa.n_splits > 1 && aa.n_splits <= 64 &&
                   (size_t)aa.n_splits * max_vh * HD * 4 <= (two ? 1 : 2) * stage_bytes;
-  const bool merge = aa.n_splits > 1 && !cluster && !aa.tail_merge;
+  const bool merge = aa.n_splits > 1 && !aa.tail_merge;
   if (merge) {
     e = cudaFuncSetAttribute((const void*)attn_merge_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)TC_MERGE_SMEM);
@@ -1950,15 +1954,8 @@ static cudaError_t tc_go(const AttnArgs& a, cudaStream_t st, bool pdl, int n_seq
   for (int row0 = 0; row0 < a.m; row0 += max_rows) {
     int n_rows = min(max_rows, a.m - row0);
     void* args[] = {&aa, (void*)&row0, (void*)&n_rows};
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[1];
     int na = 0;
-    if (cluster) {
-      attr[na].id = cudaLaunchAttributeClusterDimension;
-      attr[na].val.clusterDim.x = cluster;
-      attr[na].val.clusterDim.y = 1;
-      attr[na].val.clusterDim.z = 1;
-      na++;
-    }
     if (pdl && row0 == 0) {
       attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
       attr[na].val.programmaticStreamSerializationAllowed = 1;

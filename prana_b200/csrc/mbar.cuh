@@ -31,6 +31,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
       : "memory");
   return ok != 0;
 }
+// non-blocking: has the phase of the given parity completed?
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
 // ~2^22 polls, each of which may itself suspend for a hardware-chosen time:
 // far beyond any healthy copy.  Returns false on timeout.
 constexpr uint32_t kMbarPolls = 1u << 22;
