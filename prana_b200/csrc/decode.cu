@@ -36,9 +36,11 @@ constexpr int DG_THREADS = DG_WARPS * 32;
 constexpr int DG_RPW = 2;  // rows per warp; even, so RoPE and gate/up pairs never straddle warps
 
 // Units a lane loads per chunk: enough 128-bit loads in flight per lane
-// without spilling (a Q4_0 unit is 18 bytes, Q8_0 34, Q4_K 48, Q6_K 58).
-template <int T> constexpr int chunk_units() { return T == T_Q4_0 ? 4 : 2; }
-int gemv_chunk_units(int type) { return type == T_Q4_0 ? 4 : 2; }
+// without spilling (a Q4_0 unit is 18 bytes, Q8_0 34, Q4_K 48, Q6_K 58).  At
+// batch 1 two chunks per lane are in flight (the next one's while the current
+// one computes), so the 48- and 58-byte units go one per chunk.
+template <int T> constexpr int chunk_units() { return T == T_Q4_0 ? 4 : (T == T_Q4_K || T == T_Q6_K) ? 1 : 2; }
+int gemv_chunk_units(int type) { return type == T_Q4_0 ? 4 : (type == T_Q4_K || type == T_Q6_K) ? 1 : 2; }
 
 // Byte offset of the f32 staging row in a CTA's shared memory: after the int8
 // rows, scales, sums and partial sums, rounded up to 16 bytes.
@@ -356,7 +358,7 @@ __global__ void __launch_bounds__(DG_THREADS, 2) stream_gemv(const StreamArgs g)
   bool first = true;
   // Batch 1 with whole rows per warp: a flat sequence of (row group, chunk)
   // items with the next item's weights in flight while the current one computes.
-  constexpr bool kPipe = M == 1 && (T == T_Q4_0 || T == T_Q8_0 || T == T_Q8S);
+  constexpr bool kPipe = M == 1;
   if (kPipe && ks == 1) {
     Unit<T> nb[DG_RPW][CH];
     int c0 = u_lo, gcur = g_first;

@@ -164,6 +164,18 @@ __device__ __forceinline__ void q4k_scale_min(int j, const uint8_t* s, int& sc, 
     mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
   }
 }
+// Q4_K (scale, min) of sub-blocks 2p and 2p + 1 (kquant.rs:52-61) taken from
+// the header's packed words y = bytes 0-3, z = 4-7, w = 8-11 with shifts, so
+// the twelve bytes never go through a local array (p differs per lane).
+__device__ __forceinline__ void q4k_pair_scales(int p, const uint4& meta, int& sc1, int& m1, int& sc2, int& m2) {
+  const int sh = 8 * ((2 * p) & 3);
+  const unsigned y = meta.y >> sh, z = meta.z >> sh, w = meta.w >> sh;
+  const bool hi = p >= 2;
+  sc1 = hi ? (int)((w & 0xFu) | (((y >> 6) & 3u) << 4)) : (int)(y & 63u);
+  m1 = hi ? (int)(((w >> 4) & 0xFu) | (((z >> 6) & 3u) << 4)) : (int)(z & 63u);
+  sc2 = hi ? (int)(((w >> 8) & 0xFu) | (((y >> 14) & 3u) << 4)) : (int)((y >> 8) & 63u);
+  m2 = hi ? (int)(((w >> 12) & 0xFu) | (((z >> 14) & 3u) << 4)) : (int)((z >> 8) & 63u);
+}
 // Q6_K quarter: per-group (g = 0..3) sums over 16 elements of (q6 − 32)·qa.
 __device__ __forceinline__ void q6_words(unsigned lo, unsigned hi, unsigned qh, unsigned q[4]) {
   const unsigned m4 = 0x0F0F0F0Fu, m2 = 0x03030303u;
@@ -228,14 +240,9 @@ __device__ __forceinline__ void accum_unit(const Unit<T_Q4_0>& x, int u, const A
 template <int M>
 __device__ __forceinline__ void accum_unit(const Unit<T_Q4_K>& x, int u, const Acts& a, int m_rt, float (&acc)[M]) {
   const float d = h2f((unsigned short)(x.meta.x & 0xffffu)), dmin = h2f((unsigned short)(x.meta.x >> 16));
-  uint8_t sb[12];
-  *reinterpret_cast<unsigned*>(sb) = x.meta.y;
-  *reinterpret_cast<unsigned*>(sb + 4) = x.meta.z;
-  *reinterpret_cast<unsigned*>(sb + 8) = x.meta.w;
   const int p = u & 3;
   int sc1, m1, sc2, m2;
-  q4k_scale_min(2 * p, sb, sc1, m1);
-  q4k_scale_min(2 * p + 1, sb, sc2, m2);
+  q4k_pair_scales(p, x.meta, sc1, m1, sc2, m2);
   const float dsc1 = __fmul_rn(d, (float)sc1), dm1 = __fmul_rn(dmin, (float)m1);
   const float dsc2 = __fmul_rn(d, (float)sc2), dm2 = __fmul_rn(dmin, (float)m2);
   const int g_lo = (u >> 2) * 8 + 2 * p;
@@ -254,7 +261,12 @@ template <int M>
 __device__ __forceinline__ void accum_unit(const Unit<T_Q6_K>& x, int u, const Acts& a, int m_rt, float (&acc)[M]) {
   const float d = h2f(x.d);
   const int b = u >> 2, h = (u >> 1) & 1, half16 = u & 1;
-  const int8_t* scb = reinterpret_cast<const int8_t*>(&x.sc);
+  float scf[4];  // sub-block scales of this quarter: int8 at byte 2g + half16 of x.sc
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    const unsigned word = g < 2 ? x.sc.x : x.sc.y;
+    scf[g] = (float)(int)(int8_t)((word >> (8 * ((g * 2 + half16) & 3))) & 0xffu);
+  }
 #pragma unroll
   for (int m = 0; m < M; m++)
     if (m < m_rt) {
@@ -263,7 +275,7 @@ __device__ __forceinline__ void accum_unit(const Unit<T_Q6_K>& x, int u, const A
 #pragma unroll
       for (int g = 0; g < 4; g++) {
         const float sa = a.s[m * a.G + b * 8 + h * 4 + g];
-        acc[m] = fmaf(__fmul_rn(__fmul_rn(d, sa), (float)scb[g * 2 + half16]), (float)s[g], acc[m]);
+        acc[m] = fmaf(__fmul_rn(__fmul_rn(d, sa), scf[g]), (float)s[g], acc[m]);
       }
     }
 }
@@ -350,14 +362,9 @@ __device__ __forceinline__ void accum_r(const Unit<T_Q4_0>& x, const ActU<T_Q4_0
 }
 __device__ __forceinline__ void accum_r(const Unit<T_Q4_K>& x, const ActU<T_Q4_K>& a, int u, float& acc) {
   const float d = h2f((unsigned short)(x.meta.x & 0xffffu)), dmin = h2f((unsigned short)(x.meta.x >> 16));
-  uint8_t sb[12];
-  *reinterpret_cast<unsigned*>(sb) = x.meta.y;
-  *reinterpret_cast<unsigned*>(sb + 4) = x.meta.z;
-  *reinterpret_cast<unsigned*>(sb + 8) = x.meta.w;
   const int p = u & 3;
   int sc1, m1, sc2, m2;
-  q4k_scale_min(2 * p, sb, sc1, m1);
-  q4k_scale_min(2 * p + 1, sb, sc2, m2);
+  q4k_pair_scales(p, x.meta, sc1, m1, sc2, m2);
   const float dsc1 = __fmul_rn(d, (float)sc1), dm1 = __fmul_rn(dmin, (float)m1);
   const float dsc2 = __fmul_rn(d, (float)sc2), dm2 = __fmul_rn(dmin, (float)m2);
   const unsigned m = 0x0F0F0F0Fu;

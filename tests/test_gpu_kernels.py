@@ -106,6 +106,21 @@ def test_gemv_large_rows(gpu, oracle):
         assert rel(fn(cuda(a), gw, 1).cpu().numpy(), om.matmul(a, oracle.TIER_SCALAR)) < GEMV_TOL
 
 
+@pytest.mark.parametrize("ty", TYPES)
+@pytest.mark.parametrize("k", [768, 4096])
+def test_gemv_batch1_pipeline(gpu, oracle, ty, k):
+    """Batch 1 with enough rows that every warp streams whole rows (no K split):
+    the double-buffered path that walks (row group, chunk) items, including
+    rows of several chunks (K = 4096) and rows shorter than one warp's chunk."""
+    rows = 2402
+    w = synth.matrix(ty, rows, k, seed=400 + ty + k)
+    gw = K.QuantMatrix(ty, rows, k, w)
+    om = oracle.OMatrix(ty, rows, k, w)
+    a = np.random.default_rng(k).standard_normal((1, k)).astype(np.float32)
+    fn = K.matmul_q8_f32 if ty == TYPE_Q8_0 else K.matmul_kquant_f32
+    assert rel(fn(cuda(a), gw, 1).cpu().numpy(), om.matmul(a, oracle.TIER_SCALAR)) < GEMV_TOL
+
+
 def test_rmsnorm(gpu, oracle):
     import ctypes as C
 
