@@ -399,6 +399,11 @@ static int matmul_common(prana_ctx* c, const prana_weight* w, const float* a, co
     PRANA_CK(e);
     return PRANA_OK;
   }
+  // Consecutive calls chain by programmatic dependent launch, as the decode
+  // step's GEMVs do: the only reads a GEMV issues before its wait on the
+  // previous kernel are of its weights, which no kernel writes (uploads
+  // synchronize before they return), so its first weight loads overlap the
+  // previous kernel's tail while activations and outputs wait for it.
   for (size_t t0 = 0; t0 < n_tokens; t0 += 8) {
     const int m = (int)(n_tokens - t0 < 8 ? n_tokens - t0 : 8);
     StreamArgs sa{};
@@ -411,7 +416,7 @@ static int matmul_common(prana_ctx* c, const prana_weight* w, const float* a, co
     sa.asum = sum + t0 * G;
     sa.out = out + t0 * w->dw.rows;
     sa.err = c->err;
-    PRANA_CK(launch_stream(sa, EPI_STORE, PRO_Q, c->stream, false));
+    PRANA_CK(launch_stream(sa, EPI_STORE, PRO_Q, c->stream, true));
   }
   return PRANA_OK;
 }
