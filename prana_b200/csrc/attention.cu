@@ -2027,6 +2027,228 @@ cudaError_t launch_attn_decode_seqs(const AttnArgs& a, int n_seq, cudaStream_t s
   return cluster_go<64>(a, pl, st, pdl, n_seq);
 }
 
+// ---------------------------------------------------------------- tensor-core prefill attention
+//
+// Causal attention of the prompt rows over their own f32 K/V (attention.rs:
+// 236-284) with Q.K^T and P.V on the tensor cores: mma.sync m16n8k8 TF32, each
+// f32 operand split into a TF32 head and its remainder (x = hi + lo), three
+// MMAs per product (lo.hi + hi.lo + hi.hi), so scores and outputs keep about
+// 2^-21 relative accuracy.  A CTA owns PT_M consecutive virtual heads
+// (query row x head of the group) of one kv head, 16 per warp, and walks the
+// key positions up to its last row in tiles of KT (cp.async, two stages) with
+// a running maximum and sum per row; the division by the sum comes last.
+constexpr int PT_WARPS = 4;
+constexpr int PT_M = 16 * PT_WARPS;  // virtual heads per CTA
+
+template <int HD>
+struct PtCfg {
+  static constexpr int KT = HD <= 64 ? 64 : 32;  // key positions per tile
+  // row pitches (floats) that make every fragment load of a warp hit 32
+  // distinct banks: K, Q and P rows at 4g + t, V rows at 8t + g
+  static constexpr int ROWK = HD + 4, ROWV = HD + 8, ROWQ = HD + 4, ROWP = KT + 4;
+  static constexpr int STAGE = KT * (ROWK + ROWV);  // floats
+  static constexpr size_t SMEM = sizeof(float) * ((size_t)2 * STAGE + (size_t)PT_M * ROWQ + (size_t)PT_M * ROWP);
+};
+
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+  const uint32_t h = __float_as_uint(x) & 0xffffe000u;
+  hi = h;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(x - __uint_as_float(h)));
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// d += a.b with split operands: the two small cross terms first
+__device__ __forceinline__ void mma_tf32x3(float (&d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                           const uint32_t (&bh)[2], const uint32_t (&bl)[2]) {
+  mma_tf32(d, al, bh);
+  mma_tf32(d, ah, bl);
+  mma_tf32(d, ah, bh);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(PT_WARPS * 32) attn_prefill_tc(const PrefillAttnArgs a) {
+  using C = PtCfg<HD>;
+  constexpr int KT = C::KT, NTS = KT / 8, NTO = HD / 8, KS = HD / 8, CPR = HD / 4;
+  extern __shared__ __align__(16) float pt_sm[];
+  float* kv_s = pt_sm;                     // [2][K: KT x ROWK, V: KT x ROWV]
+  float* q_s = kv_s + 2 * C::STAGE;        // [PT_M][ROWQ]
+  float* p_s = q_s + PT_M * C::ROWQ;       // [PT_M][ROWP]
+  const int group = a.n_heads / a.n_kv, kvh = blockIdx.y;
+  const int VH = a.n * group;
+  const int vh0 = ((int)gridDim.x - 1 - (int)blockIdx.x) * PT_M;  // the longest rows start first
+  const int tid = threadIdx.x, lane = tid & 31, wi = tid >> 5, g = lane >> 2, t4 = lane & 3;
+  const int q_stride = a.n_heads * HD, kv_stride = a.n_kv * HD;
+  const int n_tiles = (min(VH, vh0 + PT_M) - 1) / group / KT + 1;
+
+  auto load_tile = [&](int stage, int t0) {
+    float* ks = kv_s + stage * C::STAGE;
+    float* vs = ks + KT * C::ROWK;
+    for (int c = tid; c < 2 * KT * CPR; c += PT_WARPS * 32) {
+      const int which = c / (KT * CPR), rem = c - which * (KT * CPR), r = rem / CPR, ch = rem - r * CPR;
+      const int t = t0 + r;
+      float* dst = (which ? vs + r * C::ROWV : ks + r * C::ROWK) + ch * 4;
+      if (t < a.n)
+        cp_async16(dst, (which ? a.v : a.k) + (size_t)t * kv_stride + kvh * HD + ch * 4);
+      else  // past the prompt: zeros, masked below (finite, so 0 x V stays 0)
+        *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    cp_async_commit();
+  };
+  load_tile(0, 0);
+  for (int i = tid; i < PT_M * CPR; i += PT_WARPS * 32) {
+    const int r = i / CPR, c = i - r * CPR, vh = vh0 + r;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (vh < VH) {
+      const int row = vh / group, head = kvh * group + vh % group;
+      v = *reinterpret_cast<const float4*>(a.q + (size_t)row * q_stride + head * HD + c * 4);
+    }
+    *reinterpret_cast<float4*>(q_s + r * C::ROWQ + c * 4) = v;
+  }
+
+  // this thread's two fragment rows: virtual heads vw + g and vw + g + 8
+  const int vw = vh0 + 16 * wi;
+  const int va = min(vw + g, VH - 1), vb = min(vw + g + 8, VH - 1);  // rows past the end compute, never store
+  const int qa = va / group, qb = vb / group;                         // their query positions
+  const int wmax = min(vw + 15, VH - 1) / group;                      // the warp's last query position
+  const float scale = 1.0f / sqrtf((float)HD);
+  float o[NTO][4];
+#pragma unroll
+  for (int n = 0; n < NTO; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  const float* qw = q_s + 16 * wi * C::ROWQ;
+  float* pw = p_s + 16 * wi * C::ROWP;
+
+  for (int it = 0; it < n_tiles; it++) {
+    const int t0 = it * KT;
+    if (it + 1 < n_tiles) {
+      load_tile((it + 1) & 1, t0 + KT);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float* ks = kv_s + (it & 1) * C::STAGE;
+    const float* vs = ks + KT * C::ROWK;
+    if (t0 <= wmax) {
+      // ---- S = Q K^T (rows: virtual heads, columns: key positions t0 ..)
+      float s[NTS][4];
+#pragma unroll
+      for (int n = 0; n < NTS; n++) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll 2
+      for (int kk = 0; kk < KS; kk++) {
+        uint32_t ah[4], al[4];
+        tf32_split(qw[g * C::ROWQ + kk * 8 + t4], ah[0], al[0]);
+        tf32_split(qw[(g + 8) * C::ROWQ + kk * 8 + t4], ah[1], al[1]);
+        tf32_split(qw[g * C::ROWQ + kk * 8 + t4 + 4], ah[2], al[2]);
+        tf32_split(qw[(g + 8) * C::ROWQ + kk * 8 + t4 + 4], ah[3], al[3]);
+#pragma unroll
+        for (int n = 0; n < NTS; n++) {
+          uint32_t bh[2], bl[2];
+          tf32_split(ks[(n * 8 + g) * C::ROWK + kk * 8 + t4], bh[0], bl[0]);
+          tf32_split(ks[(n * 8 + g) * C::ROWK + kk * 8 + t4 + 4], bh[1], bl[1]);
+          mma_tf32x3(s[n], ah, al, bh, bl);
+        }
+      }
+      // ---- scale, causal mask, running maximum (a row's four lanes agree)
+      float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+      for (int n = 0; n < NTS; n++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+          const int tc = t0 + n * 8 + 2 * t4 + j;
+          s[n][j] = tc <= qa ? __fmul_rn(s[n][j], scale) : -INFINITY;
+          s[n][2 + j] = tc <= qb ? __fmul_rn(s[n][2 + j], scale) : -INFINITY;
+          mx_a = fmaxf(mx_a, s[n][j]);
+          mx_b = fmaxf(mx_b, s[n][2 + j]);
+        }
+#pragma unroll
+      for (int x = 1; x <= 2; x <<= 1) {
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, x));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, x));
+      }
+      // key 0 is in every row's first tile, so the running maxima are finite from then on
+      const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+      const float al_a = m_a == -INFINITY ? 0.f : expf(m_a - mn_a);
+      const float al_b = m_b == -INFINITY ? 0.f : expf(m_b - mn_b);
+      m_a = mn_a;
+      m_b = mn_b;
+      float ls_a = 0.f, ls_b = 0.f;
+#pragma unroll
+      for (int n = 0; n < NTS; n++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+          const float pa = s[n][j] == -INFINITY ? 0.f : expf(s[n][j] - mn_a);
+          const float pb = s[n][2 + j] == -INFINITY ? 0.f : expf(s[n][2 + j] - mn_b);
+          ls_a += pa;
+          ls_b += pb;
+          pw[g * C::ROWP + n * 8 + 2 * t4 + j] = pa;
+          pw[(g + 8) * C::ROWP + n * 8 + 2 * t4 + j] = pb;
+        }
+      l_a = fmaf(l_a, al_a, ls_a);
+      l_b = fmaf(l_b, al_b, ls_b);
+#pragma unroll
+      for (int n = 0; n < NTO; n++) {
+        o[n][0] *= al_a;
+        o[n][1] *= al_a;
+        o[n][2] *= al_b;
+        o[n][3] *= al_b;
+      }
+      __syncwarp();
+      // ---- O += P V
+#pragma unroll 2
+      for (int kk = 0; kk < KT / 8; kk++) {
+        uint32_t ah[4], al[4];
+        tf32_split(pw[g * C::ROWP + kk * 8 + t4], ah[0], al[0]);
+        tf32_split(pw[(g + 8) * C::ROWP + kk * 8 + t4], ah[1], al[1]);
+        tf32_split(pw[g * C::ROWP + kk * 8 + t4 + 4], ah[2], al[2]);
+        tf32_split(pw[(g + 8) * C::ROWP + kk * 8 + t4 + 4], ah[3], al[3]);
+#pragma unroll
+        for (int n = 0; n < NTO; n++) {
+          uint32_t bh[2], bl[2];
+          tf32_split(vs[(kk * 8 + t4) * C::ROWV + n * 8 + g], bh[0], bl[0]);
+          tf32_split(vs[(kk * 8 + t4 + 4) * C::ROWV + n * 8 + g], bh[1], bl[1]);
+          mma_tf32x3(o[n], ah, al, bh, bl);
+        }
+      }
+      __syncwarp();  // P is rewritten by the next tile
+    }
+    __syncthreads();  // every warp is done with this stage before it is refilled
+  }
+
+  // ---- out = O / sum
+#pragma unroll
+  for (int x = 1; x <= 2; x <<= 1) {
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, x);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, x);
+  }
+  const float inv_a = 1.0f / l_a, inv_b = 1.0f / l_b;
+  const int ra = vw + g, rb = vw + g + 8;
+  float* out_a = ra < VH ? a.out + (size_t)(ra / group) * q_stride + (kvh * group + ra % group) * HD : nullptr;
+  float* out_b = rb < VH ? a.out + (size_t)(rb / group) * q_stride + (kvh * group + rb % group) * HD : nullptr;
+#pragma unroll
+  for (int n = 0; n < NTO; n++) {
+    const int d = n * 8 + 2 * t4;
+    if (out_a) *reinterpret_cast<float2*>(out_a + d) = make_float2(o[n][0] * inv_a, o[n][1] * inv_a);
+    if (out_b) *reinterpret_cast<float2*>(out_b + d) = make_float2(o[n][2] * inv_b, o[n][3] * inv_b);
+  }
+}
+
+template <int HD>
+static cudaError_t prefill_tc_go(const PrefillAttnArgs& a, cudaStream_t st) {
+  using C = PtCfg<HD>;
+  auto k = attn_prefill_tc<HD>;
+  const cudaError_t e = cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+  if (e != cudaSuccess) return e;
+  const long long vh = (long long)a.n * (a.n_heads / a.n_kv);
+  k<<<dim3((unsigned)((vh + PT_M - 1) / PT_M), a.n_kv), PT_WARPS * 32, C::SMEM, st>>>(a);
+  return cudaGetLastError();
+}
+
 template <int HD>
 static cudaError_t prefill_go(const PrefillAttnArgs& a, cudaStream_t st) {
   const int group = a.n_heads / a.n_kv;
@@ -2044,12 +2266,16 @@ static cudaError_t prefill_go(const PrefillAttnArgs& a, cudaStream_t st) {
 
 cudaError_t launch_attn_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
   if (a.n_kv <= 0 || a.n_heads % a.n_kv || a.n < 1) return cudaErrorInvalidValue;
-  switch (a.hd) {
-    case 32: return prefill_go<32>(a, st);
-    case 48: return prefill_go<48>(a, st);
-    case 64: return prefill_go<64>(a, st);
-    case 96: return prefill_go<96>(a, st);
-    case 128: return prefill_go<128>(a, st);
+  // f32 K/V rows are read with 16-byte copies
+  if ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v) |
+       reinterpret_cast<uintptr_t>(a.out)) & 15)
+    return cudaErrorInvalidValue;
+  switch (a.hd) {  // tensor cores up to head dim 128; the CUDA-core kernel beyond
+    case 32: return prefill_tc_go<32>(a, st);
+    case 48: return prefill_tc_go<48>(a, st);
+    case 64: return prefill_tc_go<64>(a, st);
+    case 96: return prefill_tc_go<96>(a, st);
+    case 128: return prefill_tc_go<128>(a, st);
     case 256: return prefill_go<256>(a, st);
   }
   return cudaErrorInvalidValue;

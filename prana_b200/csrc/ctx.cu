@@ -583,6 +583,9 @@ int prana_attention(prana_ctx* c, const float* q, const float* k, const float* v
   NEED(c && q && k && v && out, "null argument");
   NEED(nkv > 0 && nh % nkv == 0, "n_heads must be a multiple of n_kv_heads");
   NEED(hd * (nh / nkv) <= 4096, "head_dim x group exceeds 4096");
+  NEED(!((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+          reinterpret_cast<uintptr_t>(out)) & 15),
+       "attention: q, k, v and out must be 16-byte aligned");
   if (!seq) return PRANA_OK;
   DevScope ds(c->device);
   PrefillAttnArgs a{q, k, v, (int)seq, (int)nh, (int)nkv, (int)hd, out};

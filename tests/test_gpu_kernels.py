@@ -210,10 +210,15 @@ def test_attention_verify(gpu, oracle, nh, nkv, hd, seq):
     assert rel(got, ref) < 2e-5
 
 
-@pytest.mark.parametrize("nh,nkv,hd,seq", [(6, 6, 48, 7), (14, 2, 64, 300), (32, 8, 128, 130)])
-def test_attention_prefill(gpu, oracle, nh, nkv, hd, seq):
+@pytest.mark.parametrize("nh,nkv,hd,seq,qscale", [(6, 6, 48, 7, 1.0), (14, 2, 64, 300, 1.0), (32, 8, 128, 130, 1.0),
+                                                  (14, 2, 64, 1100, 1.0), (8, 8, 32, 200, 4.0), (12, 4, 96, 77, 1.0),
+                                                  (4, 2, 256, 40, 1.0), (16, 2, 128, 257, 3.0), (3, 1, 64, 1, 1.0)])
+def test_attention_prefill(gpu, oracle, nh, nkv, hd, seq, qscale):
+    """Causal prefill attention over f32 in-window K/V: rows that end inside a
+    key tile, partial CTAs, one row, sharp softmaxes (qscale) and the CUDA-core
+    kernel at head dim 256."""
     rng = np.random.default_rng(7)
-    q = rng.standard_normal((seq, nh * hd)).astype(np.float32)
+    q = (qscale * rng.standard_normal((seq, nh * hd))).astype(np.float32)
     k = rng.standard_normal((seq, nkv * hd)).astype(np.float32)
     v = rng.standard_normal((seq, nkv * hd)).astype(np.float32)
     ref = np.empty_like(q)
