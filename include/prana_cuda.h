@@ -188,7 +188,7 @@ int prana_attention_decode_noalloc(prana_ctx *ctx, const float *q, const uint16_
 int prana_attention_verify(prana_ctx *ctx, const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
                            size_t pos0, size_t seq, size_t n_heads, size_t n_kv_heads, size_t head_dim,
                            float *out);
-/* attention (attention.rs:236-284): causal over f32 in-window K/V */
+/* attention (attention.rs:236-284): causal over f32 in-window K/V; q, k, v and out 16-byte aligned */
 int prana_attention(prana_ctx *ctx, const float *q, const float *k, const float *v, size_t seq, size_t n_heads,
                     size_t n_kv_heads, size_t head_dim, float *out);
 /* first index of the row maximum (infer.rs:560-568, sampler.rs:40-48) */
