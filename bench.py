@@ -814,7 +814,7 @@ def prana_arm(args):
         from datetime import timedelta
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     from prana_b200 import model as pm
 

@@ -186,7 +186,9 @@ def _cache(seed, rows, kv_dim):
 # tensor-core path: hd 64/128 with <= 16 query heads per kv head; CUDA-core path otherwise
 @pytest.mark.parametrize("nh,nkv,hd,pos", [(6, 6, 48, 0), (6, 6, 48, 255), (14, 2, 64, 2047), (32, 8, 128, 700),
                                            (12, 2, 128, 1023), (32, 8, 128, 4095), (8, 1, 64, 5), (4, 4, 64, 16),
-                                           (4, 4, 64, 129), (64, 2, 128, 300), (16, 16, 32, 77)])
+                                           (4, 4, 64, 129), (64, 2, 128, 300), (16, 16, 32, 77),
+                                           # one rank's shard of the 8B shape at 8, 4 and 2 GPUs
+                                           (4, 1, 128, 4095), (8, 2, 128, 4095), (16, 4, 128, 4095)])
 def test_attention_decode(gpu, oracle, nh, nkv, hd, pos):
     kc = _cache(1, pos + 1, nkv * hd)
     vc = _cache(2, pos + 1, nkv * hd)
