@@ -408,6 +408,11 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
     int grp = 0;
     bool ok = true;
     constexpr int NB = (32 / NC) < 1 ? 1 : ((32 / NC) < GS ? (32 / NC) : GS);  // slots per load batch (<= 32 registers)
+    // A stage that is one slot group read in one load batch (16-token tiles,
+    // one MMA per block): the group and batch offsets below are always 0, and
+    // saying so lets every block index, and with it the choice of the block's
+    // weight scale, resolve at compile time.
+    constexpr bool kOneGroup = GS == BLK * MPB && NB == GS;
     for (int s = 0; s < n_stage && ok; s++) {
       const int st = s % NS, sg = gstage(s);
       const uint8_t* sm = stage(st);
@@ -434,7 +439,8 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
         }
         tc_fence_after();
         const int cnt = min(GS, total - i0);
-        for (int b0 = 0; b0 < cnt; b0 += NB) {
+        for (int b0_ = 0; b0_ < cnt; b0_ += NB) {
+          const int b0 = kOneGroup ? 0 : b0_, ib = kOneGroup ? 0 : i0 + b0_;
           uint32_t v[NB][NC];
 #pragma unroll
           for (int k = 0; k < NB; k++)
@@ -451,7 +457,7 @@ __global__ void __launch_bounds__(QgLayout<T, NT>::THREADS, 1)
 #pragma unroll
           for (int k = 0; k < NB; k++) {
             if (b0 + k >= cnt) break;
-            const int i = i0 + b0 + k, j = i / MPB, h = i % MPB;
+            const int i = ib + k, j = i / MPB, h = i % MPB;
             const int b = sg * BLK + j;  // global block
             if (g.dots) {
               if (r < N)
