@@ -573,7 +573,8 @@ def suite_c2(torch, args, peak):
             "results": out,
             "algorithmic_bytes": "N*K*bpw (GGUF bytes) + M*(K + 8*K/32) + M*N*4",
             "l2": "weights rotate over copies totalling > 2.2 x 126 MB",
-            "path": "M <= 8: streaming dp4a GEMV; M > 8: tcgen05 block-scaled int8 GEMM (qgemm); "
+            "path": "M <= 8: streaming dp4a GEMV (6-8 rows of Q8_0 / Q4_0 / Q4_K with >= 8192 weight rows: qgemm); "
+                    "M > 8: tcgen05 block-scaled int8 GEMM (qgemm); "
                     "consecutive calls chained by programmatic dependent launch, as in the decode step",
             "cpu_baseline": {"results_m1_n4096": cpu, "cores": os.cpu_count(), "kind": "port",
                              "sample": "oracle matmul at batch 1, 1 s per format"},

@@ -367,11 +367,17 @@ static int matmul_common(prana_ctx* c, const prana_weight* w, const float* a, co
     }
     return PRANA_OK;
   }
+  // Rows go to the tensor cores above 8, and from 6 on for tall weights: the
+  // dp4a GEMV repeats its per-block dots for every row (issue-bound from about
+  // 5 rows) while the GEMM's cost is flat up to 16 (8 rows on [14336 x 4096]:
+  // Q8_0 48 -> 26 us, Q4_0 45 -> 28, Q4_K 73 -> 34; no gain at 4096 rows, nor
+  // for Q6_K, whose GEMM issues two MMAs per block).
+  const bool tc = n_tokens > 8 || (n_tokens >= 6 && w->dw.rows >= 8192 && w->dw.type != T_Q6_K);
   // scratch: the quantized rows when given f32 rows (quantize_acts first,
   // matmul.rs:169, kquant.rs:329), then the tensor-core GEMM's scale tables
   const size_t qb = (n_tokens * K + 255) & ~(size_t)255;
   const size_t act = a ? qb + ((n_tokens * G * 8 + 255) & ~(size_t)255) : 0;
-  const size_t gemm = n_tokens > 8 ? qgemm_scratch_bytes((int)n_tokens, (int)K) : 0;
+  const size_t gemm = tc ? qgemm_scratch_bytes((int)n_tokens, (int)K) : 0;
   void* sp = nullptr;
   if (act + gemm) {
     int rc = ctx_scratch(c, act + gemm, &sp);
@@ -386,7 +392,7 @@ static int matmul_common(prana_ctx* c, const prana_weight* w, const float* a, co
     s = ss;
     sum = mm;
   }
-  if (n_tokens > 8) {  // more than 8 rows: the tensor cores (qgemm.cu)
+  if (tc) {  // the tensor cores (qgemm.cu)
     QgemmArgs g{};
     g.w = w->dw;
     g.N = w->dw.rows;

@@ -94,6 +94,23 @@ def test_gemv_prefill_matches_oracle(gpu, oracle, ty):
     assert rel(got, ref) < GEMV_TOL
 
 
+@pytest.mark.parametrize("ty", TYPES)
+@pytest.mark.parametrize("n_tokens", [6, 8])
+def test_matmul_tall_weight_tensor_cores(gpu, oracle, ty, n_tokens):
+    """6-8 rows against a weight of >= 8192 rows take the tensor-core GEMM at
+    kernel level (the GEMV's cost grows with the rows, the GEMM's does not);
+    Q6_K stays on the GEMV."""
+    rows, k = 8200, 1024
+    w = synth.matrix(ty, rows, k, seed=50 + ty + n_tokens)
+    gw = K.QuantMatrix(ty, rows, k, w)
+    om = oracle.OMatrix(ty, rows, k, w)
+    a = acts(60 + n_tokens, n_tokens, k)
+    ref = om.matmul(a, oracle.TIER_SCALAR)
+    fn = K.matmul_q8_f32 if ty == TYPE_Q8_0 else K.matmul_kquant_f32
+    got = fn(cuda(a), gw, n_tokens).cpu().numpy()
+    assert rel(got, ref) < GEMV_TOL
+
+
 def test_gemv_large_rows(gpu, oracle):
     """Shapes of the 8B microbench at K=4096 (rows trimmed for oracle time)."""
     for ty in TYPES:
