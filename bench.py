@@ -656,7 +656,7 @@ def suite_c3(torch, args, peak):
             "metric": "decode tok/s at batch 1 (after a 2048-token prefill)", "unit": UNIT,
             "value": round(1000.0 / ms, 1), "ms_per_step": round(ms, 4),
             "e2e": {"value": round(1000.0 / ms_e2e, 1), "unit": UNIT, "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 4},
+                    "d2h_bytes_per_step": 8},
             "prefill": {"tokens": len(prompt) - 1, "ms": round(ms_prefill, 2),
                         "tok_s": round((len(prompt) - 1) * 1000.0 / ms_prefill, 1),
                         "path": "tensor-core GEMMs over the prompt rows; f32 in-window attention"},
@@ -718,7 +718,7 @@ def suite_c4q8(torch, args, peak):
         return {
             "metric": METRIC, "unit": UNIT, "value": round(1000.0 / ms, 2), "ms_per_step": round(ms, 4),
             "e2e": {"value": round(1000.0 / ms_e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 4},
+                    "d2h_bytes_per_step": 8},
             "step_roofline": {"bytes_per_token": bt, "achieved_gbs": round(bt / ms / 1e6, 1),
                               "frac": round(bt / ms / 1e6 / peak, 4)},
             "cpu_baseline": {"value": round(tps, 4), "unit": UNIT, "cores": threads, "kind": "port",
@@ -949,7 +949,7 @@ def prana_arm(args):
                        "exchange": ("peer memory" if model.peer_exchange else "nccl") if world > 1 else None,
                        "l2": "inputs larger than L2 (4.2 GB weights per step)"},
             "e2e": {"value": round(1000.0 / ms_e2e, 3), "unit": UNIT, "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 4},
+                    "d2h_bytes_per_step": 8},
             "roofline": roof, "peak_kind": peak_kind,
             "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": round(step_gbs, 1),
                               "frac": round(step_gbs / peak, 4)},

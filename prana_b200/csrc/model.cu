@@ -863,6 +863,20 @@ int check_err(prana_model* m) {
   return PRANA_OK;
 }
 
+// The error word read back beside a step's token (m->h_tok[1], pinned): one
+// synchronization per token instead of check_err's second copy and wait.
+static cudaError_t enqueue_err_read(prana_model* m, cudaStream_t st) {
+  return cudaMemcpyAsync(m->h_tok + 1, m->err, 4, cudaMemcpyDeviceToHost, st);
+}
+static int err_after_sync(prana_model* m) {
+  const unsigned e = m->h_tok[1];
+  if (e) {
+    cudaMemsetAsync(m->err, 0, 4, m->ctx->own);
+    return fail(PRANA_E_TIMEOUT, "a bounded device-side wait expired (error %u)", e);
+  }
+  return PRANA_OK;
+}
+
 int capture(prana_model* m, prana_kv* kv, bool loop, bool sampled, cudaGraphExec_t* out) {
   cudaStream_t st = m->ctx->own;
   for (int attempt = 0; attempt < 2; attempt++) {
@@ -1372,11 +1386,12 @@ int prana_forward(prana_model* m, prana_kv* kv, uint32_t token, size_t pos, floa
   PRANA_CK(cudaMemcpyAsync(m->d_tokpos, m->h_io, 8, cudaMemcpyHostToDevice, st));
   PRANA_CK(cudaGraphLaunch(kv->g_step, st));
   PRANA_CK(cudaMemcpyAsync(m->h_tok, m->dec->tok_out, 4, cudaMemcpyDeviceToHost, st));
+  PRANA_CK(enqueue_err_read(m, st));
   if (logits) PRANA_CK(cudaMemcpyAsync(logits, m->dec->logits, (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, st));
   PRANA_CK(cudaStreamSynchronize(st));
   if (next) *next = m->h_tok[0];
   kv->loop_active = false;
-  return check_err(m);
+  return err_after_sync(m);
   API_END
 }
 
@@ -1402,11 +1417,12 @@ int prana_forward_sampled(prana_model* m, prana_kv* kv, uint32_t token, size_t p
   PRANA_CK(cudaGraphLaunch(kv->g_step, st));  // the step leaves the whole logits row in HBM
   PRANA_CK(launch_sample(m->dec->logits, (int)m->cfg.vocab_size, m->d_sample, m->dec->tok_out, nullptr, st));
   PRANA_CK(cudaMemcpyAsync(m->h_tok, m->dec->tok_out, 4, cudaMemcpyDeviceToHost, st));
+  PRANA_CK(enqueue_err_read(m, st));
   PRANA_CK(cudaStreamSynchronize(st));
   *next = m->h_tok[0];
   s->next_u64();  // the draw the kernel took
   kv->loop_active = false;
-  return check_err(m);
+  return err_after_sync(m);
   API_END
 }
 
